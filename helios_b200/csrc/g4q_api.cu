@@ -1,0 +1,351 @@
+// g4q_api.cu -- the extern "C" boundary of libg4q (include/g4q.h).
+//
+// Mirrors the reference's C ABI conventions (native/gemma4_mlx/src/runtime.cc): a status
+// code per call, a thread-local last-error buffer (runtime.cc:46, 115-133, 816-823),
+// magic-tagged opaque handles allocated with new(std::nothrow) and invalidated on free
+// (runtime.cc:41-45, 841-846, 900-912), and no C++ exception crossing the boundary.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+
+#include "g4q.h"
+#include "g4q_internal.h"
+
+namespace g4q {
+
+static thread_local char g_last_error[512] = "";
+
+static G4qStatus fail(G4qStatus s, const std::string& msg) {
+    std::snprintf(g_last_error, sizeof(g_last_error), "%s", msg.c_str());
+    return s;
+}
+
+static G4qStatus ok() {
+    g_last_error[0] = '\0';
+    return G4Q_OK;
+}
+
+int current_device() {
+    int d = 0;
+    check_cuda(cudaGetDevice(&d), "cudaGetDevice");
+    return d;
+}
+
+int device_sm_count() {
+    static int cache[64] = {0};
+    const int d = current_device();
+    if (cache[d & 63] == 0) {
+        int n = 0;
+        check_cuda(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d), "cudaDeviceGetAttribute");
+        cache[d & 63] = n;
+    }
+    return cache[d & 63];
+}
+
+// Runs an entry point body, translating exceptions into a status + message.
+template <typename F>
+static G4qStatus guarded(const char* fn, F&& body) {
+    try {
+        body();
+        return ok();
+    } catch (const Error& e) {
+        return fail(e.status, std::string(fn) + ": " + e.what());
+    } catch (const std::bad_alloc&) {
+        return fail(G4Q_ERR_MEMORY_GUARD, std::string(fn) + ": host allocation failed");
+    } catch (const std::exception& e) {
+        return fail(G4Q_ERR_RUNTIME, std::string(fn) + ": " + e.what());
+    } catch (...) {
+        return fail(G4Q_ERR_RUNTIME, std::string(fn) + ": unknown native error");
+    }
+}
+
+static void require(bool cond, G4qStatus s, const std::string& msg) {
+    if (!cond) throw Error(s, msg);
+}
+
+static Weight* checked(const G4qWeight* h, const char* what) {
+    auto* w = reinterpret_cast<Weight*>(const_cast<G4qWeight*>(h));
+    require(w != nullptr, G4Q_ERR_INVALID_ARGUMENT, std::string(what) + " requires a non-null weight handle");
+    require(w->magic == kWeightMagic, G4Q_ERR_INVALID_ARGUMENT, std::string(what) + " received an invalid weight handle");
+    require(w->device == current_device(), G4Q_ERR_INVALID_ARGUMENT,
+            std::string(what) + ": the current CUDA device is not the handle's device");
+    return w;
+}
+
+static bool device_accessible(const void* p) {
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
+}
+
+static void require_aligned16(const void* p, const char* what) {
+    require((reinterpret_cast<uintptr_t>(p) & 15u) == 0, G4Q_ERR_INVALID_ARGUMENT,
+            std::string(what) + " must be 16-byte aligned");
+}
+
+}  // namespace g4q
+
+using namespace g4q;
+
+extern "C" {
+
+G4qStatus g4q_runtime_version(G4qVersionInfo* out) {
+    if (out == nullptr) return fail(G4Q_ERR_INVALID_ARGUMENT, "g4q_runtime_version requires a non-null out pointer");
+    out->abi_version = G4Q_ABI_VERSION;
+    out->backend_name = "g4q_b200";
+    out->backend_version = "sm_100a tcgen05/mma-sync affine-q4g64 v1";
+    return ok();
+}
+
+G4qStatus g4q_get_last_error(char* buffer, size_t buffer_len) {
+    if (buffer == nullptr || buffer_len == 0)
+        return fail(G4Q_ERR_INVALID_ARGUMENT, "g4q_get_last_error requires a writable buffer");
+    std::snprintf(buffer, buffer_len, "%s", g_last_error);
+    return G4Q_OK;
+}
+
+G4qStatus g4q_weight_create(int64_t rows, int64_t cols, int32_t bits, int32_t group_size, G4qWeight** out) {
+    return guarded("g4q_weight_create", [&] {
+        require(out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null out pointer");
+        *out = nullptr;
+        require(rows > 0 && cols > 0, G4Q_ERR_INVALID_ARGUMENT, "rows and cols must be positive");
+        require(bits == 4 && group_size == 64, G4Q_ERR_UNSUPPORTED_CONFIG,
+                "the kernel layout supports bits=4, group_size=64 (got bits=" + std::to_string(bits) +
+                    ", group_size=" + std::to_string(group_size) + ")");
+        require(rows % 16 == 0, G4Q_ERR_UNSUPPORTED_CONFIG, "rows must be a multiple of 16");
+        require(cols % 64 == 0, G4Q_ERR_UNSUPPORTED_CONFIG, "cols must be a multiple of 64");
+        Weight* w = new (std::nothrow) Weight();
+        require(w != nullptr, G4Q_ERR_MEMORY_GUARD, "host allocation failed");
+        w->N = rows;
+        w->K = cols;
+        w->bits = bits;
+        w->group_size = group_size;
+        w->device = current_device();
+        const size_t packed_bytes = (size_t)rows * cols / 2, sb_bytes = (size_t)rows * (cols / 64) * 4;
+        cudaError_t e = cudaMalloc(&w->packed, packed_bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&w->sb, sb_bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&w->d_flags, sizeof(int));
+        if (e == cudaSuccess) e = cudaMalloc(&w->argmax_scratch, 17 * sizeof(unsigned long long));
+        if (e == cudaSuccess) e = cudaMemset(w->d_flags, 0, sizeof(int));
+        if (e == cudaSuccess) e = cudaMemset(w->argmax_scratch, 0, 17 * sizeof(unsigned long long));
+        if (e != cudaSuccess) {
+            cudaFree(w->packed);
+            cudaFree(w->sb);
+            cudaFree(w->d_flags);
+            cudaFree(w->argmax_scratch);
+            delete w;
+            cudaGetLastError();
+            throw Error(G4Q_ERR_MEMORY_GUARD, std::string("device allocation failed: ") + cudaGetErrorString(e));
+        }
+        w->bytes = packed_bytes + sb_bytes;
+        w->magic = kWeightMagic;
+        *out = reinterpret_cast<G4qWeight*>(w);
+    });
+}
+
+G4qStatus g4q_weight_free(G4qWeight* h) {
+    return guarded("g4q_weight_free", [&] {
+        auto* w = reinterpret_cast<Weight*>(h);
+        require(w != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null weight handle");
+        require(w->magic == kWeightMagic, G4Q_ERR_INVALID_ARGUMENT, "received an invalid weight handle");
+        w->magic = 0;
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(w->device);
+        cudaFree(w->packed);
+        cudaFree(w->sb);
+        cudaFree(w->d_flags);
+        cudaFree(w->argmax_scratch);
+        cudaSetDevice(prev);
+        delete w;
+    });
+}
+
+G4qStatus g4q_weight_info(const G4qWeight* h, G4qWeightInfo* out) {
+    return guarded("g4q_weight_info", [&] {
+        Weight* w = checked(h, "g4q_weight_info");
+        require(out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null out pointer");
+        int flags = 0;
+        check_cuda(cudaMemcpy(&flags, w->d_flags, sizeof(int), cudaMemcpyDeviceToHost), "read handle flags");
+        out->rows = w->N;
+        out->cols = w->K;
+        out->bits = w->bits;
+        out->group_size = w->group_size;
+        out->device_bytes = w->bytes;
+        out->device = w->device;
+        out->fast_path_ok = (flags & 1) ? 0 : 1;
+        out->error_flags = flags & ~1;
+    });
+}
+
+G4qStatus g4q_weight_load(G4qWeight* h, int64_t dst_row0, const uint32_t* packed, const uint16_t* scales,
+                          const uint16_t* biases, int64_t src_rows, int64_t src_cols, int64_t src_row0,
+                          int64_t src_k0, int64_t n_rows, void* stream) {
+    return guarded("g4q_weight_load", [&] {
+        Weight* w = checked(h, "g4q_weight_load");
+        require(packed && scales && biases, G4Q_ERR_INVALID_ARGUMENT, "packed, scales and biases must be non-null");
+        require(src_rows > 0 && src_cols > 0 && src_cols % 64 == 0, G4Q_ERR_INVALID_ARGUMENT,
+                "source shape must be positive with cols % 64 == 0");
+        require(src_k0 >= 0 && src_k0 % 64 == 0 && src_k0 + w->K <= src_cols, G4Q_ERR_INVALID_ARGUMENT,
+                "column window must be group aligned and inside the source");
+        require(n_rows > 0 && n_rows % 16 == 0 && src_row0 >= 0 && src_row0 + n_rows <= src_rows,
+                G4Q_ERR_INVALID_ARGUMENT, "row window must be a positive multiple of 16 inside the source");
+        require(dst_row0 >= 0 && dst_row0 % 16 == 0 && dst_row0 + n_rows <= w->N, G4Q_ERR_INVALID_ARGUMENT,
+                "destination rows must be 16-aligned and inside the handle");
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        const int64_t ld_words = src_cols / 8, ld_groups = src_cols / 64;
+        const bool on_device = device_accessible(packed) && device_accessible(scales) && device_accessible(biases);
+        if (on_device) {
+            launch_repack(packed, scales, biases, ld_words, ld_groups, src_row0, src_k0, n_rows, *w, dst_row0, st);
+        } else {
+            // host source: stage the row window on the device, then repack
+            uint32_t* dw = nullptr;
+            uint16_t *ds = nullptr, *db = nullptr;
+            const size_t wb = (size_t)n_rows * ld_words * 4, gb = (size_t)n_rows * ld_groups * 2;
+            cudaError_t e = cudaMalloc(&dw, wb);
+            if (e == cudaSuccess) e = cudaMalloc(&ds, gb);
+            if (e == cudaSuccess) e = cudaMalloc(&db, gb);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(dw, packed + src_row0 * ld_words, wb, cudaMemcpyHostToDevice, st);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(ds, scales + src_row0 * ld_groups, gb, cudaMemcpyHostToDevice, st);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(db, biases + src_row0 * ld_groups, gb, cudaMemcpyHostToDevice, st);
+            if (e == cudaSuccess) {
+                try {
+                    launch_repack(dw, ds, db, ld_words, ld_groups, 0, src_k0, n_rows, *w, dst_row0, st);
+                } catch (...) {
+                    e = cudaErrorLaunchFailure;
+                }
+            }
+            if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+            cudaFree(dw);
+            cudaFree(ds);
+            cudaFree(db);
+            check_cuda(e, "staging a host-memory source");
+        }
+        check_cuda(cudaStreamSynchronize(st), "repack");
+        int flags = 0;
+        check_cuda(cudaMemcpy(&flags, w->d_flags, sizeof(int), cudaMemcpyDeviceToHost), "read handle flags");
+        w->fast_ok = (flags & 1) == 0;   // cached so compute calls never read device memory
+    });
+}
+
+G4qStatus g4q_weight_export(const G4qWeight* h, uint32_t* packed, uint16_t* scales, uint16_t* biases,
+                            void* stream) {
+    return guarded("g4q_weight_export", [&] {
+        Weight* w = checked(h, "g4q_weight_export");
+        require(packed && scales && biases, G4Q_ERR_INVALID_ARGUMENT, "outputs must be non-null device pointers");
+        launch_export(*w, packed, scales, biases, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+G4qStatus g4q_dequantize(const G4qWeight* h, const int32_t* row_ids, int64_t n_ids, uint16_t* out, int32_t chain,
+                         void* stream) {
+    return guarded("g4q_dequantize", [&] {
+        Weight* w = checked(h, "g4q_dequantize");
+        require(out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "out must be non-null");
+        require(chain == G4Q_CHAIN_R1 || chain == G4Q_CHAIN_R2, G4Q_ERR_INVALID_ARGUMENT, "chain must be 1 (R1) or 2 (R2)");
+        require(row_ids == nullptr || n_ids >= 0, G4Q_ERR_INVALID_ARGUMENT, "n_ids must be >= 0");
+        require_aligned16(out, "out");
+        launch_dequantize(*w, row_ids, n_ids, out, chain, w->d_flags, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+G4qStatus g4q_dequantize_mlx(const uint32_t* packed, const uint16_t* scales, const uint16_t* biases, int64_t rows,
+                             int64_t cols, int32_t bits, int32_t group_size, int32_t chain, uint16_t* out,
+                             void* stream) {
+    return guarded("g4q_dequantize_mlx", [&] {
+        require(packed && scales && biases && out, G4Q_ERR_INVALID_ARGUMENT, "pointers must be non-null");
+        require(bits == 4 || bits == 8, G4Q_ERR_UNSUPPORTED_CONFIG, "bits must be 4 or 8");
+        require(group_size == 32 || group_size == 64 || group_size == 128, G4Q_ERR_UNSUPPORTED_CONFIG,
+                "group_size must be 32, 64 or 128");
+        require(rows >= 0 && cols > 0 && cols % group_size == 0, G4Q_ERR_INVALID_ARGUMENT,
+                "cols must be a positive multiple of group_size");
+        require(chain == G4Q_CHAIN_R1 || chain == G4Q_CHAIN_R2, G4Q_ERR_INVALID_ARGUMENT, "chain must be 1 (R1) or 2 (R2)");
+        require((reinterpret_cast<uintptr_t>(out) & 3u) == 0, G4Q_ERR_INVALID_ARGUMENT, "out must be 4-byte aligned");
+        if (rows == 0) return;
+        launch_dequantize_mlx(packed, scales, biases, rows, cols, bits, group_size, chain, out,
+                              reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+static void qmm_common(const char* fn, const G4qWeight* h, const uint16_t* x, int64_t M, int64_t ldx, void* y,
+                       int64_t ldy, uint32_t flags, float eps, void* stream) {
+    Weight* w = checked(h, fn);
+    require(M >= 0, G4Q_ERR_INVALID_ARGUMENT, "M must be >= 0");
+    if (M == 0) return;
+    require(x != nullptr && y != nullptr, G4Q_ERR_INVALID_ARGUMENT, "x and y must be non-null");
+    require((flags & ~(G4Q_QMM_RMS_SCALE | G4Q_QMM_OUT_F32)) == 0, G4Q_ERR_INVALID_ARGUMENT, "unknown flag bits");
+    require(ldx >= w->K && ldx % 8 == 0, G4Q_ERR_INVALID_ARGUMENT, "ldx must be >= cols and a multiple of 8");
+    require(ldy >= w->N, G4Q_ERR_INVALID_ARGUMENT, "ldy must be >= rows");
+    require_aligned16(x, "x");
+    require(w->fast_ok, G4Q_ERR_UNSUPPORTED_CONFIG,
+            "a scale is non-finite or |scale| >= 2^120; use g4q_dequantize for such weights");
+    QmmCall c{w, x, M, ldx, y, ldy, flags, eps};
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (M <= 16)
+        launch_gemv(c, st);
+    else
+        launch_gemm(c, st);
+}
+
+G4qStatus g4q_qmm(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t ldx, uint16_t* y, int64_t ldy,
+                  void* stream) {
+    return guarded("g4q_qmm", [&] { qmm_common("g4q_qmm", h, x, M, ldx, y, ldy, 0u, 1e-6f, stream); });
+}
+
+G4qStatus g4q_qmm_ex(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t ldx, void* y, int64_t ldy,
+                     uint32_t flags, float eps, void* stream) {
+    return guarded("g4q_qmm_ex", [&] { qmm_common("g4q_qmm_ex", h, x, M, ldx, y, ldy, flags, eps, stream); });
+}
+
+G4qStatus g4q_lm_head_argmax(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t ldx, float softcap,
+                             uint32_t flags, float eps, int64_t row_offset, uint16_t* logits, int64_t ld_logits,
+                             int32_t* tokens, float* values, uint64_t* keys, void* stream) {
+    return guarded("g4q_lm_head_argmax", [&] {
+        Weight* w = checked(h, "g4q_lm_head_argmax");
+        require(M >= 1 && M <= 16, G4Q_ERR_INVALID_ARGUMENT, "M must be in [1, 16]");
+        require(x != nullptr, G4Q_ERR_INVALID_ARGUMENT, "x must be non-null");
+        require((flags & ~G4Q_QMM_RMS_SCALE) == 0, G4Q_ERR_INVALID_ARGUMENT, "only G4Q_QMM_RMS_SCALE is accepted");
+        require(ldx >= w->K && ldx % 8 == 0, G4Q_ERR_INVALID_ARGUMENT, "ldx must be >= cols and a multiple of 8");
+        require(logits == nullptr || ld_logits >= w->N, G4Q_ERR_INVALID_ARGUMENT, "ld_logits must be >= rows");
+        require(row_offset >= 0 && row_offset + w->N <= 0xFFFFFFFFll, G4Q_ERR_INVALID_ARGUMENT,
+                "row_offset + rows must fit in 32 bits");
+        require_aligned16(x, "x");
+        require(w->fast_ok, G4Q_ERR_UNSUPPORTED_CONFIG, "a scale is non-finite or |scale| >= 2^120");
+        launch_lm_head(*w, x, M, ldx, softcap, flags, eps, row_offset, logits, ld_logits, tokens, values,
+                       reinterpret_cast<unsigned long long*>(keys), reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+G4qStatus g4q_synth_matrix(uint64_t seed, int64_t rows, int64_t cols, int32_t bits, int32_t group_size,
+                           uint32_t* packed, uint16_t* scales, uint16_t* biases, void* stream) {
+    return guarded("g4q_synth_matrix", [&] {
+        require(bits == 4 || bits == 8, G4Q_ERR_UNSUPPORTED_CONFIG, "bits must be 4 or 8");
+        require(group_size > 0 && cols % group_size == 0 && cols % (32 / bits) == 0, G4Q_ERR_INVALID_ARGUMENT,
+                "cols must be a multiple of group_size");
+        require(rows >= 0, G4Q_ERR_INVALID_ARGUMENT, "rows must be >= 0");
+        require(scales != nullptr, G4Q_ERR_INVALID_ARGUMENT, "scales must be non-null");
+        if (rows == 0) return;
+        launch_synth_matrix(seed, rows, cols, bits, group_size, packed, scales, biases,
+                            reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+G4qStatus g4q_synth_normal_bf16(uint64_t seed, int64_t count, uint16_t* out, void* stream) {
+    return guarded("g4q_synth_normal_bf16", [&] {
+        require(out != nullptr && count >= 0, G4Q_ERR_INVALID_ARGUMENT, "out must be non-null, count >= 0");
+        if (count == 0) return;
+        launch_synth_normal(seed, count, out, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,78 @@
+// g4q_internal.h -- host-side internals shared by the g4q translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "g4q.h"
+
+namespace g4q {
+
+constexpr uint64_t kWeightMagic = 0x4734515745494748ull;  // "G4QWEIGH"
+
+struct Weight {
+    uint64_t magic = 0;
+    int64_t N = 0, K = 0;        // logical shape of this handle (after any TP split)
+    int bits = 4, group_size = 64;
+    int device = -1;
+    uint32_t* packed = nullptr;  // layout v1
+    uint32_t* sb = nullptr;
+    size_t bytes = 0;
+    int* d_flags = nullptr;      // device word: bit0 = a scale outside |s| < 2^120 or non-finite,
+                                 // bit1 = a gathered row id was out of range
+    bool fast_ok = true;         // host copy of !(bit0), refreshed by every load
+    // lazily created scratch for the LM-head argmax (keys[16] + counter), zeroed once
+    unsigned long long* argmax_scratch = nullptr;
+};
+
+// Raised inside entry points; converted to a status + last-error message at the C-ABI edge.
+struct Error : std::runtime_error {
+    G4qStatus status;
+    Error(G4qStatus s, const std::string& m) : std::runtime_error(m), status(s) {}
+};
+
+inline void check_cuda(cudaError_t e, const char* what) {
+    if (e != cudaSuccess)
+        throw Error(G4Q_ERR_RUNTIME, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int device_sm_count();
+int current_device();
+
+// kernels (g4q_layout.cu)
+void launch_synth_matrix(uint64_t seed, int64_t N, int64_t K, int bits, int group_size, uint32_t* w,
+                         uint16_t* s, uint16_t* b, cudaStream_t st);
+void launch_synth_normal(uint64_t seed, int64_t count, uint16_t* out, cudaStream_t st);
+void launch_repack(const uint32_t* src_w, const uint16_t* src_s, const uint16_t* src_b, int64_t src_ld_words,
+                   int64_t src_ld_groups, int64_t src_row0, int64_t src_k0, int64_t n_rows, Weight& w,
+                   int64_t dst_row0, cudaStream_t st);
+void launch_export(const Weight& w, uint32_t* dst_w, uint16_t* dst_s, uint16_t* dst_b, cudaStream_t st);
+void launch_dequantize(const Weight& w, const int32_t* ids, int64_t n_ids, uint16_t* out, int chain,
+                       int* d_err, cudaStream_t st);
+void launch_dequantize_mlx(const uint32_t* w, const uint16_t* s, const uint16_t* b, int64_t N, int64_t K,
+                           int bits, int group_size, int chain, uint16_t* out, cudaStream_t st);
+
+// kernels (g4q_gemv.cu)
+struct QmmCall {
+    const Weight* w;
+    const uint16_t* x;
+    int64_t M, ldx;
+    void* y;
+    int64_t ldy;
+    uint32_t flags;
+    float eps;
+};
+void launch_gemv(const QmmCall& c, cudaStream_t st);
+void launch_lm_head(const Weight& w, const uint16_t* x, int64_t M, int64_t ldx, float softcap, uint32_t flags,
+                    float eps, int64_t row_offset, uint16_t* logits, int64_t ld_logits, int32_t* tokens,
+                    float* values, unsigned long long* keys, cudaStream_t st);
+
+// kernels (g4q_gemm.cu): tcgen05 dequant-GEMM for M > 16
+void launch_gemm(const QmmCall& c, cudaStream_t st);
+bool gemm_supported(const QmmCall& c);
+
+}  // namespace g4q

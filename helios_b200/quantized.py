@@ -1,0 +1,288 @@
+"""Host-side mirror of the MLX affine-quantization operators that Helios's native graph calls.
+
+The reference graph (native/gemma4_mlx/src/native_model.cc) uses exactly these MLX ops on
+its weights:
+
+* ``quantized_linear`` (:349-362): ``mlx::core::quantized_matmul(x, W, scales, biases,
+  transpose=true, group_size, bits, "affine")`` then a bf16 cast;
+* ``quantized_embedding`` (:364-376): ``take`` rows, then ``mlx::core::dequantize``;
+* ``target_logits_for_hidden`` (:1782-1795): the tied LM head, bf16 ``tanh(l/30)*30`` softcap,
+  followed by ``argmax`` (:3825).
+
+``quantized_matmul`` / ``dequantize`` below keep MLX's names, argument meaning and shape rules
+(``w`` is uint32 ``[N, K*bits/32]``, scales/biases ``[N, K/group_size]``, ``transpose=True``
+computes ``x @ dequantize(w).T``) and raise ``ValueError`` on bad arguments as MLX does. All
+compute runs in libg4q.so (sm_100a kernels) on the current CUDA stream; tensors are torch
+CUDA tensors. There is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import CHAIN_R1, CHAIN_R2, QMM_OUT_F32, QMM_RMS_SCALE, G4qError, G4qInvalidArgument
+
+__all__ = [
+    "QuantizedWeight", "quantized_matmul", "dequantize", "lm_head_argmax", "synth_matrix", "synth_normal",
+    "CHAIN_R1", "CHAIN_R2", "G4qError", "G4qInvalidArgument",
+]
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[ctypes.c_void_p]:
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _as_bits16(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype in (torch.bfloat16, torch.int16, torch.uint16):
+        return t
+    raise ValueError(f"{name} must be bfloat16 (got {t.dtype})")
+
+
+def _check_format(group_size: int, bits: int, mode: str) -> None:
+    if mode != "affine":
+        raise ValueError(f"[quantize] only mode='affine' is supported (got {mode!r})")
+    if bits not in (4, 8):
+        raise ValueError(f"[quantize] bits must be 4 or 8 (got {bits})")
+    if group_size not in (32, 64, 128):
+        raise ValueError(f"[quantize] group_size must be 32, 64 or 128 (got {group_size})")
+
+
+class QuantizedWeight:
+    """A 4-bit, group-64 affine matrix resident on one GPU in libg4q's kernel layout.
+
+    Build it from MLX-layout tensors (host or device) with :meth:`from_mlx`, optionally taking a
+    row window (tensor-parallel column split) and/or a group-aligned column window (row split),
+    or concatenating several matrices that share an input with :meth:`concat`.
+    """
+
+    def __init__(self, rows: int, cols: int, bits: int = 4, group_size: int = 64):
+        self._h = ctypes.c_void_p()
+        _lib.call("g4q_weight_create", rows, cols, bits, group_size, ctypes.byref(self._h))
+        self.rows, self.cols, self.bits, self.group_size = rows, cols, bits, group_size
+        self.device = torch.cuda.current_device()
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        if not self._h:
+            raise ValueError("QuantizedWeight has been freed")
+        return self._h
+
+    @property
+    def shape(self) -> Tuple[int, int]:
+        return (self.rows, self.cols)
+
+    def load(self, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *, dst_row: int = 0,
+             src_row: int = 0, src_col: int = 0, n_rows: Optional[int] = None) -> "QuantizedWeight":
+        if w.dtype not in (torch.uint32, torch.int32):
+            raise ValueError(f"w must be uint32 packed words (got {w.dtype})")
+        _as_bits16(scales, "scales")
+        _as_bits16(biases, "biases")
+        if w.dim() != 2 or scales.dim() != 2 or biases.dim() != 2:
+            raise ValueError("w, scales and biases must be 2-D")
+        src_rows, src_cols = w.shape[0], w.shape[1] * 32 // self.bits
+        if scales.shape != (src_rows, src_cols // self.group_size) or biases.shape != scales.shape:
+            raise ValueError(f"scales/biases must be [{src_rows}, {src_cols // self.group_size}] "
+                             f"(got {tuple(scales.shape)}, {tuple(biases.shape)})")
+        w, scales, biases = w.contiguous(), scales.contiguous(), biases.contiguous()
+        n = self.rows - dst_row if n_rows is None else n_rows
+        _lib.call("g4q_weight_load", self.handle, dst_row, _ptr(w), _ptr(scales), _ptr(biases), src_rows,
+                  src_cols, src_row, src_col, n, _stream())
+        return self
+
+    @classmethod
+    def from_mlx(cls, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *, group_size: int = 64,
+                 bits: int = 4, rows: Optional[Tuple[int, int]] = None,
+                 cols: Optional[Tuple[int, int]] = None) -> "QuantizedWeight":
+        """Upload an MLX-layout matrix; ``rows=(start, stop)`` / ``cols=(start, stop)`` take a window."""
+        src_rows, src_cols = w.shape[0], w.shape[1] * 32 // bits
+        r0, r1 = rows if rows is not None else (0, src_rows)
+        c0, c1 = cols if cols is not None else (0, src_cols)
+        q = cls(r1 - r0, c1 - c0, bits, group_size)
+        return q.load(w, scales, biases, src_row=r0, src_col=c0)
+
+    @classmethod
+    def concat(cls, parts, *, group_size: int = 64, bits: int = 4) -> "QuantizedWeight":
+        """Stack several (w, scales, biases[, (row0, row1)]) MLX-layout matrices along N."""
+        spans, cols = [], None
+        for p in parts:
+            w = p[0]
+            r0, r1 = p[3] if len(p) > 3 and p[3] is not None else (0, w.shape[0])
+            c = w.shape[1] * 32 // bits
+            if cols is not None and c != cols:
+                raise ValueError("concatenated matrices must share K")
+            cols = c
+            spans.append((p, r0, r1))
+        q = cls(sum(r1 - r0 for _, r0, r1 in spans), cols, bits, group_size)
+        dst = 0
+        for p, r0, r1 in spans:
+            q.load(p[0], p[1], p[2], dst_row=dst, src_row=r0, n_rows=r1 - r0)
+            dst += r1 - r0
+        return q
+
+    def info(self) -> dict:
+        info = _lib.G4qWeightInfo()
+        _lib.call("g4q_weight_info", self.handle, ctypes.byref(info))
+        return {f: getattr(info, f) for f, _ in info._fields_}
+
+    def export(self) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Inverse repack: MLX-layout (w uint32, scales bf16, biases bf16) on this GPU."""
+        dev = torch.device("cuda", self.device)
+        w = torch.empty((self.rows, self.cols * self.bits // 32), dtype=torch.uint32, device=dev)
+        s = torch.empty((self.rows, self.cols // self.group_size), dtype=torch.bfloat16, device=dev)
+        b = torch.empty_like(s)
+        _lib.call("g4q_weight_export", self.handle, _ptr(w), _ptr(s), _ptr(b), _stream())
+        return w, s, b
+
+    def free(self) -> None:
+        if self._h:
+            _lib.call("g4q_weight_free", self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def _rows2d(x: torch.Tensor, K: int, name: str = "x") -> torch.Tensor:
+    if x.dtype != torch.bfloat16:
+        raise ValueError(f"{name} must be bfloat16 (got {x.dtype})")
+    if not x.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if x.shape[-1] != K:
+        raise ValueError(f"[quantized_matmul] last dimension of {name} ({x.shape[-1]}) must equal K = {K}")
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+        x2 = x2.contiguous()
+    return x2
+
+
+def quantized_matmul(x: torch.Tensor, w, scales: Optional[torch.Tensor] = None,
+                     biases: Optional[torch.Tensor] = None, transpose: bool = True, group_size: int = 64,
+                     bits: int = 4, mode: str = "affine", *, rms_scale: bool = False, eps: float = 1e-6,
+                     out_dtype: torch.dtype = torch.bfloat16, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``x @ dequantize(w).T`` with fp32 accumulation and bf16 (or fp32) output.
+
+    ``w`` is a :class:`QuantizedWeight` (scales/biases None) or MLX-layout tensors (uploaded per
+    call; use a QuantizedWeight for repeated calls). ``rms_scale`` folds the input RMSNorm
+    ``1/sqrt(mean(x^2)+eps)`` into the output.
+    """
+    _check_format(group_size, bits, mode)
+    if not transpose:
+        raise ValueError("[quantized_matmul] only transpose=True (x @ W.T) is on the Helios path")
+    if isinstance(w, QuantizedWeight):
+        if scales is not None or biases is not None:
+            raise ValueError("scales/biases are part of a QuantizedWeight")
+        qw = w
+    else:
+        if scales is None or biases is None:
+            raise ValueError("[quantized_matmul] affine mode needs scales and biases")
+        qw = QuantizedWeight.from_mlx(w, scales, biases, group_size=group_size, bits=bits)
+    if (qw.group_size, qw.bits) != (group_size, bits):
+        raise ValueError("group_size/bits do not match the uploaded weight")
+    x2 = _rows2d(x, qw.cols)
+    M = x2.shape[0]
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("out_dtype must be bfloat16 or float32")
+    shape = tuple(x.shape[:-1]) + (qw.rows,)
+    y = torch.empty(shape, dtype=out_dtype, device=x.device) if out is None else out
+    if y.dtype != out_dtype or y.shape[-1] != qw.rows:
+        raise ValueError("out has the wrong dtype or shape")
+    y2 = y.view(-1, qw.rows) if y.is_contiguous() else None
+    if y2 is None:
+        raise ValueError("out must be contiguous")
+    flags = (QMM_RMS_SCALE if rms_scale else 0) | (QMM_OUT_F32 if out_dtype == torch.float32 else 0)
+    _lib.call("g4q_qmm_ex", qw.handle, _ptr(x2), M, x2.stride(0), _ptr(y2), y2.stride(0), flags, eps, _stream())
+    return y
+
+
+def dequantize(w, scales: Optional[torch.Tensor] = None, biases: Optional[torch.Tensor] = None,
+               group_size: int = 64, bits: int = 4, mode: str = "affine", *, rows: Optional[torch.Tensor] = None,
+               chain: int = CHAIN_R2) -> torch.Tensor:
+    """bf16 ``scale * q + bias`` of every element (or of the rows ``rows``, an int32 index tensor).
+
+    ``w`` is a :class:`QuantizedWeight` or MLX-layout device tensors (any of bits 4/8, group
+    32/64/128). Bit-exact with rounding chain ``chain`` (R2 default: bf16(bf16(s*q) + b)).
+    """
+    _check_format(group_size, bits, mode)
+    if chain not in (CHAIN_R1, CHAIN_R2):
+        raise ValueError("chain must be CHAIN_R1 or CHAIN_R2")
+    if isinstance(w, QuantizedWeight):
+        dev = torch.device("cuda", w.device)
+        if rows is None:
+            out = torch.empty((w.rows, w.cols), dtype=torch.bfloat16, device=dev)
+            _lib.call("g4q_dequantize", w.handle, None, 0, _ptr(out), chain, _stream())
+        else:
+            ids = rows.to(device=dev, dtype=torch.int32).contiguous().view(-1)
+            out = torch.empty(tuple(rows.shape) + (w.cols,), dtype=torch.bfloat16, device=dev)
+            _lib.call("g4q_dequantize", w.handle, _ptr(ids), ids.numel(), _ptr(out), chain, _stream())
+        return out
+    if scales is None or biases is None:
+        raise ValueError("[dequantize] affine mode needs scales and biases")
+    if not w.is_cuda:
+        raise ValueError("w must be a CUDA tensor")
+    N, K = w.shape[0], w.shape[1] * 32 // bits
+    if rows is not None:
+        ids = rows.to(device=w.device, dtype=torch.long).view(-1)
+        w, scales, biases = w[ids], scales[ids], biases[ids]
+        N = ids.numel()
+    w, scales, biases = w.contiguous(), scales.contiguous(), biases.contiguous()
+    if scales.shape != (N, K // group_size) or biases.shape != scales.shape:
+        raise ValueError("scales/biases must be [N, K/group_size]")
+    out = torch.empty((N, K), dtype=torch.bfloat16, device=w.device)
+    _lib.call("g4q_dequantize_mlx", _ptr(w), _ptr(scales), _ptr(biases), N, K, bits, group_size, chain, _ptr(out),
+              _stream())
+    return out if rows is None else out.view(tuple(rows.shape) + (K,))
+
+
+def lm_head_argmax(x: torch.Tensor, w: QuantizedWeight, *, softcap: float = 30.0, rms_scale: bool = False,
+                   eps: float = 1e-6, row_offset: int = 0, logits: Optional[torch.Tensor] = None,
+                   tokens: Optional[torch.Tensor] = None, values: Optional[torch.Tensor] = None,
+                   keys: Optional[torch.Tensor] = None):
+    """Tied LM head + bf16 softcap + greedy argmax (first index wins ties), one pass over W.
+
+    Returns (tokens int32 [M], values float32 [M], keys int64 [M]); ``logits`` (bf16 [M, N]),
+    if given, receives the pre-softcap logits.
+    """
+    x2 = _rows2d(x, w.cols)
+    M = x2.shape[0]
+    dev = x.device
+    tokens = torch.empty(M, dtype=torch.int32, device=dev) if tokens is None else tokens
+    values = torch.empty(M, dtype=torch.float32, device=dev) if values is None else values
+    keys = torch.empty(M, dtype=torch.int64, device=dev) if keys is None else keys
+    ld = 0
+    if logits is not None:
+        if logits.dtype != torch.bfloat16 or logits.shape[-1] != w.rows or not logits.is_contiguous():
+            raise ValueError("logits must be contiguous bf16 [M, rows]")
+        ld = w.rows
+    _lib.call("g4q_lm_head_argmax", w.handle, _ptr(x2), M, x2.stride(0), softcap,
+              QMM_RMS_SCALE if rms_scale else 0, eps, row_offset, _ptr(logits), ld, _ptr(tokens), _ptr(values),
+              _ptr(keys), _stream())
+    return tokens, values, keys
+
+
+def synth_matrix(seed: int, rows: int, cols: int, bits: int = 4, group_size: int = 64, device=None):
+    """Seeded synthetic MLX-layout matrix generated on the GPU (same values as the CPU oracle)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    w = torch.empty((rows, cols * bits // 32), dtype=torch.uint32, device=dev)
+    s = torch.empty((rows, cols // group_size), dtype=torch.bfloat16, device=dev)
+    b = torch.empty_like(s)
+    _lib.call("g4q_synth_matrix", seed & (2 ** 64 - 1), rows, cols, bits, group_size, _ptr(w), _ptr(s), _ptr(b),
+              _stream())
+    return w, s, b
+
+
+def synth_normal(seed: int, shape, device=None) -> torch.Tensor:
+    """Seeded bf16 ~ N(0, 1) tensor generated on the GPU (same values as the CPU oracle)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    out = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+    _lib.call("g4q_synth_normal_bf16", seed & (2 ** 64 - 1), out.numel(), _ptr(out), _stream())
+    return out

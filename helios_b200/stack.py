@@ -1,0 +1,178 @@
+"""Synthetic Gemma-style decoder stack built from the quantized linears only.
+
+This is the workload of the benchmark configs (48 layers of the seven 4-bit g64 projections
+plus the quantized tied LM head). It stands in for the linear part of the reference's decode
+and prefill drivers (native_model.cc:1843-1911 ``decode_last_logits``, :1682-1780
+``decode_block_hidden``/``forward_hidden``, :1819-1841 chunked prefill): the same 336 + 1
+quantized matmuls per step in the same order, with attention, RoPE, GeGLU and the KV cache left
+out (outside the quantized-linear path). Data flow per layer, with ``rms(v)`` the RMSNorm scale
+``1/sqrt(mean(v^2)+eps)`` folded into the consuming matmul's epilogue:
+
+    qkv = rms(h) * (h @ [Wq|Wk|Wv]^T)        # q|k|v share their input: one fused launch
+    o   = q @ Wo^T                           # q stands in for the attention output
+    gu  = rms(o) * (o @ [Wgate|Wup]^T)       # gate|up share their input: one fused launch
+    h   = up @ Wdown^T                       # up stands in for the GeGLU output
+    logits = rms(h) * (h @ Wlm^T); token = argmax(softcap(logits))
+
+Tensor parallelism over ``tp_size`` GPUs (one process each): q/k/v/gate/up/LM-head rows are
+split (column-parallel), o/down columns are split along K at group boundaries (row-parallel),
+o/down emit fp32 partial sums that are summed across ranks (allreduce) and rounded to bf16,
+and the LM-head shards combine their 64-bit argmax keys with a max.
+"""
+from __future__ import annotations
+
+import struct
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+
+from .quantized import QuantizedWeight, lm_head_argmax, quantized_matmul, synth_matrix
+
+BASE_SEED = 0x48454C494F53
+PROJ_IDS = {"q": 0, "k": 1, "v": 2, "o": 3, "gate": 4, "up": 5, "down": 6, "lm": 7}
+
+
+def matrix_seed(layer: int, proj: str) -> int:
+    return BASE_SEED ^ ((0 if proj == "lm" else layer) * 16 + PROJ_IDS[proj])
+
+
+def activation_seed(chunk: int) -> int:
+    return BASE_SEED ^ 0xF00 ^ chunk
+
+
+@dataclass
+class StackConfig:
+    layers: int = 48
+    hidden: int = 3840
+    q_out: int = 4096       # 16 heads x 256
+    kv_out: int = 2048      # 8 KV heads x 256
+    inter: int = 15360
+    vocab: int = 262144
+    softcap: float = 30.0
+    eps: float = 1e-6
+
+    def shapes(self):
+        return {"q": (self.q_out, self.hidden), "k": (self.kv_out, self.hidden), "v": (self.kv_out, self.hidden),
+                "o": (self.hidden, self.q_out), "gate": (self.inter, self.hidden), "up": (self.inter, self.hidden),
+                "down": (self.hidden, self.inter), "lm": (self.vocab, self.hidden)}
+
+    def weight_bytes(self) -> int:
+        """Packed + scale/bias bytes of every matrix (0.5625 B per weight)."""
+        sh = self.shapes()
+        per_layer = sum(n * k for p, (n, k) in sh.items() if p != "lm")
+        return int((per_layer * self.layers + sh["lm"][0] * sh["lm"][1]) * 9 // 16)
+
+    def flops_per_token(self) -> int:
+        sh = self.shapes()
+        per_layer = sum(n * k for p, (n, k) in sh.items() if p != "lm")
+        return 2 * per_layer * self.layers
+
+
+def _split(n: int, rank: int, size: int, align: int) -> tuple:
+    if n % (size * align) != 0:
+        raise ValueError(f"dimension {n} does not split into {size} shards of multiples of {align}")
+    step = n // size
+    return rank * step, (rank + 1) * step
+
+
+class SyntheticStack:
+    """Seeded random-init weights of the synthetic stack, sharded for rank ``tp_rank`` of ``tp_size``."""
+
+    def __init__(self, cfg: StackConfig, tp_rank: int = 0, tp_size: int = 1, group=None,
+                 max_tokens: int = 16):
+        self.cfg, self.rank, self.size, self.group = cfg, tp_rank, tp_size, group
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        sh = cfg.shapes()
+        self.q_rows = _split(cfg.q_out, tp_rank, tp_size, 16)
+        self.kv_rows = _split(cfg.kv_out, tp_rank, tp_size, 16)
+        self.i_rows = _split(cfg.inter, tp_rank, tp_size, 16)
+        self.o_cols = _split(cfg.q_out, tp_rank, tp_size, 64)
+        self.d_cols = _split(cfg.inter, tp_rank, tp_size, 64)
+        self.v_rows = _split(cfg.vocab, tp_rank, tp_size, 16)
+        self.nq = self.q_rows[1] - self.q_rows[0]
+        self.nkv = self.kv_rows[1] - self.kv_rows[0]
+        self.ni = self.i_rows[1] - self.i_rows[0]
+        self.layers: List[dict] = []
+        for layer in range(cfg.layers):
+            mats = {p: synth_matrix(matrix_seed(layer, p), *sh[p]) for p in ("q", "k", "v")}
+            qkv = QuantizedWeight.concat([(*mats["q"], self.q_rows), (*mats["k"], self.kv_rows),
+                                          (*mats["v"], self.kv_rows)])
+            del mats
+            o = QuantizedWeight.from_mlx(*synth_matrix(matrix_seed(layer, "o"), *sh["o"]), cols=self.o_cols)
+            mats = {p: synth_matrix(matrix_seed(layer, p), *sh[p]) for p in ("gate", "up")}
+            gu = QuantizedWeight.concat([(*mats["gate"], self.i_rows), (*mats["up"], self.i_rows)])
+            del mats
+            down = QuantizedWeight.from_mlx(*synth_matrix(matrix_seed(layer, "down"), *sh["down"]), cols=self.d_cols)
+            self.layers.append({"qkv": qkv, "o": o, "gu": gu, "down": down})
+        self.lm = QuantizedWeight.from_mlx(*synth_matrix(matrix_seed(0, "lm"), *sh["lm"]), rows=self.v_rows)
+        torch.cuda.synchronize()
+        self._alloc(max_tokens)
+
+    def _alloc(self, M: int):
+        dev, c = self.device, self.cfg
+        self.max_tokens = M
+        self.qkv_out = torch.empty((M, self.nq + 2 * self.nkv), dtype=torch.bfloat16, device=dev)
+        self.o_out = torch.empty((M, c.hidden), dtype=torch.bfloat16, device=dev)
+        self.gu_out = torch.empty((M, 2 * self.ni), dtype=torch.bfloat16, device=dev)
+        self.h_out = torch.empty((M, c.hidden), dtype=torch.bfloat16, device=dev)
+        self.part = torch.empty((M, c.hidden), dtype=torch.float32, device=dev)
+        self.tokens = torch.empty(M, dtype=torch.int32, device=dev)
+        self.values = torch.empty(M, dtype=torch.float32, device=dev)
+        self.keys = torch.empty(M, dtype=torch.int64, device=dev)
+
+    def _row_parallel(self, w: QuantizedWeight, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        if self.size == 1:
+            return quantized_matmul(x, w, out=out)
+        quantized_matmul(x, w, out_dtype=torch.float32, out=self.part[: x.shape[0]])
+        p = self.part[: x.shape[0]]
+        torch.distributed.all_reduce(p, group=self.group)
+        out.copy_(p)
+        return out
+
+    def forward(self, h: torch.Tensor):
+        """One decode step (M <= max_tokens rows) or one prefill chunk; returns (tokens, values, h)."""
+        M = h.shape[0]
+        if M > self.max_tokens:
+            self._alloc(M)
+        c = self.cfg
+        x = h
+        for L in self.layers:
+            qkv = quantized_matmul(x, L["qkv"], rms_scale=True, eps=c.eps, out=self.qkv_out[:M])
+            o = self._row_parallel(L["o"], qkv[:, : self.nq], self.o_out[:M])
+            gu = quantized_matmul(o, L["gu"], rms_scale=True, eps=c.eps, out=self.gu_out[:M])
+            x = self._row_parallel(L["down"], gu[:, self.ni:], self.h_out[:M])
+        return self.head(x)
+
+    def head(self, x: torch.Tensor):
+        c = self.cfg
+        M = x.shape[0]
+        tok, val, key = lm_head_argmax(x, self.lm, softcap=c.softcap, rms_scale=True, eps=c.eps,
+                                       row_offset=self.v_rows[0], tokens=self.tokens[:M], values=self.values[:M],
+                                       keys=self.keys[:M])
+        if self.size > 1:
+            # order-preserving u64 keys: flip the top bit so a signed int64 max orders them
+            k = key ^ (-(2 ** 63))
+            torch.distributed.all_reduce(k, op=torch.distributed.ReduceOp.MAX, group=self.group)
+            key = k ^ (-(2 ** 63))
+        return key, x
+
+    def free(self):
+        for L in self.layers:
+            for w in L.values():
+                w.free()
+        self.lm.free()
+
+
+def decode_keys(keys: torch.Tensor):
+    """(token, value) per 64-bit argmax key (inverse of the kernel's key encoding)."""
+    k = keys.to(torch.int64).cpu()
+    tokens, values = [], []
+    for v in k.tolist():
+        u = v & (2 ** 64 - 1)
+        idx = 0xFFFFFFFF - (u & 0xFFFFFFFF)
+        o = u >> 32
+        bits = (o & 0x7FFFFFFF) if (o & 0x80000000) else (~o & 0xFFFFFFFF)
+        tokens.append(idx)
+        values.append(struct.unpack("<f", struct.pack("<I", bits))[0])
+    return tokens, values

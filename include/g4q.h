@@ -1,0 +1,154 @@
+/*
+ * g4q.h -- C ABI of libg4q, the B200 (sm_100a) implementation of Helios/gemma4d's
+ * quantized-linear hot path: every mlx::core::quantized_matmul / mlx::core::dequantize
+ * call that native/gemma4_mlx makes for the Gemma-style decoder, in MLX's affine format
+ * (4-bit, group_size 64 along K, eight nibbles per uint32 little-endian, bf16 scale and
+ * bias per group, w = scale * q + bias).
+ *
+ * Conventions (mirroring the reference's narrow C ABI, native/gemma4_mlx/include/gemma4_mlx.h):
+ *   - Every call returns G4qStatus; the message of the last failure on the calling thread is
+ *     kept in a thread-local buffer read with g4q_get_last_error (runtime.cc:46, 115-133,
+ *     816-823). No C++ exception crosses this boundary.
+ *   - Handles are opaque, allocated by the library, tagged with a 64-bit magic and freed
+ *     with the matching g4q_*_free (runtime.cc:41-45, 900-912).
+ *   - Device pointers are plain pointers on the current CUDA device; `stream` is a
+ *     cudaStream_t passed as void* (NULL = legacy default stream). All compute calls are
+ *     asynchronous on that stream. Uploads accept host or device source pointers.
+ *   - Element types: bf16 values travel as uint16_t bit patterns; packed weights as uint32_t.
+ *   - A handle or a stream is not safe for concurrent use by two host threads (the
+ *     reference's single scheduler thread owns a target: crates/gemma4d-server/src/http.rs:421-470).
+ */
+#ifndef G4Q_H
+#define G4Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define G4Q_ABI_VERSION 1u
+
+/* Same numbering as Gemma4Status (native/gemma4_mlx/include/gemma4_mlx.h:12-21). */
+typedef enum G4qStatus {
+    G4Q_OK = 0,
+    G4Q_ERR_INVALID_ARGUMENT = 1,
+    G4Q_ERR_UNSUPPORTED_CONFIG = 2,
+    G4Q_ERR_MODEL_LOAD = 3,
+    G4Q_ERR_RUNTIME = 4,
+    G4Q_ERR_MEMORY_GUARD = 5
+} G4qStatus;
+
+/* Rounding chain of the bf16 `scale * q + bias` (MLX's cannot be observed here). */
+typedef enum G4qChain {
+    G4Q_CHAIN_R1 = 1, /* bf16(scale*q + bias), one rounding */
+    G4Q_CHAIN_R2 = 2  /* bf16(bf16(scale*q) + bias), one rounding per bf16 op (default) */
+} G4qChain;
+
+/* g4q_qmm_ex / g4q_lm_head_argmax flags */
+#define G4Q_QMM_RMS_SCALE 0x1u /* y[m,:] *= 1/sqrt(mean(x[m,:]^2) + eps) (RMSNorm folded as an output scale) */
+#define G4Q_QMM_OUT_F32 0x2u   /* y is fp32 instead of bf16 */
+
+typedef struct G4qVersionInfo {
+    uint32_t abi_version;
+    const char* backend_name;
+    const char* backend_version;
+} G4qVersionInfo;
+
+typedef struct G4qWeightInfo {
+    int64_t rows;          /* N (output features) */
+    int64_t cols;          /* K (input features) */
+    int32_t bits;
+    int32_t group_size;
+    uint64_t device_bytes; /* packed + scales/biases in the kernel layout */
+    int32_t device;
+    int32_t fast_path_ok;  /* 1 when every scale is finite with |s| < 2^120 (qmm/GEMM requirement) */
+    int32_t error_flags;   /* bit 1: g4q_dequantize saw a row id outside [0, rows) (that row was zeroed) */
+} G4qWeightInfo;
+
+typedef struct G4qWeight G4qWeight;
+
+/* Replaces gemma4_runtime_version (gemma4_mlx.h:198; runtime.cc:798-808). */
+G4qStatus g4q_runtime_version(G4qVersionInfo* out);
+/* Replaces gemma4_get_last_error (gemma4_mlx.h:199; runtime.cc:816-823). */
+G4qStatus g4q_get_last_error(char* buffer, size_t buffer_len);
+
+/* ---- weights: the loader repack -------------------------------------------------------
+ * Replaces the tensor residency of NativeTextModel::load (native_model.cc:3506-3590) for the
+ * `{prefix}.weight/.scales/.biases` triple consumed by quantized_linear (native_model.cc:349-362).
+ * g4q_weight_create allocates an empty N x K handle (N % 16 == 0, K % 64 == 0; bits 4, group 64).
+ * g4q_weight_load copies the window [src_row0, src_row0+n_rows) x [src_k0, src_k0+K) of an
+ * MLX-layout matrix (packed uint32 [src_rows, src_cols/8], scales/biases bf16
+ * [src_rows, src_cols/64], host or device memory) into rows [dst_row0, dst_row0+n_rows) of the
+ * handle, in the kernel layout. One call per matrix uploads it whole; windows give the tensor-
+ * parallel column split (rows) and row split (K, group aligned), and several loads into one
+ * handle concatenate projections that share an input (q|k|v, gate|up). Dequantised values are
+ * preserved exactly (g4q_weight_export inverts the repack). */
+G4qStatus g4q_weight_create(int64_t rows, int64_t cols, int32_t bits, int32_t group_size, G4qWeight** out);
+G4qStatus g4q_weight_load(G4qWeight* w, int64_t dst_row0, const uint32_t* packed, const uint16_t* scales,
+                          const uint16_t* biases, int64_t src_rows, int64_t src_cols, int64_t src_row0,
+                          int64_t src_k0, int64_t n_rows, void* stream);
+G4qStatus g4q_weight_free(G4qWeight* w);
+G4qStatus g4q_weight_info(const G4qWeight* w, G4qWeightInfo* out);
+/* Inverse repack into MLX layout (device pointers: packed [rows, cols/8], scales/biases [rows, cols/64]). */
+G4qStatus g4q_weight_export(const G4qWeight* w, uint32_t* packed, uint16_t* scales, uint16_t* biases,
+                            void* stream);
+
+/* ---- dequantize --------------------------------------------------------------------------
+ * Replaces mlx::core::dequantize(..., "affine") -> bf16: the embedding gather of
+ * quantized_embedding (native_model.cc:364-376: take rows, then dequantize) when row_ids is
+ * non-NULL (out = bf16 [n_ids, cols]), or the whole matrix when row_ids is NULL
+ * (out = bf16 [rows, cols]). Bit-exact with the chain selected. */
+G4qStatus g4q_dequantize(const G4qWeight* w, const int32_t* row_ids, int64_t n_ids, uint16_t* out,
+                         int32_t chain, void* stream);
+/* Same op straight from MLX-layout device arrays (bits 4 or 8, group 32/64/128), as
+ * mx.dequantize(w, scales, biases, group_size, bits, mode="affine") is called in
+ * scripts/xr54_dequant_assistant.py:117-125. out = bf16 [rows, cols]. */
+G4qStatus g4q_dequantize_mlx(const uint32_t* packed, const uint16_t* scales, const uint16_t* biases,
+                             int64_t rows, int64_t cols, int32_t bits, int32_t group_size, int32_t chain,
+                             uint16_t* out, void* stream);
+
+/* ---- quantized matmul ----------------------------------------------------------------------
+ * Replaces mlx::core::quantized_matmul(x, W, scales, biases, transpose=true, 64, 4, "affine")
+ * followed by the bf16 cast of quantized_linear (native_model.cc:349-362; call sites :802,
+ * :813, :821, :892, :934, :939, :949 and their decode/verify twins :993-1128, :1158-1281):
+ * y[m, n] = sum_k x[m, k] * deq(W)[n, k], fp32 accumulation, bf16 out. x: bf16 [M, ldx],
+ * y: bf16 [M, ldy], device memory, row strides in elements (multiples of 8). M <= 16 runs the
+ * decode GEMV; larger M runs the tcgen05 dequant-GEMM. */
+G4qStatus g4q_qmm(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t ldx, uint16_t* y, int64_t ldy,
+                  void* stream);
+/* As g4q_qmm with G4Q_QMM_* flags: RMS_SCALE multiplies each output row by
+ * 1/sqrt(mean(x[m,:]^2) + eps) (the RMSNorm of the input folded into the epilogue), OUT_F32
+ * writes fp32 y (ldy in fp32 elements). */
+G4qStatus g4q_qmm_ex(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t ldx, void* y, int64_t ldy,
+                     uint32_t flags, float eps, void* stream);
+
+/* ---- tied LM head with fused softcap + greedy argmax ----------------------------------------
+ * Replaces target_logits_for_hidden (native_model.cc:1782-1795: quantized_matmul against
+ * embed_tokens, bf16, tanh(l/30)*30 in bf16) and the greedy argmax of its callers (:3825,
+ * :3934; first index wins ties) in one pass over the 262144 x 3840 table. softcap <= 0 skips
+ * the softcap. Per row m of x (M <= 16): tokens[m] = row_offset + argmax, values[m] = the
+ * softcapped logit (as float), keys[m] = order-preserving 64-bit key
+ * ((ordered float bits) << 32 | (0xFFFFFFFF - token)) for combining vocabulary shards with
+ * a max. Any of tokens/values/keys/logits may be NULL; logits (bf16 [M, ld_logits]) receives
+ * the pre-softcap bf16 logits when given. Uses a small scratch owned by the handle: calls on
+ * one handle must not overlap on the GPU. */
+G4qStatus g4q_lm_head_argmax(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t ldx, float softcap,
+                             uint32_t flags, float eps, int64_t row_offset, uint16_t* logits,
+                             int64_t ld_logits, int32_t* tokens, float* values, uint64_t* keys,
+                             void* stream);
+
+/* ---- seeded synthetic data (no reference counterpart: benchmark / test inputs) ---------------
+ * Counter-based splitmix64 generator identical to the CPU oracle's: MLX-layout packed
+ * (q ~ U{0..15}), scale = bf16(U(0.002, 0.02)), bias = bf16(-8*scale + 1e-3*N(0,1)); and
+ * bf16 ~ N(0,1) activations. Device pointers. */
+G4qStatus g4q_synth_matrix(uint64_t seed, int64_t rows, int64_t cols, int32_t bits, int32_t group_size,
+                           uint32_t* packed, uint16_t* scales, uint16_t* biases, void* stream);
+G4qStatus g4q_synth_normal_bf16(uint64_t seed, int64_t count, uint16_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* G4Q_H */

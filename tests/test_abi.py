@@ -1,0 +1,63 @@
+"""The C-ABI library loads and exports every entry point include/g4q.h declares (no GPU needed)."""
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+
+
+def declared_functions():
+    text = (ROOT / "include" / "g4q.h").read_text()
+    return sorted(set(re.findall(r"^G4qStatus\s+(g4q_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for required in ("g4q_weight_create", "g4q_weight_load", "g4q_qmm", "g4q_dequantize", "g4q_lm_head_argmax",
+                     "g4q_get_last_error", "g4q_runtime_version"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    from helios_b200 import _lib
+    L = _lib.load()
+    missing = [n for n in declared_functions() if not hasattr(L, n)]
+    assert not missing, missing
+    # the Python binding declares a signature for every exported entry point
+    assert set(declared_functions()) <= set(_lib.SIGNATURES), set(declared_functions()) - set(_lib.SIGNATURES)
+
+
+def test_version_and_last_error_without_gpu():
+    from helios_b200 import _lib
+    v = _lib.version()
+    assert v["abi_version"] == 1 and v["backend_name"] == "g4q_b200"
+    assert _lib.last_error() == ""
+
+
+def test_status_and_message_on_invalid_arguments_without_gpu():
+    from helios_b200 import _lib
+    L = _lib.load()
+    st = L.g4q_weight_create(64, 128, 4, 64, None)
+    assert st == _lib.G4Q_ERR_INVALID_ARGUMENT
+    assert "non-null out pointer" in _lib.last_error()
+    st = L.g4q_qmm(None, None, 1, 64, None, 64, None)
+    assert st == _lib.G4Q_ERR_INVALID_ARGUMENT
+    assert "weight handle" in _lib.last_error()
+    bogus = ctypes.create_string_buffer(256)       # not a handle: the magic check rejects it
+    st = L.g4q_weight_free(ctypes.cast(bogus, ctypes.c_void_p))
+    assert st == _lib.G4Q_ERR_INVALID_ARGUMENT and "invalid weight handle" in _lib.last_error()
+    assert L.g4q_get_last_error(None, 0) == _lib.G4Q_ERR_INVALID_ARGUMENT
+    with pytest.raises(_lib.G4qInvalidArgument):
+        _lib.call("g4q_runtime_version", None)
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    from helios_b200 import _lib
+    saved = _lib._lib
+    try:
+        _lib._lib = None
+        with pytest.raises(_lib.G4qUnavailable):
+            _lib.load(tmp_path / "nope.so")
+    finally:
+        _lib._lib = saved

@@ -1,0 +1,97 @@
+"""GPU: the synthetic decoder stack end to end (fused q|k|v and gate|up launches, RMS scales
+folded into epilogues, LM-head softcap + argmax) against the oracle's stack, eager and
+replayed from a CUDA graph; plus error statuses of invalid calls (no GPU fault involved)."""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import qmm_error, u16
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(layers=3, hidden=256, q_out=256, kv_out=128, inter=512, vocab=4096)
+
+
+def oracle_stack(oracle, cfg, h0):
+    shapes = oracle.stack_shapes(cfg.hidden, cfg.q_out, cfg.kv_out, cfg.inter, cfg.vocab)
+    return oracle.stack_forward(h0, cfg.layers, shapes, cap=cfg.softcap, eps=cfg.eps)
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_small_stack_matches_oracle(cuda, oracle, M):
+    from helios_b200.quantized import synth_normal
+    from helios_b200.stack import StackConfig, SyntheticStack, activation_seed, decode_keys
+    cfg = StackConfig(**SMALL)
+    st = SyntheticStack(cfg)
+    h0 = synth_normal(activation_seed(M), (M, cfg.hidden))
+    keys, h = st.forward(h0)
+    ref = oracle_stack(oracle, cfg, u16(h0))
+    excess, rms = qmm_error(oracle.bf16_to_f32(u16(h)), ref["hidden"].astype(np.float64), bf16_out=True)
+    assert excess <= 2e-2 * rms
+    toks, vals = decode_keys(keys)
+    for m in range(M):
+        if toks[m] != ref["tokens"][m]:
+            assert abs(vals[m] - ref["values"][m]) <= 0.125
+    st.free()
+
+
+def test_cuda_graph_replay_equals_eager(cuda, oracle):
+    from helios_b200.quantized import synth_normal
+    from helios_b200.stack import StackConfig, SyntheticStack, activation_seed
+    cfg = StackConfig(**SMALL)
+    st = SyntheticStack(cfg)
+    static_h = synth_normal(activation_seed(0), (1, cfg.hidden))
+    k_eager, h_eager = st.forward(static_h)
+    k_eager, h_eager = k_eager.clone(), h_eager.clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        st.forward(static_h)     # warm-up on the capture stream
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        k_g, h_g = st.forward(static_h)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(k_g, k_eager) and torch.equal(h_g, h_eager)
+    static_h.copy_(synth_normal(activation_seed(5), (1, cfg.hidden)))
+    g.replay()
+    k2, h2 = st.forward(static_h.clone())
+    torch.cuda.synchronize()
+    assert torch.equal(k_g, k2)
+    del g
+    st.free()
+
+
+def test_invalid_calls_return_status(cuda, oracle):
+    from helios_b200 import _lib
+    from helios_b200 import quantized as Q
+    w, s, b = Q.synth_matrix(1, 64, 256)
+    with pytest.raises(_lib.G4qError) as e:
+        Q.QuantizedWeight(60, 256)                       # rows % 16 != 0
+    assert e.value.status == _lib.G4Q_ERR_UNSUPPORTED_CONFIG
+    with pytest.raises(_lib.G4qError):
+        Q.QuantizedWeight(64, 256, bits=8)               # 8-bit not in the kernel layout
+    q = Q.QuantizedWeight.from_mlx(w, s, b)
+    with pytest.raises(ValueError):
+        Q.quantized_matmul(torch.zeros((1, 128), dtype=torch.bfloat16, device=cuda), q)   # K mismatch
+    with pytest.raises(_lib.G4qInvalidArgument):
+        q.load(w, s, b, src_row=32, n_rows=48)           # window past the source
+    with pytest.raises(_lib.G4qInvalidArgument):
+        _lib.call("g4q_qmm", q.handle, 12345, 1, 256, 0, 64, None)   # misaligned x (checked on host)
+    with pytest.raises(_lib.G4qInvalidArgument):
+        Q.lm_head_argmax(torch.zeros((17, 256), dtype=torch.bfloat16, device=cuda), q)   # M > 16
+    # a huge scale disables the fast path with a clear status, while dequantize still works
+    s2 = s.clone()
+    s2[0, 0] = torch.tensor(2.0 ** 121, dtype=torch.bfloat16)
+    q2 = Q.QuantizedWeight.from_mlx(w, s2, b)
+    assert q2.info()["fast_path_ok"] == 0
+    with pytest.raises(_lib.G4qError) as e:
+        Q.quantized_matmul(torch.zeros((1, 256), dtype=torch.bfloat16, device=cuda), q2)
+    assert e.value.status == _lib.G4Q_ERR_UNSUPPORTED_CONFIG
+    Q.dequantize(q2)
+    torch.cuda.synchronize()
+    q.free()
+    q2.free()
+    with pytest.raises(ValueError):
+        q.handle
