@@ -65,6 +65,7 @@ SIGNATURES = {
     "g4q_qmm": [_P, _P, _I64, _I64, _P, _I64, _P],
     "g4q_qmm_ex": [_P, _P, _I64, _I64, _P, _I64, _U32, _F, _P],
     "g4q_lm_head_argmax": [_P, _P, _I64, _I64, _F, _U32, _F, _I64, _P, _I64, _P, _P, _P, _P],
+    "g4q_device_error": [ctypes.POINTER(_I32), _I32],
     "g4q_synth_matrix": [_U64, _I64, _I64, _I32, _I32, _P, _P, _P, _P],
     "g4q_synth_normal_bf16": [_U64, _I64, _P, _P],
 }
@@ -124,6 +125,13 @@ def call(name: str, *args) -> None:
         msg = last_error()
         cls = G4qInvalidArgument if status == G4Q_ERR_INVALID_ARGUMENT else G4qError
         raise cls(status, msg, name)
+
+
+def device_error(reset: bool = True) -> int:
+    """Nonzero when a bounded in-kernel wait gave up since the last reset (results invalid)."""
+    code = ctypes.c_int32(0)
+    call("g4q_device_error", ctypes.byref(code), 1 if reset else 0)
+    return code.value
 
 
 def version() -> dict:

@@ -46,6 +46,41 @@ int device_sm_count() {
     return cache[d & 63];
 }
 
+size_t max_dynamic_smem(const void* kernel) {
+    int optin = 0;
+    check_cuda(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, current_device()),
+               "cudaDeviceGetAttribute(smem optin)");
+    cudaFuncAttributes fa;
+    check_cuda(cudaFuncGetAttributes(&fa, kernel), "cudaFuncGetAttributes");
+    return (size_t)optin - fa.sharedSizeBytes;
+}
+
+static std::mutex g_scratch_mu;
+
+DeviceScratch& device_scratch() {
+    static DeviceScratch per_dev[64];
+    const int d = current_device();
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    DeviceScratch& s = per_dev[d & 63];
+    if (s.err == nullptr) {
+        constexpr int64_t kRows = 65536;
+        int* err = nullptr;
+        float* rms = nullptr;
+        check_cuda(cudaMalloc(&err, sizeof(int)), "cudaMalloc(device error word)");
+        cudaError_t e = cudaMalloc(&rms, kRows * sizeof(float));
+        if (e == cudaSuccess) e = cudaMemset(err, 0, sizeof(int));
+        if (e != cudaSuccess) {
+            cudaFree(err);
+            cudaFree(rms);
+            check_cuda(e, "device scratch");
+        }
+        s.rms = rms;
+        s.rms_rows = kRows;
+        s.err = err;
+    }
+    return s;
+}
+
 // Runs an entry point body, translating exceptions into a status + message.
 template <typename F>
 static G4qStatus guarded(const char* fn, F&& body) {
@@ -121,6 +156,7 @@ G4qStatus g4q_weight_create(int64_t rows, int64_t cols, int32_t bits, int32_t gr
                     ", group_size=" + std::to_string(group_size) + ")");
         require(rows % 16 == 0, G4Q_ERR_UNSUPPORTED_CONFIG, "rows must be a multiple of 16");
         require(cols % 64 == 0, G4Q_ERR_UNSUPPORTED_CONFIG, "cols must be a multiple of 64");
+        (void)device_scratch();   // per-device library state exists before any compute call
         Weight* w = new (std::nothrow) Weight();
         require(w != nullptr, G4Q_ERR_MEMORY_GUARD, "host allocation failed");
         w->N = rows;
@@ -323,6 +359,17 @@ G4qStatus g4q_lm_head_argmax(const G4qWeight* h, const uint16_t* x, int64_t M, i
         require(w->fast_ok, G4Q_ERR_UNSUPPORTED_CONFIG, "a scale is non-finite or |scale| >= 2^120");
         launch_lm_head(*w, x, M, ldx, softcap, flags, eps, row_offset, logits, ld_logits, tokens, values,
                        reinterpret_cast<unsigned long long*>(keys), reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+G4qStatus g4q_device_error(int32_t* code, int32_t reset) {
+    return guarded("g4q_device_error", [&] {
+        require(code != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null code pointer");
+        DeviceScratch& ds = device_scratch();
+        int v = 0;
+        check_cuda(cudaMemcpy(&v, ds.err, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
+        if (reset && v != 0) check_cuda(cudaMemset(ds.err, 0, sizeof(int)), "reset device error word");
+        *code = v;
     });
 }
 

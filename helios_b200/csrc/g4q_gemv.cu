@@ -334,7 +334,8 @@ __global__ void __launch_bounds__(kThreads) lm_head_kernel(GemvArgs a, float cap
 template <typename Kern>
 void set_max_smem(Kern kern) {
     // once per process and kernel instance: opt in to the full 227 KB of dynamic shared memory
-    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)max_dynamic_smem(reinterpret_cast<const void*>(kern))),
                "cudaFuncSetAttribute(smem)");
 }
 
@@ -384,7 +385,7 @@ void launch_gemv_t(GemvArgs a, cudaStream_t st) {
         const int S_eff = (a.G + gps - 1) / gps;
         if (S_eff != S || gps < 4) continue;
         const size_t smem = gemv_smem_bytes(gps, a.M, MT);
-        if (smem > 227 * 1024) continue;
+        if (smem > max_dynamic_smem(reinterpret_cast<const void*>(gemv_kernel<MT, true>))) continue;
         const int cap = occupancy(gemv_kernel<MT, true>, smem) * sms;
         if (chunks * S <= cap) {
             best_S = S;
@@ -393,7 +394,8 @@ void launch_gemv_t(GemvArgs a, cudaStream_t st) {
     }
     a.gps = best_gps;
     const size_t smem = gemv_smem_bytes(a.gps, a.M, MT);
-    if (smem > 227 * 1024) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "qmm: activation slice does not fit in shared memory");
+    if (smem > max_dynamic_smem(reinterpret_cast<const void*>(gemv_kernel<MT, false>)))
+        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "qmm: activation slice does not fit in shared memory");
     if (best_S == 1) {
         gemv_kernel<MT, false><<<dim3(chunks, 1), kThreads, smem, st>>>(a);
     } else {
@@ -426,7 +428,8 @@ void launch_lm_t(GemvArgs a, float cap, int64_t row_offset, uint16_t* logits, in
     }
     a.gps = a.G;
     const size_t smem = gemv_smem_bytes(a.G, a.M, MT);
-    if (smem > 227 * 1024) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "lm_head: activations do not fit in shared memory");
+    if (smem > max_dynamic_smem(reinterpret_cast<const void*>(lm_head_kernel<MT>)))
+        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "lm_head: activations do not fit in shared memory");
     const int chunks = (a.R + kWarps - 1) / kWarps;
     int grid = occupancy(lm_head_kernel<MT>, smem) * device_sm_count();
     if (grid < 1) grid = 1;

@@ -36,12 +36,26 @@ struct Error : std::runtime_error {
 };
 
 inline void check_cuda(cudaError_t e, const char* what) {
-    if (e != cudaSuccess)
+    if (e != cudaSuccess) {
+        cudaGetLastError();   // do not leave a non-sticky error behind for the next launch check
         throw Error(G4Q_ERR_RUNTIME, std::string(what) + ": " + cudaGetErrorString(e));
+    }
 }
 
 int device_sm_count();
 int current_device();
+// Largest dynamic shared memory a kernel may opt in to, given its static shared memory.
+size_t max_dynamic_smem(const void* kernel);
+
+// Per-device library state, created by the first g4q_weight_create on that device (never
+// inside a stream capture): a device error word written by bounded waits that gave up, and the
+// per-row RMS scales of the prefill GEMM.
+struct DeviceScratch {
+    int* err = nullptr;
+    float* rms = nullptr;
+    int64_t rms_rows = 0;
+};
+DeviceScratch& device_scratch();
 
 // kernels (g4q_layout.cu)
 void launch_synth_matrix(uint64_t seed, int64_t N, int64_t K, int bits, int group_size, uint32_t* w,

@@ -139,6 +139,13 @@ G4qStatus g4q_lm_head_argmax(const G4qWeight* w, const uint16_t* x, int64_t M, i
                              int64_t ld_logits, int32_t* tokens, float* values, uint64_t* keys,
                              void* stream);
 
+/* ---- device-side failure detection ----------------------------------------------------------
+ * Every wait inside a libg4q kernel is bounded; a wait that gives up records a nonzero code in a
+ * per-device error word and the kernel runs to its end (its results are then invalid). This
+ * reads the word for the current device (synchronising it) and optionally clears it. No
+ * reference counterpart: the reference's MLX graph has no device-side waits. */
+G4qStatus g4q_device_error(int32_t* code, int32_t reset);
+
 /* ---- seeded synthetic data (no reference counterpart: benchmark / test inputs) ---------------
  * Counter-based splitmix64 generator identical to the CPU oracle's: MLX-layout packed
  * (q ~ U{0..15}), scale = bf16(U(0.002, 0.02)), bias = bf16(-8*scale + 1e-3*N(0,1)); and

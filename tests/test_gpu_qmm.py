@@ -93,6 +93,28 @@ def test_prefill_widths_small_n(cuda, oracle, M):
     qw.free()
 
 
+@pytest.mark.parametrize("M,N,K", [(100, 1920, 3840), (129, 272, 640), (300, 3840, 4096)])
+def test_prefill_gemm_ragged_rms_f32(cuda, oracle, M, N, K):
+    """tcgen05 GEMM: M not a multiple of 128, N not a multiple of 256 (TP-8 gate shard, 17 row
+    tiles), RMS row scale and fp32 output; no bounded wait may have given up."""
+    from helios_b200 import _lib
+    from helios_b200 import quantized as Q
+    seed = oracle.matrix_seed(2, 4) ^ N
+    w, s, b = Q.synth_matrix(seed, N, K)
+    qw = Q.QuantizedWeight.from_mlx(w, s, b)
+    x = Q.synth_normal(oracle.activation_seed(M), (M, K))
+    xn = u16(x)
+    ow, os_, ob = oracle.synth_matrix(seed, N, K)
+    r = np.array([oracle.rms_scale(xn[m]) for m in range(M)], dtype=np.float32)
+    ye, _ = oracle.qmm(xn, ow, os_, ob, row_scale=r)
+    yf = Q.quantized_matmul(x, qw, rms_scale=True, out_dtype=torch.float32).cpu().numpy()
+    assert_qmm_close(yf, ye, bf16_out=False)
+    yb = Q.quantized_matmul(x, qw, rms_scale=True)
+    assert_qmm_close(oracle.bf16_to_f32(u16(yb)), ye, bf16_out=True)
+    assert _lib.device_error() == 0
+    qw.free()
+
+
 def test_prefill_chunk_2048(cuda, oracle):
     """A full 2048-token prefill chunk (BASELINE config 3 width) on a 256-row slice of up_proj."""
     from helios_b200 import quantized as Q
