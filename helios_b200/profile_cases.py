@@ -1,0 +1,77 @@
+"""Small, self-contained kernel cases for ncu captures (one GPU, a few GB at most).
+
+    python -m helios_b200.profile_cases gemv      # fused gate|up GEMV, 30720 x 3840, M = 1
+    python -m helios_b200.profile_cases gemv8     # same at M = 8 (MTP verify width)
+    python -m helios_b200.profile_cases lmhead    # LM head 262144 x 3840 + softcap + argmax, M = 1
+    python -m helios_b200.profile_cases gemm      # prefill dequant-GEMM, q|k|v 8192 x 3840, M = 2048
+    python -m helios_b200.profile_cases dequant   # bit-exact dequantize of 15360 x 3840
+
+Each case uploads seeded synthetic weights (several copies where the matrix is smaller than L2,
+so consecutive launches read cold data), runs a few warm-up launches and then `--launches`
+timed launches, and prints the CUDA-event average per launch.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from .quantized import QuantizedWeight, dequantize, lm_head_argmax, quantized_matmul, synth_matrix, synth_normal
+from .stack import activation_seed, matrix_seed
+
+CASES = {
+    "gemv": dict(N=30720, K=3840, M=1, copies=4),
+    "gemv8": dict(N=30720, K=3840, M=8, copies=4),
+    "lmhead": dict(N=262144, K=3840, M=1, copies=1),
+    "gemm": dict(N=8192, K=3840, M=2048, copies=1),
+    "dequant": dict(N=15360, K=3840, M=0, copies=1),
+}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=sorted(CASES))
+    ap.add_argument("--launches", type=int, default=6)
+    ap.add_argument("--warmup", type=int, default=2)
+    a = ap.parse_args()
+    c = CASES[a.case]
+    torch.cuda.set_device(0)
+    ws = []
+    for i in range(c["copies"]):
+        w, s, b = synth_matrix(matrix_seed(i, "gate"), c["N"], c["K"])
+        ws.append(QuantizedWeight.from_mlx(w, s, b))
+        del w, s, b
+    M = max(c["M"], 1)
+    x = synth_normal(activation_seed(0), (M, c["K"]))
+    y = torch.empty((M, c["N"]), dtype=torch.bfloat16, device="cuda")
+
+    def run(i):
+        q = ws[i % len(ws)]
+        if a.case == "lmhead":
+            lm_head_argmax(x, q, softcap=30.0, rms_scale=True)
+        elif a.case == "dequant":
+            dequantize(q)
+        else:
+            quantized_matmul(x, q, rms_scale=True, out=y)
+
+    for i in range(a.warmup):
+        run(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(a.launches):
+        run(i)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / a.launches
+    wbytes = c["N"] * c["K"] * 9 // 16
+    out = {"case": a.case, "us_per_launch": round(us, 3), "weight_bytes": wbytes,
+           "weight_GBps": round(wbytes / us / 1e3, 1)}
+    if a.case == "gemm":
+        out["TFLOPs"] = round(2 * c["M"] * c["N"] * c["K"] / us / 1e6, 1)
+    print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()

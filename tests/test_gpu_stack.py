@@ -26,7 +26,8 @@ def test_small_stack_matches_oracle(cuda, oracle, M):
     h0 = synth_normal(activation_seed(M), (M, cfg.hidden))
     keys, h = st.forward(h0)
     ref = oracle_stack(oracle, cfg, u16(h0))
-    excess, rms = qmm_error(oracle.bf16_to_f32(u16(h)), ref["hidden"].astype(np.float64), bf16_out=True)
+    excess, rms = qmm_error(oracle.bf16_to_f32(u16(h)), oracle.bf16_to_f32(ref["hidden"]).astype(np.float64),
+                            bf16_out=True)
     assert excess <= 2e-2 * rms
     toks, vals = decode_keys(keys)
     for m in range(M):

@@ -94,6 +94,28 @@ def test_qmm_f32_baseline_close(oracle):
     assert np.abs(y - z["y_r2"]).max() <= 1e-2 * rms + 0.5 * np.abs(z["y_r2"]).max() * 2 ** -7
 
 
+def test_qmm_f32_table_equals_exact_dequant(oracle):
+    """The CPU baseline's fp32 R2 table reproduces the exact dequantized bits: with one-hot rows
+    of x, y[m, n] = deq(W)[n, k_m] exactly."""
+    kat = json.loads((GOLDEN / "deq_kat.json").read_text())["cases"]
+    # keep every q of every group finite (0 * inf in an fp32 accumulation would be NaN)
+    kat = [c for c in kat if (c["scale"] >> 7) & 0xFF < 240 and (c["bias"] >> 7) & 0xFF < 240][:512]
+    N, G = 8, 64
+    s = np.full((N, G), 0x3F80, dtype=np.uint16)
+    b = np.zeros((N, G), dtype=np.uint16)
+    for i, c in enumerate(kat):
+        s[i // G, i % G], b[i // G, i % G] = c["scale"], c["bias"]
+    w = np.random.default_rng(3).integers(0, 2 ** 32, size=(N, G * 8), dtype=np.uint32)
+    K = G * 64
+    ks = np.arange(0, K, 37)
+    x = np.zeros((ks.size, K), dtype=np.uint16)
+    x[np.arange(ks.size), ks] = 0x3F80
+    y = oracle.qmm_f32(x, w, s, b)
+    ref = oracle.dequantize(w, s, b)[:, ks].T
+    zero = lambda a: np.where(a == 0x8000, 0, a)   # an fp32 sum starting at +0 turns -0 into +0
+    assert (zero(y) == zero(ref)).all()
+
+
 def test_layout_v1_fixture_and_roundtrip(oracle):
     z = np.load(GOLDEN / "small_matrix.npz")
     packed, sb = oracle.repack(z["w"], z["scales"], z["biases"])
