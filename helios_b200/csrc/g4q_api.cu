@@ -63,22 +63,42 @@ DeviceScratch& device_scratch() {
     std::lock_guard<std::mutex> lock(g_scratch_mu);
     DeviceScratch& s = per_dev[d & 63];
     if (s.err == nullptr) {
-        constexpr int64_t kRows = 65536;
+        constexpr int64_t kRows = 65536, kQuads = 65536;
         int* err = nullptr;
         float* rms = nullptr;
+        int* counters = nullptr;
         check_cuda(cudaMalloc(&err, sizeof(int)), "cudaMalloc(device error word)");
         cudaError_t e = cudaMalloc(&rms, kRows * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&counters, kQuads * sizeof(int));
         if (e == cudaSuccess) e = cudaMemset(err, 0, sizeof(int));
+        if (e == cudaSuccess) e = cudaMemset(counters, 0, kQuads * sizeof(int));
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e != cudaSuccess) {
             cudaFree(err);
             cudaFree(rms);
+            cudaFree(counters);
             check_cuda(e, "device scratch");
         }
         s.rms = rms;
         s.rms_rows = kRows;
+        s.counters = counters;
+        s.counters_n = kQuads;
         s.err = err;
     }
     return s;
+}
+
+void reserve_gemv_scratch(int64_t N, int64_t K) {
+    DeviceScratch& s = device_scratch();
+    const size_t need = gemv2_slots_bytes(N, K, device_sm_count());
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (need <= s.slots_bytes) return;
+    // cudaFree/cudaMalloc synchronise with the device, so no kernel is still using the old slots
+    cudaFree(s.slots);
+    s.slots = nullptr;
+    s.slots_bytes = 0;
+    check_cuda(cudaMalloc(&s.slots, need), "cudaMalloc(gemv slots)");
+    s.slots_bytes = need;
 }
 
 // Runs an entry point body, translating exceptions into a status + message.
@@ -157,6 +177,8 @@ G4qStatus g4q_weight_create(int64_t rows, int64_t cols, int32_t bits, int32_t gr
         require(rows % 16 == 0, G4Q_ERR_UNSUPPORTED_CONFIG, "rows must be a multiple of 16");
         require(cols % 64 == 0, G4Q_ERR_UNSUPPORTED_CONFIG, "cols must be a multiple of 64");
         (void)device_scratch();   // per-device library state exists before any compute call
+        require(rows / 64 <= device_scratch().counters_n, G4Q_ERR_UNSUPPORTED_CONFIG, "rows exceed 4,194,304");
+        reserve_gemv_scratch(rows, cols);
         Weight* w = new (std::nothrow) Weight();
         require(w != nullptr, G4Q_ERR_MEMORY_GUARD, "host allocation failed");
         w->N = rows;

@@ -441,6 +441,10 @@ void launch_lm_t(GemvArgs a, float cap, int64_t row_offset, uint16_t* logits, in
 }  // namespace
 
 void launch_gemv(const QmmCall& c, cudaStream_t st) {
+    if (gemv2_supported(c)) {
+        launch_gemv2(c, st);
+        return;
+    }
     GemvArgs a = make_args(*c.w, c.x, c.M, c.ldx, c.y, c.ldy, c.flags, c.eps);
     if (c.M <= 8)
         launch_gemv_t<1>(a, st);

@@ -54,8 +54,17 @@ struct DeviceScratch {
     int* err = nullptr;
     float* rms = nullptr;
     int64_t rms_rows = 0;
+    float* slots = nullptr;      // stream-K GEMV partial sums
+    size_t slots_bytes = 0;
+    int* counters = nullptr;     // stream-K GEMV per-quad arrival counters, zero between launches
+    int64_t counters_n = 0;
 };
 DeviceScratch& device_scratch();
+// Grows the GEMV partial-sum slots to cover an N x K weight (called by g4q_weight_create).
+void reserve_gemv_scratch(int64_t N, int64_t K);
+
+// kernels (g4q_gemv2.cu): persistent stream-K GEMV for M <= 8
+size_t gemv2_slots_bytes(int64_t N, int64_t K, int sms);
 
 // kernels (g4q_layout.cu)
 void launch_synth_matrix(uint64_t seed, int64_t N, int64_t K, int bits, int group_size, uint32_t* w,
@@ -81,6 +90,8 @@ struct QmmCall {
     float eps;
 };
 void launch_gemv(const QmmCall& c, cudaStream_t st);
+bool gemv2_supported(const QmmCall& c);
+void launch_gemv2(const QmmCall& c, cudaStream_t st);
 void launch_lm_head(const Weight& w, const uint16_t* x, int64_t M, int64_t ldx, float softcap, uint32_t flags,
                     float eps, int64_t row_offset, uint16_t* logits, int64_t ld_logits, int32_t* tokens,
                     float* values, unsigned long long* keys, cudaStream_t st);

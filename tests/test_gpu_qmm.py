@@ -53,10 +53,12 @@ def test_decode_gemv_odd_widths(cuda, oracle, M):
     qw.free()
 
 
-@pytest.mark.parametrize("N,K", [(16, 64), (48, 192), (80, 1024), (272, 640)])
+@pytest.mark.parametrize("N,K", [(16, 64), (48, 192), (80, 1024), (272, 640), (128, 768), (320, 192),
+                                 (1088, 512)])
 @pytest.mark.parametrize("M", [1, 7, 16])
 def test_ragged_small_shapes(cuda, oracle, N, K, M):
-    """N not a multiple of the 64-row CTA chunk, K of a few groups: idle warps, 1-group splits."""
+    """Small and ragged shapes: N not a multiple of 64 (cluster split-K kernel), and tiny stream-K
+    grids where one 64-row quad is reduced from many warps' partial sums."""
     from helios_b200 import quantized as Q
     w, s, b = oracle.synth_matrix(N * 7 + K, N, K)
     x = oracle.synth_normal_bf16(N + K + M, M * K).reshape(M, K)
@@ -66,6 +68,17 @@ def test_ragged_small_shapes(cuda, oracle, N, K, M):
     ye, _ = oracle.qmm(x, w, s, b)
     yf = Q.quantized_matmul(dev_u16(x, cuda), qw, out_dtype=torch.float32).cpu().numpy()
     assert_qmm_close(yf, ye, bf16_out=False)
+    qw.free()
+
+
+def test_stream_k_is_deterministic(cuda, oracle):
+    """Split quads are summed in a fixed contributor order: repeated launches are bit-identical."""
+    from helios_b200 import _lib
+    from helios_b200 import quantized as Q
+    qw, x, _ = make(oracle, Q, "down", 3840, 15360, 1, layer=2)
+    ys = [Q.quantized_matmul(x, qw, out_dtype=torch.float32) for _ in range(3)]
+    assert all(torch.equal(ys[0], y) for y in ys[1:])
+    assert _lib.device_error() == 0
     qw.free()
 
 
