@@ -5,17 +5,19 @@
 //  * Work unit = one 64-wide quantization group of a "quad" of four 16-row tiles (64 rows): 2 KB of
 //    packed words (contiguous in layout v1) + 256 B of scale|bias words.
 //  * Persistent grid, one 16-warp CTA per SM. The (quad, group) unit space, quad-major, is cut into
-//    equal contiguous CTA ranges, so every SM streams the same number of bytes whatever N and K are.
-//    Inside a CTA the units of each quad go round-robin to the 16 warps.
+//    equal contiguous CTA ranges, so every SM streams the same number of bytes whatever N and K are;
+//    inside a CTA, unit cs + w + 16k belongs to warp w (per-warp counts differ by at most one).
 //  * Each warp owns a private ring of kStages unit buffers in shared memory. Lane 0 refills a buffer
-//    with two cp.async.bulk copies (mbarrier completion) as soon as the warp has the unit in
-//    registers, running kStages units ahead through the warp's sequence, across quad boundaries.
+//    with two cp.async.bulk copies (mbarrier completion) as soon as the warp holds the unit in
+//    registers, so kStages units per warp (~110 KB per SM) are always in flight.
 //  * x (M <= 8 tokens, full K) is staged once per CTA in B-fragment order while the first weight
-//    copies are in flight; the RMS scale (sum of squares over K) is reduced there too.
-//  * Per quad the 16 warps' fp32 partials are summed in shared memory in warp order. A quad cut by
-//    a CTA-range boundary (2-3 CTAs) is finished through global slots: each CTA stores its partial
-//    in its own slot and bumps the quad's counter; the last arriver sums the slots in CTA order,
-//    applies the epilogue and resets the counter to zero. Results are bit-reproducible.
+//    copies land; the RMS scale (sum of squares over K) is reduced there too.
+//  * When a warp leaves a quad it parks its fp32 partial in shared memory (double-buffered by quad
+//    parity); the last warp to park a quad sums the partials in warp order, so no CTA-wide barrier
+//    sits in the loop. A quad cut by a CTA-range boundary is finished through global slots: each
+//    CTA stores its partial in its own slot and bumps the quad's counter; the last arriver sums the
+//    slots in CTA order, applies the epilogue and resets the counter to zero. Results are
+//    bit-reproducible.
 #include "g4q_common.cuh"
 #include "g4q_internal.h"
 
@@ -29,7 +31,7 @@ constexpr uint32_t kUnitPacked = 4 * 512;     // four 16-row tiles x one group
 constexpr uint32_t kUnitSb = 64 * 4;
 constexpr uint32_t kUnitBytes = kUnitPacked + kUnitSb;
 constexpr uint32_t kRingBytes = kStages * kUnitBytes;
-constexpr uint32_t kRedBytesPerTok = kWarpsV2 * 64 * 4;
+constexpr uint32_t kRedBytesPerTok = 2 * kWarpsV2 * 64 * 4;   // [quad parity][tok][warp][row]
 constexpr long long kWaitLimitCycles2 = 4000000000ll;
 
 struct Gemv2Args {
@@ -43,30 +45,37 @@ struct Gemv2Args {
     int64_t ldy;
     uint32_t flags;
     float eps;
-    float* slots;           // [Q][maxc][64 rows][8 tokens]
-    int maxc;
+    float* slots;           // [Q][8][64 rows][8 tokens]
     int* counters;          // [Q], zero between launches
     int* err;
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-__device__ __forceinline__ void wait_parity(uint32_t bar, uint32_t parity, int* err) {
+__device__ __forceinline__ bool try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __noinline__ void wait_slow(uint32_t bar, uint32_t parity, int* err) {
     const long long t0 = clock64();
     for (uint32_t it = 0;; ++it) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (done) return;
+        if (try_wait(bar, parity)) return;
         if ((it & 1023u) == 1023u && *reinterpret_cast<volatile int*>(err) != 0) return;
         if (clock64() - t0 > kWaitLimitCycles2) {
             atomicCAS(err, 0, 16);
             return;
         }
     }
+}
+
+__device__ __forceinline__ void wait_parity(uint32_t bar, uint32_t parity, int* err) {
+    if (!try_wait(bar, parity)) wait_slow(bar, parity, err);
 }
 
 __device__ __forceinline__ void issue_unit(const Gemv2Args& a, int q, int g, uint32_t dst, uint32_t bar) {
@@ -91,76 +100,159 @@ __device__ __forceinline__ int cta_of_unit(int u, int U, int C) {
     return c;
 }
 
-// A warp's walk over its units: quads [q, q_last] of the CTA range [cs, ce), and inside each quad
-// every kWarpsV2-th unit starting at the warp index.
-struct Walk {
-    int q, u, hi;
-    bool done;
-    __device__ __forceinline__ void settle(int G, int ce, int q_last, int w) {
-        while (!done && u >= hi) {
-            ++q;
-            if (q > q_last) {
-                done = true;
+// advance a (quad, group) position by kWarpsV2 units
+__device__ __forceinline__ void step(int& q, int& g, int G) {
+    g += kWarpsV2;
+    while (g >= G) {
+        g -= G;
+        ++q;
+    }
+}
+
+__device__ __forceinline__ void store_out(const Gemv2Args& a, int q, int row, int tok, float v, float r) {
+    const float o = __fmul_rn(v, r);
+    const int64_t idx = (int64_t)tok * a.ldy + q * 64 + row;
+    if (a.flags & G4Q_QMM_OUT_F32)
+        reinterpret_cast<float*>(a.y)[idx] = o;
+    else
+        reinterpret_cast<uint16_t*>(a.y)[idx] = f32_to_bf16_bits(o);
+}
+
+// Shared state of one CTA for the per-quad reduction: partial sums are double-buffered by quad
+// parity; the last warp to park a quad reduces it and frees the buffer.
+struct QuadRed {
+    int cnt[2];
+    int done[2];
+    int last_cta;
+};
+
+// Park this warp's partial of quad q; the last warp of the quad reduces it (fixed warp order),
+// stores whole quads and finishes cut quads through the global slots.
+__device__ __forceinline__ void park_quad(const Gemv2Args& a, QuadRed& qr, float* red, int q, int cs, int ce, int cta,
+                                          int C, const float (&acc)[4][4], const float* rs) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
+    const int M = a.M, G = a.G;
+    const int b = q & 1;
+    // the buffer was last used by quad q - 2: wait until that quad has been reduced
+    if (*reinterpret_cast<volatile int*>(&qr.done[b]) < q - 2) {
+        const long long t0 = clock64();
+        while (*reinterpret_cast<volatile int*>(&qr.done[b]) < q - 2) {
+            if (clock64() - t0 > kWaitLimitCycles2) {
+                atomicCAS(a.err, 0, 17);
                 break;
             }
-            hi = min(ce, (q + 1) * G);
-            u = q * G + w;
         }
     }
-    __device__ __forceinline__ void init(int cs, int ce, int G, int q_first, int q_last, int w) {
-        done = cs >= ce;
-        q = q_first;
-        hi = min(ce, (q + 1) * G);
-        u = cs + w;
-        settle(G, ce, q_last, w);
+    float* rb = red + (size_t)b * M * kWarpsV2 * 64;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int tok = 2 * t + (e & 1);
+            if (tok < M) rb[(tok * kWarpsV2 + warp) * 64 + i * 16 + gi + ((e & 2) ? 8 : 0)] = acc[i][e];
+        }
+    __threadfence_block();
+    __syncwarp();
+    const int lo = max(cs, q * G), hi = min(ce, (q + 1) * G);
+    const int nw = min(kWarpsV2, hi - lo);          // warps holding a partial of this quad
+    const int w0 = (lo - cs) % kWarpsV2;            // first of them (cyclically)
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&qr.cnt[b], 1) == nw - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence_block();
+    const bool whole = cs <= q * G && ce >= (q + 1) * G;
+    const int nout = 64 * M;
+    float* base = a.slots + (size_t)q * 8 * 512;
+    int cf = 0, nc = 1;
+    if (!whole) {
+        cf = cta_of_unit(q * G, a.U, C);
+        nc = cta_of_unit((q + 1) * G - 1, a.U, C) - cf + 1;
     }
-    __device__ __forceinline__ void next(int G, int ce, int q_last, int w) {
-        u += kWarpsV2;
-        settle(G, ce, q_last, w);
+    for (int o = lane; o < nout; o += 32) {
+        const int tok = o >> 6, row = o & 63;
+        float v = 0.0f;
+        for (int w = 0; w < kWarpsV2; ++w) {
+            const int d = (w - w0 + kWarpsV2) % kWarpsV2;
+            if (d < nw) v += rb[(tok * kWarpsV2 + w) * 64 + row];
+        }
+        if (whole)
+            store_out(a, q, row, tok, v, rs[tok]);
+        else
+            base[(size_t)(cta - cf) * 512 + row * 8 + tok] = v;
     }
-};
+    __syncwarp();
+    if (lane == 0) qr.cnt[b] = 0;
+    if (!whole) {
+        __threadfence();
+        __syncwarp();
+        int lastc = 0;
+        if (lane == 0) lastc = atomicAdd(a.counters + q, 1) == nc - 1;
+        lastc = __shfl_sync(0xffffffffu, lastc, 0);
+        if (lastc) {
+            __threadfence();
+            for (int o = lane; o < nout; o += 32) {
+                const int tok = o >> 6, row = o & 63;
+                float s = 0.0f;
+                for (int c = 0; c < nc; ++c) s += __ldcg(base + (size_t)c * 512 + row * 8 + tok);
+                store_out(a, q, row, tok, s, rs[tok]);
+            }
+            __syncwarp();
+            if (lane == 0) atomicExch(a.counters + q, 0);
+        }
+    }
+    __threadfence_block();
+    __syncwarp();
+    if (lane == 0) *reinterpret_cast<volatile int*>(&qr.done[b]) = q;
+}
 
 __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) unsigned long long bars[kWarpsV2][kStages];
     __shared__ float wss[kWarpsV2][8];
     __shared__ float rs[8];
-    __shared__ int last_flag;
+    __shared__ QuadRed qr;
+    __shared__ uint2 zero_frag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
     const int C = gridDim.x, cta = blockIdx.x;
     const int cs = range_start(cta, a.U, C), ce = range_start(cta + 1, a.U, C);
-    const int G = a.G;
-    const int q_first = cs / G, q_last = (ce - 1) / G;
+    const int G = a.G, M = a.M;
+    const int q_first = cs / G;
     uint8_t* ring = smem + (size_t)warp * kRingBytes;
     const uint32_t ring_s = smem_addr(ring);
+    const uint32_t bar0 = smem_addr(&bars[warp][0]);
     float* red = reinterpret_cast<float*>(smem + (size_t)kWarpsV2 * kRingBytes);
-    uint2* xf = reinterpret_cast<uint2*>(smem + (size_t)kWarpsV2 * kRingBytes + (size_t)kRedBytesPerTok * a.M);
+    uint2* xf = reinterpret_cast<uint2*>(smem + (size_t)kWarpsV2 * kRingBytes + (size_t)kRedBytesPerTok * M);
 
-    Walk pre;
-    pre.init(cs, ce, G, q_first, q_last, warp);
+    // this warp's units: cs + warp + 16k < ce
+    const int n_units = ce - cs > warp ? (ce - cs - warp + kWarpsV2 - 1) / kWarpsV2 : 0;
+    int pq = (cs + warp) / G, pg = (cs + warp) - pq * G;   // producer position
     if (lane == 0) {
-        for (int s = 0; s < kStages; ++s)
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&bars[warp][s])));
+        for (int s = 0; s < kStages; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * s));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int s = 0; s < kStages && !pre.done; ++s) {
-            issue_unit(a, pre.q, pre.u - pre.q * G, ring_s + s * kUnitBytes, smem_addr(&bars[warp][s]));
-            pre.next(G, ce, q_last, warp);
-        }
-    } else {
-        for (int s = 0; s < kStages && !pre.done; ++s) pre.next(G, ce, q_last, warp);
     }
     __syncwarp();
+    for (int s = 0; s < kStages && s < n_units; ++s) {
+        if (lane == 0) issue_unit(a, pq, pg, ring_s + s * kUnitBytes, bar0 + 8 * s);
+        step(pq, pg, G);
+    }
+    if (threadIdx.x == 0) {
+        qr.cnt[0] = qr.cnt[1] = 0;
+        qr.done[q_first & 1] = q_first - 2;
+        qr.done[(q_first + 1) & 1] = q_first - 1;
+        zero_frag = make_uint2(0u, 0u);
+    }
 
     // stage x (full K, M <= 8 tokens) into B-fragment order; sums of squares per token
     const bool rms = (a.flags & G4Q_QMM_RMS_SCALE) != 0;
     const int units8 = a.K / 8;
-    for (int m = 0; m < a.M; ++m) {
+    for (int m = 0; m < M; ++m) {
         float ss = 0.0f;
         const uint16_t* xr = a.x + (int64_t)m * a.ldx;
         for (int u = threadIdx.x; u < units8; u += kThreadsV2) {
             const uint4 v = *reinterpret_cast<const uint4*>(xr + u * 8);
             const int kk = u >> 1, h = u & 1;
-            uint32_t* e = reinterpret_cast<uint32_t*>(xf + (kk * a.M + m) * 4);
+            uint32_t* e = reinterpret_cast<uint32_t*>(xf + (kk * M + m) * 4);
             e[0 + h] = v.x;
             e[2 + h] = v.y;
             e[4 + h] = v.z;
@@ -184,7 +276,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
     __syncthreads();
     if (threadIdx.x < 8) {
         float r = 1.0f;
-        if (rms && threadIdx.x < a.M) {
+        if (rms && threadIdx.x < M) {
             float s = 0.0f;
             for (int w = 0; w < kWarpsV2; ++w) s = __fadd_rn(s, wss[w][threadIdx.x]);
             r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)a.K), a.eps)));
@@ -193,113 +285,70 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
     }
     __syncthreads();
 
-    const bool tok_ok = gi < a.M;
-    const bool f32 = (a.flags & G4Q_QMM_OUT_F32) != 0;
-    Walk cur;
-    cur.init(cs, ce, G, q_first, q_last, warp);
+    // B fragments: lanes whose token is >= M read a fixed zero pair
+    const bool tok_ok = gi < M;
+    const uint2* xlane = tok_ok ? xf + gi * 4 + t : &zero_frag;
+    const int kstride = tok_ok ? M * 4 : 0;
+
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
+    int cq = (cs + warp) / G, cg = (cs + warp) - cq * G;   // consumer position
+    int acc_q = cq;
     int stage = 0;
     uint32_t phase = 0;
-    for (int q = q_first; q <= q_last; ++q) {
-        float acc[4][4];
+    for (int k = 0; k < n_units; ++k) {
+        if (cq != acc_q) {
+            park_quad(a, qr, red, acc_q, cs, ce, cta, C, acc, rs);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 4; ++i)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
-        while (!cur.done && cur.q == q) {
-            const int g = cur.u - q * G;
-            wait_parity(smem_addr(&bars[warp][stage]), phase, a.err);
-            const uint8_t* st = ring + stage * kUnitBytes;
-            uint4 wv[4];
-            uint32_t sb0[4], sb1[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                wv[i] = reinterpret_cast<const uint4*>(st + i * 512)[lane];
-                const uint32_t* sbw = reinterpret_cast<const uint32_t*>(st + kUnitPacked) + i * 16 + gi;
-                sb0[i] = sbw[0];
-                sb1[i] = sbw[8];
-            }
-            // the unit is in registers: lane 0 refills this buffer with the warp's next-but-(kStages-1) unit
-            __syncwarp();
-            if (lane == 0 && !pre.done) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                issue_unit(a, pre.q, pre.u - pre.q * G, ring_s + stage * kUnitBytes, smem_addr(&bars[warp][stage]));
-            }
-            pre.next(G, ce, q_last, warp);
-            if (++stage == kStages) {
-                stage = 0;
-                phase ^= 1u;
-            }
-            uint2 bf[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) bf[j] = tok_ok ? xf[((g * 4 + j) * a.M + gi) * 4 + t] : make_uint2(0u, 0u);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const RowConsts c0 = row_consts(sb0[i]), c1 = row_consts(sb1[i]);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t w = j == 0 ? wv[i].x : j == 1 ? wv[i].y : j == 2 ? wv[i].z : wv[i].w;
-                    const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
-                    const uint32_t a1 = deq_r2_fast(lop_nibbles(w >> 4), c1);
-                    const uint32_t a2 = deq_r2_fast(lop_nibbles(w >> 8), c0);
-                    const uint32_t a3 = deq_r2_fast(lop_nibbles(w >> 12), c1);
-                    mma_bf16_16816(acc[i], a0, a1, a2, a3, bf[j].x, bf[j].y);
-                }
-            }
-            cur.next(G, ce, q_last, warp);
+                for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
+            acc_q = cq;
         }
-        // ---- reduce quad q over the 16 warps: red[tok][warp][row]
+        wait_parity(bar0 + 8 * stage, phase, a.err);
+        const uint8_t* st = ring + stage * kUnitBytes;
+        uint4 wv[4];
+        uint32_t sb0[4], sb1[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int tok = 2 * t + (e & 1);
-                const int row = i * 16 + gi + ((e & 2) ? 8 : 0);
-                if (tok < a.M) red[(tok * kWarpsV2 + warp) * 64 + row] = acc[i][e];
-            }
-        __syncthreads();
-        const int lo = max(cs, q * G), hi = min(ce, (q + 1) * G);
-        const bool whole = lo == q * G && hi == (q + 1) * G;
-        const int nout = 64 * a.M;
-        float v = 0.0f;
-        const int row = threadIdx.x & 63, tok = threadIdx.x >> 6;
-        if (threadIdx.x < nout) {
-            for (int w = 0; w < kWarpsV2; ++w) v += red[(tok * kWarpsV2 + w) * 64 + row];
+        for (int i = 0; i < 4; ++i) {
+            wv[i] = reinterpret_cast<const uint4*>(st + i * 512)[lane];
+            const uint32_t* sbw = reinterpret_cast<const uint32_t*>(st + kUnitPacked) + i * 16 + gi;
+            sb0[i] = sbw[0];
+            sb1[i] = sbw[8];
         }
-        if (whole) {
-            if (threadIdx.x < nout) {
-                const float o = __fmul_rn(v, rs[tok]);
-                const int64_t idx = (int64_t)tok * a.ldy + q * 64 + row;
-                if (f32)
-                    reinterpret_cast<float*>(a.y)[idx] = o;
-                else
-                    reinterpret_cast<uint16_t*>(a.y)[idx] = f32_to_bf16_bits(o);
-            }
-        } else {
-            const int cf = cta_of_unit(q * G, a.U, C), cl = cta_of_unit((q + 1) * G - 1, a.U, C);
-            const int nc = cl - cf + 1;
-            float* base = a.slots + (size_t)q * a.maxc * 64 * 8;
-            if (threadIdx.x < nout) base[(size_t)(cta - cf) * 512 + row * 8 + tok] = v;
-            __threadfence();
-            __syncthreads();
-            if (threadIdx.x == 0) last_flag = (atomicAdd(a.counters + q, 1) == nc - 1);
-            __syncthreads();
-            if (last_flag) {
-                __threadfence();
-                if (threadIdx.x < nout) {
-                    float s = 0.0f;
-                    for (int c = 0; c < nc; ++c) s += __ldcg(base + (size_t)c * 512 + row * 8 + tok);
-                    const float o = __fmul_rn(s, rs[tok]);
-                    const int64_t idx = (int64_t)tok * a.ldy + q * 64 + row;
-                    if (f32)
-                        reinterpret_cast<float*>(a.y)[idx] = o;
-                    else
-                        reinterpret_cast<uint16_t*>(a.y)[idx] = f32_to_bf16_bits(o);
-                }
-                if (threadIdx.x == 0) atomicExch(a.counters + q, 0);
+        const uint2* xg = xlane + cg * 4 * kstride;
+        uint2 bf[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) bf[j] = xg[j * kstride];
+        // the unit is in registers: refill this buffer kStages units ahead
+        __syncwarp();
+        if (k + kStages < n_units) {
+            if (lane == 0) issue_unit(a, pq, pg, ring_s + stage * kUnitBytes, bar0 + 8 * stage);
+            step(pq, pg, G);
+        }
+        if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const RowConsts c0 = row_consts(sb0[i]), c1 = row_consts(sb1[i]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t w = j == 0 ? wv[i].x : j == 1 ? wv[i].y : j == 2 ? wv[i].z : wv[i].w;
+                const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
+                const uint32_t a1 = deq_r2_fast(lop_nibbles(w >> 4), c1);
+                const uint32_t a2 = deq_r2_fast(lop_nibbles(w >> 8), c0);
+                const uint32_t a3 = deq_r2_fast(lop_nibbles(w >> 12), c1);
+                mma_bf16_16816(acc[i], a0, a1, a2, a3, bf[j].x, bf[j].y);
             }
         }
-        __syncthreads();   // red is rewritten by the next quad
+        step(cq, cg, G);
     }
+    if (n_units > 0) park_quad(a, qr, red, acc_q, cs, ce, cta, C, acc, rs);
 }
 
 }  // namespace
@@ -311,11 +360,20 @@ size_t gemv2_slots_bytes(int64_t N, int64_t K, int sms) {
     return (size_t)(N / 64) * 8 * 64 * 8 * sizeof(float);
 }
 
+// grid for a U-unit, G-group problem: every CTA owns >= 1 unit and a quad meets <= 8 CTA ranges
+static int gemv2_grid(int U, int G, int sms) {
+    int grid = sms < U ? sms : U;
+    while (grid > 1 && (G - 1) / (U / grid) + 2 > 8) --grid;
+    return grid;
+}
+
 bool gemv2_supported(const QmmCall& c) {
     const size_t xbytes = (size_t)c.w->K * c.M * 2;
+    if (c.M < 1 || c.M > 8 || c.w->N % 64 != 0) return false;
     const long long units = (c.w->N / 64) * (c.w->K / 64);
-    return c.M >= 1 && c.M <= 8 && c.w->N % 64 == 0 && units >= 1 && units < (1ll << 31) &&
-           (size_t)kWarpsV2 * kRingBytes + (size_t)kRedBytesPerTok * c.M + xbytes <= 220 * 1024;
+    if (units < 1 || units >= (1ll << 31)) return false;
+    if ((size_t)kWarpsV2 * kRingBytes + (size_t)kRedBytesPerTok * c.M + xbytes > 220 * 1024) return false;
+    return gemv2_grid((int)units, (int)(c.w->K / 64), device_sm_count()) > 0;
 }
 
 void launch_gemv2(const QmmCall& c, cudaStream_t st) {
@@ -329,7 +387,6 @@ void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     }
     const Weight& w = *c.w;
     DeviceScratch& ds = device_scratch();
-    const int sms = device_sm_count();
     Gemv2Args a;
     a.packed = w.packed;
     a.sb = w.sb;
@@ -340,10 +397,8 @@ void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     a.M = (int)c.M;
     a.Q = a.R / 4;
     a.U = a.Q * a.G;
-    // every CTA owns at least one unit, and a quad (G units) meets at most (G-1)/min_range + 2 CTA
-    // ranges: shrink the grid until that is within the 8 slots reserved per quad
-    int grid = sms < a.U ? sms : a.U;
-    while (grid > 1 && (a.G - 1) / (a.U / grid) + 2 > 8) --grid;
+    const int grid = gemv2_grid(a.U, a.G, device_sm_count());
+    if (grid <= 0) throw Error(G4Q_ERR_RUNTIME, "gemv2: no valid grid for this shape");
     if ((size_t)a.Q * 8 * 64 * 8 * sizeof(float) > ds.slots_bytes)
         throw Error(G4Q_ERR_RUNTIME, "gemv scratch too small for this shape (create the weight before capture)");
     a.x = c.x;
@@ -353,7 +408,6 @@ void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     a.flags = c.flags;
     a.eps = c.eps;
     a.slots = ds.slots;
-    a.maxc = 8;
     a.counters = ds.counters;
     a.err = ds.err;
     const size_t smem = (size_t)kWarpsV2 * kRingBytes + (size_t)kRedBytesPerTok * a.M + (size_t)a.K * a.M * 2;
