@@ -195,17 +195,22 @@ def main():
         if world > 1:
             dist.barrier()
 
-    # capture the whole decode step once; replay it per token
+    # one GPU: the whole decode step is one persistent-kernel launch (decode plan); several GPUs:
+    # the per-matmul kernels with an NCCL allreduce after o/down. Captured once, replayed per token.
+    single = world == 1
+    if single:
+        st.build_plan(1)
+    step = (lambda: st.decode(h_static)) if single else (lambda: st.forward(h_static))
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
         for _ in range(2):
-            st.forward(h_static)
+            step()
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        keys, _ = st.forward(h_static)
+        keys, _ = step()
     for _ in range(max(args.warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()
@@ -247,30 +252,39 @@ def main():
     clk = clocks.stop() if rank == 0 else None
     tok, _ = decode_keys(key_host)
 
-    # ---- dominant kernel alone: fused gate|up GEMV over all layers' weights (cold L2)
-    gu_bytes = st.layers[0]["gu"].rows * cfg.hidden * 9 // 16
-    o_in = torch.zeros((1, cfg.hidden), dtype=torch.bfloat16, device=dev).normal_()
-    gu_out = torch.empty((1, st.layers[0]["gu"].rows), dtype=torch.bfloat16, device=dev)
-    for L in st.layers[:4]:
-        quantized_matmul(o_in, L["gu"], rms_scale=True, out=gu_out)
-    reps = 4
-    barrier()
-    torch.cuda.synchronize()
-    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    k0.record()
-    for _ in range(reps):
-        for L in st.layers:
-            quantized_matmul(o_in, L["gu"], rms_scale=True, out=gu_out)
-    k1.record()
-    torch.cuda.synchronize()
-    gu_us = max_over_ranks(k0.elapsed_time(k1)) * 1e3 / (reps * len(st.layers))
-    alg_bytes = gu_bytes + cfg.hidden * 2 + st.layers[0]["gu"].rows * 2
     hbm_peak, tf_peak, peak_kind = measured_peaks()
-    achieved = alg_bytes / (gu_us * 1e-6) / 1e9
+    reps = 0
+    if single:
+        # the dominant (only) kernel is the persistent decode kernel: one launch per step
+        kname = "decode_kernel (persistent: 48x{q|k|v, o, gate|up, down} + LM head, one launch)"
+        alg_bytes = cfg.weight_bytes() + 2 * cfg.hidden * 2 * (4 * cfg.layers + 1)
+        launch_us = ms * 1e3
+        traffic_file = ROOT / "profiles" / "decode_kernel_traffic.json"
+    else:
+        # dominant kernel: the fused gate|up GEMV, timed alone over all layers' weights (cold L2)
+        kname = "gemv2_kernel (fused gate|up shard, M=1)"
+        gu_bytes = st.layers[0]["gu"].rows * cfg.hidden * 9 // 16
+        o_in = torch.zeros((1, cfg.hidden), dtype=torch.bfloat16, device=dev).normal_()
+        gu_out = torch.empty((1, st.layers[0]["gu"].rows), dtype=torch.bfloat16, device=dev)
+        for L in st.layers[:4]:
+            quantized_matmul(o_in, L["gu"], rms_scale=True, out=gu_out)
+        reps = 4
+        barrier()
+        torch.cuda.synchronize()
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record()
+        for _ in range(reps):
+            for L in st.layers:
+                quantized_matmul(o_in, L["gu"], rms_scale=True, out=gu_out)
+        k1.record()
+        torch.cuda.synchronize()
+        launch_us = max_over_ranks(k0.elapsed_time(k1)) * 1e3 / (reps * len(st.layers))
+        alg_bytes = gu_bytes + cfg.hidden * 2 + st.layers[0]["gu"].rows * 2
+        traffic_file = ROOT / "profiles" / "gemv_gate_up_traffic.json"
+    achieved = alg_bytes / (launch_us * 1e-6) / 1e9
     traffic = None
-    tf = ROOT / "profiles" / "gemv_gate_up_traffic.json"
-    if tf.exists():
-        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+    if traffic_file.exists():
+        traffic = json.loads(traffic_file.read_text()).get("dram_bytes_per_launch")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -291,11 +305,12 @@ def main():
             "decode_tok_s_e2e": round(1e3 / ms_e2e, 2),
             "e2e": {"value": round(gbs_e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": cfg.hidden * 2,
                     "d2h_bytes_per_step": 8, "path": "pinned host hidden -> CUDA graph of the step -> token key"},
-            "roofline": {"kernel": "gemv_kernel (fused gate|up, M=1)", "bound": "hbm", "achieved": round(achieved, 1),
+            "roofline": {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1),
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                          "peak_kind": f"{peak_kind} hbm_gbs", "traffic": traffic,
-                         "alg_bytes_per_launch": alg_bytes, "avg_launch_us": round(gu_us, 3)},
-            "gpu_launches": (4 * cfg.layers + 1) * args.steps * 2 + reps * len(st.layers) + 4,
+                         "alg_bytes_per_launch": alg_bytes, "avg_launch_us": round(launch_us, 3)},
+            "gpu_launches": (1 if single else 4 * cfg.layers + 1) * args.steps * 2 + reps * len(st.layers)
+                            + (0 if single else 4),
             "clocks": clk,
             "last_token": tok[0],
         }

@@ -52,6 +52,13 @@ class G4qWeightInfo(ctypes.Structure):
                 ("fast_path_ok", ctypes.c_int32), ("error_flags", ctypes.c_int32)]
 
 
+class G4qDecodePhase(ctypes.Structure):
+    _fields_ = [("weight", ctypes.c_void_p), ("x", ctypes.c_void_p), ("ldx", ctypes.c_int64), ("y", ctypes.c_void_p),
+                ("ldy", ctypes.c_int64), ("flags", ctypes.c_uint32)]
+
+
+PHASE_ARGMAX = 0x4
+
 SIGNATURES = {
     "g4q_runtime_version": [ctypes.POINTER(G4qVersionInfo)],
     "g4q_get_last_error": [ctypes.c_char_p, ctypes.c_size_t],
@@ -66,6 +73,9 @@ SIGNATURES = {
     "g4q_qmm_ex": [_P, _P, _I64, _I64, _P, _I64, _U32, _F, _P],
     "g4q_lm_head_argmax": [_P, _P, _I64, _I64, _F, _U32, _F, _I64, _P, _I64, _P, _P, _P, _P],
     "g4q_device_error": [ctypes.POINTER(_I32), _I32],
+    "g4q_decode_plan_create": [ctypes.POINTER(G4qDecodePhase), _I32, _I32, ctypes.POINTER(_P)],
+    "g4q_decode_plan_run": [_P, _I64, _F, _F, _I64, _P, _P, _P, _P, _I64, _P],
+    "g4q_decode_plan_free": [_P],
     "g4q_synth_matrix": [_U64, _I64, _I64, _I32, _I32, _P, _P, _P, _P],
     "g4q_synth_normal_bf16": [_U64, _I64, _P, _P],
 }

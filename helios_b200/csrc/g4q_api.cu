@@ -384,6 +384,29 @@ G4qStatus g4q_lm_head_argmax(const G4qWeight* h, const uint16_t* x, int64_t M, i
     });
 }
 
+G4qStatus g4q_decode_plan_create(const G4qDecodePhase* phases, int32_t n_phases, int32_t max_tokens,
+                                 G4qDecodePlan** out) {
+    return guarded("g4q_decode_plan_create", [&] {
+        require(out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null out pointer");
+        *out = nullptr;
+        *out = reinterpret_cast<G4qDecodePlan*>(decode_plan_create(phases, n_phases, max_tokens));
+    });
+}
+
+G4qStatus g4q_decode_plan_run(G4qDecodePlan* plan, int64_t M, float eps, float softcap, int64_t row_offset,
+                              int32_t* tokens, float* values, uint64_t* keys, uint16_t* logits, int64_t ld_logits,
+                              void* stream) {
+    return guarded("g4q_decode_plan_run", [&] {
+        require(row_offset >= 0 && row_offset < 0xFFFFFFFFll, G4Q_ERR_INVALID_ARGUMENT, "row_offset out of range");
+        decode_plan_run(plan, (int)M, eps, softcap, row_offset, tokens, values, keys, logits, ld_logits,
+                        reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+G4qStatus g4q_decode_plan_free(G4qDecodePlan* plan) {
+    return guarded("g4q_decode_plan_free", [&] { decode_plan_free(plan); });
+}
+
 G4qStatus g4q_device_error(int32_t* code, int32_t reset) {
     return guarded("g4q_device_error", [&] {
         require(code != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null code pointer");

@@ -96,6 +96,12 @@ void launch_lm_head(const Weight& w, const uint16_t* x, int64_t M, int64_t ldx, 
                     float eps, int64_t row_offset, uint16_t* logits, int64_t ld_logits, int32_t* tokens,
                     float* values, unsigned long long* keys, cudaStream_t st);
 
+// kernels (g4q_decode.cu): persistent decode-step kernel
+void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens);
+void decode_plan_free(void* plan);
+void decode_plan_run(void* plan, int M, float eps, float softcap, int64_t row_offset, int32_t* tokens, float* values,
+                     uint64_t* keys, uint16_t* logits, int64_t ld_logits, cudaStream_t st);
+
 // kernels (g4q_gemm.cu): tcgen05 dequant-GEMM for M > 16
 void launch_gemm(const QmmCall& c, cudaStream_t st);
 bool gemm_supported(const QmmCall& c);

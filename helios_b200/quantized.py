@@ -23,11 +23,12 @@ from typing import Optional, Tuple
 import torch
 
 from . import _lib
-from ._lib import CHAIN_R1, CHAIN_R2, QMM_OUT_F32, QMM_RMS_SCALE, G4qError, G4qInvalidArgument
+from ._lib import CHAIN_R1, CHAIN_R2, PHASE_ARGMAX, QMM_OUT_F32, QMM_RMS_SCALE, G4qError, G4qInvalidArgument
 
 __all__ = [
-    "QuantizedWeight", "quantized_matmul", "dequantize", "lm_head_argmax", "synth_matrix", "synth_normal",
-    "CHAIN_R1", "CHAIN_R2", "G4qError", "G4qInvalidArgument",
+    "QuantizedWeight", "quantized_matmul", "dequantize", "lm_head_argmax", "DecodePlan", "synth_matrix",
+    "synth_normal", "CHAIN_R1", "CHAIN_R2", "QMM_RMS_SCALE", "QMM_OUT_F32", "PHASE_ARGMAX", "G4qError",
+    "G4qInvalidArgument",
 ]
 
 
@@ -267,6 +268,51 @@ def lm_head_argmax(x: torch.Tensor, w: QuantizedWeight, *, softcap: float = 30.0
               QMM_RMS_SCALE if rms_scale else 0, eps, row_offset, _ptr(logits), ld, _ptr(tokens), _ptr(values),
               _ptr(keys), _stream())
     return tokens, values, keys
+
+
+class DecodePlan:
+    """All quantized matmuls of one decode step as ONE persistent kernel launch (g4q_decode_plan_*).
+
+    ``phases`` is a list of ``(weight, x, y, flags)``: ``x`` a bf16 CUDA tensor view [M, K] (row stride a
+    multiple of 8), ``y`` a bf16/fp32 CUDA tensor view [M, N] or None for the final argmax phase;
+    ``flags`` from QMM_RMS_SCALE / QMM_OUT_F32 / PHASE_ARGMAX. Phase i may read phase i-1's output.
+    Tensor addresses are baked into the plan: keep the tensors alive and reuse them.
+    """
+
+    def __init__(self, phases, max_tokens: int = 1):
+        self._keep = []
+        arr = (_lib.G4qDecodePhase * len(phases))()
+        for i, (w, x, y, flags) in enumerate(phases):
+            if x.dtype != torch.bfloat16 or x.stride(-1) != 1:
+                raise ValueError(f"phase {i}: x must be a bf16 view with unit column stride")
+            arr[i].weight = w.handle
+            arr[i].x = x.data_ptr()
+            arr[i].ldx = x.stride(0)
+            arr[i].y = None if y is None else y.data_ptr()
+            arr[i].ldy = 0 if y is None else y.stride(0)
+            arr[i].flags = flags
+            self._keep += [w, x, y]
+        self._h = ctypes.c_void_p()
+        _lib.call("g4q_decode_plan_create", arr, len(phases), max_tokens, ctypes.byref(self._h))
+        self.max_tokens = max_tokens
+
+    def run(self, M: int, *, eps: float = 1e-6, softcap: float = 30.0, row_offset: int = 0, tokens=None,
+            values=None, keys=None, logits=None):
+        ld = 0 if logits is None else logits.stride(0)
+        _lib.call("g4q_decode_plan_run", self._h, M, eps, softcap, row_offset, _ptr(tokens), _ptr(values), _ptr(keys),
+                  _ptr(logits), ld, _stream())
+
+    def free(self):
+        if self._h:
+            _lib.call("g4q_decode_plan_free", self._h)
+            self._h = ctypes.c_void_p()
+        self._keep = []
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 def synth_matrix(seed: int, rows: int, cols: int, bits: int = 4, group_size: int = 64, device=None):

@@ -27,7 +27,8 @@ from typing import List, Optional
 
 import torch
 
-from .quantized import QuantizedWeight, lm_head_argmax, quantized_matmul, synth_matrix
+from .quantized import (PHASE_ARGMAX, QMM_RMS_SCALE, DecodePlan, QuantizedWeight, lm_head_argmax,
+                        quantized_matmul, synth_matrix)
 
 BASE_SEED = 0x48454C494F53
 PROJ_IDS = {"q": 0, "k": 1, "v": 2, "o": 3, "gate": 4, "up": 5, "down": 6, "lm": 7}
@@ -110,6 +111,8 @@ class SyntheticStack:
         self._alloc(max_tokens)
 
     def _alloc(self, M: int):
+        if getattr(self, "plan", None) is not None:
+            raise RuntimeError("activation buffers are baked into the decode plan; build the stack with max_tokens >= M")
         dev, c = self.device, self.cfg
         self.max_tokens = M
         self.qkv_out = torch.empty((M, self.nq + 2 * self.nkv), dtype=torch.bfloat16, device=dev)
@@ -144,6 +147,31 @@ class SyntheticStack:
             x = self._row_parallel(L["down"], gu[:, self.ni:], self.h_out[:M])
         return self.head(x)
 
+    def build_plan(self, max_tokens: int = 1) -> DecodePlan:
+        """The whole decode step (48 x 4 matmuls + LM head argmax) as one persistent-kernel plan."""
+        if self.size != 1:
+            raise NotImplementedError("the single-launch decode plan covers one GPU")
+        c = self.cfg
+        self.h_in = torch.zeros((max(max_tokens, 1), c.hidden), dtype=torch.bfloat16, device=self.device)
+        phases, x = [], self.h_in
+        for L in self.layers:
+            phases.append((L["qkv"], x, self.qkv_out, QMM_RMS_SCALE))
+            phases.append((L["o"], self.qkv_out[:, : self.nq], self.o_out, 0))
+            phases.append((L["gu"], self.o_out, self.gu_out, QMM_RMS_SCALE))
+            phases.append((L["down"], self.gu_out[:, self.ni:], self.h_out, 0))
+            x = self.h_out
+        phases.append((self.lm, x, None, QMM_RMS_SCALE | PHASE_ARGMAX))
+        self.plan = DecodePlan(phases, max_tokens)
+        return self.plan
+
+    def decode(self, h: torch.Tensor):
+        """One decode step through the single-launch plan: h [M, hidden] -> (keys, final hidden)."""
+        M = h.shape[0]
+        self.h_in[:M].copy_(h)
+        self.plan.run(M, eps=self.cfg.eps, softcap=self.cfg.softcap, row_offset=self.v_rows[0],
+                      tokens=self.tokens[:M], values=self.values[:M], keys=self.keys[:M])
+        return self.keys[:M], self.h_out[:M]
+
     def head(self, x: torch.Tensor):
         c = self.cfg
         M = x.shape[0]
@@ -158,6 +186,9 @@ class SyntheticStack:
         return key, x
 
     def free(self):
+        if getattr(self, "plan", None) is not None:
+            self.plan.free()
+            self.plan = None
         for L in self.layers:
             for w in L.values():
                 w.free()

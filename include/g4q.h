@@ -139,6 +139,37 @@ G4qStatus g4q_lm_head_argmax(const G4qWeight* w, const uint16_t* x, int64_t M, i
                              int64_t ld_logits, int32_t* tokens, float* values, uint64_t* keys,
                              void* stream);
 
+/* ---- decode plan: every quantized matmul of one decode step in one persistent kernel ----------
+ * Replaces the per-token chain of quantized_linear calls of the decode drivers
+ * (native_model.cc:1843-1911 decode_last_logits -> 48 x target_layer_decode_forward :1284-1328 ->
+ * target_logits_for_hidden :1782-1795 -> argmax :3825). Phase i computes
+ * y_i = x_i . deq(W_i)^T (RMS_SCALE / OUT_F32 as for g4q_qmm_ex); x_i may be the output of phase
+ * i-1 (the kernel waits for phase i-1 to finish on every SM before staging x_i). The last phase may
+ * carry G4Q_PHASE_ARGMAX: its y is not stored; instead each row's bf16 logits go through the
+ * softcap and a first-index argmax, reported as in g4q_lm_head_argmax. Pointers are fixed at plan
+ * creation (device memory); g4q_decode_plan_run launches one cooperative grid on `stream` and
+ * allocates nothing, so it can be captured in a CUDA graph. M (tokens per step) <= 2. Runs of one
+ * plan must not overlap on the GPU. */
+#define G4Q_PHASE_ARGMAX 0x4u
+
+typedef struct G4qDecodePhase {
+    const G4qWeight* weight;
+    const uint16_t* x; /* bf16 [M, ldx] */
+    int64_t ldx;
+    void* y;           /* bf16 or fp32 [M, ldy]; unused by the argmax phase */
+    int64_t ldy;
+    uint32_t flags;
+} G4qDecodePhase;
+
+typedef struct G4qDecodePlan G4qDecodePlan;
+
+G4qStatus g4q_decode_plan_create(const G4qDecodePhase* phases, int32_t n_phases, int32_t max_tokens,
+                                 G4qDecodePlan** out);
+G4qStatus g4q_decode_plan_run(G4qDecodePlan* plan, int64_t M, float eps, float softcap, int64_t row_offset,
+                              int32_t* tokens, float* values, uint64_t* keys, uint16_t* logits, int64_t ld_logits,
+                              void* stream);
+G4qStatus g4q_decode_plan_free(G4qDecodePlan* plan);
+
 /* ---- device-side failure detection ----------------------------------------------------------
  * Every wait inside a libg4q kernel is bounded; a wait that gives up records a nonzero code in a
  * per-device error word and the kernel runs to its end (its results are then invalid). This

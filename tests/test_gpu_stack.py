@@ -64,6 +64,68 @@ def test_cuda_graph_replay_equals_eager(cuda, oracle):
     st.free()
 
 
+PLAN = dict(layers=2, hidden=2048, q_out=2048, kv_out=1024, inter=4096, vocab=16384)
+
+
+def test_decode_plan_single_launch(cuda, oracle):
+    """The persistent decode-step kernel (one launch for all phases) against the per-matmul path
+    and the oracle; bit-reproducible across runs and under CUDA-graph replay."""
+    from helios_b200 import _lib
+    from helios_b200.quantized import synth_normal
+    from helios_b200.stack import StackConfig, SyntheticStack, activation_seed, decode_keys
+    cfg = StackConfig(**PLAN)
+    st = SyntheticStack(cfg)
+    h0 = synth_normal(activation_seed(3), (1, cfg.hidden))
+    k_eager, h_eager = st.forward(h0)
+    k_eager, h_eager = k_eager.clone(), h_eager.clone()
+    st.build_plan(1)
+    k1, h1 = st.decode(h0)
+    k1, h1 = k1.clone(), h1.clone()
+    assert _lib.device_error() == 0
+    ex, rms = qmm_error(oracle.bf16_to_f32(u16(h1)), oracle.bf16_to_f32(u16(h_eager)).astype(np.float64), True)
+    assert ex <= 2e-2 * rms
+    k2, h2 = st.decode(h0)
+    assert torch.equal(k2, k1) and torch.equal(h2, h1)          # deterministic reductions
+    ref = oracle_stack(oracle, cfg, u16(h0))
+    t1, v1 = decode_keys(k1)
+    assert t1[0] == ref["tokens"][0] or abs(v1[0] - ref["values"][0]) <= 0.125
+    # graph replay of the single launch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        st.decode(h0)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        kg, hg = st.decode(h0)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(kg, k1) and torch.equal(hg, h1)
+    assert _lib.device_error() == 0
+    del g
+    st.free()
+
+
+def test_decode_plan_rejects_bad_phases(cuda, oracle):
+    from helios_b200 import _lib
+    from helios_b200 import quantized as Q
+    w = Q.QuantizedWeight.from_mlx(*Q.synth_matrix(1, 64, 256))
+    x = torch.zeros((1, 256), dtype=torch.bfloat16, device=cuda)
+    y = torch.zeros((1, 64), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(_lib.G4qError):                       # too few units for a full grid
+        Q.DecodePlan([(w, x, y, 0)])
+    big = Q.QuantizedWeight.from_mlx(*Q.synth_matrix(2, 4096, 4096))
+    xb = torch.zeros((1, 4096), dtype=torch.bfloat16, device=cuda)
+    yb = torch.zeros((1, 4096), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(_lib.G4qInvalidArgument):              # argmax phase must be last
+        Q.DecodePlan([(big, xb, yb, Q.PHASE_ARGMAX), (big, yb, xb, 0)])
+    with pytest.raises(_lib.G4qError):                        # more tokens than the plan supports
+        Q.DecodePlan([(big, xb, yb, 0)], max_tokens=4)
+    w.free()
+    big.free()
+
+
 def test_invalid_calls_return_status(cuda, oracle):
     from helios_b200 import _lib
     from helios_b200 import quantized as Q
