@@ -384,6 +384,29 @@ G4qStatus g4q_lm_head_argmax(const G4qWeight* h, const uint16_t* x, int64_t M, i
     });
 }
 
+G4qStatus g4q_lm_head_argmax_noalloc(const uint32_t* packed, const uint32_t* sb, int64_t rows, int64_t cols,
+                                     const uint16_t* x, int64_t M, int64_t ldx, float softcap, uint32_t flags,
+                                     float eps, int64_t row_offset, uint16_t* logits, int64_t ld_logits,
+                                     int32_t* tokens, float* values, uint64_t* keys, void* stream) {
+    return guarded("g4q_lm_head_argmax_noalloc", [&] {
+        require(packed && sb && x, G4Q_ERR_INVALID_ARGUMENT, "packed, sb and x must be non-null device pointers");
+        require(rows > 0 && rows % 16 == 0 && cols > 0 && cols % 64 == 0, G4Q_ERR_INVALID_ARGUMENT,
+                "rows must be a positive multiple of 16 and cols of 64");
+        require(M >= 1 && M <= 16, G4Q_ERR_INVALID_ARGUMENT,
+                "M must be in [1, 16] (the static scratch holds 16 keys); got " + std::to_string(M));
+        require((flags & ~G4Q_QMM_RMS_SCALE) == 0, G4Q_ERR_INVALID_ARGUMENT, "only G4Q_QMM_RMS_SCALE is accepted");
+        require(ldx >= cols && ldx % 8 == 0, G4Q_ERR_INVALID_ARGUMENT, "ldx must be >= cols and a multiple of 8");
+        require(logits == nullptr || ld_logits >= rows, G4Q_ERR_INVALID_ARGUMENT, "ld_logits must be >= rows");
+        require(row_offset >= 0 && row_offset + rows <= 0xFFFFFFFFll, G4Q_ERR_INVALID_ARGUMENT,
+                "row_offset + rows must fit in 32 bits");
+        require_aligned16(x, "x");
+        require_aligned16(packed, "packed");
+        launch_lm_head_noalloc(packed, sb, rows, cols, x, M, ldx, softcap, flags, eps, row_offset, logits, ld_logits,
+                               tokens, values, reinterpret_cast<unsigned long long*>(keys),
+                               reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
 G4qStatus g4q_decode_plan_create(const G4qDecodePhase* phases, int32_t n_phases, int32_t max_tokens,
                                  G4qDecodePlan** out) {
     return guarded("g4q_decode_plan_create", [&] {

@@ -19,6 +19,9 @@
 //    combined through distributed shared memory by cluster rank 0, in a fixed order.
 #include <cooperative_groups.h>
 
+#include <mutex>
+#include <string>
+
 #include "g4q_common.cuh"
 #include "g4q_internal.h"
 
@@ -450,6 +453,54 @@ void launch_gemv(const QmmCall& c, cudaStream_t st) {
         launch_gemv_t<1>(a, st);
     else
         launch_gemv_t<2>(a, st);
+}
+
+// ---- allocation-free LM head (g4q_lm_head_argmax_noalloc) --------------------------------------
+// For callers that cannot allocate device memory at call time: code running inside a CUDA stream
+// capture (cudaMalloc is not allowed there) and host runtimes that own every device byte through a
+// pre-sized arena and forbid driver allocations once serving starts. The argmax scratch (16
+// running keys + a ticket counter) lives in this static array instead of handle-owned memory.
+// Every GPU that loads the library holds these 136 bytes until the process exits; all calls on a
+// device share them, so calls that overlap on the GPU race and must be serialised by the caller.
+constexpr int kNoAllocScratchWords = kMaxTokens + 1;
+static __device__ __align__(256) unsigned long long g_noalloc_scratch[kNoAllocScratchWords];
+
+static unsigned long long* noalloc_scratch_ptr() {
+    // The symbol's host-side name is only a stand-in: its device address is looked up once per
+    // device (with that device current) on the first call, which must therefore precede any capture.
+    static unsigned long long* ptrs[64] = {nullptr};
+    static std::mutex mu;
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lock(mu);
+    if (ptrs[dev & 63] == nullptr) {
+        void* p = nullptr;
+        check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(noalloc scratch)");
+        ptrs[dev & 63] = static_cast<unsigned long long*>(p);
+    }
+    return ptrs[dev & 63];
+}
+
+void launch_lm_head_noalloc(const uint32_t* packed, const uint32_t* sb, int64_t N, int64_t K, const uint16_t* x,
+                            int64_t M, int64_t ldx, float softcap, uint32_t flags, float eps, int64_t row_offset,
+                            uint16_t* logits, int64_t ld_logits, int32_t* tokens, float* values,
+                            unsigned long long* keys, cudaStream_t st) {
+    if (M < 1 || M > kMaxTokens)
+        throw Error(G4Q_ERR_INVALID_ARGUMENT, "M must be in [1, " + std::to_string(kMaxTokens) +
+                                                  "]: the static scratch holds " + std::to_string(kMaxTokens) + " keys");
+    unsigned long long* scratch = noalloc_scratch_ptr();
+    // the scratch keeps the previous call's contents: start from zero keys and a zero ticket
+    check_cuda(cudaMemsetAsync(scratch, 0, sizeof(unsigned long long) * kNoAllocScratchWords, st),
+               "cudaMemsetAsync(noalloc scratch)");
+    Weight w;   // a view of caller memory: nothing is allocated
+    w.N = N;
+    w.K = K;
+    w.packed = const_cast<uint32_t*>(packed);
+    w.sb = const_cast<uint32_t*>(sb);
+    GemvArgs a = make_args(w, x, M, ldx, nullptr, 0, flags, eps);
+    if (M <= 8)
+        launch_lm_t<1>(a, softcap, row_offset, logits, ld_logits, scratch, tokens, values, keys, st);
+    else
+        launch_lm_t<2>(a, softcap, row_offset, logits, ld_logits, scratch, tokens, values, keys, st);
 }
 
 void launch_lm_head(const Weight& w, const uint16_t* x, int64_t M, int64_t ldx, float softcap, uint32_t flags,

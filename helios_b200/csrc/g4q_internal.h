@@ -92,6 +92,10 @@ struct QmmCall {
 void launch_gemv(const QmmCall& c, cudaStream_t st);
 bool gemv2_supported(const QmmCall& c);
 void launch_gemv2(const QmmCall& c, cudaStream_t st);
+void launch_lm_head_noalloc(const uint32_t* packed, const uint32_t* sb, int64_t N, int64_t K, const uint16_t* x,
+                            int64_t M, int64_t ldx, float softcap, uint32_t flags, float eps, int64_t row_offset,
+                            uint16_t* logits, int64_t ld_logits, int32_t* tokens, float* values,
+                            unsigned long long* keys, cudaStream_t st);
 void launch_lm_head(const Weight& w, const uint16_t* x, int64_t M, int64_t ldx, float softcap, uint32_t flags,
                     float eps, int64_t row_offset, uint16_t* logits, int64_t ld_logits, int32_t* tokens,
                     float* values, unsigned long long* keys, cudaStream_t st);

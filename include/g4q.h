@@ -139,6 +139,26 @@ G4qStatus g4q_lm_head_argmax(const G4qWeight* w, const uint16_t* x, int64_t M, i
                              int64_t ld_logits, int32_t* tokens, float* values, uint64_t* keys,
                              void* stream);
 
+/* ---- allocation-free LM head ---------------------------------------------------------------------
+ * No counterpart in the reference. Same result as g4q_lm_head_argmax (same kernel), for callers
+ * that cannot allocate device memory when they call it: code inside a CUDA stream capture, where
+ * cudaMalloc is not allowed, and host runtimes that own every device byte through a pre-sized
+ * arena and forbid driver allocations once serving starts. It allocates nothing and needs no
+ * weight handle: the caller passes the weight in kernel layout v1 in memory it owns (packed:
+ * (cols/64) x (rows/16) blocks of 128 uint32, block (g, r) at word (g*rows/16 + r)*128; sb:
+ * (cols/64) x rows words scale | bias << 16 -- the layout g4q_weight_load builds, documented with
+ * the oracle's g4o_repack), plus x and the outputs. Its scratch (16 argmax keys and a ticket
+ * counter, 136 bytes) is a static array inside the library: every GPU that loads libg4q holds it
+ * until the process exits, so M is limited to 16 rows (larger M is rejected with
+ * G4Q_ERR_INVALID_ARGUMENT). Each call clears the scratch on `stream` before its kernel. All calls
+ * on one device share that scratch, so calls that overlap on the GPU race: serialise them. The
+ * first call on a device looks up the scratch's device address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture. */
+G4qStatus g4q_lm_head_argmax_noalloc(const uint32_t* packed, const uint32_t* sb, int64_t rows, int64_t cols,
+                                     const uint16_t* x, int64_t M, int64_t ldx, float softcap, uint32_t flags,
+                                     float eps, int64_t row_offset, uint16_t* logits, int64_t ld_logits,
+                                     int32_t* tokens, float* values, uint64_t* keys, void* stream);
+
 /* ---- decode plan: every quantized matmul of one decode step in one persistent kernel ----------
  * Replaces the per-token chain of quantized_linear calls of the decode drivers
  * (native_model.cc:1843-1911 decode_last_logits -> 48 x target_layer_decode_forward :1284-1328 ->
