@@ -77,6 +77,25 @@ def _split(n: int, rank: int, size: int, align: int) -> tuple:
     return rank * step, (rank + 1) * step
 
 
+def shard_plan(cfg: "StackConfig", rank: int, size: int) -> dict:
+    """Tensor-parallel windows of rank ``rank`` of ``size``: row windows (column-parallel q/k/v,
+    gate/up, LM head; whole 16-row tiles) and K windows (row-parallel o, down; whole 64-groups)."""
+    return {"q_rows": _split(cfg.q_out, rank, size, 16), "kv_rows": _split(cfg.kv_out, rank, size, 16),
+            "i_rows": _split(cfg.inter, rank, size, 16), "v_rows": _split(cfg.vocab, rank, size, 16),
+            "o_cols": _split(cfg.q_out, rank, size, 64), "d_cols": _split(cfg.inter, rank, size, 64)}
+
+
+_SIGN = -(2 ** 63)
+
+
+def combine_keys(keys: torch.Tensor, group=None) -> torch.Tensor:
+    """Max over ranks of the 64-bit argmax keys (unsigned order): flip the top bit so a signed int64
+    max orders them, all-reduce with MAX, flip back. Ties keep the smallest vocabulary index."""
+    k = keys ^ _SIGN
+    torch.distributed.all_reduce(k, op=torch.distributed.ReduceOp.MAX, group=group)
+    return k ^ _SIGN
+
+
 class SyntheticStack:
     """Seeded random-init weights of the synthetic stack, sharded for rank ``tp_rank`` of ``tp_size``."""
 
@@ -85,12 +104,9 @@ class SyntheticStack:
         self.cfg, self.rank, self.size, self.group = cfg, tp_rank, tp_size, group
         self.device = torch.device("cuda", torch.cuda.current_device())
         sh = cfg.shapes()
-        self.q_rows = _split(cfg.q_out, tp_rank, tp_size, 16)
-        self.kv_rows = _split(cfg.kv_out, tp_rank, tp_size, 16)
-        self.i_rows = _split(cfg.inter, tp_rank, tp_size, 16)
-        self.o_cols = _split(cfg.q_out, tp_rank, tp_size, 64)
-        self.d_cols = _split(cfg.inter, tp_rank, tp_size, 64)
-        self.v_rows = _split(cfg.vocab, tp_rank, tp_size, 16)
+        plan = shard_plan(cfg, tp_rank, tp_size)
+        self.q_rows, self.kv_rows, self.i_rows = plan["q_rows"], plan["kv_rows"], plan["i_rows"]
+        self.o_cols, self.d_cols, self.v_rows = plan["o_cols"], plan["d_cols"], plan["v_rows"]
         self.nq = self.q_rows[1] - self.q_rows[0]
         self.nkv = self.kv_rows[1] - self.kv_rows[0]
         self.ni = self.i_rows[1] - self.i_rows[0]
@@ -179,10 +195,7 @@ class SyntheticStack:
                                        row_offset=self.v_rows[0], tokens=self.tokens[:M], values=self.values[:M],
                                        keys=self.keys[:M])
         if self.size > 1:
-            # order-preserving u64 keys: flip the top bit so a signed int64 max orders them
-            k = key ^ (-(2 ** 63))
-            torch.distributed.all_reduce(k, op=torch.distributed.ReduceOp.MAX, group=self.group)
-            key = k ^ (-(2 ** 63))
+            key = combine_keys(key, self.group)
         return key, x
 
     def free(self):

@@ -1,0 +1,66 @@
+"""GPU, 2 ranks (skipped with fewer GPUs): the tensor-parallel synthetic stack over NCCL against the
+CPU oracle of the unsharded stack. Each rank is a spawned process on its own GPU; NVLS is off
+(NCCL_NVLS_ENABLE=0) and the process group has a short timeout so a failing rank cannot hang the
+other."""
+import os
+import socket
+import sys
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+SMALL = dict(layers=2, hidden=256, q_out=256, kv_out=128, inter=512, vocab=2048)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, out_q):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from helios_b200.quantized import synth_normal
+        from helios_b200.stack import StackConfig, SyntheticStack, activation_seed
+        cfg = StackConfig(**SMALL)
+        st = SyntheticStack(cfg, rank, world, dist.group.WORLD)
+        h0 = synth_normal(activation_seed(21), (2, cfg.hidden))
+        keys, h = st.forward(h0)
+        torch.cuda.synchronize()
+        if rank == 0:
+            out_q.put((keys.cpu().numpy().copy(), h.view(torch.int16).cpu().numpy().view(np.uint16).copy()))
+        st.free()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_stack_two_gpus(cuda, oracle):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    mp.start_processes(_worker, args=(2, _free_port(), q), nprocs=2, join=True, start_method="spawn")
+    keys, h = q.get()
+    from helios_b200.stack import StackConfig, decode_keys
+    cfg = StackConfig(**SMALL)
+    h0 = oracle.synth_normal_bf16(oracle.activation_seed(21), 2 * cfg.hidden).reshape(2, -1)
+    ref = oracle.stack_forward(h0, cfg.layers, oracle.stack_shapes(cfg.hidden, cfg.q_out, cfg.kv_out, cfg.inter,
+                                                                   cfg.vocab))
+    a, b = oracle.bf16_to_f32(h).astype(np.float64), oracle.bf16_to_f32(ref["hidden"]).astype(np.float64)
+    assert np.abs(a - b).max() <= 2e-2 * np.sqrt((b ** 2).mean())
+    toks, vals = decode_keys(torch.from_numpy(keys))
+    for m in range(2):
+        assert toks[m] == ref["tokens"][m] or abs(vals[m] - ref["values"][m]) <= 0.125
