@@ -4,23 +4,29 @@
 // issue (native_model.cc:1843-1911 decode_last_logits, 48 x target_layer_decode_forward at
 // :1284-1328, then the tied LM head :1782-1795 and argmax :3825): a "plan" lists the phases
 // (one quantized matmul each, e.g. q|k|v, o, gate|up, down per layer, then the LM head with the
-// fused softcap + argmax); each phase reads the previous phase's output.
+// fused softcap + argmax); each phase may read (a column window of) the previous phase's output.
 //
 // Why one kernel: at batch 1 every phase is a few microseconds of HBM streaming, so separate
 // launches spend a large share of the step in prologues (staging x) and epilogues (reductions,
-// tails). Here one cooperative grid (one 16-warp CTA per SM) stays resident for the whole step:
-//  * every warp streams its weight units through a private ring of cp.async.bulk buffers that
-//    runs ahead ACROSS phase boundaries, so the next phase's weights are already landing while the
-//    grid waits for the current phase to finish;
-//  * phase p+1 starts in a CTA once the per-phase completion counter says all CTAs have stored
-//    phase p (bounded spin), then x is re-staged in shared memory (with the RMS scale if asked);
-//  * inside a phase the units are split exactly as in the stream-K GEMV (g4q_gemv2.cu): equal
-//    contiguous CTA ranges over (64-row quad, 64-wide group) units, warp w takes every 16th unit,
-//    deterministic per-quad reductions in shared memory and through global slots for quads cut by a
-//    CTA-range boundary;
-//  * the argmax phase keeps per-token 64-bit keys (order-preserving logit bits | ~row) and the last
-//    CTA publishes tokens/values/keys; the last CTA to leave resets every counter, so the plan is
-//    ready for the next launch (and for CUDA-graph replay) without a memset.
+// tails). Here one cooperative grid (one 24-warp CTA per SM) stays resident for the whole step:
+//  * every warp streams its weight units (64 rows x one 64-wide group: 2 KB of packed words +
+//    256 B of scale|bias) through a private ring of cp.async.bulk buffers that runs ahead ACROSS
+//    phase boundaries, so the next phase's weights land while the grid finishes the current one;
+//  * the units of a phase are cut into equal contiguous CTA ranges (quad-major), warp w taking
+//    every 24th; a 64-row quad's partial sums are reduced in shared memory in warp order;
+//  * every CTA leaves its unscaled fp32 partial of each quad it touched in a slot (a quad cut by
+//    CTA-range boundaries has one slot per contributing CTA); nobody waits for a cut quad: the
+//    CTAs that consume the phase output sum the slots themselves (fixed CTA order) while staging
+//    their x, and one CTA per cut quad writes the finished values back to y during the next phase
+//    (the first of its warps to run out of units). Slots are double-buffered by phase parity. The
+//    only cross-CTA synchronisation is one completion counter per phase (one release atomic per
+//    CTA, one acquire poll per CTA);
+//  * phase p+1 starts in a CTA once that counter says every CTA has stored phase p (bounded spin);
+//    the x of phase p+1 (and its RMS scale if asked) is then staged in shared memory;
+//  * the argmax phase keeps per-token 64-bit keys (order-preserving logit bits | ~row); its cut
+//    quads are finished by the last contributing CTA (slot + arrival counter), and the last CTA to
+//    complete the phase publishes tokens/values/keys. The last CTA to leave resets every counter,
+//    so a plan is ready for the next launch (and for CUDA-graph replay) without a memset.
 #include <string>
 #include <vector>
 
@@ -30,16 +36,15 @@
 namespace g4q {
 namespace {
 
-constexpr int kWarps = 16;
+constexpr int kWarps = 24;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr uint32_t kUnitPacked = 4 * 512;
 constexpr uint32_t kUnitSb = 64 * 4;
 constexpr uint32_t kUnitBytes = kUnitPacked + kUnitSb;
 constexpr uint32_t kRingBytes = kStages * kUnitBytes;
-constexpr int kMaxTok = 2;
-constexpr int kSlots = 16;   // CTA ranges one 64-row quad may be cut into
-constexpr long long kSpinLimit = 4000000000ll;   // ~2 s of SM clocks
+constexpr int kSlots = 16;                        // CTA ranges one 64-row quad may be cut into
+constexpr long long kSpinLimit = 4000000000ll;    // ~2 s of SM clocks
 
 struct PhaseDev {
     const uint32_t* packed;
@@ -49,24 +54,25 @@ struct PhaseDev {
     int64_t ldx, ldy;
     int N, K, R, G, Q, U;
     uint32_t flags;
+    int src;       // phase whose output x is (-1: external input, ready at launch)
+    int src_col;   // first column of x inside that phase's output (multiple of 64)
 };
 
 struct DecodeArgs {
     const PhaseDev* ph;
     int n_phases;
-    int M;
     float eps, softcap;
     int64_t row_offset;          // global index of the argmax phase's row 0 (vocabulary shard)
     unsigned int* done;          // [n_phases] CTAs that finished each phase
     unsigned int* exit_count;    // [1]
-    unsigned long long* keys;    // [kMaxTok] running argmax keys
-    float* slots;                // [max quads][kSlots][64][kMaxTok], shared by the phases (they run one at a time)
-    int* qcount;                 // [max quads], zero between phases
+    unsigned long long* key;     // running argmax key
+    float* slots;                // [2 parities][max quads][kSlots][64 rows]
+    int64_t slot_stride;         // floats per parity
+    int* qcount;                 // [max quads] arrival counters of the argmax phase's cut quads
     int32_t* tokens;
     float* values;
     unsigned long long* keys_out;
     uint16_t* logits;            // optional bf16 logits of the argmax phase
-    int64_t ld_logits;
     int* err;
 };
 
@@ -98,20 +104,24 @@ __device__ __forceinline__ void wait_parity(uint32_t bar, uint32_t parity, int* 
     if (!try_wait(bar, parity)) wait_slow(bar, parity, err);
 }
 
-__device__ __forceinline__ int range_start(int c, int U, int C) { return (int)(((long long)c * U) / C); }
+// CTA c of C owns units [range_start(c), range_start(c + 1)) of a phase with U units. The owner of
+// unit u is the largest c with floor(c*U/C) <= u, i.e. c*U < (u+1)*C: c = ((u+1)*C - 1) / U.
+// (U*C < 2^32 is checked when the plan is made.)
+__device__ __forceinline__ int range_start(int c, int U, int C) { return (int)(((uint32_t)c * (uint32_t)U) / (uint32_t)C); }
 
 __device__ __forceinline__ int cta_of_unit(int u, int U, int C) {
-    int c = (int)(((long long)u * C) / U);
-    while (c + 1 < C && range_start(c + 1, U, C) <= u) ++c;
-    while (c > 0 && range_start(c, U, C) > u) --c;
-    return c;
+    return (int)(((uint32_t)(u + 1) * (uint32_t)C - 1u) / (uint32_t)U);
 }
 
-// Position of one warp in its unit sequence across all phases.
-struct Cursor {
-    int p;      // phase
-    int k, n;   // unit k of n in this phase
-    int q, g;   // current (quad, group)
+// CTA range [cf, cl] covering quad q of a phase (cf == cl: the quad is whole in one CTA).
+__device__ __forceinline__ void quad_ctas(const PhaseDev& P, int q, int C, int& cf, int& cl) {
+    cf = cta_of_unit(q * P.G, P.U, C);
+    cl = cta_of_unit((q + 1) * P.G - 1, P.U, C);
+}
+
+// The prefetching position of one warp, across phases (unit q*G+g of phase p; k of n done).
+struct Pre {
+    int p, k, n, q, g, G;
     __device__ __forceinline__ void enter(const DecodeArgs& a, int cta, int C, int w) {
         while (p < a.n_phases) {
             const PhaseDev& P = a.ph[p];
@@ -119,8 +129,9 @@ struct Cursor {
             n = ce - cs > w ? (ce - cs - w + kWarps - 1) / kWarps : 0;
             k = 0;
             if (n > 0) {
-                q = (cs + w) / P.G;
-                g = (cs + w) - q * P.G;
+                G = P.G;
+                q = (cs + w) / G;
+                g = (cs + w) - q * G;
                 return;
             }
             ++p;
@@ -128,7 +139,6 @@ struct Cursor {
     }
     __device__ __forceinline__ void next(const DecodeArgs& a, int cta, int C, int w) {
         if (++k < n) {
-            const int G = a.ph[p].G;
             g += kWarps;
             while (g >= G) {
                 g -= G;
@@ -139,58 +149,59 @@ struct Cursor {
         ++p;
         enter(a, cta, C, w);
     }
+    __device__ __forceinline__ void issue(const DecodeArgs& a, uint32_t dst, uint32_t bar) const {
+        const PhaseDev& P = a.ph[p];
+        const uint32_t* src_p = P.packed + ((size_t)g * P.R + (size_t)q * 4) * 128;
+        const uint32_t* src_s = P.sb + (size_t)g * P.N + (size_t)q * 64;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kUnitBytes) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         dst),
+                     "l"(src_p), "r"(kUnitPacked), "r"(bar)
+                     : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         dst + kUnitPacked),
+                     "l"(src_s), "r"(kUnitSb), "r"(bar)
+                     : "memory");
+    }
 };
-
-__device__ __forceinline__ void issue_unit(const PhaseDev& P, int q, int g, uint32_t dst, uint32_t bar) {
-    const uint32_t* src_p = P.packed + ((size_t)g * P.R + (size_t)q * 4) * 128;
-    const uint32_t* src_s = P.sb + (size_t)g * P.N + (size_t)q * 64;
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kUnitBytes) : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src_p), "r"(kUnitPacked), "r"(bar)
-                 : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     dst + kUnitPacked),
-                 "l"(src_s), "r"(kUnitSb), "r"(bar)
-                 : "memory");
-}
 
 struct CtaShared {
     unsigned long long bars[kWarps][kStages];
-    float wss[kWarps][kMaxTok];
-    float rs[kMaxTok];
+    float wss[kWarps];
+    float rs, rs_prev;
     int cnt[2];
     int seq_done[2];
     int warps_finished;
-    unsigned long long best[kMaxTok];
+    int wb_claim;
+    unsigned long long best;
     int last_cta;
-    uint2 zero;
+    uint32_t zero[2];
 };
 
-// Final value of one output element of phase P: store, or (argmax phase) fold into the running key.
-__device__ __forceinline__ void emit(const DecodeArgs& a, const PhaseDev& P, int q, int row, int tok, float v,
-                                     const float* rs, unsigned long long& best) {
-    const float o = __fmul_rn(v, rs[tok]);
-    const int n = q * 64 + row;
-    if (P.flags & G4Q_PHASE_ARGMAX) {
-        const uint16_t lb = f32_to_bf16_bits(o);
-        if (a.logits) a.logits[(int64_t)tok * a.ld_logits + n] = lb;
-        const float lv = bf16_bits_to_f32(lb);
-        const float sv = a.softcap > 0.0f ? softcap_bf16(lv, a.softcap) : lv;
-        const unsigned long long key = argmax_key(sv, (uint32_t)(a.row_offset + n));
-        if (key > best) best = key;
-        return;
-    }
-    const int64_t idx = (int64_t)tok * P.ldy + n;
+__device__ __forceinline__ void store_y(const PhaseDev& P, int n, float v) {
     if (P.flags & G4Q_QMM_OUT_F32)
-        reinterpret_cast<float*>(P.y)[idx] = o;
+        reinterpret_cast<float*>(P.y)[n] = v;
     else
-        reinterpret_cast<uint16_t*>(P.y)[idx] = f32_to_bf16_bits(o);
+        reinterpret_cast<uint16_t*>(P.y)[n] = f32_to_bf16_bits(v);
 }
 
-__device__ void park(const DecodeArgs& a, const PhaseDev& P, CtaShared& sh, float* red, int seq, int q, int cs,
-                     int ce, int cta, int C, const float (&acc)[4][4], unsigned long long (&best)[kMaxTok]) {
+// argmax phase: fold one finished output into the running key
+__device__ __forceinline__ void fold_logit(const DecodeArgs& a, int n, float o, unsigned long long& best) {
+    const uint16_t lb = f32_to_bf16_bits(o);
+    if (a.logits) a.logits[n] = lb;
+    const float lv = bf16_bits_to_f32(lb);
+    const float sv = a.softcap > 0.0f ? softcap_bf16(lv, a.softcap) : lv;
+    const unsigned long long key = argmax_key(sv, (uint32_t)(a.row_offset + n));
+    if (key > best) best = key;
+}
+
+// Park this warp's partial of quad q (sequence number seq in this CTA); the last warp of the quad
+// sums the partials in warp order and stores it (whole quad), leaves it in this CTA's slot (cut
+// quad), or -- argmax phase -- folds the finished logits into the running key.
+__device__ void park(const DecodeArgs& a, const PhaseDev& P, int p, CtaShared& sh, float* red, int seq, int q, int cs,
+                     int ce, int cta, int C, const float (&acc)[4][4], unsigned long long& best) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
-    const int M = a.M, G = P.G;
+    const int G = P.G;
     const int b = seq & 1;
     if (*reinterpret_cast<volatile int*>(&sh.seq_done[b]) < seq - 2) {
         const long long t0 = clock64();
@@ -201,14 +212,14 @@ __device__ void park(const DecodeArgs& a, const PhaseDev& P, CtaShared& sh, floa
             }
         }
     }
-    float* rb = red + (size_t)b * kMaxTok * kWarps * 64;
+    float* rb = red + (size_t)b * kWarps * 64;
+    if (t == 0) {   // token 0 lives in the t == 0 lanes (C fragment column 0)
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int tok = 2 * t + (e & 1);
-            if (tok < M) rb[(tok * kWarps + warp) * 64 + i * 16 + gi + ((e & 2) ? 8 : 0)] = acc[i][e];
+        for (int i = 0; i < 4; ++i) {
+            rb[warp * 64 + i * 16 + gi] = acc[i][0];
+            rb[warp * 64 + i * 16 + gi + 8] = acc[i][2];
         }
+    }
     __threadfence_block();
     __syncwarp();
     const int lo = max(cs, q * G), hi = min(ce, (q + 1) * G);
@@ -220,45 +231,51 @@ __device__ void park(const DecodeArgs& a, const PhaseDev& P, CtaShared& sh, floa
     if (!last) return;
     __threadfence_block();
     const bool whole = cs <= q * G && ce >= (q + 1) * G;
-    const int nout = 64 * M;
-    float* base = a.slots + ((size_t)q * kSlots) * 64 * kMaxTok;
-    int cf = 0, nc = 1;
-    if (!whole) {
-        cf = cta_of_unit(q * G, P.U, C);
-        nc = cta_of_unit((q + 1) * G - 1, P.U, C) - cf + 1;
-    }
-    for (int o = lane; o < nout; o += 32) {
-        const int tok = o >> 6, row = o & 63;
-        float v = 0.0f;
+    const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
+    float v[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int row = lane + 32 * h;
+        float s = 0.0f;
         for (int w = 0; w < kWarps; ++w) {
             const int d = (w - w0 + kWarps) % kWarps;
-            if (d < nw) v += rb[(tok * kWarps + w) * 64 + row];
+            if (d < nw) s += rb[w * 64 + row];
         }
-        if (whole)
-            emit(a, P, q, row, tok, v, sh.rs, best[tok]);
-        else
-            base[((size_t)(cta - cf) * 64 + row) * kMaxTok + tok] = v;
+        v[h] = s;
     }
     __syncwarp();
     if (lane == 0) sh.cnt[b] = 0;
-    if (whole) __threadfence();   // outputs visible GPU-wide before the phase counter moves
-    if (!whole) {
-        __threadfence();
-        __syncwarp();
-        int lastc = 0;
-        if (lane == 0) lastc = atomicAdd(a.qcount + q, 1) == nc - 1;
-        lastc = __shfl_sync(0xffffffffu, lastc, 0);
-        if (lastc) {
-            __threadfence();
-            for (int o = lane; o < nout; o += 32) {
-                const int tok = o >> 6, row = o & 63;
-                float s = 0.0f;
-                for (int c = 0; c < nc; ++c) s += __ldcg(base + ((size_t)c * 64 + row) * kMaxTok + tok);
-                emit(a, P, q, row, tok, s, sh.rs, best[tok]);
-            }
+    if (whole && argmax) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) fold_logit(a, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs), best);
+    } else {
+        // the unscaled partial goes to this CTA's slot of the quad (slot 0 of a whole quad); the
+        // consumers of the phase rebuild their x from the slots alone
+        int cf, cl;
+        quad_ctas(P, q, C, cf, cl);
+        float* base = a.slots + (size_t)(p & 1) * a.slot_stride + (size_t)q * kSlots * 64;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) base[(size_t)(cta - cf) * 64 + lane + 32 * h] = v[h];
+        if (whole) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) store_y(P, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs));
+        } else if (argmax) {   // the logits are needed now: the last contributing CTA finishes the quad
             __threadfence();
             __syncwarp();
-            if (lane == 0) atomicExch(a.qcount + q, 0);
+            int lastc = 0;
+            if (lane == 0) lastc = atomicAdd(a.qcount + q, 1) == cl - cf;
+            lastc = __shfl_sync(0xffffffffu, lastc, 0);
+            if (lastc) {
+                __threadfence();
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    float s = __ldcg(base + lane + 32 * h);
+                    for (int c = 1; c <= cl - cf; ++c) s += __ldcg(base + (size_t)c * 64 + lane + 32 * h);
+                    fold_logit(a, q * 64 + lane + 32 * h, __fmul_rn(s, sh.rs), best);
+                }
+                __syncwarp();
+                if (lane == 0) atomicExch(a.qcount + q, 0);
+            }
         }
     }
     __threadfence_block();
@@ -266,14 +283,142 @@ __device__ void park(const DecodeArgs& a, const PhaseDev& P, CtaShared& sh, floa
     if (lane == 0) *reinterpret_cast<volatile int*>(&sh.seq_done[b]) = seq;
 }
 
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned int atom_add_acq_rel(unsigned int* p, unsigned int v) {
+    unsigned int old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 __device__ __forceinline__ void spin_until(const unsigned int* ctr, unsigned int target, int* err) {
-    if (*reinterpret_cast<const volatile unsigned int*>(ctr) >= target) return;
+    if (ld_acquire(ctr) >= target) return;
     const long long t0 = clock64();
-    while (*reinterpret_cast<const volatile unsigned int*>(ctr) < target) {
+    while (ld_acquire(ctr) < target) {
         if (*reinterpret_cast<volatile int*>(err) != 0) return;
         if (clock64() - t0 > kSpinLimit) {
             atomicCAS(err, 0, 34);
             return;
+        }
+    }
+}
+
+// Finished outputs from the slots of a quad: s = slot[0] + slot[1] + ... (the CTA order), then
+// the producer's row scale and bf16 rounding. Every reader of a cut quad (x staging in every CTA,
+// the write-back to y) goes through these so they all see the same bits.
+__device__ __forceinline__ float4 sum_slots4(const float* base, int nc) {
+    float4 s = __ldcg(reinterpret_cast<const float4*>(base));
+    for (int c = 1; c < nc; c += 4) {
+        float4 t[3];
+#pragma unroll
+        for (int e = 0; e < 3; ++e)
+            t[e] = c + e < nc ? __ldcg(reinterpret_cast<const float4*>(base + (size_t)(c + e) * 64))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 u = c + 3 < nc ? __ldcg(reinterpret_cast<const float4*>(base + (size_t)(c + 3) * 64))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int e = 0; e < 3; ++e)
+            if (c + e < nc) {
+                s.x += t[e].x;
+                s.y += t[e].y;
+                s.z += t[e].z;
+                s.w += t[e].w;
+            }
+        if (c + 3 < nc) {
+            s.x += u.x;
+            s.y += u.y;
+            s.z += u.z;
+            s.w += u.w;
+        }
+    }
+    return s;
+}
+
+__device__ __forceinline__ uint2 finish4(float4 s, float rs) {
+    return make_uint2((uint32_t)f32_to_bf16_bits(__fmul_rn(s.x, rs)) | ((uint32_t)f32_to_bf16_bits(__fmul_rn(s.y, rs)) << 16),
+                      (uint32_t)f32_to_bf16_bits(__fmul_rn(s.z, rs)) | ((uint32_t)f32_to_bf16_bits(__fmul_rn(s.w, rs)) << 16));
+}
+
+// Stage the x of phase P (K bf16 values) into shared memory; returns this thread's sum of squares.
+// From an external input: plain 16-byte copies. From the previous phase's output: every thread
+// owns 4-row cells (16 per producer quad) and sums the cell's slots; the loads of two cells and
+// four slots each are in flight together.
+__device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P, uint16_t* xs, int C, float rs_prev,
+                                         bool rms) {
+    float ss = 0.0f;
+    auto acc_sq = [&](uint32_t w) {
+        const float lo = bf16_bits_to_f32(w & 0xffffu), hi = bf16_bits_to_f32(w >> 16);
+        ss = __fadd_rn(ss, __fmul_rn(lo, lo));
+        ss = __fadd_rn(ss, __fmul_rn(hi, hi));
+    };
+    if (P.src < 0) {
+        for (int u = threadIdx.x; u < P.K / 8; u += kThreads) {
+            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(P.x) + u);
+            *reinterpret_cast<uint4*>(xs + u * 8) = v;
+            if (rms) {
+                acc_sq(v.x);
+                acc_sq(v.y);
+                acc_sq(v.z);
+                acc_sq(v.w);
+            }
+        }
+        return ss;
+    }
+    const PhaseDev& S = a.ph[P.src];
+    const float* sl = a.slots + (size_t)(P.src & 1) * a.slot_stride;
+    const int q0 = P.src_col >> 6;
+    const int cells = P.K / 4;
+    for (int e0 = threadIdx.x; e0 < cells; e0 += 2 * kThreads) {
+        float4 s[2];
+        int idx[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            idx[h] = e0 + h * kThreads;
+            if (idx[h] < cells) {
+                const int q = q0 + (idx[h] >> 4);
+                int cf, cl;
+                quad_ctas(S, q, C, cf, cl);
+                s[h] = sum_slots4(sl + (size_t)q * kSlots * 64 + (idx[h] & 15) * 4, cl - cf + 1);
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            if (idx[h] < cells) {
+                const uint2 w = finish4(s[h], rs_prev);
+                *reinterpret_cast<uint2*>(xs + idx[h] * 4) = w;
+                if (rms) {
+                    acc_sq(w.x);
+                    acc_sq(w.y);
+                }
+            }
+    }
+    return ss;
+}
+
+// One warp writes phase pp's cut quads owned by this CTA (quad q goes to CTA q mod C) back to y.
+__device__ void write_back_warp(const DecodeArgs& a, int pp, int cta, int C, float rs_prev) {
+    const PhaseDev& Q = a.ph[pp];
+    if (Q.flags & G4Q_PHASE_ARGMAX) return;
+    const int lane = threadIdx.x & 31;
+    const float* sl = a.slots + (size_t)(pp & 1) * a.slot_stride;
+    for (int q = cta; q < Q.Q; q += C) {
+        int cf, cl;
+        quad_ctas(Q, q, C, cf, cl);
+        if (cf == cl || lane >= 16) continue;
+        const float4 s = sum_slots4(sl + (size_t)q * kSlots * 64 + lane * 4, cl - cf + 1);
+        const int n = q * 64 + lane * 4;
+        if (Q.flags & G4Q_QMM_OUT_F32) {
+            float* y = reinterpret_cast<float*>(Q.y) + n;
+            y[0] = __fmul_rn(s.x, rs_prev);
+            y[1] = __fmul_rn(s.y, rs_prev);
+            y[2] = __fmul_rn(s.z, rs_prev);
+            y[3] = __fmul_rn(s.w, rs_prev);
+        } else {
+            *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(Q.y) + n) = finish4(s, rs_prev);
         }
     }
 }
@@ -283,11 +428,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     __shared__ CtaShared sh;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
     const int C = gridDim.x, cta = blockIdx.x;
-    const int M = a.M;
     uint8_t* ring = smem + (size_t)warp * kRingBytes;
     const uint32_t ring_s = saddr(ring);
     float* red = reinterpret_cast<float*>(smem + (size_t)kWarps * kRingBytes);
-    uint32_t* xs = reinterpret_cast<uint32_t*>(smem + (size_t)kWarps * kRingBytes + 2 * kMaxTok * kWarps * 64 * 4);
+    uint16_t* xs = reinterpret_cast<uint16_t*>(smem + (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4);
     const uint32_t bar0 = saddr(&sh.bars[warp][0]);
 
     if (lane == 0) {
@@ -299,75 +443,65 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         sh.seq_done[0] = -2;
         sh.seq_done[1] = -1;
         sh.warps_finished = 0;
-        for (int m = 0; m < kMaxTok; ++m) sh.best[m] = 0ull;
-        sh.zero = make_uint2(0u, 0u);
+        sh.wb_claim = 0;
+        sh.best = 0ull;
+        sh.zero[0] = sh.zero[1] = 0u;
+        sh.rs = 1.0f;
     }
     __syncwarp();
-    Cursor pre;
+    Pre pre;
     pre.p = 0;
     pre.enter(a, cta, C, warp);
     for (int s = 0; s < kStages && pre.p < a.n_phases; ++s) {
-        if (lane == 0) issue_unit(a.ph[pre.p], pre.q, pre.g, ring_s + s * kUnitBytes, bar0 + 8 * s);
+        if (lane == 0) pre.issue(a, ring_s + s * kUnitBytes, bar0 + 8 * s);
         pre.next(a, cta, C, warp);
     }
 
     int stage = 0;
     uint32_t phase_bit = 0;
     int seq_base = 0;   // CTA-wide ordinal of the first quad of the current phase (parity picks the red buffer)
-    unsigned long long best[kMaxTok];
-#pragma unroll
-    for (int m = 0; m < kMaxTok; ++m) best[m] = 0ull;
+    unsigned long long best = 0ull;
 
     for (int p = 0; p < a.n_phases; ++p) {
         const PhaseDev& P = a.ph[p];
         const int cs = range_start(cta, P.U, C), ce = range_start(cta + 1, P.U, C);
         const int G = P.G;
         const int q_first = cs / G;
-        // ---- phase entry: wait for the producing phase everywhere, then stage x (row stride K+8)
+        // ---- phase entry: wait until every CTA has finished phase p-1
         __syncthreads();
-        if (p > 0 && threadIdx.x == 0) spin_until(a.done + (p - 1), (unsigned)C, a.err);
-        __syncthreads();
-        const int xstride = P.K + 8;   // bf16 elements; +16 bytes keeps the B-fragment reads conflict-free
-        const bool rms = (P.flags & G4Q_QMM_RMS_SCALE) != 0;
-        for (int m = 0; m < M; ++m) {
-            float ss = 0.0f;
-            const uint16_t* xr = P.x + (int64_t)m * P.ldx;
-            for (int u = threadIdx.x; u < P.K / 8; u += kThreads) {
-                const uint4 v = __ldcg(reinterpret_cast<const uint4*>(xr + u * 8));
-                *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(xs) + m * xstride + u * 8) = v;
-                if (rms) {
-                    const uint32_t pv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float lo = bf16_bits_to_f32(pv[i] & 0xffffu), hi = bf16_bits_to_f32(pv[i] >> 16);
-                        ss = __fadd_rn(ss, __fmul_rn(lo, lo));
-                        ss = __fadd_rn(ss, __fmul_rn(hi, hi));
-                    }
-                }
-            }
-            if (rms) {
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-                if (lane == 0) sh.wss[warp][m] = ss;
-            }
+        if (threadIdx.x == 0) {
+            if (p > 0) spin_until(a.done + (p - 1), (unsigned)C, a.err);
+            sh.rs_prev = sh.rs;
+            sh.wb_claim = 0;
         }
         __syncthreads();
-        if (threadIdx.x < kMaxTok) {
+        const float rs_prev = sh.rs_prev;
+        // ---- stage x (bf16; B-fragment reads of one token are conflict free)
+        const bool rms = (P.flags & G4Q_QMM_RMS_SCALE) != 0;
+        float ss = stage_x(a, P, xs, C, rs_prev, rms);
+        if (rms) {
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+            if (lane == 0) sh.wss[warp] = ss;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
             float r = 1.0f;
-            if (rms && threadIdx.x < M) {
+            if (rms) {
                 float s = 0.0f;
-                for (int w = 0; w < kWarps; ++w) s = __fadd_rn(s, sh.wss[w][threadIdx.x]);
+                for (int w = 0; w < kWarps; ++w) s = __fadd_rn(s, sh.wss[w]);
                 r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)P.K), a.eps)));
             }
-            sh.rs[threadIdx.x] = r;
+            sh.rs = r;
         }
         __syncthreads();
 
         // ---- this warp's units of phase p
         const int n_units = ce - cs > warp ? (ce - cs - warp + kWarps - 1) / kWarps : 0;
-        const bool tok_ok = gi < M;
-        const uint32_t* xw = tok_ok ? xs + gi * (xstride / 2) + t : reinterpret_cast<const uint32_t*>(&sh.zero);
+        const bool tok_ok = gi == 0;   // one token: B-fragment column 0 lives in lanes 0..3
+        const uint32_t* xw = tok_ok ? reinterpret_cast<const uint32_t*>(xs) + t : sh.zero;
         const int kst = tok_ok ? 8 : 0;   // 32-bit words per k16 step
+        const int hi_off = tok_ok ? 4 : 1;
         float acc[4][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
@@ -376,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         int cq = (cs + warp) / G, cg = (cs + warp) - cq * G, acc_q = cq;
         for (int k = 0; k < n_units; ++k) {
             if (cq != acc_q) {
-                park(a, P, sh, red, seq_base + (acc_q - q_first), acc_q, cs, ce, cta, C, acc, best);
+                park(a, P, p, sh, red, seq_base + (acc_q - q_first), acc_q, cs, ce, cta, C, acc, best);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -385,37 +519,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             }
             wait_parity(bar0 + 8 * stage, phase_bit, a.err);
             const uint8_t* st = ring + stage * kUnitBytes;
-            uint4 wv[4];
-            uint32_t sb0[4], sb1[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                wv[i] = reinterpret_cast<const uint4*>(st + i * 512)[lane];
-                const uint32_t* sbw = reinterpret_cast<const uint32_t*>(st + kUnitPacked) + i * 16 + gi;
-                sb0[i] = sbw[0];
-                sb1[i] = sbw[8];
-            }
             const uint32_t* xg = xw + cg * 4 * kst;
             uint32_t b0[4], b1[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 b0[j] = xg[j * kst];
-                b1[j] = xg[j * kst + (tok_ok ? 4 : 1)];
-            }
-            __syncwarp();
-            if (pre.p < a.n_phases) {
-                if (lane == 0) issue_unit(a.ph[pre.p], pre.q, pre.g, ring_s + stage * kUnitBytes, bar0 + 8 * stage);
-                pre.next(a, cta, C, warp);
-            }
-            if (++stage == kStages) {
-                stage = 0;
-                phase_bit ^= 1u;
+                b1[j] = xg[j * kst + hi_off];
             }
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const RowConsts c0 = row_consts(sb0[i]), c1 = row_consts(sb1[i]);
+                const uint4 wv = reinterpret_cast<const uint4*>(st + i * 512)[lane];
+                const uint32_t* sbw = reinterpret_cast<const uint32_t*>(st + kUnitPacked) + i * 16 + gi;
+                const RowConsts c0 = row_consts(sbw[0]), c1 = row_consts(sbw[8]);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const uint32_t w = j == 0 ? wv[i].x : j == 1 ? wv[i].y : j == 2 ? wv[i].z : wv[i].w;
+                    const uint32_t w = j == 0 ? wv.x : j == 1 ? wv.y : j == 2 ? wv.z : wv.w;
                     const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
                     const uint32_t a1 = deq_r2_fast(lop_nibbles(w >> 4), c1);
                     const uint32_t a2 = deq_r2_fast(lop_nibbles(w >> 8), c0);
@@ -423,56 +541,75 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
                     mma_bf16_16816(acc[i], a0, a1, a2, a3, b0[j], b1[j]);
                 }
             }
+            // the unit has been read: refill the buffer with the warp's next unit (maybe of a later phase)
+            __syncwarp();
+            if (pre.p < a.n_phases) {
+                if (lane == 0) pre.issue(a, ring_s + stage * kUnitBytes, bar0 + 8 * stage);
+                pre.next(a, cta, C, warp);
+            }
+            if (++stage == kStages) {
+                stage = 0;
+                phase_bit ^= 1u;
+            }
             cg += kWarps;
             while (cg >= G) {
                 cg -= G;
                 ++cq;
             }
         }
-        if (n_units > 0) park(a, P, sh, red, seq_base + (acc_q - q_first), acc_q, cs, ce, cta, C, acc, best);
+        if (n_units > 0) park(a, P, p, sh, red, seq_base + (acc_q - q_first), acc_q, cs, ce, cta, C, acc, best);
         seq_base += (ce - 1) / G - q_first + 1;
-        // ---- argmax phase: fold the warp's best keys into the CTA's
-        if (P.flags & G4Q_PHASE_ARGMAX) {
-            for (int m = 0; m < M; ++m) {
-                unsigned long long k = best[m];
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) {
-                    const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, off);
-                    k = o > k ? o : k;
-                }
-                if (lane == 0) atomicMax(&sh.best[m], k);
-            }
+        // ---- the first warp of the CTA to run out of units writes phase p-1's cut quads back to y
+        if (p > 0) {
+            int claim = 0;
+            if (lane == 0) claim = atomicAdd(&sh.wb_claim, 1) == 0;
+            claim = __shfl_sync(0xffffffffu, claim, 0);
+            if (claim) write_back_warp(a, p - 1, cta, C, rs_prev);
         }
-        // ---- the CTA has stored everything it owes for phase p
-        __threadfence_block();
+        const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
+        if (argmax) {
+            unsigned long long kk = best;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                const unsigned long long o = __shfl_xor_sync(0xffffffffu, kk, off);
+                kk = o > kk ? o : kk;
+            }
+            if (lane == 0) atomicMax(&sh.best, kk);
+        }
+        // ---- one completion count per CTA: the warps meet on a shared counter (CTA scope), the last
+        //      one publishes all of the CTA's stores with a gpu-scope release atomic
         __syncwarp();
         int last_warp = 0;
-        if (lane == 0) last_warp = atomicAdd(&sh.warps_finished, 1) == kWarps - 1;
+        if (lane == 0) {
+            __threadfence_block();
+            last_warp = atomicAdd(&sh.warps_finished, 1) == kWarps - 1;
+        }
         last_warp = __shfl_sync(0xffffffffu, last_warp, 0);
-        if (last_warp) {
-            if (lane == 0) {
-                sh.warps_finished = 0;
-                if (P.flags & G4Q_PHASE_ARGMAX)
-                    for (int m = 0; m < M; ++m) atomicMax(a.keys + m, sh.best[m]);
-                __threadfence();
-                const unsigned int prev = atomicAdd(a.done + p, 1u);
-                sh.last_cta = (P.flags & G4Q_PHASE_ARGMAX) && prev == (unsigned)C - 1;
-            }
-            __syncwarp();
-            if ((P.flags & G4Q_PHASE_ARGMAX) && sh.last_cta && lane < M) {
-                __threadfence();
-                const unsigned long long k = atomicExch(a.keys + lane, 0ull);
-                if (a.tokens) a.tokens[lane] = (int32_t)key_index(k);
-                if (a.values) a.values[lane] = key_value(k);
-                if (a.keys_out) a.keys_out[lane] = k;
+        if (last_warp && lane == 0) {
+            __threadfence_block();
+            sh.warps_finished = 0;
+            if (argmax) atomicMax(a.key, sh.best);
+            const unsigned int prev = atom_add_acq_rel(a.done + p, 1u);
+            if (argmax && prev == (unsigned)C - 1) {
+                const unsigned long long k = atomicExch(a.key, 0ull);
+                if (a.tokens) a.tokens[0] = (int32_t)key_index(k);
+                if (a.values) a.values[0] = key_value(k);
+                if (a.keys_out) a.keys_out[0] = k;
             }
         }
+    }
+    // ---- a plan that ends with a regular phase: finish its cut quads
+    const int last = a.n_phases - 1;
+    if (!(a.ph[last].flags & G4Q_PHASE_ARGMAX)) {
+        __syncthreads();
+        if (threadIdx.x == 0) spin_until(a.done + last, (unsigned)C, a.err);
+        __syncthreads();
+        if (threadIdx.x < 32) write_back_warp(a, last, cta, C, sh.rs);
     }
     // ---- the last CTA out resets the phase counters for the next launch
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned int prev = atomicAdd(a.exit_count, 1u);
+        const unsigned int prev = atom_add_acq_rel(a.exit_count, 1u);
         if (prev == (unsigned)C - 1) {
             for (int p = 0; p < a.n_phases; ++p) a.done[p] = 0u;
             __threadfence();
@@ -486,11 +623,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
 struct DecodePlan {
     uint64_t magic = 0;
     int device = -1;
-    int n_phases = 0, max_tokens = 0, grid = 0, argmax_phase = -1;
+    int n_phases = 0, grid = 0;
     size_t smem = 0;
+    int64_t slot_stride = 0;
     PhaseDev* d_ph = nullptr;
     unsigned int* d_done = nullptr;   // n_phases + 1 (exit counter last)
-    unsigned long long* d_keys = nullptr;
+    unsigned long long* d_key = nullptr;
     float* d_slots = nullptr;
     int* d_qcount = nullptr;
 };
@@ -499,29 +637,27 @@ constexpr uint64_t kPlanMagic = 0x4734514445434f44ull;
 
 void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens) {
     if (n <= 0 || phases == nullptr) throw Error(G4Q_ERR_INVALID_ARGUMENT, "a plan needs at least one phase");
-    if (max_tokens < 1 || max_tokens > kMaxTok)
-        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "the decode plan supports 1.." + std::to_string(kMaxTok) + " tokens");
+    if (max_tokens != 1)
+        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "the decode plan runs one token per step (max_tokens = 1)");
     const int dev = current_device();
     const int sms = device_sm_count();
     std::vector<PhaseDev> ph(n);
-    int total_quads = 0, kmax = 0, argmax = -1;
+    int max_q = 0, kmax = 0;
     for (int i = 0; i < n; ++i) {
         const Weight* w = reinterpret_cast<const Weight*>(phases[i].weight);
-        if (!w || w->magic != kWeightMagic) throw Error(G4Q_ERR_INVALID_ARGUMENT, "phase " + std::to_string(i) + ": invalid weight");
-        if (w->device != dev) throw Error(G4Q_ERR_INVALID_ARGUMENT, "phase weight lives on another device");
-        if (!w->fast_ok) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "phase weight has scales outside |s| < 2^120");
-        if (w->N % 64 != 0) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan phases need rows % 64 == 0");
+        const std::string tag = "phase " + std::to_string(i) + ": ";
+        if (!w || w->magic != kWeightMagic) throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "invalid weight");
+        if (w->device != dev) throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "weight lives on another device");
+        if (!w->fast_ok) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "scales outside |s| < 2^120");
+        if (w->N % 64 != 0) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "rows must be a multiple of 64");
         const uint32_t fl = phases[i].flags;
         if (fl & ~(G4Q_QMM_RMS_SCALE | G4Q_QMM_OUT_F32 | G4Q_PHASE_ARGMAX))
-            throw Error(G4Q_ERR_INVALID_ARGUMENT, "unknown phase flag bits");
-        if (fl & G4Q_PHASE_ARGMAX) {
-            if (i != n - 1) throw Error(G4Q_ERR_INVALID_ARGUMENT, "the argmax phase must be the last phase");
-            argmax = i;
-        } else if (!phases[i].y) {
-            throw Error(G4Q_ERR_INVALID_ARGUMENT, "phase " + std::to_string(i) + " needs an output");
-        }
-        if (!phases[i].x || (reinterpret_cast<uintptr_t>(phases[i].x) & 15u) || phases[i].ldx % 8 || phases[i].ldx < w->K)
-            throw Error(G4Q_ERR_INVALID_ARGUMENT, "phase x must be 16-byte aligned with ldx % 8 == 0, ldx >= K");
+            throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "unknown flag bits");
+        if ((fl & G4Q_PHASE_ARGMAX) && i != n - 1)
+            throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "the argmax phase must be the last phase");
+        if (!(fl & G4Q_PHASE_ARGMAX) && !phases[i].y) throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "needs an output");
+        if (!phases[i].x || (reinterpret_cast<uintptr_t>(phases[i].x) & 15u))
+            throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "x must be 16-byte aligned");
         PhaseDev& d = ph[i];
         d.packed = w->packed;
         d.sb = w->sb;
@@ -536,38 +672,52 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens) {
         d.Q = d.R / 4;
         d.U = d.Q * d.G;
         d.flags = fl;
-        if (d.Q > total_quads) total_quads = d.Q;   // slots are shared: size them for the largest phase
+        d.src = -1;
+        d.src_col = 0;
+        // x inside the previous phase's (bf16) output row: consume it with the slot rebuild
+        if (i > 0 && !(ph[i - 1].flags & (G4Q_PHASE_ARGMAX | G4Q_QMM_OUT_F32))) {
+            const uint16_t* y0 = static_cast<const uint16_t*>(ph[i - 1].y);
+            if (phases[i].x >= y0 && phases[i].x < y0 + ph[i - 1].N) {
+                const int64_t col = phases[i].x - y0;
+                if (col % 64 != 0 || col + d.K > ph[i - 1].N)
+                    throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "x must be a 64-aligned column window of phase " +
+                                                                std::to_string(i - 1) + "'s output");
+                d.src = i - 1;
+                d.src_col = (int)col;
+            }
+        }
         if (d.K > kmax) kmax = d.K;
-        if (d.U < sms) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "phase too small for a full-grid decode plan");
+        if (d.Q > max_q) max_q = d.Q;
+        if (d.U < sms) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too small for a full-grid decode plan");
+        if ((uint64_t)(d.U + 1) * (uint64_t)sms >= (1ull << 32))
+            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too many units for 32-bit partition arithmetic");
         // a quad (G units) meets at most (G-1)/min_range + 2 CTA ranges
-        if ((d.G - 1) / (d.U / sms) + 2 > kSlots)
-            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "phase " + std::to_string(i) + " is split too finely for the grid");
+        if ((d.G - 1) / (d.U / sms) + 2 > kSlots) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "split too finely");
     }
     auto* plan = new DecodePlan();
     plan->device = dev;
     plan->n_phases = n;
-    plan->max_tokens = max_tokens;
     plan->grid = sms;
-    plan->argmax_phase = argmax;
-    plan->smem = (size_t)kWarps * kRingBytes + 2 * kMaxTok * kWarps * 64 * 4 + (size_t)kMaxTok * (kmax + 8) * 2;
+    plan->slot_stride = (int64_t)max_q * kSlots * 64;
+    plan->smem = (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4 + (size_t)(kmax + 8) * 2;
     if (plan->smem > max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel))) {
         delete plan;
         throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: K too large for shared memory");
     }
     cudaError_t e = cudaMalloc(&plan->d_ph, sizeof(PhaseDev) * n);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_done, sizeof(unsigned int) * (n + 1));
-    if (e == cudaSuccess) e = cudaMalloc(&plan->d_keys, sizeof(unsigned long long) * kMaxTok);
-    if (e == cudaSuccess) e = cudaMalloc(&plan->d_slots, sizeof(float) * (size_t)total_quads * kSlots * 64 * kMaxTok);
-    if (e == cudaSuccess) e = cudaMalloc(&plan->d_qcount, sizeof(int) * (size_t)total_quads);
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_key, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_slots, sizeof(float) * 2 * (size_t)plan->slot_stride);
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_qcount, sizeof(int) * (size_t)max_q);
     if (e == cudaSuccess) e = cudaMemcpy(plan->d_ph, ph.data(), sizeof(PhaseDev) * n, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(plan->d_done, 0, sizeof(unsigned int) * (n + 1));
-    if (e == cudaSuccess) e = cudaMemset(plan->d_keys, 0, sizeof(unsigned long long) * kMaxTok);
-    if (e == cudaSuccess) e = cudaMemset(plan->d_qcount, 0, sizeof(int) * (size_t)total_quads);
+    if (e == cudaSuccess) e = cudaMemset(plan->d_key, 0, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(plan->d_qcount, 0, sizeof(int) * (size_t)max_q);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaFree(plan->d_ph);
         cudaFree(plan->d_done);
-        cudaFree(plan->d_keys);
+        cudaFree(plan->d_key);
         cudaFree(plan->d_slots);
         cudaFree(plan->d_qcount);
         delete plan;
@@ -592,7 +742,7 @@ void decode_plan_free(void* h) {
     cudaSetDevice(plan->device);
     cudaFree(plan->d_ph);
     cudaFree(plan->d_done);
-    cudaFree(plan->d_keys);
+    cudaFree(plan->d_key);
     cudaFree(plan->d_slots);
     cudaFree(plan->d_qcount);
     cudaSetDevice(prev);
@@ -601,27 +751,27 @@ void decode_plan_free(void* h) {
 
 void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offset, int32_t* tokens, float* values,
                      uint64_t* keys, uint16_t* logits, int64_t ld_logits, cudaStream_t st) {
+    (void)ld_logits;
     auto* plan = static_cast<DecodePlan*>(h);
     if (!plan || plan->magic != kPlanMagic) throw Error(G4Q_ERR_INVALID_ARGUMENT, "invalid decode plan handle");
     if (plan->device != current_device()) throw Error(G4Q_ERR_INVALID_ARGUMENT, "plan belongs to another device");
-    if (M < 1 || M > plan->max_tokens) throw Error(G4Q_ERR_INVALID_ARGUMENT, "M outside the plan's token range");
+    if (M != 1) throw Error(G4Q_ERR_INVALID_ARGUMENT, "the decode plan runs one token per step (M = 1)");
     DecodeArgs a;
     a.ph = plan->d_ph;
     a.n_phases = plan->n_phases;
-    a.M = M;
     a.eps = eps;
     a.softcap = softcap;
     a.row_offset = row_offset;
     a.done = plan->d_done;
     a.exit_count = plan->d_done + plan->n_phases;
-    a.keys = plan->d_keys;
+    a.key = plan->d_key;
     a.slots = plan->d_slots;
+    a.slot_stride = plan->slot_stride;
     a.qcount = plan->d_qcount;
     a.tokens = tokens;
     a.values = values;
     a.keys_out = reinterpret_cast<unsigned long long*>(keys);
     a.logits = logits;
-    a.ld_logits = ld_logits;
     a.err = device_scratch().err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(plan->grid);

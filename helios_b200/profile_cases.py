@@ -5,6 +5,7 @@
     python -m helios_b200.profile_cases lmhead    # LM head 262144 x 3840 + softcap + argmax, M = 1
     python -m helios_b200.profile_cases gemm      # prefill dequant-GEMM, q|k|v 8192 x 3840, M = 2048
     python -m helios_b200.profile_cases dequant   # bit-exact dequantize of 15360 x 3840
+    python -m helios_b200.profile_cases decode    # persistent decode-step kernel, 2 full-size layers + LM head
 
 Each case uploads seeded synthetic weights (several copies where the matrix is smaller than L2,
 so consecutive launches read cold data), runs a few warm-up launches and then `--launches`
@@ -26,7 +27,31 @@ CASES = {
     "lmhead": dict(N=262144, K=3840, M=1, copies=1),
     "gemm": dict(N=8192, K=3840, M=2048, copies=1),
     "dequant": dict(N=15360, K=3840, M=0, copies=1),
+    "decode": dict(layers=2),
 }
+
+
+def decode_case(a, c):
+    """The single-launch decode plan of a 2-layer full-width stack (about 0.8 GB of weights)."""
+    from .stack import StackConfig, SyntheticStack
+    cfg = StackConfig(layers=c["layers"])
+    st = SyntheticStack(cfg, max_tokens=1)
+    st.build_plan(1)
+    h = synth_normal(activation_seed(0), (1, cfg.hidden))
+    for _ in range(a.warmup):
+        st.decode(h)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.launches):
+        st.decode(h)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / a.launches
+    wbytes = cfg.weight_bytes()
+    print(json.dumps({"case": "decode", "us_per_launch": round(us, 3), "weight_bytes": wbytes,
+                      "weight_GBps": round(wbytes / us / 1e3, 1)}))
+    st.free()
 
 
 def main():
@@ -37,6 +62,8 @@ def main():
     a = ap.parse_args()
     c = CASES[a.case]
     torch.cuda.set_device(0)
+    if a.case == "decode":
+        return decode_case(a, c)
     ws = []
     for i in range(c["copies"]):
         w, s, b = synth_matrix(matrix_seed(i, "gate"), c["N"], c["K"])
