@@ -239,7 +239,7 @@ G4qStatus g4q_weight_info(const G4qWeight* h, G4qWeightInfo* out) {
         out->device_bytes = w->bytes;
         out->device = w->device;
         out->fast_path_ok = (flags & 1) ? 0 : 1;
-        out->error_flags = flags & ~1;
+        out->error_flags = flags & 2;
     });
 }
 
@@ -293,6 +293,7 @@ G4qStatus g4q_weight_load(G4qWeight* h, int64_t dst_row0, const uint32_t* packed
         int flags = 0;
         check_cuda(cudaMemcpy(&flags, w->d_flags, sizeof(int), cudaMemcpyDeviceToHost), "read handle flags");
         w->fast_ok = (flags & 1) == 0;   // cached so compute calls never read device memory
+        w->small_scales = (flags & 4) == 0;
     });
 }
 

@@ -36,15 +36,19 @@
 namespace g4q {
 namespace {
 
-constexpr int kWarps = 24;
+constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 3;
+constexpr int kStages = 4;
 constexpr uint32_t kUnitPacked = 4 * 512;
 constexpr uint32_t kUnitSb = 64 * 4;
 constexpr uint32_t kUnitBytes = kUnitPacked + kUnitSb;
 constexpr uint32_t kRingBytes = kStages * kUnitBytes;
 constexpr int kSlots = 16;                        // CTA ranges one 64-row quad may be cut into
+constexpr int kMaxCtaQuads = 64;                  // quads one CTA range may touch in a phase
 constexpr long long kSpinLimit = 4000000000ll;    // ~2 s of SM clocks
+constexpr uint32_t kOddNibbleMask = 0x00F000F0u;  // q at bits 4-7 of each half: bf16 value q * 2^-129
+constexpr uint32_t kPow64x2 = 0x5F805F80u;        // bf16x2 (2^64, 2^64)
+constexpr uint32_t kPow65x2 = 0x60006000u;        // bf16x2 (2^65, 2^65)
 
 struct PhaseDev {
     const uint32_t* packed;
@@ -119,48 +123,70 @@ __device__ __forceinline__ void quad_ctas(const PhaseDev& P, int q, int C, int& 
     cl = cta_of_unit((q + 1) * P.G - 1, P.U, C);
 }
 
-// The prefetching position of one warp, across phases (unit q*G+g of phase p; k of n done).
+// Warp w owns the contiguous units [wstart(w), wstart(w + 1)) of its CTA's n units of a phase
+// (relative numbering): the first n % kWarps warps take one unit more, warps past n own none.
+__device__ __forceinline__ int wstart(int w, int n) {
+    const int b = n / kWarps, r = n - b * kWarps;
+    return w * b + min(w, r);
+}
+
+__device__ __forceinline__ int warp_of(int u, int n) {   // owner of relative unit u, 0 <= u < n
+    const int b = n / kWarps, r = n - b * kWarps, big = r * (b + 1);
+    return u < big ? u / (b + 1) : r + (u - big) / b;
+}
+
+// The prefetching position of one warp, across phases: the next unit to issue is group g of the
+// current quad of phase p, at byte offsets off_p / off_s of that phase's packed words / sb.
 struct Pre {
-    int p, k, n, q, g, G;
+    int p, left, g, G;
+    uint32_t off_p, off_s, step_p, step_s;
+    const char* base_p;
+    const char* base_s;
     __device__ __forceinline__ void enter(const DecodeArgs& a, int cta, int C, int w) {
         while (p < a.n_phases) {
             const PhaseDev& P = a.ph[p];
-            const int cs = range_start(cta, P.U, C), ce = range_start(cta + 1, P.U, C);
-            n = ce - cs > w ? (ce - cs - w + kWarps - 1) / kWarps : 0;
-            k = 0;
-            if (n > 0) {
+            const int cs = range_start(cta, P.U, C), n = range_start(cta + 1, P.U, C) - cs;
+            const int u0 = wstart(w, n);
+            left = wstart(w + 1, n) - u0;
+            if (left > 0) {
                 G = P.G;
-                q = (cs + w) / G;
-                g = (cs + w) - q * G;
+                const int u = cs + u0, q = u / G;
+                g = u - q * G;
+                step_p = (uint32_t)P.R * 512u;
+                step_s = (uint32_t)P.N * 4u;
+                off_p = (uint32_t)g * step_p + (uint32_t)q * 2048u;
+                off_s = (uint32_t)g * step_s + (uint32_t)q * 256u;
+                base_p = reinterpret_cast<const char*>(P.packed);
+                base_s = reinterpret_cast<const char*>(P.sb);
                 return;
             }
             ++p;
         }
     }
     __device__ __forceinline__ void next(const DecodeArgs& a, int cta, int C, int w) {
-        if (++k < n) {
-            g += kWarps;
-            while (g >= G) {
-                g -= G;
-                ++q;
+        if (--left > 0) {
+            if (++g == G) {   // next quad: group 0, four row tiles further
+                g = 0;
+                off_p += 2048u - (uint32_t)(G - 1) * step_p;
+                off_s += 256u - (uint32_t)(G - 1) * step_s;
+            } else {
+                off_p += step_p;
+                off_s += step_s;
             }
             return;
         }
         ++p;
         enter(a, cta, C, w);
     }
-    __device__ __forceinline__ void issue(const DecodeArgs& a, uint32_t dst, uint32_t bar) const {
-        const PhaseDev& P = a.ph[p];
-        const uint32_t* src_p = P.packed + ((size_t)g * P.R + (size_t)q * 4) * 128;
-        const uint32_t* src_s = P.sb + (size_t)g * P.N + (size_t)q * 64;
+    __device__ __forceinline__ void issue(uint32_t dst, uint32_t bar) const {
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kUnitBytes) : "memory");
         asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                          dst),
-                     "l"(src_p), "r"(kUnitPacked), "r"(bar)
+                     "l"(base_p + off_p), "r"(kUnitPacked), "r"(bar)
                      : "memory");
         asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                          dst + kUnitPacked),
-                     "l"(src_s), "r"(kUnitSb), "r"(bar)
+                     "l"(base_s + off_s), "r"(kUnitSb), "r"(bar)
                      : "memory");
     }
 };
@@ -169,8 +195,7 @@ struct CtaShared {
     unsigned long long bars[kWarps][kStages];
     float wss[kWarps];
     float rs, rs_prev;
-    int cnt[2];
-    int seq_done[2];
+    int qcnt[kMaxCtaQuads];   // arrivals per quad of the CTA's range (reset by the last arriver)
     int warps_finished;
     int wb_claim;
     unsigned long long best;
@@ -195,56 +220,48 @@ __device__ __forceinline__ void fold_logit(const DecodeArgs& a, int n, float o, 
     if (key > best) best = key;
 }
 
-// Park this warp's partial of quad q (sequence number seq in this CTA); the last warp of the quad
-// sums the partials in warp order and stores it (whole quad), leaves it in this CTA's slot (cut
-// quad), or -- argmax phase -- folds the finished logits into the running key.
-__device__ void park(const DecodeArgs& a, const PhaseDev& P, int p, CtaShared& sh, float* red, int seq, int q, int cs,
-                     int ce, int cta, int C, const float (&acc)[4][4], unsigned long long& best) {
+// Park this warp's partial of quad q. A warp keeps the partial of the first quad of its range in
+// red[warp][0] (the previous warp may need it) and everything else in red[warp][1] (only the last
+// quad of the range is read by another warp, and it comes last). The last contributing warp sums
+// the partials in warp order and stores the quad (whole quad), leaves it in this CTA's slot (cut
+// quad), or -- argmax phase -- folds the finished logits into the running key. No warp ever waits.
+__device__ void park(const DecodeArgs& a, const PhaseDev& P, int p, CtaShared& sh, float* red, int q, int first_q,
+                     int cs, int ce, int cta, int C, const float (&acc)[4][4], unsigned long long& best) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
-    const int G = P.G;
-    const int b = seq & 1;
-    if (*reinterpret_cast<volatile int*>(&sh.seq_done[b]) < seq - 2) {
-        const long long t0 = clock64();
-        while (*reinterpret_cast<volatile int*>(&sh.seq_done[b]) < seq - 2) {
-            if (clock64() - t0 > kSpinLimit) {
-                atomicCAS(a.err, 0, 33);
-                break;
-            }
-        }
-    }
-    float* rb = red + (size_t)b * kWarps * 64;
+    const int G = P.G, n = ce - cs;
+    float* rb = red + (size_t)(warp * 2 + (q == first_q ? 0 : 1)) * 64;
     if (t == 0) {   // token 0 lives in the t == 0 lanes (C fragment column 0)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            rb[warp * 64 + i * 16 + gi] = acc[i][0];
-            rb[warp * 64 + i * 16 + gi + 8] = acc[i][2];
+            rb[i * 16 + gi] = acc[i][0];
+            rb[i * 16 + gi + 8] = acc[i][2];
         }
     }
     __threadfence_block();
     __syncwarp();
     const int lo = max(cs, q * G), hi = min(ce, (q + 1) * G);
-    const int nw = min(kWarps, hi - lo);
-    const int w0 = (lo - cs) % kWarps;
-    int last = 0;
-    if (lane == 0) last = atomicAdd(&sh.cnt[b], 1) == nw - 1;
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence_block();
-    const bool whole = cs <= q * G && ce >= (q + 1) * G;
-    const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
+    const int wa = warp_of(lo - cs, n), wb = warp_of(hi - 1 - cs, n);
+    const int qi = q - cs / G;
+    int last = 1;
+    if (wb > wa) {
+        if (lane == 0) last = atomicAdd(&sh.qcnt[qi], 1) == wb - wa;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) return;
+        __threadfence_block();
+    }
+    // warp wa holds q in slot 0 only if q is also its first quad; the others hold it as their first
+    const int slot_a = (cs + wstart(wa, n)) / G == q ? 0 : 1;
     float v[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         const int row = lane + 32 * h;
-        float s = 0.0f;
-        for (int w = 0; w < kWarps; ++w) {
-            const int d = (w - w0 + kWarps) % kWarps;
-            if (d < nw) s += rb[w * 64 + row];
-        }
+        float s = red[(wa * 2 + slot_a) * 64 + row];
+        for (int w = wa + 1; w <= wb; ++w) s += red[w * 2 * 64 + row];
         v[h] = s;
     }
-    __syncwarp();
-    if (lane == 0) sh.cnt[b] = 0;
+    if (wb > wa && lane == 0) sh.qcnt[qi] = 0;
+    const bool whole = cs <= q * G && ce >= (q + 1) * G;
+    const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
     if (whole && argmax) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) fold_logit(a, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs), best);
@@ -278,9 +295,7 @@ __device__ void park(const DecodeArgs& a, const PhaseDev& P, int p, CtaShared& s
             }
         }
     }
-    __threadfence_block();
     __syncwarp();
-    if (lane == 0) *reinterpret_cast<volatile int*>(&sh.seq_done[b]) = seq;
 }
 
 __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
@@ -343,11 +358,19 @@ __device__ __forceinline__ uint2 finish4(float4 s, float rs) {
                       (uint32_t)f32_to_bf16_bits(__fmul_rn(s.z, rs)) | ((uint32_t)f32_to_bf16_bits(__fmul_rn(s.w, rs)) << 16));
 }
 
+// Shared-memory order of x: inside each 64-wide group, lane t's B-fragment words for the four k16
+// steps (j) sit together: word w = 8j + t + 4hi of the group goes to slot 8t + 2j + hi, so a lane
+// fetches the whole group's fragments with two 16-byte loads.
+__device__ __forceinline__ int xperm(int w) {
+    const int r = w & 7;
+    return (w & ~31) | ((r & 3) << 3) | (((w >> 3) & 3) << 1) | (r >> 2);
+}
+
 // Stage the x of phase P (K bf16 values) into shared memory; returns this thread's sum of squares.
 // From an external input: plain 16-byte copies. From the previous phase's output: every thread
 // owns 4-row cells (16 per producer quad) and sums the cell's slots; the loads of two cells and
 // four slots each are in flight together.
-__device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P, uint16_t* xs, int C, float rs_prev,
+__device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P, uint32_t* xs, int C, float rs_prev,
                                          bool rms) {
     float ss = 0.0f;
     auto acc_sq = [&](uint32_t w) {
@@ -358,7 +381,10 @@ __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P,
     if (P.src < 0) {
         for (int u = threadIdx.x; u < P.K / 8; u += kThreads) {
             const uint4 v = __ldcg(reinterpret_cast<const uint4*>(P.x) + u);
-            *reinterpret_cast<uint4*>(xs + u * 8) = v;
+            xs[xperm(4 * u)] = v.x;
+            xs[xperm(4 * u + 1)] = v.y;
+            xs[xperm(4 * u + 2)] = v.z;
+            xs[xperm(4 * u + 3)] = v.w;
             if (rms) {
                 acc_sq(v.x);
                 acc_sq(v.y);
@@ -389,7 +415,8 @@ __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P,
         for (int h = 0; h < 2; ++h)
             if (idx[h] < cells) {
                 const uint2 w = finish4(s[h], rs_prev);
-                *reinterpret_cast<uint2*>(xs + idx[h] * 4) = w;
+                xs[xperm(2 * idx[h])] = w.x;
+                xs[xperm(2 * idx[h] + 1)] = w.y;
                 if (rms) {
                     acc_sq(w.x);
                     acc_sq(w.y);
@@ -431,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     uint8_t* ring = smem + (size_t)warp * kRingBytes;
     const uint32_t ring_s = saddr(ring);
     float* red = reinterpret_cast<float*>(smem + (size_t)kWarps * kRingBytes);
-    uint16_t* xs = reinterpret_cast<uint16_t*>(smem + (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4);
+    uint32_t* xs = reinterpret_cast<uint32_t*>(smem + (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4);
     const uint32_t bar0 = saddr(&sh.bars[warp][0]);
 
     if (lane == 0) {
@@ -439,9 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (threadIdx.x == 0) {
-        sh.cnt[0] = sh.cnt[1] = 0;
-        sh.seq_done[0] = -2;
-        sh.seq_done[1] = -1;
+        for (int i = 0; i < kMaxCtaQuads; ++i) sh.qcnt[i] = 0;
         sh.warps_finished = 0;
         sh.wb_claim = 0;
         sh.best = 0ull;
@@ -453,20 +478,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     pre.p = 0;
     pre.enter(a, cta, C, warp);
     for (int s = 0; s < kStages && pre.p < a.n_phases; ++s) {
-        if (lane == 0) pre.issue(a, ring_s + s * kUnitBytes, bar0 + 8 * s);
+        if (lane == 0) pre.issue(ring_s + s * kUnitBytes, bar0 + 8 * s);
         pre.next(a, cta, C, warp);
     }
 
     int stage = 0;
     uint32_t phase_bit = 0;
-    int seq_base = 0;   // CTA-wide ordinal of the first quad of the current phase (parity picks the red buffer)
     unsigned long long best = 0ull;
 
     for (int p = 0; p < a.n_phases; ++p) {
         const PhaseDev& P = a.ph[p];
         const int cs = range_start(cta, P.U, C), ce = range_start(cta + 1, P.U, C);
         const int G = P.G;
-        const int q_first = cs / G;
         // ---- phase entry: wait until every CTA has finished phase p-1
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -497,20 +520,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         __syncthreads();
 
         // ---- this warp's units of phase p
-        const int n_units = ce - cs > warp ? (ce - cs - warp + kWarps - 1) / kWarps : 0;
-        const bool tok_ok = gi == 0;   // one token: B-fragment column 0 lives in lanes 0..3
-        const uint32_t* xw = tok_ok ? reinterpret_cast<const uint32_t*>(xs) + t : sh.zero;
-        const int kst = tok_ok ? 8 : 0;   // 32-bit words per k16 step
-        const int hi_off = tok_ok ? 4 : 1;
+        const int u0 = wstart(warp, ce - cs);
+        const int n_units = wstart(warp + 1, ce - cs) - u0;
+        // every lane loads the token's x: all eight B columns hold token 0 (reads broadcast, no
+        // bank conflicts), and column 0 of the accumulators is the one kept
+        const uint4* xt = reinterpret_cast<const uint4*>(xs) + 2 * t;
         float acc[4][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
-        int cq = (cs + warp) / G, cg = (cs + warp) - cq * G, acc_q = cq;
+        int cq = (cs + u0) / G, cg = (cs + u0) - cq * G, acc_q = cq;
+        const int first_q = cq;
         for (int k = 0; k < n_units; ++k) {
             if (cq != acc_q) {
-                park(a, P, p, sh, red, seq_base + (acc_q - q_first), acc_q, cs, ce, cta, C, acc, best);
+                park(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -519,46 +543,45 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             }
             wait_parity(bar0 + 8 * stage, phase_bit, a.err);
             const uint8_t* st = ring + stage * kUnitBytes;
-            const uint32_t* xg = xw + cg * 4 * kst;
-            uint32_t b0[4], b1[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                b0[j] = xg[j * kst];
-                b1[j] = xg[j * kst + hi_off];
-            }
+            const uint4 xa = xt[cg * 8], xb = xt[cg * 8 + 1];
+            const uint32_t b0[4] = {xa.x, xa.z, xb.x, xb.z}, b1[4] = {xa.y, xa.w, xb.y, xb.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const uint4 wv = reinterpret_cast<const uint4*>(st + i * 512)[lane];
                 const uint32_t* sbw = reinterpret_cast<const uint32_t*>(st + kUnitPacked) + i * 16 + gi;
-                const RowConsts c0 = row_consts(sbw[0]), c1 = row_consts(sbw[8]);
+                // row n0 (nibbles at bits 0-3 / 8-11): (128 + q) magic, RN(q*s) = fma((128+q), s, -128 s);
+                // row n1 (bits 4-7 / 12-15): the masked bits read as bf16 are exactly q * 2^-129, so
+                // RN(q*s) = RN((q * 2^-129) * (s * 2^129)) with s * 2^129 exact for |s| < 2^-1
+                const RowConsts c0 = row_consts(sbw[0]);
+                const uint32_t s1 = prmt(sbw[8], 0u, 0x1010u), b1s = prmt(sbw[8], 0u, 0x3232u);
+                const uint32_t s1h = mul_bf16x2(mul_bf16x2(s1, kPow64x2), kPow65x2);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const uint32_t w = j == 0 ? wv.x : j == 1 ? wv.y : j == 2 ? wv.z : wv.w;
+                    const uint32_t w8 = w >> 8;
                     const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
-                    const uint32_t a1 = deq_r2_fast(lop_nibbles(w >> 4), c1);
-                    const uint32_t a2 = deq_r2_fast(lop_nibbles(w >> 8), c0);
-                    const uint32_t a3 = deq_r2_fast(lop_nibbles(w >> 12), c1);
+                    const uint32_t a1 = add_bf16x2(mul_bf16x2(w & kOddNibbleMask, s1h), b1s);
+                    const uint32_t a2 = deq_r2_fast(lop_nibbles(w8), c0);
+                    const uint32_t a3 = add_bf16x2(mul_bf16x2(w8 & kOddNibbleMask, s1h), b1s);
                     mma_bf16_16816(acc[i], a0, a1, a2, a3, b0[j], b1[j]);
                 }
             }
             // the unit has been read: refill the buffer with the warp's next unit (maybe of a later phase)
             __syncwarp();
             if (pre.p < a.n_phases) {
-                if (lane == 0) pre.issue(a, ring_s + stage * kUnitBytes, bar0 + 8 * stage);
+                if (lane == 0) pre.issue(ring_s + stage * kUnitBytes, bar0 + 8 * stage);
                 pre.next(a, cta, C, warp);
             }
             if (++stage == kStages) {
                 stage = 0;
                 phase_bit ^= 1u;
             }
-            cg += kWarps;
-            while (cg >= G) {
-                cg -= G;
+            if (++cg == G) {
+                cg = 0;
                 ++cq;
             }
         }
-        if (n_units > 0) park(a, P, p, sh, red, seq_base + (acc_q - q_first), acc_q, cs, ce, cta, C, acc, best);
-        seq_base += (ce - 1) / G - q_first + 1;
+        if (n_units > 0) park(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
         // ---- the first warp of the CTA to run out of units writes phase p-1's cut quads back to y
         if (p > 0) {
             int claim = 0;
@@ -648,7 +671,8 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens) {
         const std::string tag = "phase " + std::to_string(i) + ": ";
         if (!w || w->magic != kWeightMagic) throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "invalid weight");
         if (w->device != dev) throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "weight lives on another device");
-        if (!w->fast_ok) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "scales outside |s| < 2^120");
+        if (!w->fast_ok || !w->small_scales)
+            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "the decode plan needs every |scale| < 2^-1");
         if (w->N % 64 != 0) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "rows must be a multiple of 64");
         const uint32_t fl = phases[i].flags;
         if (fl & ~(G4Q_QMM_RMS_SCALE | G4Q_QMM_OUT_F32 | G4Q_PHASE_ARGMAX))
@@ -689,8 +713,11 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens) {
         if (d.K > kmax) kmax = d.K;
         if (d.Q > max_q) max_q = d.Q;
         if (d.U < sms) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too small for a full-grid decode plan");
-        if ((uint64_t)(d.U + 1) * (uint64_t)sms >= (1ull << 32))
+        if ((uint64_t)(d.U + 1) * (uint64_t)sms >= (1ull << 32) || (uint64_t)w->N * (uint64_t)w->K / 2 >= (1ull << 32))
             throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too many units for 32-bit partition arithmetic");
+        // a CTA range (at most ceil(U/C) units) touches at most (ceil(U/C) + G - 2) / G + 1 quads
+        if ((d.U + sms - 1) / sms + d.G - 2 >= (kMaxCtaQuads - 1) * d.G)
+            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too many quads per CTA range");
         // a quad (G units) meets at most (G-1)/min_range + 2 CTA ranges
         if ((d.G - 1) / (d.U / sms) + 2 > kSlots) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "split too finely");
     }

@@ -25,6 +25,7 @@ struct Weight {
     int* d_flags = nullptr;      // device word: bit0 = a scale outside |s| < 2^120 or non-finite,
                                  // bit1 = a gathered row id was out of range
     bool fast_ok = true;         // host copy of !(bit0), refreshed by every load
+    bool small_scales = true;    // host copy of !(bit2): every |scale| < 2^-1
     // lazily created scratch for the LM-head argmax (keys[16] + counter), zeroed once
     unsigned long long* argmax_scratch = nullptr;
 };

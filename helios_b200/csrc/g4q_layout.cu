@@ -97,8 +97,10 @@ __global__ void repack_sb_kernel(const uint16_t* __restrict__ s, const uint16_t*
         const int64_t src = (src_row0 + n) * src_ld_groups + src_g0 + g;
         const uint32_t sv = s[src], bv = b[src];
         sb[g * N + dst_row0 + n] = sv | (bv << 16);
-        // fast dequant path needs -128*s exact: |s| < 2^120 and finite (exponent field < 247)
-        if (((sv >> 7) & 0xFFu) >= 247u) atomicOr(flags, 1);
+        // fast dequant path needs -128*s exact: |s| < 2^120 and finite (exponent field < 247);
+        // the decode plan also scales s by 2^129 exactly: |s| < 2^-1 (exponent field < 126)
+        const uint32_t e = (sv >> 7) & 0xFFu;
+        if (e >= 126u) atomicOr(flags, e >= 247u ? 5 : 4);
     }
 }
 

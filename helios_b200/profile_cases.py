@@ -6,6 +6,7 @@
     python -m helios_b200.profile_cases gemm      # prefill dequant-GEMM, q|k|v 8192 x 3840, M = 2048
     python -m helios_b200.profile_cases dequant   # bit-exact dequantize of 15360 x 3840
     python -m helios_b200.profile_cases decode    # persistent decode-step kernel, 2 full-size layers + LM head
+    python -m helios_b200.profile_cases decode_lm # the same kernel with the LM-head phase alone (steady streaming)
 
 Each case uploads seeded synthetic weights (several copies where the matrix is smaller than L2,
 so consecutive launches read cold data), runs a few warm-up launches and then `--launches`
@@ -28,6 +29,7 @@ CASES = {
     "gemm": dict(N=8192, K=3840, M=2048, copies=1),
     "dequant": dict(N=15360, K=3840, M=0, copies=1),
     "decode": dict(layers=2),
+    "decode_lm": dict(layers=0),
 }
 
 
@@ -49,7 +51,7 @@ def decode_case(a, c):
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / a.launches
     wbytes = cfg.weight_bytes()
-    print(json.dumps({"case": "decode", "us_per_launch": round(us, 3), "weight_bytes": wbytes,
+    print(json.dumps({"case": a.case, "us_per_launch": round(us, 3), "weight_bytes": wbytes,
                       "weight_GBps": round(wbytes / us / 1e3, 1)}))
     st.free()
 
@@ -62,7 +64,7 @@ def main():
     a = ap.parse_args()
     c = CASES[a.case]
     torch.cuda.set_device(0)
-    if a.case == "decode":
+    if a.case.startswith("decode"):
         return decode_case(a, c)
     ws = []
     for i in range(c["copies"]):
