@@ -4,16 +4,18 @@
 Workload: one synthetic greedy decode step at batch 1 -- 48 layers of the
 seven 4-bit g64 projections (q|k|v fused, o, gate|up fused, down) plus the quantized tied LM
 head 262144 x 3840 with fused softcap + argmax; tensor-parallel over --gpus N (one process per
-GPU, torchrun for N > 1). Seeded synthetic weights and activations (no checkpoint).
+GPU, torchrun for N > 1). Seeded synthetic weights and activations (no checkpoint). Every rank
+runs the step as ONE persistent-kernel launch (decode plan); for N > 1 the o/down partial sums
+cross NVLink inside that kernel (peer stores) and the LM-head keys are combined there too.
 
 value   = whole-job HBM GB/s of the quantized matmuls: 6,617,825,280 weight bytes streamed per
           token / device time of one decode step (CUDA graph replay, inputs already in HBM,
           weights 6.6 GB >> the 126 MB L2, so no flush is needed), max over ranks.
 e2e     = the same metric through the public API with a host hidden state copied in (pinned H2D)
           and the token read back (D2H) inside the timed region, every step.
-roofline: the dominant kernel (the fused gate|up GEMV, 53% of a layer's bytes) timed alone
-          with CUDA events over all 48 layers' weights; achieved = its algorithmic bytes /
-          average launch duration; peak = MEASURED_PEAKS.json hbm_gbs.
+roofline: the dominant (only) kernel is the persistent decode kernel, one launch per step;
+          achieved = the rank's algorithmic bytes per launch (its weight shards + activations) /
+          the launch's CUDA-event duration (max over ranks); peak = MEASURED_PEAKS.json hbm_gbs.
 cpu_baseline: the CPU oracle (fp32 accumulation, OpenMP on every host core) on a bounded sample
           (layer 0's seven projections at M = 1), rank 0 at N = 1 only.
 --impl reference: MLX (the reference's library) is absent, so the reference arm times the CPU
@@ -170,7 +172,7 @@ def main():
     import torch.distributed as dist
 
     from helios_b200 import _lib
-    from helios_b200.quantized import quantized_matmul, synth_normal
+    from helios_b200.quantized import synth_normal
     from helios_b200.stack import StackConfig, SyntheticStack, activation_seed, decode_keys
 
     _lib.load()
@@ -195,12 +197,10 @@ def main():
         if world > 1:
             dist.barrier()
 
-    # one GPU: the whole decode step is one persistent-kernel launch (decode plan); several GPUs:
-    # the per-matmul kernels with an NCCL allreduce after o/down. Captured once, replayed per token.
-    single = world == 1
-    if single:
-        st.build_plan(1)
-    step = (lambda: st.decode(h_static)) if single else (lambda: st.forward(h_static))
+    # the whole decode step is one persistent-kernel launch per GPU (decode plan; tensor-parallel
+    # plans reduce o/down over NVLink inside the kernel). Captured once, replayed per token.
+    st.build_plan(1)
+    step = lambda: st.decode(h_static)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
@@ -253,34 +253,11 @@ def main():
     tok, _ = decode_keys(key_host)
 
     hbm_peak, tf_peak, peak_kind = measured_peaks()
-    reps = 0
-    if single:
-        # the dominant (only) kernel is the persistent decode kernel: one launch per step
-        kname = "decode_kernel (persistent: 48x{q|k|v, o, gate|up, down} + LM head, one launch)"
-        alg_bytes = cfg.weight_bytes() + 2 * cfg.hidden * 2 * (4 * cfg.layers + 1)
-        launch_us = ms * 1e3
-        traffic_file = ROOT / "profiles" / "decode_kernel_traffic.json"
-    else:
-        # dominant kernel: the fused gate|up GEMV, timed alone over all layers' weights (cold L2)
-        kname = "gemv2_kernel (fused gate|up shard, M=1)"
-        gu_bytes = st.layers[0]["gu"].rows * cfg.hidden * 9 // 16
-        o_in = torch.zeros((1, cfg.hidden), dtype=torch.bfloat16, device=dev).normal_()
-        gu_out = torch.empty((1, st.layers[0]["gu"].rows), dtype=torch.bfloat16, device=dev)
-        for L in st.layers[:4]:
-            quantized_matmul(o_in, L["gu"], rms_scale=True, out=gu_out)
-        reps = 4
-        barrier()
-        torch.cuda.synchronize()
-        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        k0.record()
-        for _ in range(reps):
-            for L in st.layers:
-                quantized_matmul(o_in, L["gu"], rms_scale=True, out=gu_out)
-        k1.record()
-        torch.cuda.synchronize()
-        launch_us = max_over_ranks(k0.elapsed_time(k1)) * 1e3 / (reps * len(st.layers))
-        alg_bytes = gu_bytes + cfg.hidden * 2 + st.layers[0]["gu"].rows * 2
-        traffic_file = ROOT / "profiles" / "gemv_gate_up_traffic.json"
+    # the dominant (only) kernel is the persistent decode kernel: one launch per step per rank
+    kname = "decode_kernel (persistent: 48x{q|k|v, o, gate|up, down} + LM head, one launch per rank)"
+    alg_bytes = st.local_weight_bytes() + 2 * cfg.hidden * 2 * (4 * cfg.layers + 1)
+    launch_us = ms * 1e3
+    traffic_file = ROOT / "profiles" / ("decode_kernel_traffic.json" if world == 1 else f"decode_kernel_tp{world}_traffic.json")
     achieved = alg_bytes / (launch_us * 1e-6) / 1e9
     traffic = None
     if traffic_file.exists():
@@ -309,8 +286,7 @@ def main():
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                          "peak_kind": f"{peak_kind} hbm_gbs", "traffic": traffic,
                          "alg_bytes_per_launch": alg_bytes, "avg_launch_us": round(launch_us, 3)},
-            "gpu_launches": (1 if single else 4 * cfg.layers + 1) * args.steps * 2 + reps * len(st.layers)
-                            + (0 if single else 4),
+            "gpu_launches": 2 * args.steps,
             "clocks": clk,
             "last_token": tok[0],
         }

@@ -58,6 +58,8 @@ class G4qDecodePhase(ctypes.Structure):
 
 
 PHASE_ARGMAX = 0x4
+PHASE_ALLREDUCE = 0x8
+IPC_HANDLE_BYTES = 64
 
 SIGNATURES = {
     "g4q_runtime_version": [ctypes.POINTER(G4qVersionInfo)],
@@ -77,6 +79,13 @@ SIGNATURES = {
     "g4q_decode_plan_create": [ctypes.POINTER(G4qDecodePhase), _I32, _I32, ctypes.POINTER(_P)],
     "g4q_decode_plan_run": [_P, _I64, _F, _F, _I64, _P, _P, _P, _P, _I64, _P],
     "g4q_decode_plan_free": [_P],
+    "g4q_decode_plan_create_tp": [ctypes.POINTER(G4qDecodePhase), _I32, _I32, _I32, _I32, ctypes.POINTER(_P)],
+    "g4q_decode_plan_buffers": [_P, ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_P),
+                                ctypes.POINTER(ctypes.c_uint64)],
+    "g4q_decode_plan_set_peers": [_P, ctypes.POINTER(_P), ctypes.POINTER(_P)],
+    "g4q_ipc_handle": [_P, ctypes.POINTER(ctypes.c_uint8)],
+    "g4q_ipc_open": [ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(_P)],
+    "g4q_ipc_close": [_P],
     "g4q_synth_matrix": [_U64, _I64, _I64, _I32, _I32, _P, _P, _P, _P],
     "g4q_synth_normal_bf16": [_U64, _I64, _P, _P],
 }

@@ -413,7 +413,53 @@ G4qStatus g4q_decode_plan_create(const G4qDecodePhase* phases, int32_t n_phases,
     return guarded("g4q_decode_plan_create", [&] {
         require(out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null out pointer");
         *out = nullptr;
-        *out = reinterpret_cast<G4qDecodePlan*>(decode_plan_create(phases, n_phases, max_tokens));
+        *out = reinterpret_cast<G4qDecodePlan*>(decode_plan_create(phases, n_phases, max_tokens, 0, 1));
+    });
+}
+
+G4qStatus g4q_decode_plan_create_tp(const G4qDecodePhase* phases, int32_t n_phases, int32_t max_tokens,
+                                    int32_t rank, int32_t n_ranks, G4qDecodePlan** out) {
+    return guarded("g4q_decode_plan_create_tp", [&] {
+        require(out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null out pointer");
+        *out = nullptr;
+        *out = reinterpret_cast<G4qDecodePlan*>(decode_plan_create(phases, n_phases, max_tokens, rank, n_ranks));
+    });
+}
+
+G4qStatus g4q_decode_plan_buffers(G4qDecodePlan* plan, void** slots, uint64_t* slot_bytes, void** xkeys,
+                                  uint64_t* xkey_bytes) {
+    return guarded("g4q_decode_plan_buffers",
+                   [&] { decode_plan_buffers(plan, slots, slot_bytes, xkeys, xkey_bytes); });
+}
+
+G4qStatus g4q_decode_plan_set_peers(G4qDecodePlan* plan, void* const* slots, void* const* xkeys) {
+    return guarded("g4q_decode_plan_set_peers", [&] { decode_plan_set_peers(plan, slots, xkeys); });
+}
+
+G4qStatus g4q_ipc_handle(const void* device_ptr, uint8_t* handle) {
+    return guarded("g4q_ipc_handle", [&] {
+        require(device_ptr != nullptr && handle != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires non-null pointers");
+        cudaIpcMemHandle_t h;
+        check_cuda(cudaIpcGetMemHandle(&h, const_cast<void*>(device_ptr)), "cudaIpcGetMemHandle");
+        static_assert(sizeof(h) == G4Q_IPC_HANDLE_BYTES, "CUDA IPC handle size");
+        memcpy(handle, &h, sizeof(h));
+    });
+}
+
+G4qStatus g4q_ipc_open(const uint8_t* handle, void** device_ptr) {
+    return guarded("g4q_ipc_open", [&] {
+        require(device_ptr != nullptr && handle != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires non-null pointers");
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handle, sizeof(h));
+        *device_ptr = nullptr;
+        check_cuda(cudaIpcOpenMemHandle(device_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    });
+}
+
+G4qStatus g4q_ipc_close(void* device_ptr) {
+    return guarded("g4q_ipc_close", [&] {
+        require(device_ptr != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null pointer");
+        check_cuda(cudaIpcCloseMemHandle(device_ptr), "cudaIpcCloseMemHandle");
     });
 }
 

@@ -8,25 +8,30 @@
 //
 // Why one kernel: at batch 1 every phase is a few microseconds of HBM streaming, so separate
 // launches spend a large share of the step in prologues (staging x) and epilogues (reductions,
-// tails). Here one cooperative grid (one 24-warp CTA per SM) stays resident for the whole step:
+// tails). Here one cooperative grid (one 16-warp CTA per SM) stays resident for the whole step:
 //  * every warp streams its weight units (64 rows x one 64-wide group: 2 KB of packed words +
 //    256 B of scale|bias) through a private ring of cp.async.bulk buffers that runs ahead ACROSS
 //    phase boundaries, so the next phase's weights land while the grid finishes the current one;
-//  * the units of a phase are cut into equal contiguous CTA ranges (quad-major), warp w taking
-//    every 24th; a 64-row quad's partial sums are reduced in shared memory in warp order;
-//  * every CTA leaves its unscaled fp32 partial of each quad it touched in a slot (a quad cut by
-//    CTA-range boundaries has one slot per contributing CTA); nobody waits for a cut quad: the
-//    CTAs that consume the phase output sum the slots themselves (fixed CTA order) while staging
-//    their x, and one CTA per cut quad writes the finished values back to y during the next phase
-//    (the first of its warps to run out of units). Slots are double-buffered by phase parity. The
-//    only cross-CTA synchronisation is one completion counter per phase (one release atomic per
-//    CTA, one acquire poll per CTA);
-//  * phase p+1 starts in a CTA once that counter says every CTA has stored phase p (bounded spin);
-//    the x of phase p+1 (and its RMS scale if asked) is then staged in shared memory;
-//  * the argmax phase keeps per-token 64-bit keys (order-preserving logit bits | ~row); its cut
-//    quads are finished by the last contributing CTA (slot + arrival counter), and the last CTA to
-//    complete the phase publishes tokens/values/keys. The last CTA to leave resets every counter,
-//    so a plan is ready for the next launch (and for CUDA-graph replay) without a memset.
+//  * the units of a phase are cut into equal contiguous CTA ranges (quad-major) and each CTA range
+//    into contiguous warp runs; a quad's warp partials are reduced in shared memory, wait-free;
+//  * dataflow instead of grid barriers: every CTA stores its unscaled fp32 partial of each quad it
+//    touched into a slot as one 64-bit word (value | phase tag). A CTA consuming the phase output
+//    polls the slots of the quads it needs and sums them in a fixed (rank, CTA) order while
+//    staging its x, so a phase starts on an SM as soon as its inputs exist and no SM ever waits
+//    for a whole-grid barrier. Tags are unique per (launch, phase); slot buffers rotate over three
+//    phases, which the host proves safe (or falls back to a barrier) when the plan is made;
+//  * tensor parallel plans (one process per GPU): a row-parallel phase (G4Q_PHASE_ALLREDUCE) stores
+//    its partials into the slot buffers of every rank over NVLink (peer stores), so the allreduce
+//    after o/down costs no separate collective: consumers on every rank sum the same partials in
+//    the same order. The LM-head keys are exchanged the same way at the end of the step;
+//  * the argmax phase keeps 64-bit keys (order-preserving logit bits | ~row); its cut quads are
+//    finished by the last contributing CTA (slot + arrival counter), and the last CTA to finish
+//    publishes tokens/values/keys. The last CTA to leave resets the counters and advances the
+//    launch counter (the tag base), so a plan is ready for the next launch and for CUDA-graph
+//    replay without a memset.
+// Every wait is bounded (about two seconds of clocks); a wait that gives up records an error code
+// in the per-device error word and the kernel runs to its end.
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -44,7 +49,9 @@ constexpr uint32_t kUnitSb = 64 * 4;
 constexpr uint32_t kUnitBytes = kUnitPacked + kUnitSb;
 constexpr uint32_t kRingBytes = kStages * kUnitBytes;
 constexpr int kSlots = 16;                        // CTA ranges one 64-row quad may be cut into
+constexpr int kSlotBufs = 3;                      // slot buffers rotate over three phases
 constexpr int kMaxCtaQuads = 64;                  // quads one CTA range may touch in a phase
+constexpr int kMaxRanks = 8;
 constexpr long long kSpinLimit = 4000000000ll;    // ~2 s of SM clocks
 constexpr uint32_t kOddNibbleMask = 0x00F000F0u;  // q at bits 4-7 of each half: bf16 value q * 2^-129
 constexpr uint32_t kPow64x2 = 0x5F805F80u;        // bf16x2 (2^64, 2^64)
@@ -55,28 +62,35 @@ struct PhaseDev {
     const uint32_t* sb;
     const uint16_t* x;
     void* y;
-    int64_t ldx, ldy;
     int N, K, R, G, Q, U;
     uint32_t flags;
-    int src;       // phase whose output x is (-1: external input, ready at launch)
-    int src_col;   // first column of x inside that phase's output (multiple of 64)
+    int src;          // phase whose output x is (-1: external input or an older output)
+    int src_col;      // first column of x inside that phase's output (multiple of 64)
+    int src_ranks;    // ranks whose partials each quad of this phase sums (1, or n_ranks if ALLREDUCE)
+    int ks;           // slot rows per (quad, rank): the most CTA ranges one quad meets
+    int sync_before;  // wait for every CTA to finish the previous phase before staging x
+    int need_done;    // count finished CTAs of this phase (a later barrier or the argmax publish)
 };
 
 struct DecodeArgs {
     const PhaseDev* ph;
     int n_phases;
     float eps, softcap;
-    int64_t row_offset;          // global index of the argmax phase's row 0 (vocabulary shard)
-    unsigned int* done;          // [n_phases] CTAs that finished each phase
-    unsigned int* exit_count;    // [1]
-    unsigned long long* key;     // running argmax key
-    float* slots;                // [2 parities][max quads][kSlots][64 rows]
-    int64_t slot_stride;         // floats per parity
-    int* qcount;                 // [max quads] arrival counters of the argmax phase's cut quads
+    int64_t row_offset;                       // global index of the argmax phase's row 0
+    unsigned int* done;                       // [n_phases] CTAs that finished each phase
+    unsigned int* exit_count;                 // [1]
+    unsigned int* run;                        // [1] launches so far (tag base)
+    unsigned long long* key;                  // running argmax key of this rank
+    unsigned long long* slots;                // this rank's slot buffers
+    unsigned long long* const* peer_slots;    // [n_ranks] slot buffers of every rank (device array)
+    unsigned long long* const* peer_xkeys;    // [n_ranks] key exchange arrays ([n_ranks][2]) of every rank
+    int rank, n_ranks;
+    int64_t buf_words;                        // words per slot buffer
+    int* qcount;                              // arrival counters of the argmax phase's cut quads
     int32_t* tokens;
     float* values;
     unsigned long long* keys_out;
-    uint16_t* logits;            // optional bf16 logits of the argmax phase
+    uint16_t* logits;                         // optional bf16 logits of the argmax phase
     int* err;
 };
 
@@ -121,6 +135,25 @@ __device__ __forceinline__ int cta_of_unit(int u, int U, int C) {
 __device__ __forceinline__ void quad_ctas(const PhaseDev& P, int q, int C, int& cf, int& cl) {
     cf = cta_of_unit(q * P.G, P.U, C);
     cl = cta_of_unit((q + 1) * P.G - 1, P.U, C);
+}
+
+// Tag of phase p given the launch's tag base: unique per (launch, phase) over 2^32 - 1 phases,
+// never 0 (the value slot buffers start with).
+__device__ __forceinline__ uint32_t phase_tag(uint32_t tag0, int p) {
+    uint32_t t = tag0 + (uint32_t)p;   // tag0 < 2^32 - 1, p < 2^16
+    if (t < tag0 || t >= 0xFFFFFFFFu) t -= 0xFFFFFFFFu;
+    return t + 1u;
+}
+
+// Slots of a phase live in buffer p mod 3. A single-rank phase keeps plain fp32 partials: float
+// index of (quad q, source CTA c, row 0). An allreduce phase keeps tagged 64-bit words: word index
+// of (quad q, source rank r, source CTA c, row 0).
+__device__ __forceinline__ int64_t slot_f(const DecodeArgs& a, const PhaseDev& P, int p, int q, int c) {
+    return (int64_t)(p % kSlotBufs) * a.buf_words * 2 + (int64_t)q * P.ks * 64 + (int64_t)c * 64;
+}
+
+__device__ __forceinline__ int64_t slot_word(const DecodeArgs& a, const PhaseDev& P, int p, int q, int r, int c) {
+    return (int64_t)(p % kSlotBufs) * a.buf_words + ((int64_t)q * P.src_ranks + r) * P.ks * 64 + (int64_t)c * 64;
 }
 
 // Warp w owns the contiguous units [wstart(w), wstart(w + 1)) of its CTA's n units of a phase
@@ -195,108 +228,12 @@ struct CtaShared {
     unsigned long long bars[kWarps][kStages];
     float wss[kWarps];
     float rs, rs_prev;
+    uint32_t tag0;
     int qcnt[kMaxCtaQuads];   // arrivals per quad of the CTA's range (reset by the last arriver)
     int warps_finished;
     int wb_claim;
     unsigned long long best;
-    int last_cta;
-    uint32_t zero[2];
 };
-
-__device__ __forceinline__ void store_y(const PhaseDev& P, int n, float v) {
-    if (P.flags & G4Q_QMM_OUT_F32)
-        reinterpret_cast<float*>(P.y)[n] = v;
-    else
-        reinterpret_cast<uint16_t*>(P.y)[n] = f32_to_bf16_bits(v);
-}
-
-// argmax phase: fold one finished output into the running key
-__device__ __forceinline__ void fold_logit(const DecodeArgs& a, int n, float o, unsigned long long& best) {
-    const uint16_t lb = f32_to_bf16_bits(o);
-    if (a.logits) a.logits[n] = lb;
-    const float lv = bf16_bits_to_f32(lb);
-    const float sv = a.softcap > 0.0f ? softcap_bf16(lv, a.softcap) : lv;
-    const unsigned long long key = argmax_key(sv, (uint32_t)(a.row_offset + n));
-    if (key > best) best = key;
-}
-
-// Park this warp's partial of quad q. A warp keeps the partial of the first quad of its range in
-// red[warp][0] (the previous warp may need it) and everything else in red[warp][1] (only the last
-// quad of the range is read by another warp, and it comes last). The last contributing warp sums
-// the partials in warp order and stores the quad (whole quad), leaves it in this CTA's slot (cut
-// quad), or -- argmax phase -- folds the finished logits into the running key. No warp ever waits.
-__device__ void park(const DecodeArgs& a, const PhaseDev& P, int p, CtaShared& sh, float* red, int q, int first_q,
-                     int cs, int ce, int cta, int C, const float (&acc)[4][4], unsigned long long& best) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
-    const int G = P.G, n = ce - cs;
-    float* rb = red + (size_t)(warp * 2 + (q == first_q ? 0 : 1)) * 64;
-    if (t == 0) {   // token 0 lives in the t == 0 lanes (C fragment column 0)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            rb[i * 16 + gi] = acc[i][0];
-            rb[i * 16 + gi + 8] = acc[i][2];
-        }
-    }
-    __threadfence_block();
-    __syncwarp();
-    const int lo = max(cs, q * G), hi = min(ce, (q + 1) * G);
-    const int wa = warp_of(lo - cs, n), wb = warp_of(hi - 1 - cs, n);
-    const int qi = q - cs / G;
-    int last = 1;
-    if (wb > wa) {
-        if (lane == 0) last = atomicAdd(&sh.qcnt[qi], 1) == wb - wa;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) return;
-        __threadfence_block();
-    }
-    // warp wa holds q in slot 0 only if q is also its first quad; the others hold it as their first
-    const int slot_a = (cs + wstart(wa, n)) / G == q ? 0 : 1;
-    float v[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int row = lane + 32 * h;
-        float s = red[(wa * 2 + slot_a) * 64 + row];
-        for (int w = wa + 1; w <= wb; ++w) s += red[w * 2 * 64 + row];
-        v[h] = s;
-    }
-    if (wb > wa && lane == 0) sh.qcnt[qi] = 0;
-    const bool whole = cs <= q * G && ce >= (q + 1) * G;
-    const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
-    if (whole && argmax) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) fold_logit(a, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs), best);
-    } else {
-        // the unscaled partial goes to this CTA's slot of the quad (slot 0 of a whole quad); the
-        // consumers of the phase rebuild their x from the slots alone
-        int cf, cl;
-        quad_ctas(P, q, C, cf, cl);
-        float* base = a.slots + (size_t)(p & 1) * a.slot_stride + (size_t)q * kSlots * 64;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) base[(size_t)(cta - cf) * 64 + lane + 32 * h] = v[h];
-        if (whole) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) store_y(P, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs));
-        } else if (argmax) {   // the logits are needed now: the last contributing CTA finishes the quad
-            __threadfence();
-            __syncwarp();
-            int lastc = 0;
-            if (lane == 0) lastc = atomicAdd(a.qcount + q, 1) == cl - cf;
-            lastc = __shfl_sync(0xffffffffu, lastc, 0);
-            if (lastc) {
-                __threadfence();
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    float s = __ldcg(base + lane + 32 * h);
-                    for (int c = 1; c <= cl - cf; ++c) s += __ldcg(base + (size_t)c * 64 + lane + 32 * h);
-                    fold_logit(a, q * 64 + lane + 32 * h, __fmul_rn(s, sh.rs), best);
-                }
-                __syncwarp();
-                if (lane == 0) atomicExch(a.qcount + q, 0);
-            }
-        }
-    }
-    __syncwarp();
-}
 
 __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
     unsigned int v;
@@ -322,40 +259,213 @@ __device__ __forceinline__ void spin_until(const unsigned int* ctr, unsigned int
     }
 }
 
-// Finished outputs from the slots of a quad: s = slot[0] + slot[1] + ... (the CTA order), then
-// the producer's row scale and bf16 rounding. Every reader of a cut quad (x staging in every CTA,
-// the write-back to y) goes through these so they all see the same bits.
+// One tagged slot word: the fp32 partial in the low half, the phase tag in the high half, written
+// and read as single 64-bit accesses so a reader that sees the tag sees the value with it.
+__device__ __forceinline__ void st_slot(unsigned long long* p, float v, uint32_t tag, bool sys) {
+    const unsigned long long w = (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
+    if (sys)
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+    else
+        asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ void ld_slot2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Sums of 4 rows of a quad over its slots, s = slot[0] + slot[1] + ... in source order; every
+// reader of a quad (x staging in every CTA, the write-back to y) goes through the same function,
+// so all of them see the same bits. Single-rank phases: plain fp32 slots (complete once the
+// phase's completion counter says so), up to four in flight.
 __device__ __forceinline__ float4 sum_slots4(const float* base, int nc) {
     float4 s = __ldcg(reinterpret_cast<const float4*>(base));
     for (int c = 1; c < nc; c += 4) {
-        float4 t[3];
+        float4 t[4];
 #pragma unroll
-        for (int e = 0; e < 3; ++e)
+        for (int e = 0; e < 4; ++e)
             t[e] = c + e < nc ? __ldcg(reinterpret_cast<const float4*>(base + (size_t)(c + e) * 64))
                               : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 u = c + 3 < nc ? __ldcg(reinterpret_cast<const float4*>(base + (size_t)(c + 3) * 64))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int e = 0; e < 3; ++e)
+        for (int e = 0; e < 4; ++e)
             if (c + e < nc) {
                 s.x += t[e].x;
                 s.y += t[e].y;
                 s.z += t[e].z;
                 s.w += t[e].w;
             }
-        if (c + 3 < nc) {
-            s.x += u.x;
-            s.y += u.y;
-            s.z += u.z;
-            s.w += u.w;
-        }
     }
     return s;
+}
+
+// Allreduce phases: tagged words from every rank, rank-major then CTA order; polls until every
+// source word carries `tag` (bounded), since a peer's partials arrive on their own schedule.
+__device__ __noinline__ float4 sum_tagged4(const unsigned long long* q0, int ranks, int ks, int nc, uint32_t tag,
+                                           int* err) {
+    const int n = ranks * nc;
+    const long long t0 = clock64();
+    for (;;) {
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        bool ok = true;
+        for (int i0 = 0; i0 < n; i0 += 4) {
+            unsigned long long w[4][4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int i = i0 + e;
+                if (i < n) {
+                    const int r = i / nc, c = i - r * nc;
+                    const unsigned long long* src = q0 + ((int64_t)r * ks + c) * 64;
+                    ld_slot2(src, w[e][0], w[e][1]);
+                    ld_slot2(src + 2, w[e][2], w[e][3]);
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int i = i0 + e;
+                if (i < n) {
+                    ok &= (uint32_t)(w[e][0] >> 32) == tag && (uint32_t)(w[e][1] >> 32) == tag &&
+                          (uint32_t)(w[e][2] >> 32) == tag && (uint32_t)(w[e][3] >> 32) == tag;
+                    const float v0 = __uint_as_float((uint32_t)w[e][0]), v1 = __uint_as_float((uint32_t)w[e][1]);
+                    const float v2 = __uint_as_float((uint32_t)w[e][2]), v3 = __uint_as_float((uint32_t)w[e][3]);
+                    if (i == 0) {
+                        s = make_float4(v0, v1, v2, v3);
+                    } else {
+                        s.x += v0;
+                        s.y += v1;
+                        s.z += v2;
+                        s.w += v3;
+                    }
+                }
+            }
+        }
+        if (ok) return s;
+        if (*reinterpret_cast<volatile int*>(err) != 0) return s;
+        if (clock64() - t0 > kSpinLimit) {
+            atomicCAS(err, 0, 35);
+            return s;
+        }
+        __nanosleep(200);
+    }
+}
+
+// An allreduce phase's CTA partial of one quad (two rows per lane) into the slot buffers of every
+// rank (peer stores over NVLink for the others).
+__device__ __noinline__ void store_allreduce(unsigned long long* const* peers, int n_ranks, int64_t w0, float v0,
+                                             float v1, uint32_t tag) {
+    for (int r = 0; r < n_ranks; ++r) {
+        unsigned long long* dst = peers[r] + w0;
+        st_slot(dst, v0, tag, true);
+        st_slot(dst + 32, v1, tag, true);
+    }
 }
 
 __device__ __forceinline__ uint2 finish4(float4 s, float rs) {
     return make_uint2((uint32_t)f32_to_bf16_bits(__fmul_rn(s.x, rs)) | ((uint32_t)f32_to_bf16_bits(__fmul_rn(s.y, rs)) << 16),
                       (uint32_t)f32_to_bf16_bits(__fmul_rn(s.z, rs)) | ((uint32_t)f32_to_bf16_bits(__fmul_rn(s.w, rs)) << 16));
+}
+
+__device__ __forceinline__ void store_y(const PhaseDev& P, int n, float v) {
+    if (P.flags & G4Q_QMM_OUT_F32)
+        reinterpret_cast<float*>(P.y)[n] = v;
+    else
+        reinterpret_cast<uint16_t*>(P.y)[n] = f32_to_bf16_bits(v);
+}
+
+// argmax phase: fold one finished output into the running key
+__device__ __forceinline__ unsigned long long fold_logit(uint16_t* logits, float softcap, int64_t row_offset, int n,
+                                                         float o, unsigned long long best) {
+    const uint16_t lb = f32_to_bf16_bits(o);
+    if (logits) logits[n] = lb;
+    const float lv = bf16_bits_to_f32(lb);
+    const float sv = softcap > 0.0f ? softcap_bf16(lv, softcap) : lv;
+    const unsigned long long key = argmax_key(sv, (uint32_t)(row_offset + n));
+    return key > best ? key : best;
+}
+
+// Park this warp's partial of quad q. A warp keeps the partial of the first quad of its range in
+// red[warp][0] (the previous warp may need it) and everything else in red[warp][1] (only the last
+// quad of the range is read by another warp, and it comes last). The last contributing warp sums
+// the partials in warp order, then: argmax phase, whole quad: folds the logits into the running
+// key; otherwise leaves the CTA's unscaled partial in its slot (tagged, on every rank, for an
+// allreduce phase) and, for a whole single-rank quad, stores the finished values to y. No warp
+// ever waits.
+template <bool kTP>
+__device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int p, CtaShared& sh, float* red, int q,
+                                     int first_q, int cs, int ce, int cta, int C, const float (&acc)[4][4],
+                                     unsigned long long& best) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
+    const int G = P.G, n = ce - cs;
+    float* rb = red + (size_t)(warp * 2 + (q == first_q ? 0 : 1)) * 64;
+    if (t == 0) {   // token 0 lives in the t == 0 lanes (C fragment column 0)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            rb[i * 16 + gi] = acc[i][0];
+            rb[i * 16 + gi + 8] = acc[i][2];
+        }
+    }
+    __threadfence_block();
+    __syncwarp();
+    const int lo = max(cs, q * G), hi = min(ce, (q + 1) * G);
+    const int wa = warp_of(lo - cs, n), wb = warp_of(hi - 1 - cs, n);
+    const int qi = q - cs / G;
+    if (wb > wa) {
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&sh.qcnt[qi], 1) == wb - wa;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) return;
+        __threadfence_block();
+        if (lane == 0) sh.qcnt[qi] = 0;
+    }
+    // warp wa holds q in slot 0 only if q is also its first quad; the others hold it as their first
+    const int slot_a = (cs + wstart(wa, n)) / G == q ? 0 : 1;
+    float v[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int row = lane + 32 * h;
+        float s = red[(wa * 2 + slot_a) * 64 + row];
+        for (int w = wa + 1; w <= wb; ++w) s += red[w * 2 * 64 + row];
+        v[h] = s;
+    }
+    const bool whole = cs <= q * G && ce >= (q + 1) * G;
+    const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
+    if (whole && argmax) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            best = fold_logit(a.logits, a.softcap, a.row_offset, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs), best);
+    } else if (kTP && P.src_ranks > 1) {
+        int cf, cl;
+        quad_ctas(P, q, C, cf, cl);
+        store_allreduce(a.peer_slots, a.n_ranks, slot_word(a, P, p, q, a.rank, cta - cf) + lane, v[0], v[1],
+                        phase_tag(sh.tag0, p));
+    } else {
+        int cf, cl;
+        quad_ctas(P, q, C, cf, cl);
+        float* base = reinterpret_cast<float*>(a.slots) + slot_f(a, P, p, q, 0);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) base[(size_t)(cta - cf) * 64 + lane + 32 * h] = v[h];
+        if (whole) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) store_y(P, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs));
+        } else if (argmax) {   // the logits are needed now: the last contributing CTA finishes the quad
+            __threadfence();
+            __syncwarp();
+            int lastc = 0;
+            if (lane == 0) lastc = atomicAdd(a.qcount + q, 1) == cl - cf;
+            lastc = __shfl_sync(0xffffffffu, lastc, 0);
+            if (lastc) {
+                __threadfence();
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    float s = __ldcg(base + lane + 32 * h);
+                    for (int c = 1; c <= cl - cf; ++c) s += __ldcg(base + (size_t)c * 64 + lane + 32 * h);
+                    best = fold_logit(a.logits, a.softcap, a.row_offset, q * 64 + lane + 32 * h,
+                                      __fmul_rn(s, sh.rs), best);
+                }
+                __syncwarp();
+                if (lane == 0) atomicExch(a.qcount + q, 0);
+            }
+        }
+    }
+    __syncwarp();
 }
 
 // Shared-memory order of x: inside each 64-wide group, lane t's B-fragment words for the four k16
@@ -368,10 +478,11 @@ __device__ __forceinline__ int xperm(int w) {
 
 // Stage the x of phase P (K bf16 values) into shared memory; returns this thread's sum of squares.
 // From an external input: plain 16-byte copies. From the previous phase's output: every thread
-// owns 4-row cells (16 per producer quad) and sums the cell's slots; the loads of two cells and
-// four slots each are in flight together.
+// owns 4-row cells (16 per producer quad) and sums the cell's tagged slots (polling until the
+// producers have written them); two cells are in flight per thread.
+template <bool kTP>
 __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P, uint32_t* xs, int C, float rs_prev,
-                                         bool rms) {
+                                         uint32_t tag0, bool rms) {
     float ss = 0.0f;
     auto acc_sq = [&](uint32_t w) {
         const float lo = bf16_bits_to_f32(w & 0xffffu), hi = bf16_bits_to_f32(w >> 16);
@@ -395,48 +506,67 @@ __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P,
         return ss;
     }
     const PhaseDev& S = a.ph[P.src];
-    const float* sl = a.slots + (size_t)(P.src & 1) * a.slot_stride;
+    const bool tagged = kTP && S.src_ranks > 1;
+    const uint32_t tag = phase_tag(tag0, P.src);
     const int q0 = P.src_col >> 6;
     const int cells = P.K / 4;
     for (int e0 = threadIdx.x; e0 < cells; e0 += 2 * kThreads) {
         float4 s[2];
-        int idx[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            idx[h] = e0 + h * kThreads;
-            if (idx[h] < cells) {
-                const int q = q0 + (idx[h] >> 4);
+            const int idx = e0 + h * kThreads;
+            if (idx < cells) {
+                const int q = q0 + (idx >> 4);
                 int cf, cl;
                 quad_ctas(S, q, C, cf, cl);
-                s[h] = sum_slots4(sl + (size_t)q * kSlots * 64 + (idx[h] & 15) * 4, cl - cf + 1);
+                if constexpr (kTP) {
+                    if (tagged)
+                        s[h] = sum_tagged4(a.slots + slot_word(a, S, P.src, q, 0, 0) + (idx & 15) * 4, S.src_ranks, S.ks,
+                                           cl - cf + 1, tag, a.err);
+                }
+                if (!tagged)
+                    s[h] = sum_slots4(reinterpret_cast<const float*>(a.slots) + slot_f(a, S, P.src, q, 0) +
+                                          (idx & 15) * 4,
+                                      cl - cf + 1);
             }
         }
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
-            if (idx[h] < cells) {
+        for (int h = 0; h < 2; ++h) {
+            const int idx = e0 + h * kThreads;
+            if (idx < cells) {
                 const uint2 w = finish4(s[h], rs_prev);
-                xs[xperm(2 * idx[h])] = w.x;
-                xs[xperm(2 * idx[h] + 1)] = w.y;
+                xs[xperm(2 * idx)] = w.x;
+                xs[xperm(2 * idx + 1)] = w.y;
                 if (rms) {
                     acc_sq(w.x);
                     acc_sq(w.y);
                 }
             }
+        }
     }
     return ss;
 }
 
-// One warp writes phase pp's cut quads owned by this CTA (quad q goes to CTA q mod C) back to y.
-__device__ void write_back_warp(const DecodeArgs& a, int pp, int cta, int C, float rs_prev) {
+// One warp writes the quads of phase pp that no single CTA finished (cut across CTAs, or summed
+// over ranks) back to y; quad q goes to CTA q mod C.
+template <bool kTP>
+__device__ __forceinline__ void write_back_warp(const DecodeArgs& a, int pp, int cta, int C, float rs_prev, uint32_t tag0) {
     const PhaseDev& Q = a.ph[pp];
     if (Q.flags & G4Q_PHASE_ARGMAX) return;
     const int lane = threadIdx.x & 31;
-    const float* sl = a.slots + (size_t)(pp & 1) * a.slot_stride;
+    const uint32_t tag = phase_tag(tag0, pp);
     for (int q = cta; q < Q.Q; q += C) {
         int cf, cl;
         quad_ctas(Q, q, C, cf, cl);
-        if (cf == cl || lane >= 16) continue;
-        const float4 s = sum_slots4(sl + (size_t)q * kSlots * 64 + lane * 4, cl - cf + 1);
+        if ((cf == cl && Q.src_ranks == 1) || lane >= 16) continue;
+        float4 s;
+        if constexpr (kTP) {
+            if (Q.src_ranks > 1)
+                s = sum_tagged4(a.slots + slot_word(a, Q, pp, q, 0, 0) + lane * 4, Q.src_ranks, Q.ks, cl - cf + 1, tag,
+                                a.err);
+        }
+        if (!kTP || Q.src_ranks == 1)
+            s = sum_slots4(reinterpret_cast<const float*>(a.slots) + slot_f(a, Q, pp, q, 0) + lane * 4, cl - cf + 1);
         const int n = q * 64 + lane * 4;
         if (Q.flags & G4Q_QMM_OUT_F32) {
             float* y = reinterpret_cast<float*>(Q.y) + n;
@@ -450,6 +580,38 @@ __device__ void write_back_warp(const DecodeArgs& a, int pp, int cta, int C, flo
     }
 }
 
+// End of a step on a tensor-parallel plan: every rank's last CTA posts its argmax key to every
+// rank (key word, then the tag with release semantics) and waits for all of them; the maximum is
+// the step's key on every rank. Also keeps the ranks within one step of each other.
+__device__ __forceinline__ unsigned long long exchange_keys(const DecodeArgs& a, unsigned long long key, uint32_t tag) {
+    for (int r = 0; r < a.n_ranks; ++r) {
+        unsigned long long* dst = a.peer_xkeys[r] + 2 * a.rank;
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(key) : "memory");
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(dst + 1), "l"((unsigned long long)tag) : "memory");
+    }
+    unsigned long long best = 0ull;
+    const long long t0 = clock64();
+    for (int r = 0; r < a.n_ranks; ++r) {
+        const unsigned long long* src = a.peer_xkeys[a.rank] + 2 * r;
+        for (;;) {
+            unsigned long long t;
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(t) : "l"(src + 1) : "memory");
+            if ((uint32_t)t == tag) break;
+            if (clock64() - t0 > kSpinLimit) {
+                atomicCAS(a.err, 0, 36);
+                return key;
+            }
+        }
+        unsigned long long k;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(src) : "memory");
+        best = k > best ? k : best;
+    }
+    return best;
+}
+
+// kTP: tensor-parallel instantiation (allreduce phases, key exchange); the single-GPU one has none
+// of that code.
+template <bool kTP>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ CtaShared sh;
@@ -470,8 +632,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         sh.warps_finished = 0;
         sh.wb_claim = 0;
         sh.best = 0ull;
-        sh.zero[0] = sh.zero[1] = 0u;
         sh.rs = 1.0f;
+        const unsigned long long e = (unsigned long long)*reinterpret_cast<volatile unsigned int*>(a.run) *
+                                     (unsigned)(a.n_phases + 1);
+        sh.tag0 = (uint32_t)(e % 0xFFFFFFFFull);
     }
     __syncwarp();
     Pre pre;
@@ -490,18 +654,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         const PhaseDev& P = a.ph[p];
         const int cs = range_start(cta, P.U, C), ce = range_start(cta + 1, P.U, C);
         const int G = P.G;
-        // ---- phase entry: wait until every CTA has finished phase p-1
+        // ---- phase entry: the CTA's warps are done with the previous phase (x buffer reuse)
         __syncthreads();
         if (threadIdx.x == 0) {
-            if (p > 0) spin_until(a.done + (p - 1), (unsigned)C, a.err);
+            if (P.sync_before) spin_until(a.done + (p - 1), (unsigned)C, a.err);
             sh.rs_prev = sh.rs;
             sh.wb_claim = 0;
         }
         __syncthreads();
         const float rs_prev = sh.rs_prev;
-        // ---- stage x (bf16; B-fragment reads of one token are conflict free)
+        const uint32_t tag0 = sh.tag0;
+        // ---- stage x (polls the producers' slots) and its RMS scale
         const bool rms = (P.flags & G4Q_QMM_RMS_SCALE) != 0;
-        float ss = stage_x(a, P, xs, C, rs_prev, rms);
+        float ss = stage_x<kTP>(a, P, xs, C, rs_prev, tag0, rms);
         if (rms) {
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
@@ -534,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         const int first_q = cq;
         for (int k = 0; k < n_units; ++k) {
             if (cq != acc_q) {
-                park(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
+                park<kTP>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -581,13 +746,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
                 ++cq;
             }
         }
-        if (n_units > 0) park(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
-        // ---- the first warp of the CTA to run out of units writes phase p-1's cut quads back to y
+        if (n_units > 0) park<kTP>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
+        // ---- the first warp of the CTA to run out of units writes phase p-1's unfinished quads to y
         if (p > 0) {
             int claim = 0;
             if (lane == 0) claim = atomicAdd(&sh.wb_claim, 1) == 0;
             claim = __shfl_sync(0xffffffffu, claim, 0);
-            if (claim) write_back_warp(a, p - 1, cta, C, rs_prev);
+            if (claim) write_back_warp<kTP>(a, p - 1, cta, C, rs_prev, tag0);
         }
         const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
         if (argmax) {
@@ -599,42 +764,44 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             }
             if (lane == 0) atomicMax(&sh.best, kk);
         }
-        // ---- one completion count per CTA: the warps meet on a shared counter (CTA scope), the last
-        //      one publishes all of the CTA's stores with a gpu-scope release atomic
-        __syncwarp();
-        int last_warp = 0;
-        if (lane == 0) {
-            __threadfence_block();
-            last_warp = atomicAdd(&sh.warps_finished, 1) == kWarps - 1;
-        }
-        last_warp = __shfl_sync(0xffffffffu, last_warp, 0);
-        if (last_warp && lane == 0) {
-            __threadfence_block();
-            sh.warps_finished = 0;
-            if (argmax) atomicMax(a.key, sh.best);
-            const unsigned int prev = atom_add_acq_rel(a.done + p, 1u);
-            if (argmax && prev == (unsigned)C - 1) {
-                const unsigned long long k = atomicExch(a.key, 0ull);
-                if (a.tokens) a.tokens[0] = (int32_t)key_index(k);
-                if (a.values) a.values[0] = key_value(k);
-                if (a.keys_out) a.keys_out[0] = k;
+        // ---- completion count, only where a later barrier or the argmax publish needs it: the warps
+        //      meet on a shared counter (CTA scope), the last one publishes with a gpu-scope release
+        if (P.need_done) {
+            __syncwarp();
+            int last_warp = 0;
+            if (lane == 0) {
+                __threadfence_block();
+                last_warp = atomicAdd(&sh.warps_finished, 1) == kWarps - 1;
+            }
+            last_warp = __shfl_sync(0xffffffffu, last_warp, 0);
+            if (last_warp && lane == 0) {
+                __threadfence_block();
+                sh.warps_finished = 0;
+                if (argmax) atomicMax(a.key, sh.best);
+                atom_add_acq_rel(a.done + p, 1u);
             }
         }
     }
-    // ---- a plan that ends with a regular phase: finish its cut quads
+    // ---- a plan that ends with a regular phase: finish its unfinished quads
     const int last = a.n_phases - 1;
     if (!(a.ph[last].flags & G4Q_PHASE_ARGMAX)) {
         __syncthreads();
-        if (threadIdx.x == 0) spin_until(a.done + last, (unsigned)C, a.err);
-        __syncthreads();
-        if (threadIdx.x < 32) write_back_warp(a, last, cta, C, sh.rs);
+        if (threadIdx.x < 32) write_back_warp<kTP>(a, last, cta, C, sh.rs, sh.tag0);
     }
-    // ---- the last CTA out resets the phase counters for the next launch
+    // ---- the last CTA out publishes the step's key, resets the counters and advances the tag base
     __syncthreads();
     if (threadIdx.x == 0) {
         const unsigned int prev = atom_add_acq_rel(a.exit_count, 1u);
         if (prev == (unsigned)C - 1) {
+            unsigned long long k = atomicExch(a.key, 0ull);
+            if constexpr (kTP) k = exchange_keys(a, k, phase_tag(sh.tag0, a.n_phases));
+            if (a.ph[last].flags & G4Q_PHASE_ARGMAX) {
+                if (a.tokens) a.tokens[0] = (int32_t)key_index(k);
+                if (a.values) a.values[0] = key_value(k);
+                if (a.keys_out) a.keys_out[0] = k;
+            }
             for (int p = 0; p < a.n_phases; ++p) a.done[p] = 0u;
+            atomicAdd(a.run, 1u);
             __threadfence();
             atomicExch(a.exit_count, 0u);
         }
@@ -647,25 +814,53 @@ struct DecodePlan {
     uint64_t magic = 0;
     int device = -1;
     int n_phases = 0, grid = 0;
+    int rank = 0, n_ranks = 1;
     size_t smem = 0;
-    int64_t slot_stride = 0;
+    int64_t buf_words = 0;
     PhaseDev* d_ph = nullptr;
-    unsigned int* d_done = nullptr;   // n_phases + 1 (exit counter last)
+    unsigned int* d_done = nullptr;   // n_phases + 2 (exit counter, launch counter)
     unsigned long long* d_key = nullptr;
-    float* d_slots = nullptr;
+    unsigned long long* d_slots = nullptr;
+    unsigned long long* d_xkeys = nullptr;   // [kMaxRanks][2]
     int* d_qcount = nullptr;
+    unsigned long long** d_peers = nullptr;   // [2][kMaxRanks]: slot buffers, key arrays of every rank
+    unsigned long long* peer_slots[kMaxRanks] = {};
+    unsigned long long* peer_xkeys[kMaxRanks] = {};
 };
 
 constexpr uint64_t kPlanMagic = 0x4734514445434f44ull;
 
-void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens) {
+static void free_plan_memory(DecodePlan* plan) {
+    cudaFree(plan->d_ph);
+    cudaFree(plan->d_done);
+    cudaFree(plan->d_key);
+    cudaFree(plan->d_slots);
+    cudaFree(plan->d_xkeys);
+    cudaFree(plan->d_qcount);
+    cudaFree(plan->d_peers);
+}
+
+static void upload_peers(DecodePlan* plan) {
+    unsigned long long* table[2 * kMaxRanks];
+    for (int r = 0; r < kMaxRanks; ++r) {
+        table[r] = plan->peer_slots[r];
+        table[kMaxRanks + r] = plan->peer_xkeys[r];
+    }
+    check_cuda(cudaMemcpy(plan->d_peers, table, sizeof(table), cudaMemcpyHostToDevice), "upload peer pointers");
+}
+
+void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, int rank, int n_ranks) {
     if (n <= 0 || phases == nullptr) throw Error(G4Q_ERR_INVALID_ARGUMENT, "a plan needs at least one phase");
     if (max_tokens != 1)
         throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "the decode plan runs one token per step (max_tokens = 1)");
+    if (n_ranks < 1 || n_ranks > kMaxRanks || rank < 0 || rank >= n_ranks)
+        throw Error(G4Q_ERR_INVALID_ARGUMENT, "rank must be in [0, n_ranks) with 1 <= n_ranks <= 8");
+    if (n > 60000) throw Error(G4Q_ERR_INVALID_ARGUMENT, "too many phases");
     const int dev = current_device();
     const int sms = device_sm_count();
     std::vector<PhaseDev> ph(n);
-    int max_q = 0, kmax = 0;
+    std::vector<std::vector<char>> producers(n);   // which producer CTAs each phase's x window needs
+    int kmax = 0, max_q = 0;
     for (int i = 0; i < n; ++i) {
         const Weight* w = reinterpret_cast<const Weight*>(phases[i].weight);
         const std::string tag = "phase " + std::to_string(i) + ": ";
@@ -675,10 +870,14 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens) {
             throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "the decode plan needs every |scale| < 2^-1");
         if (w->N % 64 != 0) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "rows must be a multiple of 64");
         const uint32_t fl = phases[i].flags;
-        if (fl & ~(G4Q_QMM_RMS_SCALE | G4Q_QMM_OUT_F32 | G4Q_PHASE_ARGMAX))
+        if (fl & ~(G4Q_QMM_RMS_SCALE | G4Q_QMM_OUT_F32 | G4Q_PHASE_ARGMAX | G4Q_PHASE_ALLREDUCE))
             throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "unknown flag bits");
         if ((fl & G4Q_PHASE_ARGMAX) && i != n - 1)
             throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "the argmax phase must be the last phase");
+        if ((fl & G4Q_PHASE_ARGMAX) && (fl & G4Q_PHASE_ALLREDUCE))
+            throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "the argmax phase cannot be an allreduce phase");
+        if ((fl & G4Q_PHASE_ALLREDUCE) && (fl & G4Q_QMM_RMS_SCALE))
+            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "an allreduce phase takes no RMS scale");
         if (!(fl & G4Q_PHASE_ARGMAX) && !phases[i].y) throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "needs an output");
         if (!phases[i].x || (reinterpret_cast<uintptr_t>(phases[i].x) & 15u))
             throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "x must be 16-byte aligned");
@@ -687,8 +886,6 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens) {
         d.sb = w->sb;
         d.x = phases[i].x;
         d.y = phases[i].y;
-        d.ldx = phases[i].ldx;
-        d.ldy = phases[i].ldy;
         d.N = (int)w->N;
         d.K = (int)w->K;
         d.R = (int)(w->N / 16);
@@ -698,7 +895,24 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens) {
         d.flags = fl;
         d.src = -1;
         d.src_col = 0;
-        // x inside the previous phase's (bf16) output row: consume it with the slot rebuild
+        d.src_ranks = (fl & G4Q_PHASE_ALLREDUCE) ? n_ranks : 1;
+        d.sync_before = 0;
+        d.need_done = (fl & G4Q_PHASE_ARGMAX) ? 1 : 0;
+        if (d.U < sms) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too small for a full-grid decode plan");
+        if ((uint64_t)(d.U + 1) * (uint64_t)sms >= (1ull << 32) || (uint64_t)w->N * (uint64_t)w->K / 2 >= (1ull << 32))
+            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too many units for 32-bit partition arithmetic");
+        // a CTA range (at most ceil(U/C) units) touches at most (ceil(U/C) + G - 2) / G + 1 quads
+        if ((d.U + sms - 1) / sms + d.G - 2 >= (kMaxCtaQuads - 1) * d.G)
+            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too many quads per CTA range");
+        // the most CTA ranges one quad meets, from the partition itself
+        int ks = 1;
+        for (int q = 0; q < d.Q; ++q) {
+            const int64_t cf = ((int64_t)q * d.G + 1) * sms - 1, cl = ((int64_t)(q + 1) * d.G) * sms - 1;
+            ks = std::max<int>(ks, (int)(cl / d.U - cf / d.U + 1));
+        }
+        if (ks > kSlots) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "split too finely");
+        d.ks = ks;
+        // x inside the previous phase's (bf16) output row: consume it from the slots (dataflow)
         if (i > 0 && !(ph[i - 1].flags & (G4Q_PHASE_ARGMAX | G4Q_QMM_OUT_F32))) {
             const uint16_t* y0 = static_cast<const uint16_t*>(ph[i - 1].y);
             if (phases[i].x >= y0 && phases[i].x < y0 + ph[i - 1].N) {
@@ -710,68 +924,126 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens) {
                 d.src_col = (int)col;
             }
         }
+        // producer CTAs this phase's x depends on (all of them for an external or older input)
+        producers[i].assign(sms, d.src < 0 ? 1 : 0);
+        if (d.src >= 0) {
+            const PhaseDev& S = ph[d.src];
+            const int qa = d.src_col / 64, qb = (d.src_col + d.K) / 64;
+            const int64_t cf = (((int64_t)qa * S.G + 1) * sms - 1) / S.U, cl = (((int64_t)qb * S.G) * sms - 1) / S.U;
+            for (int64_t c = cf; c <= cl && c < sms; ++c) producers[i][c] = 1;
+        }
         if (d.K > kmax) kmax = d.K;
         if (d.Q > max_q) max_q = d.Q;
-        if (d.U < sms) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too small for a full-grid decode plan");
-        if ((uint64_t)(d.U + 1) * (uint64_t)sms >= (1ull << 32) || (uint64_t)w->N * (uint64_t)w->K / 2 >= (1ull << 32))
-            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too many units for 32-bit partition arithmetic");
-        // a CTA range (at most ceil(U/C) units) touches at most (ceil(U/C) + G - 2) / G + 1 quads
-        if ((d.U + sms - 1) / sms + d.G - 2 >= (kMaxCtaQuads - 1) * d.G)
-            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too many quads per CTA range");
-        // a quad (G units) meets at most (G-1)/min_range + 2 CTA ranges
-        if ((d.G - 1) / (d.U / sms) + 2 > kSlots) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "split too finely");
     }
+    // Every phase waits until every CTA of this rank has finished the previous one (one acquire
+    // poll of a counter that each CTA bumps with a release atomic); on one GPU that makes the slot
+    // tags redundant, across ranks they are what says a peer's partials have arrived. Slot buffers
+    // rotate over three phases so that a rank running one phase ahead of another never overwrites
+    // slots the other still reads.
+    auto full = [&](int i) {
+        for (int c = 0; c < sms; ++c)
+            if (!producers[i][c]) return false;
+        return true;
+    };
+    for (int i = 1; i < n; ++i) ph[i].sync_before = 1;
+    // Across ranks there is no barrier at all: a rank can only run ahead into the next phase that
+    // reads an allreduce phase's output, which needs every rank's partials. So every allreduce phase
+    // must feed the phase after it whole, and the step ends with the key exchange.
+    if (n_ranks > 1)
+        for (int i = 0; i < n; ++i)
+            if ((ph[i].flags & G4Q_PHASE_ALLREDUCE) && (i + 1 >= n || ph[i + 1].src != i || !full(i + 1)))
+                throw Error(G4Q_ERR_UNSUPPORTED_CONFIG,
+                            "phase " + std::to_string(i) + ": the next phase must read all of an allreduce output");
+    for (int i = 1; i < n; ++i)
+        if (ph[i].sync_before) ph[i - 1].need_done = 1;
+    int64_t buf_words = 0;
+    for (int i = 0; i < n; ++i)
+        buf_words = std::max<int64_t>(buf_words, ph[i].src_ranks > 1 ? (int64_t)ph[i].Q * ph[i].src_ranks * ph[i].ks * 64
+                                                                      : (int64_t)ph[i].Q * ph[i].ks * 32);
     auto* plan = new DecodePlan();
     plan->device = dev;
     plan->n_phases = n;
     plan->grid = sms;
-    plan->slot_stride = (int64_t)max_q * kSlots * 64;
+    plan->rank = rank;
+    plan->n_ranks = n_ranks;
+    plan->buf_words = buf_words;
     plan->smem = (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4 + (size_t)(kmax + 8) * 2;
-    if (plan->smem > max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel))) {
+    const void* kfn = n_ranks > 1 ? reinterpret_cast<const void*>(decode_kernel<true>)
+                                  : reinterpret_cast<const void*>(decode_kernel<false>);
+    if (plan->smem > max_dynamic_smem(kfn)) {
         delete plan;
         throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: K too large for shared memory");
     }
+    const size_t slot_bytes = sizeof(unsigned long long) * kSlotBufs * (size_t)buf_words;
     cudaError_t e = cudaMalloc(&plan->d_ph, sizeof(PhaseDev) * n);
-    if (e == cudaSuccess) e = cudaMalloc(&plan->d_done, sizeof(unsigned int) * (n + 1));
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_done, sizeof(unsigned int) * (n + 2));
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_key, sizeof(unsigned long long));
-    if (e == cudaSuccess) e = cudaMalloc(&plan->d_slots, sizeof(float) * 2 * (size_t)plan->slot_stride);
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_slots, slot_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_xkeys, sizeof(unsigned long long) * 2 * kMaxRanks);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_qcount, sizeof(int) * (size_t)max_q);
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_peers, sizeof(void*) * 2 * kMaxRanks);
     if (e == cudaSuccess) e = cudaMemcpy(plan->d_ph, ph.data(), sizeof(PhaseDev) * n, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemset(plan->d_done, 0, sizeof(unsigned int) * (n + 1));
+    if (e == cudaSuccess) e = cudaMemset(plan->d_done, 0, sizeof(unsigned int) * (n + 2));
     if (e == cudaSuccess) e = cudaMemset(plan->d_key, 0, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(plan->d_slots, 0, slot_bytes);
+    if (e == cudaSuccess) e = cudaMemset(plan->d_xkeys, 0, sizeof(unsigned long long) * 2 * kMaxRanks);
     if (e == cudaSuccess) e = cudaMemset(plan->d_qcount, 0, sizeof(int) * (size_t)max_q);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
-        cudaFree(plan->d_ph);
-        cudaFree(plan->d_done);
-        cudaFree(plan->d_key);
-        cudaFree(plan->d_slots);
-        cudaFree(plan->d_qcount);
+        free_plan_memory(plan);
         delete plan;
         check_cuda(e, "decode plan allocation");
     }
-    check_cuda(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan->smem),
+    plan->peer_slots[rank] = plan->d_slots;
+    plan->peer_xkeys[rank] = plan->d_xkeys;
+    upload_peers(plan);
+    check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan->smem),
                "cudaFuncSetAttribute(decode)");
     int per_sm = 0;
-    check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel, kThreads, plan->smem),
+    check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kThreads, plan->smem),
                "occupancy(decode)");
     if (per_sm < 1) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode kernel does not fit on an SM");
     plan->magic = kPlanMagic;
     return plan;
 }
 
-void decode_plan_free(void* h) {
+static DecodePlan* checked_plan(void* h) {
     auto* plan = static_cast<DecodePlan*>(h);
     if (!plan || plan->magic != kPlanMagic) throw Error(G4Q_ERR_INVALID_ARGUMENT, "invalid decode plan handle");
+    return plan;
+}
+
+void decode_plan_buffers(void* h, void** slots, uint64_t* slot_bytes, void** xkeys, uint64_t* xkey_bytes) {
+    DecodePlan* plan = checked_plan(h);
+    if (slots) *slots = plan->d_slots;
+    if (slot_bytes) *slot_bytes = sizeof(unsigned long long) * kSlotBufs * (uint64_t)plan->buf_words;
+    if (xkeys) *xkeys = plan->d_xkeys;
+    if (xkey_bytes) *xkey_bytes = sizeof(unsigned long long) * 2 * kMaxRanks;
+}
+
+void decode_plan_set_peers(void* h, void* const* slots, void* const* xkeys) {
+    DecodePlan* plan = checked_plan(h);
+    if (!slots || !xkeys) throw Error(G4Q_ERR_INVALID_ARGUMENT, "peer pointer arrays must be non-null");
+    for (int r = 0; r < plan->n_ranks; ++r) {
+        if (r == plan->rank) continue;
+        if (!slots[r] || !xkeys[r]) throw Error(G4Q_ERR_INVALID_ARGUMENT, "missing peer buffer of rank " + std::to_string(r));
+        plan->peer_slots[r] = static_cast<unsigned long long*>(slots[r]);
+        plan->peer_xkeys[r] = static_cast<unsigned long long*>(xkeys[r]);
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(plan->device);
+    upload_peers(plan);
+    cudaSetDevice(prev);
+}
+
+void decode_plan_free(void* h) {
+    DecodePlan* plan = checked_plan(h);
     plan->magic = 0;
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(plan->device);
-    cudaFree(plan->d_ph);
-    cudaFree(plan->d_done);
-    cudaFree(plan->d_key);
-    cudaFree(plan->d_slots);
-    cudaFree(plan->d_qcount);
+    free_plan_memory(plan);
     cudaSetDevice(prev);
     delete plan;
 }
@@ -779,10 +1051,12 @@ void decode_plan_free(void* h) {
 void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offset, int32_t* tokens, float* values,
                      uint64_t* keys, uint16_t* logits, int64_t ld_logits, cudaStream_t st) {
     (void)ld_logits;
-    auto* plan = static_cast<DecodePlan*>(h);
-    if (!plan || plan->magic != kPlanMagic) throw Error(G4Q_ERR_INVALID_ARGUMENT, "invalid decode plan handle");
+    DecodePlan* plan = checked_plan(h);
     if (plan->device != current_device()) throw Error(G4Q_ERR_INVALID_ARGUMENT, "plan belongs to another device");
     if (M != 1) throw Error(G4Q_ERR_INVALID_ARGUMENT, "the decode plan runs one token per step (M = 1)");
+    for (int r = 0; r < plan->n_ranks; ++r)
+        if (!plan->peer_slots[r] || !plan->peer_xkeys[r])
+            throw Error(G4Q_ERR_INVALID_ARGUMENT, "tensor-parallel plan: peer buffers not set");
     DecodeArgs a;
     a.ph = plan->d_ph;
     a.n_phases = plan->n_phases;
@@ -791,9 +1065,14 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     a.row_offset = row_offset;
     a.done = plan->d_done;
     a.exit_count = plan->d_done + plan->n_phases;
+    a.run = plan->d_done + plan->n_phases + 1;
     a.key = plan->d_key;
     a.slots = plan->d_slots;
-    a.slot_stride = plan->slot_stride;
+    a.peer_slots = plan->d_peers;
+    a.peer_xkeys = plan->d_peers + kMaxRanks;
+    a.rank = plan->rank;
+    a.n_ranks = plan->n_ranks;
+    a.buf_words = plan->buf_words;
     a.qcount = plan->d_qcount;
     a.tokens = tokens;
     a.values = values;
@@ -806,11 +1085,14 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     cfg.dynamicSmemBytes = plan->smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;   // every CTA resident: CTAs wait on each other's phases
+    attr[0].id = cudaLaunchAttributeCooperative;   // every CTA resident: CTAs wait on each other's data
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    check_cuda(cudaLaunchKernelEx(&cfg, decode_kernel, a), "cudaLaunchKernelEx(decode)");
+    if (plan->n_ranks > 1)
+        check_cuda(cudaLaunchKernelEx(&cfg, decode_kernel<true>, a), "cudaLaunchKernelEx(decode)");
+    else
+        check_cuda(cudaLaunchKernelEx(&cfg, decode_kernel<false>, a), "cudaLaunchKernelEx(decode)");
 }
 
 }  // namespace g4q

@@ -4,7 +4,7 @@
 // forward_hidden / decode_block_hidden, :1682-1780; chunk loop :1819-1841).
 //
 // One CTA computes a 128-token x 256-row tile of y = x . deq(W)^T (cta_group::1, no clusters,
-// no multicast), warp-specialised over a 3-stage mbarrier pipeline with one 64-wide
+// every copy private to its CTA), warp-specialised over a 3-stage mbarrier pipeline with one 64-wide
 // quantization group per k-step:
 //   warp 0      TMA producer: x tile [128 x 64] bf16 (tensor map, SWIZZLE_128B), the 8 KB packed
 //               tile of 16 layout-v1 blocks (tensor map over 128-byte rows, SWIZZLE_128B so the

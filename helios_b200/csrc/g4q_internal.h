@@ -102,7 +102,9 @@ void launch_lm_head(const Weight& w, const uint16_t* x, int64_t M, int64_t ldx, 
                     float* values, unsigned long long* keys, cudaStream_t st);
 
 // kernels (g4q_decode.cu): persistent decode-step kernel
-void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens);
+void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, int rank, int n_ranks);
+void decode_plan_buffers(void* plan, void** slots, uint64_t* slot_bytes, void** xkeys, uint64_t* xkey_bytes);
+void decode_plan_set_peers(void* plan, void* const* slots, void* const* xkeys);
 void decode_plan_free(void* plan);
 void decode_plan_run(void* plan, int M, float eps, float softcap, int64_t row_offset, int32_t* tokens, float* values,
                      uint64_t* keys, uint16_t* logits, int64_t ld_logits, cudaStream_t st);

@@ -23,11 +23,12 @@ from typing import Optional, Tuple
 import torch
 
 from . import _lib
-from ._lib import CHAIN_R1, CHAIN_R2, PHASE_ARGMAX, QMM_OUT_F32, QMM_RMS_SCALE, G4qError, G4qInvalidArgument
+from ._lib import (CHAIN_R1, CHAIN_R2, PHASE_ALLREDUCE, PHASE_ARGMAX, QMM_OUT_F32, QMM_RMS_SCALE, G4qError,
+                   G4qInvalidArgument)
 
 __all__ = [
     "QuantizedWeight", "quantized_matmul", "dequantize", "lm_head_argmax", "DecodePlan", "synth_matrix",
-    "synth_normal", "CHAIN_R1", "CHAIN_R2", "QMM_RMS_SCALE", "QMM_OUT_F32", "PHASE_ARGMAX", "G4qError",
+    "synth_normal", "CHAIN_R1", "CHAIN_R2", "QMM_RMS_SCALE", "QMM_OUT_F32", "PHASE_ARGMAX", "PHASE_ALLREDUCE", "G4qError",
     "G4qInvalidArgument",
 ]
 
@@ -275,12 +276,17 @@ class DecodePlan:
 
     ``phases`` is a list of ``(weight, x, y, flags)``: ``x`` a bf16 CUDA tensor view [M, K] (row stride a
     multiple of 8), ``y`` a bf16/fp32 CUDA tensor view [M, N] or None for the final argmax phase;
-    ``flags`` from QMM_RMS_SCALE / QMM_OUT_F32 / PHASE_ARGMAX. Phase i may read phase i-1's output.
-    Tensor addresses are baked into the plan: keep the tensors alive and reuse them.
+    ``flags`` from QMM_RMS_SCALE / QMM_OUT_F32 / PHASE_ARGMAX / PHASE_ALLREDUCE. Phase i may read
+    phase i-1's output. Tensor addresses are baked into the plan: keep the tensors alive and reuse them.
+
+    Tensor parallel: pass ``rank``/``n_ranks`` and the process ``group``; every rank builds the plan of
+    its own shards (collectively), the plans exchange their slot buffers by CUDA IPC over the group,
+    and ALLREDUCE phases then sum their partials across ranks inside the kernel.
     """
 
-    def __init__(self, phases, max_tokens: int = 1):
+    def __init__(self, phases, max_tokens: int = 1, *, rank: int = 0, n_ranks: int = 1, group=None):
         self._keep = []
+        self._opened = []
         arr = (_lib.G4qDecodePhase * len(phases))()
         for i, (w, x, y, flags) in enumerate(phases):
             if x.dtype != torch.bfloat16 or x.stride(-1) != 1:
@@ -293,8 +299,39 @@ class DecodePlan:
             arr[i].flags = flags
             self._keep += [w, x, y]
         self._h = ctypes.c_void_p()
-        _lib.call("g4q_decode_plan_create", arr, len(phases), max_tokens, ctypes.byref(self._h))
+        if n_ranks == 1:
+            _lib.call("g4q_decode_plan_create", arr, len(phases), max_tokens, ctypes.byref(self._h))
+        else:
+            _lib.call("g4q_decode_plan_create_tp", arr, len(phases), max_tokens, rank, n_ranks, ctypes.byref(self._h))
+            self._connect(rank, n_ranks, group)
         self.max_tokens = max_tokens
+
+    def _connect(self, rank: int, n_ranks: int, group):
+        """Exchange the plan's slot / key buffers with the other ranks (CUDA IPC handles over ``group``)."""
+        slots, xkeys = ctypes.c_void_p(), ctypes.c_void_p()
+        sb, kb = ctypes.c_uint64(), ctypes.c_uint64()
+        _lib.call("g4q_decode_plan_buffers", self._h, ctypes.byref(slots), ctypes.byref(sb), ctypes.byref(xkeys),
+                  ctypes.byref(kb))
+        mine = []
+        for ptr in (slots, xkeys):
+            h = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+            _lib.call("g4q_ipc_handle", ptr, h)
+            mine.append(bytes(h))
+        allh = [None] * n_ranks
+        torch.distributed.all_gather_object(allh, mine, group=group)
+        peer_slots = (ctypes.c_void_p * n_ranks)()
+        peer_keys = (ctypes.c_void_p * n_ranks)()
+        for r in range(n_ranks):
+            if r == rank:
+                peer_slots[r], peer_keys[r] = slots.value, xkeys.value
+                continue
+            for j, dst in enumerate((peer_slots, peer_keys)):
+                h = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES).from_buffer_copy(allh[r][j])
+                p = ctypes.c_void_p()
+                _lib.call("g4q_ipc_open", h, ctypes.byref(p))
+                self._opened.append(p)
+                dst[r] = p.value
+        _lib.call("g4q_decode_plan_set_peers", self._h, peer_slots, peer_keys)
 
     def run(self, M: int, *, eps: float = 1e-6, softcap: float = 30.0, row_offset: int = 0, tokens=None,
             values=None, keys=None, logits=None):
@@ -303,6 +340,9 @@ class DecodePlan:
                   _ptr(logits), ld, _stream())
 
     def free(self):
+        for p in getattr(self, "_opened", []):
+            _lib.call("g4q_ipc_close", p)
+        self._opened = []
         if self._h:
             _lib.call("g4q_decode_plan_free", self._h)
             self._h = ctypes.c_void_p()

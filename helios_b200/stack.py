@@ -27,7 +27,7 @@ from typing import List, Optional
 
 import torch
 
-from .quantized import (PHASE_ARGMAX, QMM_RMS_SCALE, DecodePlan, QuantizedWeight, lm_head_argmax,
+from .quantized import (PHASE_ALLREDUCE, PHASE_ARGMAX, QMM_RMS_SCALE, DecodePlan, QuantizedWeight, lm_head_argmax,
                         quantized_matmul, synth_matrix)
 
 BASE_SEED = 0x48454C494F53
@@ -164,20 +164,23 @@ class SyntheticStack:
         return self.head(x)
 
     def build_plan(self, max_tokens: int = 1) -> DecodePlan:
-        """The whole decode step (48 x 4 matmuls + LM head argmax) as one persistent-kernel plan."""
-        if self.size != 1:
-            raise NotImplementedError("the single-launch decode plan covers one GPU")
+        """The whole decode step (48 x 4 matmuls + LM head argmax) as one persistent-kernel plan.
+
+        Tensor parallel (``tp_size`` > 1, collective over the group): o and down are ALLREDUCE phases,
+        their partial sums cross NVLink inside the kernel, and the LM-head keys are combined there too,
+        so one step is one launch per GPU with no NCCL call."""
         c = self.cfg
         self.h_in = torch.zeros((max(max_tokens, 1), c.hidden), dtype=torch.bfloat16, device=self.device)
+        ar = PHASE_ALLREDUCE if self.size > 1 else 0
         phases, x = [], self.h_in
         for L in self.layers:
             phases.append((L["qkv"], x, self.qkv_out, QMM_RMS_SCALE))
-            phases.append((L["o"], self.qkv_out[:, : self.nq], self.o_out, 0))
+            phases.append((L["o"], self.qkv_out[:, : self.nq], self.o_out, ar))
             phases.append((L["gu"], self.o_out, self.gu_out, QMM_RMS_SCALE))
-            phases.append((L["down"], self.gu_out[:, self.ni:], self.h_out, 0))
+            phases.append((L["down"], self.gu_out[:, self.ni:], self.h_out, ar))
             x = self.h_out
         phases.append((self.lm, x, None, QMM_RMS_SCALE | PHASE_ARGMAX))
-        self.plan = DecodePlan(phases, max_tokens)
+        self.plan = DecodePlan(phases, max_tokens, rank=self.rank, n_ranks=self.size, group=self.group)
         return self.plan
 
     def decode(self, h: torch.Tensor):
@@ -187,6 +190,11 @@ class SyntheticStack:
         self.plan.run(M, eps=self.cfg.eps, softcap=self.cfg.softcap, row_offset=self.v_rows[0],
                       tokens=self.tokens[:M], values=self.values[:M], keys=self.keys[:M])
         return self.keys[:M], self.h_out[:M]
+
+    def local_weight_bytes(self) -> int:
+        """Packed + scale/bias bytes of this rank's shards (0.5625 B per weight)."""
+        mats = [w for L in self.layers for w in L.values()] + [self.lm]
+        return sum(w.rows * w.cols * 9 // 16 for w in mats)
 
     def head(self, x: torch.Tensor):
         c = self.cfg

@@ -171,6 +171,9 @@ G4qStatus g4q_lm_head_argmax_noalloc(const uint32_t* packed, const uint32_t* sb,
  * allocates nothing, so it can be captured in a CUDA graph. M (tokens per step) <= 2. Runs of one
  * plan must not overlap on the GPU. */
 #define G4Q_PHASE_ARGMAX 0x4u
+/* Row-parallel phase of a tensor-parallel plan (o_proj, down_proj split along K): every rank's
+ * partial sums are added across ranks inside the kernel (the allreduce after o/down). */
+#define G4Q_PHASE_ALLREDUCE 0x8u
 
 typedef struct G4qDecodePhase {
     const G4qWeight* weight;
@@ -189,6 +192,31 @@ G4qStatus g4q_decode_plan_run(G4qDecodePlan* plan, int64_t M, float eps, float s
                               int32_t* tokens, float* values, uint64_t* keys, uint16_t* logits, int64_t ld_logits,
                               void* stream);
 G4qStatus g4q_decode_plan_free(G4qDecodePlan* plan);
+
+/* ---- tensor-parallel decode plans (one process per GPU) ---------------------------------------
+ * Replaces the per-rank linears plus the NCCL allreduce after o_proj / down_proj and the vocab-shard
+ * argmax combine of a tensor-parallel decode step (the reference runs one device; its column/row
+ * split is the MLX sharding of the same linears). Each rank builds the plan of its shards with
+ * g4q_decode_plan_create_tp(rank, n_ranks); phases with G4Q_PHASE_ALLREDUCE write their partial
+ * sums into the slot buffers of every rank over NVLink and every rank sums them in the same order,
+ * so all ranks see bit-identical activations. The LM-head argmax keys are exchanged the same way at
+ * the end of each step (tokens/values/keys are the global result on every rank). Wiring: every rank
+ * exports its buffers (g4q_decode_plan_buffers -> g4q_ipc_handle), the handles are exchanged by
+ * the host (e.g. an allgather over the process group), each rank opens its peers' handles
+ * (g4q_ipc_open) and passes the pointers indexed by rank to g4q_decode_plan_set_peers (the own
+ * rank's entries are ignored). All ranks must run the same number of steps. */
+G4qStatus g4q_decode_plan_create_tp(const G4qDecodePhase* phases, int32_t n_phases, int32_t max_tokens,
+                                    int32_t rank, int32_t n_ranks, G4qDecodePlan** out);
+G4qStatus g4q_decode_plan_buffers(G4qDecodePlan* plan, void** slots, uint64_t* slot_bytes, void** xkeys,
+                                  uint64_t* xkey_bytes);
+G4qStatus g4q_decode_plan_set_peers(G4qDecodePlan* plan, void* const* slots, void* const* xkeys);
+
+/* CUDA IPC of device allocations between the processes of one node (no reference counterpart:
+ * the reference runs one process per model). */
+#define G4Q_IPC_HANDLE_BYTES 64
+G4qStatus g4q_ipc_handle(const void* device_ptr, uint8_t* handle);
+G4qStatus g4q_ipc_open(const uint8_t* handle, void** device_ptr);
+G4qStatus g4q_ipc_close(void* device_ptr);
 
 /* ---- device-side failure detection ----------------------------------------------------------
  * Every wait inside a libg4q kernel is bounded; a wait that gives up records a nonzero code in a

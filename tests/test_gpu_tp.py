@@ -1,7 +1,9 @@
-"""GPU, 2 ranks (skipped with fewer GPUs): the tensor-parallel synthetic stack over NCCL against the
-CPU oracle of the unsharded stack. Each rank is a spawned process on its own GPU; NVLS is off
-(NCCL_NVLS_ENABLE=0) and the process group has a short timeout so a failing rank cannot hang the
-other."""
+"""GPU, 2 ranks (skipped with fewer GPUs): the tensor-parallel synthetic stack against the CPU oracle
+of the unsharded stack, both through the per-matmul path with NCCL allreduces and through the
+tensor-parallel decode plan (one launch per GPU, o/down partials summed over NVLink inside the
+kernel, LM-head keys exchanged by the kernel). Each rank is a spawned process on its own GPU; NVLS
+is off (NCCL_NVLS_ENABLE=0), the process group has a short timeout and every in-kernel wait is
+bounded, so a failing rank cannot hang the other."""
 import os
 import socket
 import sys
@@ -14,6 +16,7 @@ import torch
 pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 SMALL = dict(layers=2, hidden=256, q_out=256, kv_out=128, inter=512, vocab=2048)
+PLAN = dict(layers=2, hidden=2048, q_out=2048, kv_out=1024, inter=4096, vocab=16384)
 
 
 def _free_port():
@@ -64,3 +67,55 @@ def test_tensor_parallel_stack_two_gpus(cuda, oracle):
     toks, vals = decode_keys(torch.from_numpy(keys))
     for m in range(2):
         assert toks[m] == ref["tokens"][m] or abs(vals[m] - ref["values"][m]) <= 0.125
+
+
+def _plan_worker(rank, world, port, out_q):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from helios_b200 import _lib
+        from helios_b200.quantized import synth_normal
+        from helios_b200.stack import StackConfig, SyntheticStack, activation_seed
+        cfg = StackConfig(**PLAN)
+        st = SyntheticStack(cfg, rank, world, dist.group.WORLD, max_tokens=1)
+        st.build_plan(1)
+        h0 = synth_normal(activation_seed(23), (1, cfg.hidden))
+        k1, h1 = st.decode(h0)
+        k1, h1 = k1.clone(), h1.clone()
+        k2, h2 = st.decode(h0)
+        torch.cuda.synchronize()
+        same = bool(torch.equal(k1, k2) and torch.equal(h1, h2))
+        err = _lib.device_error()
+        out_q.put((rank, k1.cpu().numpy().copy(), h1.view(torch.int16).cpu().numpy().view(np.uint16).copy(), same,
+                   err))
+        dist.barrier()
+        st.free()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_decode_plan_two_gpus(cuda, oracle):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    mp.start_processes(_plan_worker, args=(2, _free_port(), q), nprocs=2, join=True, start_method="spawn")
+    res = sorted([q.get(), q.get()], key=lambda r: r[0])
+    from helios_b200.stack import StackConfig, decode_keys
+    cfg = StackConfig(**PLAN)
+    for _, keys, h, same, err in res:
+        assert err == 0 and same                       # bounded waits all met; bit-reproducible
+    assert np.array_equal(res[0][1], res[1][1])        # every rank ends the step with the same key
+    assert np.array_equal(res[0][2], res[1][2])        # and the same (allreduced) hidden state
+    h0 = oracle.synth_normal_bf16(oracle.activation_seed(23), cfg.hidden).reshape(1, -1)
+    ref = oracle.stack_forward(h0, cfg.layers, oracle.stack_shapes(cfg.hidden, cfg.q_out, cfg.kv_out, cfg.inter,
+                                                                   cfg.vocab))
+    a, b = oracle.bf16_to_f32(res[0][2]).astype(np.float64), oracle.bf16_to_f32(ref["hidden"]).astype(np.float64)
+    assert np.abs(a - b).max() <= 2e-2 * np.sqrt((b ** 2).mean())
+    toks, vals = decode_keys(torch.from_numpy(res[0][1]))
+    assert toks[0] == ref["tokens"][0] or abs(vals[0] - ref["values"][0]) <= 0.125
