@@ -221,6 +221,7 @@ G4qStatus g4q_weight_free(G4qWeight* h) {
         cudaFree(w->sb);
         cudaFree(w->d_flags);
         cudaFree(w->argmax_scratch);
+        direct_release(*w);
         cudaSetDevice(prev);
         delete w;
     });
@@ -294,6 +295,7 @@ G4qStatus g4q_weight_load(G4qWeight* h, int64_t dst_row0, const uint32_t* packed
         check_cuda(cudaMemcpy(&flags, w->d_flags, sizeof(int), cudaMemcpyDeviceToHost), "read handle flags");
         w->fast_ok = (flags & 1) == 0;   // cached so compute calls never read device memory
         w->small_scales = (flags & 4) == 0;
+        direct_prepare(*w);
     });
 }
 
@@ -350,7 +352,9 @@ static void qmm_common(const char* fn, const G4qWeight* h, const uint16_t* x, in
             "a scale is non-finite or |scale| >= 2^120; use g4q_dequantize for such weights");
     QmmCall c{w, x, M, ldx, y, ldy, flags, eps};
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (M <= 16)
+    if (M == 1 && direct_ready(*w, y))
+        launch_direct(*w, x, y, flags, eps, st);   // the persistent decode kernel, one phase
+    else if (M <= 16)
         launch_gemv(c, st);
     else
         launch_gemm(c, st);

@@ -32,6 +32,7 @@
 // Every wait is bounded (about two seconds of clocks); a wait that gives up records an error code
 // in the per-device error word and the kernel runs to its end.
 #include <algorithm>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -52,6 +53,7 @@ constexpr int kSlots = 16;                        // CTA ranges one 64-row quad 
 constexpr int kSlotBufs = 3;                      // slot buffers rotate over three phases
 constexpr int kMaxCtaQuads = 64;                  // quads one CTA range may touch in a phase
 constexpr int kMaxRanks = 8;
+constexpr int kMaxXQuads = 256;                   // 64-wide groups of x a phase may read (K <= 16384)
 constexpr long long kSpinLimit = 4000000000ll;    // ~2 s of SM clocks
 constexpr uint32_t kOddNibbleMask = 0x00F000F0u;  // q at bits 4-7 of each half: bf16 value q * 2^-129
 constexpr uint32_t kPow64x2 = 0x5F805F80u;        // bf16x2 (2^64, 2^64)
@@ -92,7 +94,20 @@ struct DecodeArgs {
     unsigned long long* keys_out;
     uint16_t* logits;                         // optional bf16 logits of the argmax phase
     int* err;
+    // direct launch of one cached phase (a standalone quantized matmul): x, y and flags of the call
+    int direct;
+    const uint16_t* dx;
+    void* dy;
+    uint32_t dflags;
 };
+
+__device__ __forceinline__ uint32_t phase_flags(const DecodeArgs& a, const PhaseDev& P) {
+    return a.direct ? a.dflags : P.flags;
+}
+__device__ __forceinline__ void* phase_y(const DecodeArgs& a, const PhaseDev& P) { return a.direct ? a.dy : P.y; }
+__device__ __forceinline__ const uint16_t* phase_x(const DecodeArgs& a, const PhaseDev& P) {
+    return a.direct ? a.dx : P.x;
+}
 
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -230,6 +245,7 @@ struct CtaShared {
     float rs, rs_prev;
     uint32_t tag0;
     int qcnt[kMaxCtaQuads];   // arrivals per quad of the CTA's range (reset by the last arriver)
+    int2 cut[kMaxXQuads];     // per producer quad of x: (first slot float, slot count)
     int warps_finished;
     int wb_claim;
     unsigned long long best;
@@ -363,11 +379,11 @@ __device__ __forceinline__ uint2 finish4(float4 s, float rs) {
                       (uint32_t)f32_to_bf16_bits(__fmul_rn(s.z, rs)) | ((uint32_t)f32_to_bf16_bits(__fmul_rn(s.w, rs)) << 16));
 }
 
-__device__ __forceinline__ void store_y(const PhaseDev& P, int n, float v) {
-    if (P.flags & G4Q_QMM_OUT_F32)
-        reinterpret_cast<float*>(P.y)[n] = v;
+__device__ __forceinline__ void store_y(void* y, uint32_t flags, int n, float v) {
+    if (flags & G4Q_QMM_OUT_F32)
+        reinterpret_cast<float*>(y)[n] = v;
     else
-        reinterpret_cast<uint16_t*>(P.y)[n] = f32_to_bf16_bits(v);
+        reinterpret_cast<uint16_t*>(y)[n] = f32_to_bf16_bits(v);
 }
 
 // argmax phase: fold one finished output into the running key
@@ -426,7 +442,8 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
         v[h] = s;
     }
     const bool whole = cs <= q * G && ce >= (q + 1) * G;
-    const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
+    const uint32_t fl = phase_flags(a, P);
+    const bool argmax = (fl & G4Q_PHASE_ARGMAX) != 0;
     if (whole && argmax) {
 #pragma unroll
         for (int h = 0; h < 2; ++h)
@@ -444,7 +461,7 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
         for (int h = 0; h < 2; ++h) base[(size_t)(cta - cf) * 64 + lane + 32 * h] = v[h];
         if (whole) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) store_y(P, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs));
+            for (int h = 0; h < 2; ++h) store_y(phase_y(a, P), fl, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs));
         } else if (argmax) {   // the logits are needed now: the last contributing CTA finishes the quad
             __threadfence();
             __syncwarp();
@@ -481,8 +498,8 @@ __device__ __forceinline__ int xperm(int w) {
 // owns 4-row cells (16 per producer quad) and sums the cell's tagged slots (polling until the
 // producers have written them); two cells are in flight per thread.
 template <bool kTP>
-__device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P, uint32_t* xs, int C, float rs_prev,
-                                         uint32_t tag0, bool rms) {
+__device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P, uint32_t* xs, const int2* cut, int C,
+                                         float rs_prev, uint32_t tag0, bool rms) {
     float ss = 0.0f;
     auto acc_sq = [&](uint32_t w) {
         const float lo = bf16_bits_to_f32(w & 0xffffu), hi = bf16_bits_to_f32(w >> 16);
@@ -491,7 +508,7 @@ __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P,
     };
     if (P.src < 0) {
         for (int u = threadIdx.x; u < P.K / 8; u += kThreads) {
-            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(P.x) + u);
+            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(phase_x(a, P)) + u);
             xs[xperm(4 * u)] = v.x;
             xs[xperm(4 * u + 1)] = v.y;
             xs[xperm(4 * u + 2)] = v.z;
@@ -506,42 +523,76 @@ __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P,
         return ss;
     }
     const PhaseDev& S = a.ph[P.src];
-    const bool tagged = kTP && S.src_ranks > 1;
-    const uint32_t tag = phase_tag(tag0, P.src);
     const int q0 = P.src_col >> 6;
     const int cells = P.K / 4;
-    for (int e0 = threadIdx.x; e0 < cells; e0 += 2 * kThreads) {
-        float4 s[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int idx = e0 + h * kThreads;
-            if (idx < cells) {
+    (void)q0;
+    auto put = [&](int idx, float4 s) {
+        const uint2 w = finish4(s, rs_prev);
+        xs[xperm(2 * idx)] = w.x;
+        xs[xperm(2 * idx + 1)] = w.y;
+        if (rms) {
+            acc_sq(w.x);
+            acc_sq(w.y);
+        }
+    };
+    if constexpr (kTP) {
+        if (S.src_ranks > 1) {   // partials of every rank, tagged: poll until they have all arrived
+            const uint32_t tag = phase_tag(tag0, P.src);
+            for (int idx = threadIdx.x; idx < cells; idx += kThreads) {
                 const int q = q0 + (idx >> 4);
                 int cf, cl;
                 quad_ctas(S, q, C, cf, cl);
-                if constexpr (kTP) {
-                    if (tagged)
-                        s[h] = sum_tagged4(a.slots + slot_word(a, S, P.src, q, 0, 0) + (idx & 15) * 4, S.src_ranks, S.ks,
-                                           cl - cf + 1, tag, a.err);
-                }
-                if (!tagged)
-                    s[h] = sum_slots4(reinterpret_cast<const float*>(a.slots) + slot_f(a, S, P.src, q, 0) +
-                                          (idx & 15) * 4,
-                                      cl - cf + 1);
+                put(idx, sum_tagged4(a.slots + slot_word(a, S, P.src, q, 0, 0) + (idx & 15) * 4, S.src_ranks, S.ks,
+                                     cl - cf + 1, tag, a.err));
+            }
+            return ss;
+        }
+    }
+    // single-rank partials: four cells per thread with up to four slots each in flight at once,
+    // summed in slot order exactly as sum_slots4 does
+    const float* sl = reinterpret_cast<const float*>(a.slots);
+    constexpr int kB = 4;
+    for (int e0 = threadIdx.x; e0 < cells; e0 += kB * kThreads) {
+        const float* base[kB];
+        int nc[kB];
+#pragma unroll
+        for (int h = 0; h < kB; ++h) {
+            const int idx = e0 + h * kThreads;
+            nc[h] = 0;
+            base[h] = sl;
+            if (idx < cells) {
+                const int2 ct = cut[idx >> 4];
+                nc[h] = ct.y;
+                base[h] = sl + ct.x + (idx & 15) * 4;
             }
         }
+        float4 l[kB][4];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int idx = e0 + h * kThreads;
-            if (idx < cells) {
-                const uint2 w = finish4(s[h], rs_prev);
-                xs[xperm(2 * idx)] = w.x;
-                xs[xperm(2 * idx + 1)] = w.y;
-                if (rms) {
-                    acc_sq(w.x);
-                    acc_sq(w.y);
+        for (int h = 0; h < kB; ++h)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                l[h][c] = c < nc[h] ? __ldcg(reinterpret_cast<const float4*>(base[h] + c * 64))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int h = 0; h < kB; ++h) {
+            if (nc[h] == 0) continue;
+            float4 t = l[h][0];
+#pragma unroll
+            for (int c = 1; c < 4; ++c)
+                if (c < nc[h]) {
+                    t.x += l[h][c].x;
+                    t.y += l[h][c].y;
+                    t.z += l[h][c].z;
+                    t.w += l[h][c].w;
                 }
+            for (int c = 4; c < nc[h]; ++c) {
+                const float4 u = __ldcg(reinterpret_cast<const float4*>(base[h] + c * 64));
+                t.x += u.x;
+                t.y += u.y;
+                t.z += u.z;
+                t.w += u.w;
             }
+            put(e0 + h * kThreads, t);
         }
     }
     return ss;
@@ -552,7 +603,8 @@ __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P,
 template <bool kTP>
 __device__ __forceinline__ void write_back_warp(const DecodeArgs& a, int pp, int cta, int C, float rs_prev, uint32_t tag0) {
     const PhaseDev& Q = a.ph[pp];
-    if (Q.flags & G4Q_PHASE_ARGMAX) return;
+    const uint32_t fl = phase_flags(a, Q);
+    if (fl & G4Q_PHASE_ARGMAX) return;
     const int lane = threadIdx.x & 31;
     const uint32_t tag = phase_tag(tag0, pp);
     for (int q = cta; q < Q.Q; q += C) {
@@ -568,14 +620,14 @@ __device__ __forceinline__ void write_back_warp(const DecodeArgs& a, int pp, int
         if (!kTP || Q.src_ranks == 1)
             s = sum_slots4(reinterpret_cast<const float*>(a.slots) + slot_f(a, Q, pp, q, 0) + lane * 4, cl - cf + 1);
         const int n = q * 64 + lane * 4;
-        if (Q.flags & G4Q_QMM_OUT_F32) {
-            float* y = reinterpret_cast<float*>(Q.y) + n;
+        if (fl & G4Q_QMM_OUT_F32) {
+            float* y = reinterpret_cast<float*>(phase_y(a, Q)) + n;
             y[0] = __fmul_rn(s.x, rs_prev);
             y[1] = __fmul_rn(s.y, rs_prev);
             y[2] = __fmul_rn(s.z, rs_prev);
             y[3] = __fmul_rn(s.w, rs_prev);
         } else {
-            *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(Q.y) + n) = finish4(s, rs_prev);
+            *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(phase_y(a, Q)) + n) = finish4(s, rs_prev);
         }
     }
 }
@@ -641,10 +693,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     Pre pre;
     pre.p = 0;
     pre.enter(a, cta, C, warp);
-    for (int s = 0; s < kStages && pre.p < a.n_phases; ++s) {
-        if (lane == 0) pre.issue(ring_s + s * kUnitBytes, bar0 + 8 * s);
-        pre.next(a, cta, C, warp);
-    }
 
     int stage = 0;
     uint32_t phase_bit = 0;
@@ -654,8 +702,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         const PhaseDev& P = a.ph[p];
         const int cs = range_start(cta, P.U, C), ce = range_start(cta + 1, P.U, C);
         const int G = P.G;
-        // ---- phase entry: the CTA's warps are done with the previous phase (x buffer reuse)
+        // ---- phase entry: the CTA's warps are done with the previous phase (x buffer reuse). While
+        //      the previous phase finishes elsewhere, tabulate where x's producer partials live.
         __syncthreads();
+        if (P.src >= 0) {
+            const PhaseDev& S = a.ph[P.src];
+            for (int j = threadIdx.x; j < P.K / 64; j += kThreads) {
+                const int q = (P.src_col >> 6) + j;
+                int cf, cl;
+                quad_ctas(S, q, C, cf, cl);
+                sh.cut[j] = make_int2((int)slot_f(a, S, P.src, q, 0), cl - cf + 1);
+            }
+        }
         if (threadIdx.x == 0) {
             if (P.sync_before) spin_until(a.done + (p - 1), (unsigned)C, a.err);
             sh.rs_prev = sh.rs;
@@ -665,8 +723,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         const float rs_prev = sh.rs_prev;
         const uint32_t tag0 = sh.tag0;
         // ---- stage x (polls the producers' slots) and its RMS scale
-        const bool rms = (P.flags & G4Q_QMM_RMS_SCALE) != 0;
-        float ss = stage_x<kTP>(a, P, xs, C, rs_prev, tag0, rms);
+        const bool rms = (phase_flags(a, P) & G4Q_QMM_RMS_SCALE) != 0;
+        float ss = stage_x<kTP>(a, P, xs, sh.cut, C, rs_prev, tag0, rms);
+        if (p == 0) {   // first weight loads only now: the x loads above are not queued behind them
+            for (int s = 0; s < kStages && pre.p < a.n_phases; ++s) {
+                if (lane == 0) pre.issue(ring_s + s * kUnitBytes, bar0 + 8 * s);
+                pre.next(a, cta, C, warp);
+            }
+        }
         if (rms) {
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
@@ -754,7 +818,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             claim = __shfl_sync(0xffffffffu, claim, 0);
             if (claim) write_back_warp<kTP>(a, p - 1, cta, C, rs_prev, tag0);
         }
-        const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
+        const bool argmax = (phase_flags(a, P) & G4Q_PHASE_ARGMAX) != 0;
         if (argmax) {
             unsigned long long kk = best;
 #pragma unroll
@@ -782,9 +846,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             }
         }
     }
-    // ---- a plan that ends with a regular phase: finish its unfinished quads
+    // ---- a plan that ends with a regular phase: once every CTA has left its partials, finish the
+    //      quads no single CTA finished
     const int last = a.n_phases - 1;
-    if (!(a.ph[last].flags & G4Q_PHASE_ARGMAX)) {
+    if (!(phase_flags(a, a.ph[last]) & G4Q_PHASE_ARGMAX)) {
+        __syncthreads();
+        if (threadIdx.x == 0) spin_until(a.done + last, (unsigned)C, a.err);
         __syncthreads();
         if (threadIdx.x < 32) write_back_warp<kTP>(a, last, cta, C, sh.rs, sh.tag0);
     }
@@ -795,7 +862,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         if (prev == (unsigned)C - 1) {
             unsigned long long k = atomicExch(a.key, 0ull);
             if constexpr (kTP) k = exchange_keys(a, k, phase_tag(sh.tag0, a.n_phases));
-            if (a.ph[last].flags & G4Q_PHASE_ARGMAX) {
+            if (phase_flags(a, a.ph[last]) & G4Q_PHASE_ARGMAX) {
                 if (a.tokens) a.tokens[0] = (int32_t)key_index(k);
                 if (a.values) a.values[0] = key_value(k);
                 if (a.keys_out) a.keys_out[0] = k;
@@ -899,6 +966,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
         d.sync_before = 0;
         d.need_done = (fl & G4Q_PHASE_ARGMAX) ? 1 : 0;
         if (d.U < sms) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too small for a full-grid decode plan");
+        if (d.G > kMaxXQuads) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "K above 16384");
         if ((uint64_t)(d.U + 1) * (uint64_t)sms >= (1ull << 32) || (uint64_t)w->N * (uint64_t)w->K / 2 >= (1ull << 32))
             throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too many units for 32-bit partition arithmetic");
         // a CTA range (at most ceil(U/C) units) touches at most (ceil(U/C) + G - 2) / G + 1 quads
@@ -956,10 +1024,13 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
                             "phase " + std::to_string(i) + ": the next phase must read all of an allreduce output");
     for (int i = 1; i < n; ++i)
         if (ph[i].sync_before) ph[i - 1].need_done = 1;
+    ph[n - 1].need_done = 1;   // the final write-back (or the argmax publish) waits for the last phase
     int64_t buf_words = 0;
     for (int i = 0; i < n; ++i)
         buf_words = std::max<int64_t>(buf_words, ph[i].src_ranks > 1 ? (int64_t)ph[i].Q * ph[i].src_ranks * ph[i].ks * 64
                                                                       : (int64_t)ph[i].Q * ph[i].ks * 32);
+    if ((int64_t)kSlotBufs * buf_words * 2 >= (1ll << 31))
+        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: slot buffers above 2^31 floats");
     auto* plan = new DecodePlan();
     plan->device = dev;
     plan->n_phases = n;
@@ -997,7 +1068,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     plan->peer_slots[rank] = plan->d_slots;
     plan->peer_xkeys[rank] = plan->d_xkeys;
     upload_peers(plan);
-    check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan->smem),
+    check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_dynamic_smem(kfn)),
                "cudaFuncSetAttribute(decode)");
     int per_sm = 0;
     check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kThreads, plan->smem),
@@ -1057,7 +1128,7 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     for (int r = 0; r < plan->n_ranks; ++r)
         if (!plan->peer_slots[r] || !plan->peer_xkeys[r])
             throw Error(G4Q_ERR_INVALID_ARGUMENT, "tensor-parallel plan: peer buffers not set");
-    DecodeArgs a;
+    DecodeArgs a{};   // value-initialised: direct = 0, no per-call x / y overrides
     a.ph = plan->d_ph;
     a.n_phases = plan->n_phases;
     a.eps = eps;
@@ -1093,6 +1164,128 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
         check_cuda(cudaLaunchKernelEx(&cfg, decode_kernel<true>, a), "cudaLaunchKernelEx(decode)");
     else
         check_cuda(cudaLaunchKernelEx(&cfg, decode_kernel<false>, a), "cudaLaunchKernelEx(decode)");
+}
+
+// ---- direct launches: one standalone quantized matmul (M = 1) through the same kernel ----------
+// g4q_qmm / g4q_qmm_ex at M = 1 on a weight that suits the persistent kernel run it as a one-phase
+// plan. The phase descriptor is cached on the weight when it is loaded and the per-device scratch
+// (counters, slots) is sized then, so a call allocates nothing. Calls on one device share that
+// scratch: they run in stream order, like every other call that shares a stream.
+
+namespace {
+struct DirectScratch {
+    unsigned int* done = nullptr;   // [3]: phase counter, exit counter, launch counter
+    unsigned long long* key = nullptr;
+    float* slots = nullptr;
+    int64_t slot_floats = 0;
+    unsigned long long** peers = nullptr;
+};
+std::mutex g_direct_mu;
+DirectScratch g_direct[64];
+
+size_t direct_smem(int64_t K) { return (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4 + (size_t)(K + 8) * 2; }
+}  // namespace
+
+void direct_prepare(Weight& w) {
+    const int sms = device_sm_count();
+    const int64_t N = w.N, K = w.K;
+    bool ok = w.fast_ok && w.small_scales && N % 64 == 0 && K % 64 == 0;
+    const int64_t Q = N / 64, G = K / 64, U = Q * G;
+    ok = ok && U >= sms && (uint64_t)(U + 1) * (uint64_t)sms < (1ull << 32) &&
+         (uint64_t)N * (uint64_t)K / 2 < (1ull << 32) && (U + sms - 1) / sms + G - 2 < (kMaxCtaQuads - 1) * G &&
+         direct_smem(K) <= max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel<false>));
+    int ks = 1;
+    if (ok)
+        for (int64_t q = 0; q < Q; ++q) {
+            const int64_t cf = (q * G + 1) * sms - 1, cl = ((q + 1) * G) * sms - 1;
+            ks = std::max<int>(ks, (int)(cl / U - cf / U + 1));
+        }
+    ok = ok && ks <= kSlots;
+    if (!ok) {
+        cudaFree(w.d_phase);
+        w.d_phase = nullptr;
+        return;
+    }
+    PhaseDev d{};
+    d.packed = w.packed;
+    d.sb = w.sb;
+    d.N = (int)N;
+    d.K = (int)K;
+    d.R = (int)(N / 16);
+    d.G = (int)G;
+    d.Q = (int)Q;
+    d.U = (int)U;
+    d.src = -1;
+    d.src_ranks = 1;
+    d.ks = ks;
+    d.need_done = 1;
+    if (!w.d_phase) check_cuda(cudaMalloc(&w.d_phase, sizeof(PhaseDev)), "direct phase descriptor");
+    check_cuda(cudaMemcpy(w.d_phase, &d, sizeof(PhaseDev), cudaMemcpyHostToDevice), "direct phase descriptor");
+    std::lock_guard<std::mutex> lock(g_direct_mu);
+    DirectScratch& ds = g_direct[w.device];
+    if (!ds.done) {
+        check_cuda(cudaMalloc(&ds.done, sizeof(unsigned int) * 3), "direct scratch");
+        check_cuda(cudaMemset(ds.done, 0, sizeof(unsigned int) * 3), "direct scratch");
+        check_cuda(cudaMalloc(&ds.key, sizeof(unsigned long long)), "direct scratch");
+        check_cuda(cudaMemset(ds.key, 0, sizeof(unsigned long long)), "direct scratch");
+        check_cuda(cudaMalloc(&ds.peers, sizeof(void*) * 2 * kMaxRanks), "direct scratch");
+        check_cuda(cudaMemset(ds.peers, 0, sizeof(void*) * 2 * kMaxRanks), "direct scratch");
+        check_cuda(cudaFuncSetAttribute(decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel<false>))),
+                   "cudaFuncSetAttribute(decode)");
+    }
+    const int64_t need = Q * ks * 64;
+    if (need > ds.slot_floats) {
+        check_cuda(cudaDeviceSynchronize(), "direct scratch");
+        cudaFree(ds.slots);
+        ds.slots = nullptr;
+        ds.slot_floats = 0;
+        check_cuda(cudaMalloc(&ds.slots, sizeof(float) * (size_t)need), "direct scratch");
+        ds.slot_floats = need;
+    }
+}
+
+void direct_release(Weight& w) {
+    cudaFree(w.d_phase);
+    w.d_phase = nullptr;
+}
+
+bool direct_ready(const Weight& w, const void* y) {
+    return w.d_phase != nullptr && (reinterpret_cast<uintptr_t>(y) & 7u) == 0;
+}
+
+void launch_direct(const Weight& w, const uint16_t* x, void* y, uint32_t flags, float eps, cudaStream_t st) {
+    DirectScratch& ds = g_direct[w.device];
+    DecodeArgs a{};
+    a.ph = static_cast<const PhaseDev*>(w.d_phase);
+    a.n_phases = 1;
+    a.eps = eps;
+    a.done = ds.done;
+    a.exit_count = ds.done + 1;
+    a.run = ds.done + 2;
+    a.key = ds.key;
+    a.slots = reinterpret_cast<unsigned long long*>(ds.slots);
+    a.peer_slots = ds.peers;
+    a.peer_xkeys = ds.peers + kMaxRanks;
+    a.rank = 0;
+    a.n_ranks = 1;
+    a.buf_words = ds.slot_floats / 2;
+    a.err = device_scratch().err;
+    a.direct = 1;
+    a.dx = x;
+    a.dy = y;
+    a.dflags = flags;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(device_sm_count());
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = direct_smem(w.K);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    check_cuda(cudaLaunchKernelEx(&cfg, decode_kernel<false>, a), "cudaLaunchKernelEx(decode, direct)");
 }
 
 }  // namespace g4q

@@ -107,6 +107,37 @@ def test_decode_plan_single_launch(cuda, oracle):
     st.free()
 
 
+def test_decode_plan_regular_last_phase(cuda, oracle):
+    """A plan that ends with a plain matmul (no argmax): y1 = rms(x) * x W1^T, y2 = y1 W2^T. The last
+    phase's cut quads are written back after every CTA has finished it."""
+    from helios_b200 import _lib
+    from helios_b200 import quantized as Q
+    N1, K1, N2 = 2048, 2048, 1536
+    mats = [oracle.synth_matrix(oracle.matrix_seed(5, i), n, k) for i, (n, k) in enumerate(((N1, K1), (N2, N1)))]
+    ws = [Q.QuantizedWeight.from_mlx(torch.from_numpy(w.view(np.int32)).view(torch.uint32),
+                                     torch.from_numpy(s.view(np.int16)).view(torch.bfloat16),
+                                     torch.from_numpy(b.view(np.int16)).view(torch.bfloat16)) for w, s, b in mats]
+    x = Q.synth_normal(oracle.activation_seed(41), (1, K1))
+    y1 = torch.empty((1, N1), dtype=torch.bfloat16, device=cuda)
+    y2 = torch.empty((1, N2), dtype=torch.bfloat16, device=cuda)
+    plan = Q.DecodePlan([(ws[0], x, y1, Q.QMM_RMS_SCALE), (ws[1], y1, y2, 0)], 1)
+    for _ in range(2):
+        y2.fill_(float("nan"))
+        plan.run(1)
+        torch.cuda.synchronize()
+        assert _lib.device_error() == 0
+        r = np.array([oracle.rms_scale(u16(x)[0], 1e-6)], dtype=np.float32)
+        ref1 = oracle.qmm(u16(x), *mats[0], row_scale=r)[0]
+        ex, rms = qmm_error(oracle.bf16_to_f32(u16(y1)), ref1, True)
+        assert ex <= 1e-2 * rms
+        ref2 = oracle.qmm(u16(y1), *mats[1])[0]     # the second phase from the first phase's own output
+        ex, rms = qmm_error(oracle.bf16_to_f32(u16(y2)), ref2, True)
+        assert ex <= 1e-2 * rms
+    plan.free()
+    for w in ws:
+        w.free()
+
+
 def test_decode_plan_rejects_bad_phases(cuda, oracle):
     from helios_b200 import _lib
     from helios_b200 import quantized as Q
