@@ -3,18 +3,20 @@
 // Replaces mlx::core::quantized_matmul at the prefill call sites (native_model.cc:802-949 via
 // forward_hidden / decode_block_hidden, :1682-1780; chunk loop :1819-1841).
 //
-// One CTA computes a 128-token x 256-row tile of y = x . deq(W)^T (cta_group::1, no clusters,
+// One CTA computes a 256-token x 256-row tile of y = x . deq(W)^T (cta_group::1, no clusters,
 // every copy private to its CTA), warp-specialised over a 3-stage mbarrier pipeline with one 64-wide
-// quantization group per k-step:
-//   warp 0      TMA producer: x tile [128 x 64] bf16 (tensor map, SWIZZLE_128B), the 8 KB packed
+// quantization group per k-step. Every dequantized weight tile feeds two M=128 MMAs (the two token
+// halves), so the CUDA-core dequant work per tensor-core FLOP is half that of a 128-token tile:
+//   warp 0      TMA producer: x tile [256 x 64] bf16 (tensor map, SWIZZLE_128B), the 8 KB packed
 //               tile of 16 layout-v1 blocks (tensor map over 128-byte rows, SWIZZLE_128B so the
 //               dequant reads are bank-conflict free) and the 1 KB scale|bias words.
-//   warps 2..5  dequant: packed nibbles -> bit-exact bf16 (chain R2, two bf16x2 ops per pair) written
-//               straight into the canonical K-major SWIZZLE_128B layout of the B operand, then a
-//               generic->async proxy fence and an mbarrier arrive.
-//   warp 1      allocates 256 TMEM columns; one thread issues 4 x tcgen05.mma (M=128, N=256, K=16,
-//               bf16 x bf16 -> fp32 in TMEM) per k-step and tcgen05.commit frees the stage.
-//   warps 2..5  epilogue: tcgen05.ld 32x32b.x32 -> optional RMS row scale -> bf16/fp32 -> global.
+//   warps 2..9  dequant, one weight row per thread: packed nibbles -> bit-exact bf16 (chain R2, two
+//               bf16x2 ops per pair) written straight into the canonical K-major SWIZZLE_128B
+//               layout of the B operand, then a generic->async proxy fence and an mbarrier arrive.
+//   warp 1      allocates all 512 TMEM columns (two 128 x 256 fp32 accumulators); one thread
+//               issues 2 x 4 tcgen05.mma (M=128, N=256, K=16, bf16 x bf16 -> fp32) per k-step and
+//               tcgen05.commit frees the stage.
+//   warps 2..9  epilogue: tcgen05.ld 32x32b.x32 -> optional RMS row scale -> bf16/fp32 -> global.
 // Every mbarrier wait is bounded (clock64 limit); a timeout records an error code in a device word
 // (read with g4q_device_error) and the CTA still runs to its end and frees its TMEM.
 #include <cuda.h>
@@ -28,19 +30,20 @@
 namespace g4q {
 namespace {
 
-constexpr int BM = 128;
+constexpr int BM = 256;                       // two M=128 MMA halves
 constexpr int BN = 256;
 constexpr int BK = 64;
 constexpr int STAGES = 3;
-constexpr int kDequantWarps = 4;
+constexpr int kDequantWarps = 8;
 constexpr int kGemmThreads = (2 + kDequantWarps) * 32;
-constexpr uint32_t kXBytes = BM * BK * 2;     // 16 KB
+constexpr uint32_t kXBytes = BM * BK * 2;     // 32 KB (two 16 KB halves of 128 rows)
 constexpr uint32_t kBBytes = BN * BK * 2;     // 32 KB
 constexpr uint32_t kPBytes = BN * BK / 2;     // 8 KB
 constexpr uint32_t kSBBytes = BN * 4;         // 1 KB
 constexpr uint32_t kStageBytes = kXBytes + kBBytes + kPBytes + kSBBytes;
 constexpr uint32_t kSmemBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kXHalf = 128 * BK * 2;      // bytes of one 128-row half of the x tile
 constexpr long long kWaitLimitCycles = 4000000000ll;   // ~2 s at 2 GHz
 
 struct GemmParams {
@@ -113,7 +116,7 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
 }
 
 // kind::f16 instruction descriptor: D f32, A bf16, B bf16, both K-major, N = 256, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
     asm volatile(
@@ -214,9 +217,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (lane == 0) {
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; ++kk) {
-                    const uint64_t ad = umma_desc_sw128(sX + s * kXBytes + kk * 32);
                     const uint64_t bd = umma_desc_sw128(sB + s * kBBytes + kk * 32);
-                    umma_bf16(tmem, ad, bd, (kb | kk) != 0);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {   // token rows 0-127 -> columns 0-255, 128-255 -> 256-511
+                        const uint64_t ad = umma_desc_sw128(sX + s * kXBytes + h * kXHalf + kk * 32);
+                        umma_bf16(tmem + (uint32_t)(h * BN), ad, bd, (kb | kk) != 0);
+                    }
                 }
                 umma_commit(empty(s));
             }
@@ -225,10 +231,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) umma_commit(accum);
         __syncwarp();
     } else {
-        // ---------------- dequant warps (threads 64..191), then epilogue
+        // ---------------- dequant warps (threads 64..319), one weight row each, then epilogue
         const int d = threadIdx.x - 64;
-        const int rl = d >> 3, gi = d & 7;        // 16-row tile and row pair of this thread
-        const int n0l = 16 * rl + gi, n1l = n0l + 8;
+        const int rl = (d & 127) >> 3, gi = d & 7, half = d >> 7;   // 16-row tile, row pair, row of the pair
+        const int nl = 16 * rl + gi + 8 * half;
         for (int kb = 0; kb < p.KB; ++kb) {
             const int s = kb % STAGES;
             mbar_wait(full(s), (kb / STAGES) & 1, p.err, 4);
@@ -242,41 +248,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 wv[t] = lds128(sP + s * kPBytes + rho * 128 + ((ch ^ (rho & 7)) << 4));
             }
             const uint32_t* sbs = sbw + s * (kSBBytes / 4);
-            const RowConsts c0 = row_consts(sbs[n0l]), c1 = row_consts(sbs[n1l]);
-            const uint32_t bbase = sB + s * kBBytes;
+            const RowConsts c = row_consts(sbs[nl]);
+            const uint32_t bbase = sB + s * kBBytes + nl * 128;
+            const int sh0 = 4 * half;   // row n0 uses nibble slots 0/2, row n1 slots 1/3
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                uint32_t q[4][4];  // [t][pair]
+                uint32_t q[4][2];   // [t][lo/hi eight of the k16 step]
 #pragma unroll
                 for (int t = 0; t < 4; ++t) {
-                    const uint32_t w = j == 0 ? wv[t].x : j == 1 ? wv[t].y : j == 2 ? wv[t].z : wv[t].w;
-                    q[t][0] = deq_r2_fast(lop_nibbles(w), c0);
-                    q[t][1] = deq_r2_fast(lop_nibbles(w >> 4), c1);
-                    q[t][2] = deq_r2_fast(lop_nibbles(w >> 8), c0);
-                    q[t][3] = deq_r2_fast(lop_nibbles(w >> 12), c1);
+                    const uint32_t w = (j == 0 ? wv[t].x : j == 1 ? wv[t].y : j == 2 ? wv[t].z : wv[t].w) >> sh0;
+                    q[t][0] = deq_r2_fast(lop_nibbles(w), c);
+                    q[t][1] = deq_r2_fast(lop_nibbles(w >> 8), c);
                 }
                 // row n: chunk (2j) holds k 16j..16j+7, chunk (2j+1) holds k 16j+8..16j+15
                 const uint32_t c_lo = 2 * j, c_hi = 2 * j + 1;
-                sts128(bbase + n0l * 128 + ((c_lo ^ (n0l & 7)) << 4), make_uint4(q[0][0], q[1][0], q[2][0], q[3][0]));
-                sts128(bbase + n0l * 128 + ((c_hi ^ (n0l & 7)) << 4), make_uint4(q[0][2], q[1][2], q[2][2], q[3][2]));
-                sts128(bbase + n1l * 128 + ((c_lo ^ (n1l & 7)) << 4), make_uint4(q[0][1], q[1][1], q[2][1], q[3][1]));
-                sts128(bbase + n1l * 128 + ((c_hi ^ (n1l & 7)) << 4), make_uint4(q[0][3], q[1][3], q[2][3], q[3][3]));
+                sts128(bbase + ((c_lo ^ (nl & 7)) << 4), make_uint4(q[0][0], q[1][0], q[2][0], q[3][0]));
+                sts128(bbase + ((c_hi ^ (nl & 7)) << 4), make_uint4(q[0][1], q[1][1], q[2][1], q[3][1]));
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(bfull(s));
         }
-        // ---------------- epilogue: TMEM lane quarter = warp % 4
+        // ---------------- epilogue: TMEM lane quarter = warp % 4; warps 2..5 read the accumulator of
+        //                  token rows 0-127, warps 6..9 that of rows 128-255 (columns 256..511)
         mbar_wait(accum, 0, p.err, 5);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int quarter = warp & 3;
-        const int row = m0 + quarter * 32 + lane;
+        const int quarter = warp & 3, hm = (warp - 2) >> 2;
+        const int row = m0 + hm * 128 + quarter * 32 + lane;
         const bool f32 = (p.flags & G4Q_QMM_OUT_F32) != 0;
         const float scale = (p.rms != nullptr && row < p.M) ? p.rms[row] : 1.0f;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
             uint32_t v[32];
-            tmem_ld_32x32b_x32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32), v);
+            tmem_ld_32x32b_x32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(hm * BN + c * 32), v);
             const int ncol = n0 + c * 32;
             if (row >= p.M || ncol >= p.N) continue;
             if (f32) {
