@@ -51,7 +51,16 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--prefill-tokens", type=int, default=2048, help="chunk size of the prefill measurement (0: skip)")
     return p.parse_args()
+
+
+def sustained_tflops() -> float:
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return float(d.get("bf16_tflops_sustained", d["bf16_tflops"]))
+    return 1400.0
 
 
 def measured_peaks():
@@ -252,6 +261,35 @@ def main():
     clk = clocks.stop() if rank == 0 else None
     tok, _ = decode_keys(key_host)
 
+    # ---- chunked prefill (BASELINE config 5 chunk): P tokens through all layers on the tcgen05
+    #      GEMM path, then the LM head on the last row; whole-job TFLOP/s, max over ranks
+    prefill = None
+    if args.prefill_tokens > 0:
+        P = args.prefill_tokens
+        hp = synth_normal(activation_seed(1), (P, cfg.hidden), device=dev)
+        st.prefill(hp)
+        torch.cuda.synchronize()
+        barrier()
+        reps = 2
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record()
+        for _ in range(reps):
+            st.prefill(hp)
+        p1.record()
+        torch.cuda.synchronize()
+        barrier()
+        pms = max_over_ranks(p0.elapsed_time(p1)) / reps
+        _, tf_burst, _ = measured_peaks()
+        tf_sus = sustained_tflops()
+        tflops = st.prefill_flops(P) / (pms * 1e-3) / 1e12
+        prefill = {"tokens": P, "layers": cfg.layers, "ms_per_chunk": round(pms, 3), "tflops": round(tflops, 1),
+                   "unit": "TFLOP/s", "peak_sustained": tf_sus, "frac_of_sustained": round(tflops / tf_sus, 4),
+                   "peak_burst": tf_burst, "frac_of_burst": round(tflops / tf_burst, 4),
+                   "path": "per-matmul: tcgen05 dequant-GEMM for every projection"
+                           + (", NCCL allreduce of fp32 partials after o/down" if world > 1 else "")
+                           + ", LM head on the last row",
+                   "gpu_launches_per_chunk": 6 * cfg.layers + 1}   # q|k|v, gate|up: RMS rows + GEMM
+
     hbm_peak, tf_peak, peak_kind = measured_peaks()
     # the dominant (only) kernel is the persistent decode kernel: one launch per step per rank
     kname = "decode_kernel (persistent: 48x{q|k|v, o, gate|up, down} + LM head, one launch per rank)"
@@ -292,6 +330,8 @@ def main():
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if prefill is not None:
+            line["prefill"] = prefill
         print(json.dumps(line), flush=True)
     del graph
     barrier()

@@ -140,11 +140,12 @@ class SyntheticStack:
         self.values = torch.empty(M, dtype=torch.float32, device=dev)
         self.keys = torch.empty(M, dtype=torch.int64, device=dev)
 
-    def _row_parallel(self, w: QuantizedWeight, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    def _row_parallel(self, w: QuantizedWeight, x: torch.Tensor, out: torch.Tensor, part=None) -> torch.Tensor:
         if self.size == 1:
             return quantized_matmul(x, w, out=out)
-        quantized_matmul(x, w, out_dtype=torch.float32, out=self.part[: x.shape[0]])
-        p = self.part[: x.shape[0]]
+        part = self.part if part is None else part
+        quantized_matmul(x, w, out_dtype=torch.float32, out=part[: x.shape[0]])
+        p = part[: x.shape[0]]
         torch.distributed.all_reduce(p, group=self.group)
         out.copy_(p)
         return out
@@ -162,6 +163,35 @@ class SyntheticStack:
             gu = quantized_matmul(o, L["gu"], rms_scale=True, eps=c.eps, out=self.gu_out[:M])
             x = self._row_parallel(L["down"], gu[:, self.ni:], self.h_out[:M])
         return self.head(x)
+
+    def prefill(self, h: torch.Tensor):
+        """One chunked-prefill chunk: M tokens through every layer's quantized
+        linears on the tcgen05 GEMM (M > 16), then the LM head on the chunk's last row only.
+        Uses its own activation buffers (the decode buffers stay baked into the plan).
+        Returns (key of the last row, h)."""
+        M = h.shape[0]
+        c, dev = self.cfg, self.device
+        pb = getattr(self, "_pre", None)
+        if pb is None or pb["M"] < M:
+            pb = {"M": M,
+                  "qkv": torch.empty((M, self.nq + 2 * self.nkv), dtype=torch.bfloat16, device=dev),
+                  "o": torch.empty((M, c.hidden), dtype=torch.bfloat16, device=dev),
+                  "gu": torch.empty((M, 2 * self.ni), dtype=torch.bfloat16, device=dev),
+                  "h": torch.empty((M, c.hidden), dtype=torch.bfloat16, device=dev),
+                  "part": torch.empty((M, c.hidden), dtype=torch.float32, device=dev)}
+            self._pre = pb
+        x = h
+        for L in self.layers:
+            qkv = quantized_matmul(x, L["qkv"], rms_scale=True, eps=c.eps, out=pb["qkv"][:M])
+            o = self._row_parallel(L["o"], qkv[:, : self.nq], pb["o"][:M], part=pb["part"])
+            gu = quantized_matmul(o, L["gu"], rms_scale=True, eps=c.eps, out=pb["gu"][:M])
+            x = self._row_parallel(L["down"], gu[:, self.ni:], pb["h"][:M], part=pb["part"])
+        key, _ = self.head(x[M - 1:M])
+        return key, x
+
+    def prefill_flops(self, M: int) -> int:
+        """Whole-job FLOPs of one prefill chunk of M tokens (all ranks; LM head on one row)."""
+        return self.cfg.flops_per_token() * M + 2 * self.cfg.vocab * self.cfg.hidden
 
     def build_plan(self, max_tokens: int = 1) -> DecodePlan:
         """The whole decode step (48 x 4 matmuls + LM head argmax) as one persistent-kernel plan.
