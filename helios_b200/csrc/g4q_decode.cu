@@ -8,7 +8,7 @@
 //
 // Why one kernel: at batch 1 every phase is a few microseconds of HBM streaming, so separate
 // launches spend a large share of the step in prologues (staging x) and epilogues (reductions,
-// tails). Here one cooperative grid (one 16-warp CTA per SM) stays resident for the whole step:
+// tails). Here one cooperative grid (one 20-warp CTA per SM) stays resident for the whole step:
 //  * every warp streams its weight units (64 rows x one 64-wide group: 2 KB of packed words +
 //    256 B of scale|bias) through a private ring of cp.async.bulk buffers that runs ahead ACROSS
 //    phase boundaries, so the next phase's weights land while the grid finishes the current one;
@@ -42,9 +42,9 @@
 namespace g4q {
 namespace {
 
-constexpr int kWarps = 16;
+constexpr int kWarps = 20;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr uint32_t kUnitPacked = 4 * 512;
 constexpr uint32_t kUnitSb = 64 * 4;
 constexpr uint32_t kUnitBytes = kUnitPacked + kUnitSb;
@@ -548,10 +548,10 @@ __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P,
             return ss;
         }
     }
-    // single-rank partials: four cells per thread with up to four slots each in flight at once,
+    // single-rank partials: two cells per thread with up to four slots each in flight at once,
     // summed in slot order exactly as sum_slots4 does
     const float* sl = reinterpret_cast<const float*>(a.slots);
-    constexpr int kB = 4;
+    constexpr int kB = 2;
     for (int e0 = threadIdx.x; e0 < cells; e0 += kB * kThreads) {
         const float* base[kB];
         int nc[kB];
