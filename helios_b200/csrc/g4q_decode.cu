@@ -20,10 +20,12 @@
 //    staging its x, so a phase starts on an SM as soon as its inputs exist and no SM ever waits
 //    for a whole-grid barrier. Tags are unique per (launch, phase); slot buffers rotate over three
 //    phases, which the host proves safe (or falls back to a barrier) when the plan is made;
-//  * tensor parallel plans (one process per GPU): a row-parallel phase (G4Q_PHASE_ALLREDUCE) stores
-//    its partials into the slot buffers of every rank over NVLink (peer stores), so the allreduce
-//    after o/down costs no separate collective: consumers on every rank sum the same partials in
-//    the same order. The LM-head keys are exchanged the same way at the end of the step;
+//  * tensor parallel plans (one process per GPU): after a row-parallel phase (G4Q_PHASE_ALLREDUCE)
+//    each rank sums its CTAs' partials of a quad once (the CTA that owns the quad's write-back) and
+//    stores that rank partial, tagged, into every rank's rank-partial buffer over NVLink (peer
+//    stores); consumers on every rank poll the tags and add the ranks' partials in rank order, so
+//    the allreduce after o/down needs no separate collective and every rank sees the same bits.
+//    The LM-head keys are exchanged the same way at the end of the step;
 //  * the argmax phase keeps 64-bit keys (order-preserving logit bits | ~row); its cut quads are
 //    finished by the last contributing CTA (slot + arrival counter), and the last CTA to finish
 //    publishes tokens/values/keys. The last CTA to leave resets the counters and advances the
@@ -83,11 +85,13 @@ struct DecodeArgs {
     unsigned int* exit_count;                 // [1]
     unsigned int* run;                        // [1] launches so far (tag base)
     unsigned long long* key;                  // running argmax key of this rank
-    unsigned long long* slots;                // this rank's slot buffers
-    unsigned long long* const* peer_slots;    // [n_ranks] slot buffers of every rank (device array)
+    unsigned long long* slots;                // this rank's slot buffers (fp32 partials of its CTAs)
+    unsigned long long* rp;                   // this rank's rank-partial buffers (tagged, written by all ranks)
+    unsigned long long* const* peer_rp;       // [n_ranks] rank-partial buffers of every rank (device array)
     unsigned long long* const* peer_xkeys;    // [n_ranks] key exchange arrays ([n_ranks][2]) of every rank
     int rank, n_ranks;
     int64_t buf_words;                        // words per slot buffer
+    int64_t rp_words;                         // words per rank-partial buffer
     int* qcount;                              // arrival counters of the argmax phase's cut quads
     int32_t* tokens;
     float* values;
@@ -160,15 +164,15 @@ __device__ __forceinline__ uint32_t phase_tag(uint32_t tag0, int p) {
     return t + 1u;
 }
 
-// Slots of a phase live in buffer p mod 3. A single-rank phase keeps plain fp32 partials: float
-// index of (quad q, source CTA c, row 0). An allreduce phase keeps tagged 64-bit words: word index
-// of (quad q, source rank r, source CTA c, row 0).
+// Slots of a phase live in buffer p mod 3: plain fp32 partials, float index of (quad q, source
+// CTA c, row 0).
 __device__ __forceinline__ int64_t slot_f(const DecodeArgs& a, const PhaseDev& P, int p, int q, int c) {
     return (int64_t)(p % kSlotBufs) * a.buf_words * 2 + (int64_t)q * P.ks * 64 + (int64_t)c * 64;
 }
 
-__device__ __forceinline__ int64_t slot_word(const DecodeArgs& a, const PhaseDev& P, int p, int q, int r, int c) {
-    return (int64_t)(p % kSlotBufs) * a.buf_words + ((int64_t)q * P.src_ranks + r) * P.ks * 64 + (int64_t)c * 64;
+// Rank partials of an allreduce phase: word index of (quad q, rank r, row 0) of phase p.
+__device__ __forceinline__ int64_t rp_word(const DecodeArgs& a, int p, int q, int r) {
+    return (int64_t)(p % kSlotBufs) * a.rp_words + ((int64_t)q * a.n_ranks + r) * 64;
 }
 
 // Warp w owns the contiguous units [wstart(w), wstart(w + 1)) of its CTA's n units of a phase
@@ -275,16 +279,6 @@ __device__ __forceinline__ void spin_until(const unsigned int* ctr, unsigned int
     }
 }
 
-// One tagged slot word: the fp32 partial in the low half, the phase tag in the high half, written
-// and read as single 64-bit accesses so a reader that sees the tag sees the value with it.
-__device__ __forceinline__ void st_slot(unsigned long long* p, float v, uint32_t tag, bool sys) {
-    const unsigned long long w = (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
-    if (sys)
-        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-    else
-        asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-
 __device__ __forceinline__ void ld_slot2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
     asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
@@ -363,14 +357,20 @@ __device__ __noinline__ float4 sum_tagged4(const unsigned long long* q0, int ran
     }
 }
 
-// An allreduce phase's CTA partial of one quad (two rows per lane) into the slot buffers of every
-// rank (peer stores over NVLink for the others).
-__device__ __noinline__ void store_allreduce(unsigned long long* const* peers, int n_ranks, int64_t w0, float v0,
-                                             float v1, uint32_t tag) {
+// After an allreduce phase: this rank's partial of quad q (its CTAs' slots summed in CTA order,
+// four rows per lane of 16 lanes) stored, tagged, into the rank-partial buffer of every rank.
+__device__ __noinline__ void send_rank_partial(unsigned long long* const* peers, int n_ranks, int64_t w0,
+                                               const float* slots, int nc, uint32_t tag) {
+    const int lane = threadIdx.x & 31;
+    if (lane >= 16) return;
+    const float4 s = sum_slots4(slots + lane * 4, nc);
+    const unsigned long long t = (unsigned long long)tag << 32;
+    const unsigned long long e0 = __float_as_uint(s.x) | t, e1 = __float_as_uint(s.y) | t;
+    const unsigned long long e2 = __float_as_uint(s.z) | t, e3 = __float_as_uint(s.w) | t;
     for (int r = 0; r < n_ranks; ++r) {
-        unsigned long long* dst = peers[r] + w0;
-        st_slot(dst, v0, tag, true);
-        st_slot(dst + 32, v1, tag, true);
+        unsigned long long* dst = peers[r] + w0 + lane * 4;
+        asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(e0), "l"(e1) : "memory");
+        asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + 2), "l"(e2), "l"(e3) : "memory");
     }
 }
 
@@ -448,18 +448,13 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
 #pragma unroll
         for (int h = 0; h < 2; ++h)
             best = fold_logit(a.logits, a.softcap, a.row_offset, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs), best);
-    } else if (kTP && P.src_ranks > 1) {
-        int cf, cl;
-        quad_ctas(P, q, C, cf, cl);
-        store_allreduce(a.peer_slots, a.n_ranks, slot_word(a, P, p, q, a.rank, cta - cf) + lane, v[0], v[1],
-                        phase_tag(sh.tag0, p));
     } else {
         int cf, cl;
         quad_ctas(P, q, C, cf, cl);
         float* base = reinterpret_cast<float*>(a.slots) + slot_f(a, P, p, q, 0);
 #pragma unroll
         for (int h = 0; h < 2; ++h) base[(size_t)(cta - cf) * 64 + lane + 32 * h] = v[h];
-        if (whole) {
+        if (whole && P.src_ranks == 1) {   // an allreduce phase's y needs every rank: written back later
 #pragma unroll
             for (int h = 0; h < 2; ++h) store_y(phase_y(a, P), fl, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs));
         } else if (argmax) {   // the logits are needed now: the last contributing CTA finishes the quad
@@ -536,14 +531,11 @@ __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P,
         }
     };
     if constexpr (kTP) {
-        if (S.src_ranks > 1) {   // partials of every rank, tagged: poll until they have all arrived
+        if (S.src_ranks > 1) {   // rank partials of every rank, tagged: poll until all have arrived
             const uint32_t tag = phase_tag(tag0, P.src);
             for (int idx = threadIdx.x; idx < cells; idx += kThreads) {
                 const int q = q0 + (idx >> 4);
-                int cf, cl;
-                quad_ctas(S, q, C, cf, cl);
-                put(idx, sum_tagged4(a.slots + slot_word(a, S, P.src, q, 0, 0) + (idx & 15) * 4, S.src_ranks, S.ks,
-                                     cl - cf + 1, tag, a.err));
+                put(idx, sum_tagged4(a.rp + rp_word(a, P.src, q, 0) + (idx & 15) * 4, a.n_ranks, 1, 1, tag, a.err));
             }
             return ss;
         }
@@ -614,8 +606,7 @@ __device__ __forceinline__ void write_back_warp(const DecodeArgs& a, int pp, int
         float4 s;
         if constexpr (kTP) {
             if (Q.src_ranks > 1)
-                s = sum_tagged4(a.slots + slot_word(a, Q, pp, q, 0, 0) + lane * 4, Q.src_ranks, Q.ks, cl - cf + 1, tag,
-                                a.err);
+                s = sum_tagged4(a.rp + rp_word(a, pp, q, 0) + lane * 4, a.n_ranks, 1, 1, tag, a.err);
         }
         if (!kTP || Q.src_ranks == 1)
             s = sum_slots4(reinterpret_cast<const float*>(a.slots) + slot_f(a, Q, pp, q, 0) + lane * 4, cl - cf + 1);
@@ -722,6 +713,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         __syncthreads();
         const float rs_prev = sh.rs_prev;
         const uint32_t tag0 = sh.tag0;
+        if constexpr (kTP) {   // the previous phase was an allreduce phase: send this CTA's rank partials
+            if (p > 0 && warp == 0 && a.ph[p - 1].src_ranks > 1) {
+                const PhaseDev& Q = a.ph[p - 1];
+                for (int q = cta; q < Q.Q; q += C) {
+                    int cf, cl;
+                    quad_ctas(Q, q, C, cf, cl);
+                    send_rank_partial(a.peer_rp, a.n_ranks, rp_word(a, p - 1, q, a.rank),
+                                      reinterpret_cast<const float*>(a.slots) + slot_f(a, Q, p - 1, q, 0), cl - cf + 1,
+                                      phase_tag(tag0, p - 1));
+                }
+            }
+        }
         // ---- stage x (polls the producers' slots) and its RMS scale
         const bool rms = (phase_flags(a, P) & G4Q_QMM_RMS_SCALE) != 0;
         float ss = stage_x<kTP>(a, P, xs, sh.cut, C, rs_prev, tag0, rms);
@@ -888,10 +891,12 @@ struct DecodePlan {
     unsigned int* d_done = nullptr;   // n_phases + 2 (exit counter, launch counter)
     unsigned long long* d_key = nullptr;
     unsigned long long* d_slots = nullptr;
+    unsigned long long* d_rp = nullptr;      // rank partials (tensor parallel), written by every rank
+    int64_t rp_words = 0;
     unsigned long long* d_xkeys = nullptr;   // [kMaxRanks][2]
     int* d_qcount = nullptr;
     unsigned long long** d_peers = nullptr;   // [2][kMaxRanks]: slot buffers, key arrays of every rank
-    unsigned long long* peer_slots[kMaxRanks] = {};
+    unsigned long long* peer_rp[kMaxRanks] = {};
     unsigned long long* peer_xkeys[kMaxRanks] = {};
 };
 
@@ -902,6 +907,7 @@ static void free_plan_memory(DecodePlan* plan) {
     cudaFree(plan->d_done);
     cudaFree(plan->d_key);
     cudaFree(plan->d_slots);
+    cudaFree(plan->d_rp);
     cudaFree(plan->d_xkeys);
     cudaFree(plan->d_qcount);
     cudaFree(plan->d_peers);
@@ -910,7 +916,7 @@ static void free_plan_memory(DecodePlan* plan) {
 static void upload_peers(DecodePlan* plan) {
     unsigned long long* table[2 * kMaxRanks];
     for (int r = 0; r < kMaxRanks; ++r) {
-        table[r] = plan->peer_slots[r];
+        table[r] = plan->peer_rp[r];
         table[kMaxRanks + r] = plan->peer_xkeys[r];
     }
     check_cuda(cudaMemcpy(plan->d_peers, table, sizeof(table), cudaMemcpyHostToDevice), "upload peer pointers");
@@ -1027,8 +1033,10 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     ph[n - 1].need_done = 1;   // the final write-back (or the argmax publish) waits for the last phase
     int64_t buf_words = 0;
     for (int i = 0; i < n; ++i)
-        buf_words = std::max<int64_t>(buf_words, ph[i].src_ranks > 1 ? (int64_t)ph[i].Q * ph[i].src_ranks * ph[i].ks * 64
-                                                                      : (int64_t)ph[i].Q * ph[i].ks * 32);
+        buf_words = std::max<int64_t>(buf_words, (int64_t)ph[i].Q * ph[i].ks * 32);
+    int64_t rp_words = 1;
+    for (int i = 0; i < n; ++i)
+        if (ph[i].src_ranks > 1) rp_words = std::max<int64_t>(rp_words, (int64_t)ph[i].Q * n_ranks * 64);
     if ((int64_t)kSlotBufs * buf_words * 2 >= (1ll << 31))
         throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: slot buffers above 2^31 floats");
     auto* plan = new DecodePlan();
@@ -1038,6 +1046,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     plan->rank = rank;
     plan->n_ranks = n_ranks;
     plan->buf_words = buf_words;
+    plan->rp_words = rp_words;
     plan->smem = (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4 + (size_t)(kmax + 8) * 2;
     const void* kfn = n_ranks > 1 ? reinterpret_cast<const void*>(decode_kernel<true>)
                                   : reinterpret_cast<const void*>(decode_kernel<false>);
@@ -1050,6 +1059,8 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_done, sizeof(unsigned int) * (n + 2));
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_key, sizeof(unsigned long long));
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_slots, slot_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_rp, sizeof(unsigned long long) * kSlotBufs * (size_t)rp_words);
+    if (e == cudaSuccess) e = cudaMemset(plan->d_rp, 0, sizeof(unsigned long long) * kSlotBufs * (size_t)rp_words);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_xkeys, sizeof(unsigned long long) * 2 * kMaxRanks);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_qcount, sizeof(int) * (size_t)max_q);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_peers, sizeof(void*) * 2 * kMaxRanks);
@@ -1065,7 +1076,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
         delete plan;
         check_cuda(e, "decode plan allocation");
     }
-    plan->peer_slots[rank] = plan->d_slots;
+    plan->peer_rp[rank] = plan->d_rp;
     plan->peer_xkeys[rank] = plan->d_xkeys;
     upload_peers(plan);
     check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_dynamic_smem(kfn)),
@@ -1086,8 +1097,8 @@ static DecodePlan* checked_plan(void* h) {
 
 void decode_plan_buffers(void* h, void** slots, uint64_t* slot_bytes, void** xkeys, uint64_t* xkey_bytes) {
     DecodePlan* plan = checked_plan(h);
-    if (slots) *slots = plan->d_slots;
-    if (slot_bytes) *slot_bytes = sizeof(unsigned long long) * kSlotBufs * (uint64_t)plan->buf_words;
+    if (slots) *slots = plan->d_rp;
+    if (slot_bytes) *slot_bytes = sizeof(unsigned long long) * kSlotBufs * (uint64_t)plan->rp_words;
     if (xkeys) *xkeys = plan->d_xkeys;
     if (xkey_bytes) *xkey_bytes = sizeof(unsigned long long) * 2 * kMaxRanks;
 }
@@ -1098,7 +1109,7 @@ void decode_plan_set_peers(void* h, void* const* slots, void* const* xkeys) {
     for (int r = 0; r < plan->n_ranks; ++r) {
         if (r == plan->rank) continue;
         if (!slots[r] || !xkeys[r]) throw Error(G4Q_ERR_INVALID_ARGUMENT, "missing peer buffer of rank " + std::to_string(r));
-        plan->peer_slots[r] = static_cast<unsigned long long*>(slots[r]);
+        plan->peer_rp[r] = static_cast<unsigned long long*>(slots[r]);
         plan->peer_xkeys[r] = static_cast<unsigned long long*>(xkeys[r]);
     }
     int prev = 0;
@@ -1126,7 +1137,7 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     if (plan->device != current_device()) throw Error(G4Q_ERR_INVALID_ARGUMENT, "plan belongs to another device");
     if (M != 1) throw Error(G4Q_ERR_INVALID_ARGUMENT, "the decode plan runs one token per step (M = 1)");
     for (int r = 0; r < plan->n_ranks; ++r)
-        if (!plan->peer_slots[r] || !plan->peer_xkeys[r])
+        if (!plan->peer_rp[r] || !plan->peer_xkeys[r])
             throw Error(G4Q_ERR_INVALID_ARGUMENT, "tensor-parallel plan: peer buffers not set");
     DecodeArgs a{};   // value-initialised: direct = 0, no per-call x / y overrides
     a.ph = plan->d_ph;
@@ -1139,7 +1150,9 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     a.run = plan->d_done + plan->n_phases + 1;
     a.key = plan->d_key;
     a.slots = plan->d_slots;
-    a.peer_slots = plan->d_peers;
+    a.rp = plan->d_rp;
+    a.rp_words = plan->rp_words;
+    a.peer_rp = plan->d_peers;
     a.peer_xkeys = plan->d_peers + kMaxRanks;
     a.rank = plan->rank;
     a.n_ranks = plan->n_ranks;
@@ -1265,7 +1278,7 @@ void launch_direct(const Weight& w, const uint16_t* x, void* y, uint32_t flags, 
     a.run = ds.done + 2;
     a.key = ds.key;
     a.slots = reinterpret_cast<unsigned long long*>(ds.slots);
-    a.peer_slots = ds.peers;
+    a.peer_rp = ds.peers;
     a.peer_xkeys = ds.peers + kMaxRanks;
     a.rank = 0;
     a.n_ranks = 1;
