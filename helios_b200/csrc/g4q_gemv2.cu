@@ -7,9 +7,9 @@
 //  * Persistent grid, one 16-warp CTA per SM. The (quad, group) unit space, quad-major, is cut into
 //    equal contiguous CTA ranges, so every SM streams the same number of bytes whatever N and K are;
 //    inside a CTA, unit cs + w + 16k belongs to warp w (per-warp counts differ by at most one).
-//  * Each warp owns a private ring of kStages unit buffers in shared memory. Lane 0 refills a buffer
-//    with two cp.async.bulk copies (mbarrier completion) as soon as the warp holds the unit in
-//    registers, so kStages units per warp (~110 KB per SM) are always in flight.
+//  * Each warp owns a private ring of 3 unit buffers in shared memory (2 when the tokens' x would not
+//    fit beside 3). Lane 0 refills a buffer with two cp.async.bulk copies (mbarrier completion) as
+//    soon as the warp holds the unit in registers, so 74-110 KB per SM are always in flight.
 //  * x (M <= 8 tokens, full K) is staged once per CTA in B-fragment order while the first weight
 //    copies land; the RMS scale (sum of squares over K) is reduced there too.
 //  * When a warp leaves a quad it parks its fp32 partial in shared memory (double-buffered by quad
@@ -26,11 +26,10 @@ namespace {
 
 constexpr int kWarpsV2 = 16;
 constexpr int kThreadsV2 = kWarpsV2 * 32;
-constexpr int kStages = 3;
+constexpr int kStages = 3;                    // the most ring stages (the launch may use 2)
 constexpr uint32_t kUnitPacked = 4 * 512;     // four 16-row tiles x one group
 constexpr uint32_t kUnitSb = 64 * 4;
 constexpr uint32_t kUnitBytes = kUnitPacked + kUnitSb;
-constexpr uint32_t kRingBytes = kStages * kUnitBytes;
 constexpr uint32_t kRedBytesPerTok = 2 * kWarpsV2 * 64 * 4;   // [quad parity][tok][warp][row]
 constexpr long long kWaitLimitCycles2 = 4000000000ll;
 
@@ -48,6 +47,7 @@ struct Gemv2Args {
     float* slots;           // [Q][8][64 rows][8 tokens]
     int* counters;          // [Q], zero between launches
     int* err;
+    int stages;             // ring stages per warp (2 or 3)
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -218,21 +218,23 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
     const int cs = range_start(cta, a.U, C), ce = range_start(cta + 1, a.U, C);
     const int G = a.G, M = a.M;
     const int q_first = cs / G;
-    uint8_t* ring = smem + (size_t)warp * kRingBytes;
+    const int stages = a.stages;
+    const size_t ring_bytes = (size_t)stages * kUnitBytes;
+    uint8_t* ring = smem + (size_t)warp * ring_bytes;
     const uint32_t ring_s = smem_addr(ring);
     const uint32_t bar0 = smem_addr(&bars[warp][0]);
-    float* red = reinterpret_cast<float*>(smem + (size_t)kWarpsV2 * kRingBytes);
-    uint2* xf = reinterpret_cast<uint2*>(smem + (size_t)kWarpsV2 * kRingBytes + (size_t)kRedBytesPerTok * M);
+    float* red = reinterpret_cast<float*>(smem + (size_t)kWarpsV2 * ring_bytes);
+    uint2* xf = reinterpret_cast<uint2*>(smem + (size_t)kWarpsV2 * ring_bytes + (size_t)kRedBytesPerTok * M);
 
     // this warp's units: cs + warp + 16k < ce
     const int n_units = ce - cs > warp ? (ce - cs - warp + kWarpsV2 - 1) / kWarpsV2 : 0;
     int pq = (cs + warp) / G, pg = (cs + warp) - pq * G;   // producer position
     if (lane == 0) {
-        for (int s = 0; s < kStages; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * s));
+        for (int s = 0; s < stages; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * s));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncwarp();
-    for (int s = 0; s < kStages && s < n_units; ++s) {
+    for (int s = 0; s < stages && s < n_units; ++s) {
         if (lane == 0) issue_unit(a, pq, pg, ring_s + s * kUnitBytes, bar0 + 8 * s);
         step(pq, pg, G);
     }
@@ -323,13 +325,13 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
         uint2 bf[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) bf[j] = xg[j * kstride];
-        // the unit is in registers: refill this buffer kStages units ahead
+        // the unit is in registers: refill this buffer `stages` units ahead
         __syncwarp();
-        if (k + kStages < n_units) {
+        if (k + stages < n_units) {
             if (lane == 0) issue_unit(a, pq, pg, ring_s + stage * kUnitBytes, bar0 + 8 * stage);
             step(pq, pg, G);
         }
-        if (++stage == kStages) {
+        if (++stage == stages) {
             stage = 0;
             phase ^= 1u;
         }
@@ -367,12 +369,22 @@ static int gemv2_grid(int U, int G, int sms) {
     return grid;
 }
 
+static size_t gemv2_smem(int stages, int64_t M, int64_t K) {
+    return (size_t)kWarpsV2 * stages * kUnitBytes + (size_t)kRedBytesPerTok * M + (size_t)K * M * 2;
+}
+
+// 3 ring stages when they fit beside the tokens' x, else 2 (0: does not fit at all)
+static int gemv2_stages(int64_t M, int64_t K) {
+    for (int s = 3; s >= 2; --s)
+        if (gemv2_smem(s, M, K) <= 220 * 1024) return s;
+    return 0;
+}
+
 bool gemv2_supported(const QmmCall& c) {
-    const size_t xbytes = (size_t)c.w->K * c.M * 2;
     if (c.M < 1 || c.M > 8 || c.w->N % 64 != 0) return false;
     const long long units = (c.w->N / 64) * (c.w->K / 64);
     if (units < 1 || units >= (1ll << 31)) return false;
-    if ((size_t)kWarpsV2 * kRingBytes + (size_t)kRedBytesPerTok * c.M + xbytes > 220 * 1024) return false;
+    if (gemv2_stages(c.M, c.w->K) == 0) return false;
     return gemv2_grid((int)units, (int)(c.w->K / 64), device_sm_count()) > 0;
 }
 
@@ -410,7 +422,8 @@ void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     a.slots = ds.slots;
     a.counters = ds.counters;
     a.err = ds.err;
-    const size_t smem = (size_t)kWarpsV2 * kRingBytes + (size_t)kRedBytesPerTok * a.M + (size_t)a.K * a.M * 2;
+    a.stages = gemv2_stages(a.M, a.K);
+    const size_t smem = gemv2_smem(a.stages, a.M, a.K);
     gemv2_kernel<<<grid, kThreadsV2, smem, st>>>(a);
     check_cuda(cudaGetLastError(), "gemv2 launch");
 }

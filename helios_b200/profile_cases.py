@@ -1,7 +1,8 @@
 """Small, self-contained kernel cases for ncu captures (one GPU, a few GB at most).
 
     python -m helios_b200.profile_cases gemv      # fused gate|up GEMV, 30720 x 3840, M = 1
-    python -m helios_b200.profile_cases gemv8     # same at M = 8 (MTP verify width)
+    python -m helios_b200.profile_cases gemv8     # same at M = 8 (MTP verify width; also gemv2, gemv4)
+    python -m helios_b200.profile_cases down8     # down 3840 x 15360 at M = 8
     python -m helios_b200.profile_cases lmhead    # LM head 262144 x 3840 + softcap + argmax, M = 1
     python -m helios_b200.profile_cases gemm      # prefill dequant-GEMM, q|k|v 8192 x 3840, M = 2048
     python -m helios_b200.profile_cases dequant   # bit-exact dequantize of 15360 x 3840
@@ -24,7 +25,10 @@ from .stack import activation_seed, matrix_seed
 
 CASES = {
     "gemv": dict(N=30720, K=3840, M=1, copies=4),
+    "gemv2": dict(N=30720, K=3840, M=2, copies=4),
+    "gemv4": dict(N=30720, K=3840, M=4, copies=4),
     "gemv8": dict(N=30720, K=3840, M=8, copies=4),
+    "down8": dict(N=3840, K=15360, M=8, copies=4),
     "lmhead": dict(N=262144, K=3840, M=1, copies=1),
     "gemm": dict(N=8192, K=3840, M=2048, copies=1),
     "dequant": dict(N=15360, K=3840, M=0, copies=1),
