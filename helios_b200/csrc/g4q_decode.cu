@@ -71,6 +71,7 @@ struct PhaseDev {
     int src;          // phase whose output x is (-1: external input or an older output)
     int src_col;      // first column of x inside that phase's output (multiple of 64)
     int src_ranks;    // ranks whose partials each quad of this phase sums (1, or n_ranks if ALLREDUCE)
+    int ar;           // ordinal of this allreduce phase among the plan's allreduce phases (-1: none)
     int ks;           // slot rows per (quad, rank): the most CTA ranges one quad meets
     int sync_before;  // wait for every CTA to finish the previous phase before staging x
     int need_done;    // count finished CTAs of this phase (a later barrier or the argmax publish)
@@ -90,9 +91,11 @@ struct DecodeArgs {
     unsigned long long* const* peer_rp;       // [n_ranks] rank-partial buffers of every rank (device array)
     unsigned long long* const* peer_xkeys;    // [n_ranks] key exchange arrays ([n_ranks][2]) of every rank
     int rank, n_ranks;
+    int64_t qcount_stride;                    // counters per region of qcount
     int64_t buf_words;                        // words per slot buffer
     int64_t rp_words;                         // words per rank-partial buffer
-    int* qcount;                              // arrival counters of the argmax phase's cut quads
+    int* qcount;                              // [3][max quads] arrival counters of cut quads: allreduce
+                                              // phases by ordinal parity, then the argmax phase
     int32_t* tokens;
     float* values;
     unsigned long long* keys_out;
@@ -170,9 +173,11 @@ __device__ __forceinline__ int64_t slot_f(const DecodeArgs& a, const PhaseDev& P
     return (int64_t)(p % kSlotBufs) * a.buf_words * 2 + (int64_t)q * P.ks * 64 + (int64_t)c * 64;
 }
 
-// Rank partials of an allreduce phase: word index of (quad q, rank r, row 0) of phase p.
-__device__ __forceinline__ int64_t rp_word(const DecodeArgs& a, int p, int q, int r) {
-    return (int64_t)(p % kSlotBufs) * a.rp_words + ((int64_t)q * a.n_ranks + r) * 64;
+// Rank partials of the allreduce phase with ordinal ar: word index of (quad q, rank r, row 0). The
+// buffers rotate over allreduce ordinals: a rank writes buffer j mod 3 again only after every rank
+// has sent allreduce j+2, i.e. after every rank has finished reading allreduce j.
+__device__ __forceinline__ int64_t rp_word(const DecodeArgs& a, int ar, int q, int r) {
+    return (int64_t)(ar % kSlotBufs) * a.rp_words + ((int64_t)q * a.n_ranks + r) * 64;
 }
 
 // Warp w owns the contiguous units [wstart(w), wstart(w + 1)) of its CTA's n units of a phase
@@ -353,7 +358,7 @@ __device__ __noinline__ float4 sum_tagged4(const unsigned long long* q0, int ran
             atomicCAS(err, 0, 35);
             return s;
         }
-        __nanosleep(200);
+        __nanosleep(32);
     }
 }
 
@@ -371,6 +376,19 @@ __device__ __noinline__ void send_rank_partial(unsigned long long* const* peers,
         unsigned long long* dst = peers[r] + w0 + lane * 4;
         asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(e0), "l"(e1) : "memory");
         asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + 2), "l"(e2), "l"(e3) : "memory");
+    }
+}
+
+// The same for a quad that one CTA covers whole: its partial is in registers, rows lane, lane + 32.
+__device__ __noinline__ void send_rank_partial_regs(unsigned long long* const* peers, int n_ranks, int64_t w0,
+                                                    float v0, float v1, uint32_t tag) {
+    const int lane = threadIdx.x & 31;
+    const unsigned long long t = (unsigned long long)tag << 32;
+    const unsigned long long e0 = __float_as_uint(v0) | t, e1 = __float_as_uint(v1) | t;
+    for (int r = 0; r < n_ranks; ++r) {
+        unsigned long long* dst = peers[r] + w0;
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + lane), "l"(e0) : "memory");
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + lane + 32), "l"(e1) : "memory");
     }
 }
 
@@ -454,14 +472,35 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
         float* base = reinterpret_cast<float*>(a.slots) + slot_f(a, P, p, q, 0);
 #pragma unroll
         for (int h = 0; h < 2; ++h) base[(size_t)(cta - cf) * 64 + lane + 32 * h] = v[h];
-        if (whole && P.src_ranks == 1) {   // an allreduce phase's y needs every rank: written back later
+        if (kTP && P.src_ranks > 1) {
+            // allreduce phase: once this rank's partial of the quad is complete, send it to every rank
+            // (a whole quad straight from registers; a cut one by the last of its CTAs to arrive)
+            const uint32_t tag = phase_tag(sh.tag0, p);
+            const int64_t w0 = rp_word(a, P.ar, q, a.rank);
+            if (cf == cl) {
+                send_rank_partial_regs(a.peer_rp, a.n_ranks, w0, v[0], v[1], tag);
+            } else {
+                int* cnt = a.qcount + (int64_t)(P.ar & 1) * a.qcount_stride + q;
+                __threadfence();
+                __syncwarp();
+                int lastc = 0;
+                if (lane == 0) lastc = atomicAdd(cnt, 1) == cl - cf;
+                lastc = __shfl_sync(0xffffffffu, lastc, 0);
+                if (lastc) {
+                    __threadfence();
+                    send_rank_partial(a.peer_rp, a.n_ranks, w0, base, cl - cf + 1, tag);
+                    __syncwarp();
+                    if (lane == 0) atomicExch(cnt, 0);
+                }
+            }
+        } else if (whole) {   // an allreduce phase's y needs every rank: written back later
 #pragma unroll
             for (int h = 0; h < 2; ++h) store_y(phase_y(a, P), fl, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs));
         } else if (argmax) {   // the logits are needed now: the last contributing CTA finishes the quad
             __threadfence();
             __syncwarp();
             int lastc = 0;
-            if (lane == 0) lastc = atomicAdd(a.qcount + q, 1) == cl - cf;
+            if (lane == 0) lastc = atomicAdd(a.qcount + 2 * a.qcount_stride + q, 1) == cl - cf;
             lastc = __shfl_sync(0xffffffffu, lastc, 0);
             if (lastc) {
                 __threadfence();
@@ -473,7 +512,7 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
                                       __fmul_rn(s, sh.rs), best);
                 }
                 __syncwarp();
-                if (lane == 0) atomicExch(a.qcount + q, 0);
+                if (lane == 0) atomicExch(a.qcount + 2 * a.qcount_stride + q, 0);
             }
         }
     }
@@ -535,7 +574,7 @@ __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P,
             const uint32_t tag = phase_tag(tag0, P.src);
             for (int idx = threadIdx.x; idx < cells; idx += kThreads) {
                 const int q = q0 + (idx >> 4);
-                put(idx, sum_tagged4(a.rp + rp_word(a, P.src, q, 0) + (idx & 15) * 4, a.n_ranks, 1, 1, tag, a.err));
+                put(idx, sum_tagged4(a.rp + rp_word(a, S.ar, q, 0) + (idx & 15) * 4, a.n_ranks, 1, 1, tag, a.err));
             }
             return ss;
         }
@@ -606,7 +645,7 @@ __device__ __forceinline__ void write_back_warp(const DecodeArgs& a, int pp, int
         float4 s;
         if constexpr (kTP) {
             if (Q.src_ranks > 1)
-                s = sum_tagged4(a.rp + rp_word(a, pp, q, 0) + lane * 4, a.n_ranks, 1, 1, tag, a.err);
+                s = sum_tagged4(a.rp + rp_word(a, Q.ar, q, 0) + lane * 4, a.n_ranks, 1, 1, tag, a.err);
         }
         if (!kTP || Q.src_ranks == 1)
             s = sum_slots4(reinterpret_cast<const float*>(a.slots) + slot_f(a, Q, pp, q, 0) + lane * 4, cl - cf + 1);
@@ -713,18 +752,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         __syncthreads();
         const float rs_prev = sh.rs_prev;
         const uint32_t tag0 = sh.tag0;
-        if constexpr (kTP) {   // the previous phase was an allreduce phase: send this CTA's rank partials
-            if (p > 0 && warp == 0 && a.ph[p - 1].src_ranks > 1) {
-                const PhaseDev& Q = a.ph[p - 1];
-                for (int q = cta; q < Q.Q; q += C) {
-                    int cf, cl;
-                    quad_ctas(Q, q, C, cf, cl);
-                    send_rank_partial(a.peer_rp, a.n_ranks, rp_word(a, p - 1, q, a.rank),
-                                      reinterpret_cast<const float*>(a.slots) + slot_f(a, Q, p - 1, q, 0), cl - cf + 1,
-                                      phase_tag(tag0, p - 1));
-                }
-            }
-        }
         // ---- stage x (polls the producers' slots) and its RMS scale
         const bool rms = (phase_flags(a, P) & G4Q_QMM_RMS_SCALE) != 0;
         float ss = stage_x<kTP>(a, P, xs, sh.cut, C, rs_prev, tag0, rms);
@@ -895,6 +922,7 @@ struct DecodePlan {
     int64_t rp_words = 0;
     unsigned long long* d_xkeys = nullptr;   // [kMaxRanks][2]
     int* d_qcount = nullptr;
+    int64_t max_q = 0;
     unsigned long long** d_peers = nullptr;   // [2][kMaxRanks]: slot buffers, key arrays of every rank
     unsigned long long* peer_rp[kMaxRanks] = {};
     unsigned long long* peer_xkeys[kMaxRanks] = {};
@@ -969,6 +997,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
         d.src = -1;
         d.src_col = 0;
         d.src_ranks = (fl & G4Q_PHASE_ALLREDUCE) ? n_ranks : 1;
+        d.ar = -1;
         d.sync_before = 0;
         d.need_done = (fl & G4Q_PHASE_ARGMAX) ? 1 : 0;
         if (d.U < sms) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too small for a full-grid decode plan");
@@ -1019,7 +1048,17 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
             if (!producers[i][c]) return false;
         return true;
     };
-    for (int i = 1; i < n; ++i) ph[i].sync_before = 1;
+    // On one GPU every phase waits for the previous one. In a tensor-parallel plan a phase reading an
+    // allreduce output waits for nothing: its x is the rank partials, which carry their phase tag.
+    int n_ar = 0;
+    for (int i = 0; i < n; ++i)
+        if (ph[i].src_ranks > 1) ph[i].ar = n_ar++;
+    for (int i = 1; i < n; ++i)
+        ph[i].sync_before = (n_ranks > 1 && ph[i].src >= 0 && ph[ph[i].src].src_ranks > 1) ? 0 : 1;
+    // local slots of phase i are read until the end of phase i+1 and rewritten by phase i+3: some CTA
+    // barrier must sit at phase i+2 or i+3
+    for (int i = 0; i + 3 < n; ++i)
+        if (!ph[i + 2].sync_before && !ph[i + 3].sync_before) ph[i + 3].sync_before = 1;
     // Across ranks there is no barrier at all: a rank can only run ahead into the next phase that
     // reads an allreduce phase's output, which needs every rank's partials. So every allreduce phase
     // must feed the phase after it whole, and the step ends with the key exchange.
@@ -1047,6 +1086,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     plan->n_ranks = n_ranks;
     plan->buf_words = buf_words;
     plan->rp_words = rp_words;
+    plan->max_q = max_q;
     plan->smem = (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4 + (size_t)(kmax + 8) * 2;
     const void* kfn = n_ranks > 1 ? reinterpret_cast<const void*>(decode_kernel<true>)
                                   : reinterpret_cast<const void*>(decode_kernel<false>);
@@ -1062,14 +1102,14 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_rp, sizeof(unsigned long long) * kSlotBufs * (size_t)rp_words);
     if (e == cudaSuccess) e = cudaMemset(plan->d_rp, 0, sizeof(unsigned long long) * kSlotBufs * (size_t)rp_words);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_xkeys, sizeof(unsigned long long) * 2 * kMaxRanks);
-    if (e == cudaSuccess) e = cudaMalloc(&plan->d_qcount, sizeof(int) * (size_t)max_q);
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_qcount, sizeof(int) * 3 * (size_t)max_q);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_peers, sizeof(void*) * 2 * kMaxRanks);
     if (e == cudaSuccess) e = cudaMemcpy(plan->d_ph, ph.data(), sizeof(PhaseDev) * n, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(plan->d_done, 0, sizeof(unsigned int) * (n + 2));
     if (e == cudaSuccess) e = cudaMemset(plan->d_key, 0, sizeof(unsigned long long));
     if (e == cudaSuccess) e = cudaMemset(plan->d_slots, 0, slot_bytes);
     if (e == cudaSuccess) e = cudaMemset(plan->d_xkeys, 0, sizeof(unsigned long long) * 2 * kMaxRanks);
-    if (e == cudaSuccess) e = cudaMemset(plan->d_qcount, 0, sizeof(int) * (size_t)max_q);
+    if (e == cudaSuccess) e = cudaMemset(plan->d_qcount, 0, sizeof(int) * 3 * (size_t)max_q);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         free_plan_memory(plan);
@@ -1158,6 +1198,7 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     a.n_ranks = plan->n_ranks;
     a.buf_words = plan->buf_words;
     a.qcount = plan->d_qcount;
+    a.qcount_stride = plan->max_q;
     a.tokens = tokens;
     a.values = values;
     a.keys_out = reinterpret_cast<unsigned long long*>(keys);
