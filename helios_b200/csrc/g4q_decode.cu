@@ -284,6 +284,19 @@ __device__ __forceinline__ void spin_until(const unsigned int* ctr, unsigned int
     }
 }
 
+// Arrival of this CTA's finishing warp at a quad cut between CTAs (its slot row already stored):
+// the warp sync orders the lanes' slot stores before lane 0's gpu-scope release on the counter;
+// the last arriver's acquire makes every other CTA's slot rows visible to its lanes.
+__device__ __forceinline__ bool arrive_last(int* cnt, int last_value) {
+    __syncwarp();
+    int last = 0;
+    if ((threadIdx.x & 31) == 0)
+        last = atom_add_acq_rel(reinterpret_cast<unsigned int*>(cnt), 1u) == (unsigned int)last_value;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    __syncwarp();
+    return last != 0;
+}
+
 __device__ __forceinline__ void ld_slot2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
     asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
@@ -481,13 +494,7 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
                 send_rank_partial_regs(a.peer_rp, a.n_ranks, w0, v[0], v[1], tag);
             } else {
                 int* cnt = a.qcount + (int64_t)(P.ar & 1) * a.qcount_stride + q;
-                __threadfence();
-                __syncwarp();
-                int lastc = 0;
-                if (lane == 0) lastc = atomicAdd(cnt, 1) == cl - cf;
-                lastc = __shfl_sync(0xffffffffu, lastc, 0);
-                if (lastc) {
-                    __threadfence();
+                if (arrive_last(cnt, cl - cf)) {
                     send_rank_partial(a.peer_rp, a.n_ranks, w0, base, cl - cf + 1, tag);
                     __syncwarp();
                     if (lane == 0) atomicExch(cnt, 0);
@@ -497,13 +504,7 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
 #pragma unroll
             for (int h = 0; h < 2; ++h) store_y(phase_y(a, P), fl, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs));
         } else if (argmax) {   // the logits are needed now: the last contributing CTA finishes the quad
-            __threadfence();
-            __syncwarp();
-            int lastc = 0;
-            if (lane == 0) lastc = atomicAdd(a.qcount + 2 * a.qcount_stride + q, 1) == cl - cf;
-            lastc = __shfl_sync(0xffffffffu, lastc, 0);
-            if (lastc) {
-                __threadfence();
+            if (arrive_last(a.qcount + 2 * a.qcount_stride + q, cl - cf)) {
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     float s = __ldcg(base + lane + 32 * h);
