@@ -171,9 +171,43 @@ G4qStatus g4q_weight_create(int64_t rows, int64_t cols, int32_t bits, int32_t gr
         require(out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null out pointer");
         *out = nullptr;
         require(rows > 0 && cols > 0, G4Q_ERR_INVALID_ARGUMENT, "rows and cols must be positive");
-        require(bits == 4 && group_size == 64, G4Q_ERR_UNSUPPORTED_CONFIG,
-                "the kernel layout supports bits=4, group_size=64 (got bits=" + std::to_string(bits) +
+        require((bits == 4 || bits == 8) && (group_size == 32 || group_size == 64 || group_size == 128),
+                G4Q_ERR_UNSUPPORTED_CONFIG,
+                "supported quantization: bits 4 or 8, group_size 32, 64 or 128 (got bits=" + std::to_string(bits) +
                     ", group_size=" + std::to_string(group_size) + ")");
+        if (bits != 4 || group_size != 64) {
+            // other specs of the manifest stay in MLX's layout and run on the generic kernels
+            require(cols % group_size == 0, G4Q_ERR_UNSUPPORTED_CONFIG, "cols must be a multiple of group_size");
+            (void)device_scratch();
+            Weight* w = new (std::nothrow) Weight();
+            require(w != nullptr, G4Q_ERR_MEMORY_GUARD, "host allocation failed");
+            w->N = rows;
+            w->K = cols;
+            w->bits = bits;
+            w->group_size = group_size;
+            w->device = current_device();
+            w->mlx = true;
+            w->small_scales = false;
+            const size_t pb = (size_t)rows * cols * bits / 8, gb = (size_t)rows * (cols / group_size) * 2;
+            cudaError_t e = cudaMalloc(&w->packed, pb);
+            if (e == cudaSuccess) e = cudaMalloc(&w->mlx_scales, gb);
+            if (e == cudaSuccess) e = cudaMalloc(&w->mlx_biases, gb);
+            if (e == cudaSuccess) e = cudaMalloc(&w->d_flags, sizeof(int));
+            if (e == cudaSuccess) e = cudaMemset(w->d_flags, 0, sizeof(int));
+            if (e != cudaSuccess) {
+                cudaFree(w->packed);
+                cudaFree(w->mlx_scales);
+                cudaFree(w->mlx_biases);
+                cudaFree(w->d_flags);
+                delete w;
+                cudaGetLastError();
+                throw Error(G4Q_ERR_MEMORY_GUARD, std::string("device allocation failed: ") + cudaGetErrorString(e));
+            }
+            w->bytes = pb + 2 * gb;
+            w->magic = kWeightMagic;
+            *out = reinterpret_cast<G4qWeight*>(w);
+            return;
+        }
         require(rows % 16 == 0, G4Q_ERR_UNSUPPORTED_CONFIG, "rows must be a multiple of 16");
         require(cols % 64 == 0, G4Q_ERR_UNSUPPORTED_CONFIG, "cols must be a multiple of 64");
         (void)device_scratch();   // per-device library state exists before any compute call
@@ -221,6 +255,8 @@ G4qStatus g4q_weight_free(G4qWeight* h) {
         cudaFree(w->sb);
         cudaFree(w->d_flags);
         cudaFree(w->argmax_scratch);
+        cudaFree(w->mlx_scales);
+        cudaFree(w->mlx_biases);
         direct_release(*w);
         cudaSetDevice(prev);
         delete w;
@@ -250,6 +286,30 @@ G4qStatus g4q_weight_load(G4qWeight* h, int64_t dst_row0, const uint32_t* packed
     return guarded("g4q_weight_load", [&] {
         Weight* w = checked(h, "g4q_weight_load");
         require(packed && scales && biases, G4Q_ERR_INVALID_ARGUMENT, "packed, scales and biases must be non-null");
+        if (w->mlx) {   // MLX layout: copy the row / column window as it is (host or device source)
+            const int64_t gs = w->group_size, per = 32 / w->bits;
+            require(src_rows > 0 && src_cols > 0 && src_cols % gs == 0, G4Q_ERR_INVALID_ARGUMENT,
+                    "source shape must be positive with cols a multiple of group_size");
+            require(src_k0 >= 0 && src_k0 % gs == 0 && src_k0 + w->K <= src_cols, G4Q_ERR_INVALID_ARGUMENT,
+                    "column window must be group aligned and inside the source");
+            require(n_rows > 0 && src_row0 >= 0 && src_row0 + n_rows <= src_rows, G4Q_ERR_INVALID_ARGUMENT,
+                    "row window must be inside the source");
+            require(dst_row0 >= 0 && dst_row0 + n_rows <= w->N, G4Q_ERR_INVALID_ARGUMENT,
+                    "destination rows must be inside the handle");
+            cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+            const int64_t src_w = src_cols / per, dst_w = w->K / per, src_g = src_cols / gs, dst_g = w->K / gs;
+            check_cuda(cudaMemcpy2DAsync(w->packed + dst_row0 * dst_w, dst_w * 4, packed + src_row0 * src_w + src_k0 / per,
+                                         src_w * 4, dst_w * 4, n_rows, cudaMemcpyDefault, st),
+                       "copy packed words");
+            check_cuda(cudaMemcpy2DAsync(w->mlx_scales + dst_row0 * dst_g, dst_g * 2, scales + src_row0 * src_g + src_k0 / gs,
+                                         src_g * 2, dst_g * 2, n_rows, cudaMemcpyDefault, st),
+                       "copy scales");
+            check_cuda(cudaMemcpy2DAsync(w->mlx_biases + dst_row0 * dst_g, dst_g * 2, biases + src_row0 * src_g + src_k0 / gs,
+                                         src_g * 2, dst_g * 2, n_rows, cudaMemcpyDefault, st),
+                       "copy biases");
+            check_cuda(cudaStreamSynchronize(st), "weight copy");
+            return;
+        }
         require(src_rows > 0 && src_cols > 0 && src_cols % 64 == 0, G4Q_ERR_INVALID_ARGUMENT,
                 "source shape must be positive with cols % 64 == 0");
         require(src_k0 >= 0 && src_k0 % 64 == 0 && src_k0 + w->K <= src_cols, G4Q_ERR_INVALID_ARGUMENT,
@@ -304,6 +364,14 @@ G4qStatus g4q_weight_export(const G4qWeight* h, uint32_t* packed, uint16_t* scal
     return guarded("g4q_weight_export", [&] {
         Weight* w = checked(h, "g4q_weight_export");
         require(packed && scales && biases, G4Q_ERR_INVALID_ARGUMENT, "outputs must be non-null device pointers");
+        if (w->mlx) {
+            cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+            const size_t pb = (size_t)w->N * w->K * w->bits / 8, gb = (size_t)w->N * (w->K / w->group_size) * 2;
+            check_cuda(cudaMemcpyAsync(packed, w->packed, pb, cudaMemcpyDefault, st), "export packed words");
+            check_cuda(cudaMemcpyAsync(scales, w->mlx_scales, gb, cudaMemcpyDefault, st), "export scales");
+            check_cuda(cudaMemcpyAsync(biases, w->mlx_biases, gb, cudaMemcpyDefault, st), "export biases");
+            return;
+        }
         launch_export(*w, packed, scales, biases, reinterpret_cast<cudaStream_t>(stream));
     });
 }
@@ -316,6 +384,15 @@ G4qStatus g4q_dequantize(const G4qWeight* h, const int32_t* row_ids, int64_t n_i
         require(chain == G4Q_CHAIN_R1 || chain == G4Q_CHAIN_R2, G4Q_ERR_INVALID_ARGUMENT, "chain must be 1 (R1) or 2 (R2)");
         require(row_ids == nullptr || n_ids >= 0, G4Q_ERR_INVALID_ARGUMENT, "n_ids must be >= 0");
         require_aligned16(out, "out");
+        if (w->mlx) {
+            cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+            if (row_ids == nullptr)
+                launch_dequantize_mlx(w->packed, w->mlx_scales, w->mlx_biases, w->N, w->K, w->bits, w->group_size,
+                                      chain, out, st);
+            else
+                launch_dequantize_mlx_rows(*w, row_ids, n_ids, out, chain, st);
+            return;
+        }
         launch_dequantize(*w, row_ids, n_ids, out, chain, w->d_flags, reinterpret_cast<cudaStream_t>(stream));
     });
 }
@@ -348,10 +425,14 @@ static void qmm_common(const char* fn, const G4qWeight* h, const uint16_t* x, in
     require(ldx >= w->K && ldx % 8 == 0, G4Q_ERR_INVALID_ARGUMENT, "ldx must be >= cols and a multiple of 8");
     require(ldy >= w->N, G4Q_ERR_INVALID_ARGUMENT, "ldy must be >= rows");
     require_aligned16(x, "x");
-    require(w->fast_ok, G4Q_ERR_UNSUPPORTED_CONFIG,
-            "a scale is non-finite or |scale| >= 2^120; use g4q_dequantize for such weights");
     QmmCall c{w, x, M, ldx, y, ldy, flags, eps};
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (w->mlx) {   // 8-bit or non-64 groups: the generic kernel
+        launch_qmm_mlx(c, st);
+        return;
+    }
+    require(w->fast_ok, G4Q_ERR_UNSUPPORTED_CONFIG,
+            "a scale is non-finite or |scale| >= 2^120; use g4q_dequantize for such weights");
     if (M == 1 && direct_ready(*w, y))
         launch_direct(*w, x, y, flags, eps, st);   // the persistent decode kernel, one phase
     else if (M <= 16)
@@ -375,6 +456,7 @@ G4qStatus g4q_lm_head_argmax(const G4qWeight* h, const uint16_t* x, int64_t M, i
                              int32_t* tokens, float* values, uint64_t* keys, void* stream) {
     return guarded("g4q_lm_head_argmax", [&] {
         Weight* w = checked(h, "g4q_lm_head_argmax");
+        require(!w->mlx, G4Q_ERR_UNSUPPORTED_CONFIG, "the fused LM head takes a 4-bit group-64 weight");
         require(M >= 1 && M <= 16, G4Q_ERR_INVALID_ARGUMENT, "M must be in [1, 16]");
         require(x != nullptr, G4Q_ERR_INVALID_ARGUMENT, "x must be non-null");
         require((flags & ~G4Q_QMM_RMS_SCALE) == 0, G4Q_ERR_INVALID_ARGUMENT, "only G4Q_QMM_RMS_SCALE is accepted");

@@ -968,6 +968,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
         const std::string tag = "phase " + std::to_string(i) + ": ";
         if (!w || w->magic != kWeightMagic) throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "invalid weight");
         if (w->device != dev) throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "weight lives on another device");
+        if (w->mlx) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "the decode plan takes 4-bit group-64 weights");
         if (!w->fast_ok || !w->small_scales)
             throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "the decode plan needs every |scale| < 2^-1");
         if (w->N % 64 != 0) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "rows must be a multiple of 64");
@@ -1242,6 +1243,7 @@ size_t direct_smem(int64_t K) { return (size_t)kWarps * kRingBytes + 2 * kWarps 
 }  // namespace
 
 void direct_prepare(Weight& w) {
+    if (w.mlx) return;
     const int sms = device_sm_count();
     const int64_t N = w.N, K = w.K;
     bool ok = w.fast_ok && w.small_scales && N % 64 == 0 && K % 64 == 0;

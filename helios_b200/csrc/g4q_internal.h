@@ -19,8 +19,11 @@ struct Weight {
     int64_t N = 0, K = 0;        // logical shape of this handle (after any TP split)
     int bits = 4, group_size = 64;
     int device = -1;
-    uint32_t* packed = nullptr;  // layout v1
+    uint32_t* packed = nullptr;  // layout v1 (4-bit, group 64) or, for other specs, MLX's layout
     uint32_t* sb = nullptr;
+    bool mlx = false;            // kept in MLX's layout (bits 8, or groups 32 / 128): generic kernels
+    uint16_t* mlx_scales = nullptr;   // [N][K/group] bf16 (MLX layout only)
+    uint16_t* mlx_biases = nullptr;
     size_t bytes = 0;
     int* d_flags = nullptr;      // device word: bit0 = a scale outside |s| < 2^120 or non-finite,
                                  // bit1 = a gathered row id was out of range
@@ -78,6 +81,9 @@ void launch_repack(const uint32_t* src_w, const uint16_t* src_s, const uint16_t*
                    int64_t src_ld_groups, int64_t src_row0, int64_t src_k0, int64_t n_rows, Weight& w,
                    int64_t dst_row0, cudaStream_t st);
 void launch_export(const Weight& w, uint32_t* dst_w, uint16_t* dst_s, uint16_t* dst_b, cudaStream_t st);
+// kernels (g4q_generic.cu): weights kept in MLX's layout (specs other than 4-bit / group 64)
+void launch_dequantize_mlx_rows(const Weight& w, const int32_t* ids, int64_t n_ids, uint16_t* out, int chain,
+                                cudaStream_t st);
 void launch_dequantize(const Weight& w, const int32_t* ids, int64_t n_ids, uint16_t* out, int chain,
                        int* d_err, cudaStream_t st);
 void launch_dequantize_mlx(const uint32_t* w, const uint16_t* s, const uint16_t* b, int64_t N, int64_t K,
@@ -93,6 +99,8 @@ struct QmmCall {
     uint32_t flags;
     float eps;
 };
+void launch_qmm_mlx(const QmmCall& c, cudaStream_t st);
+
 void launch_gemv(const QmmCall& c, cudaStream_t st);
 bool gemv2_supported(const QmmCall& c);
 void launch_gemv2(const QmmCall& c, cudaStream_t st);

@@ -57,11 +57,15 @@ def _check_format(group_size: int, bits: int, mode: str) -> None:
 
 
 class QuantizedWeight:
-    """A 4-bit, group-64 affine matrix resident on one GPU in libg4q's kernel layout.
+    """An affine-quantized matrix resident on one GPU.
 
-    Build it from MLX-layout tensors (host or device) with :meth:`from_mlx`, optionally taking a
-    row window (tensor-parallel column split) and/or a group-aligned column window (row split),
-    or concatenating several matrices that share an input with :meth:`concat`.
+    4-bit group-64 matrices (every projection of the default manifest) are repacked into libg4q's
+    kernel layout and run on the tensor-core / persistent kernels; the 8-bit group-64 per-module
+    override a manifest may name (model_manifest.cc:146-152), and groups 32 / 128, stay in MLX's
+    layout and run on the generic kernels (quantized matmul and dequantize only: the fused LM
+    head and the decode plan reject them). Build it from MLX-layout tensors (host or device) with :meth:`from_mlx`, optionally
+    taking a row window (tensor-parallel column split) and/or a group-aligned column window (row
+    split), or concatenating several matrices that share an input with :meth:`concat`.
     """
 
     def __init__(self, rows: int, cols: int, bits: int = 4, group_size: int = 64):

@@ -77,21 +77,27 @@ G4qStatus g4q_get_last_error(char* buffer, size_t buffer_len);
 /* ---- weights: the loader repack -------------------------------------------------------
  * Replaces the tensor residency of NativeTextModel::load (native_model.cc:3506-3590) for the
  * `{prefix}.weight/.scales/.biases` triple consumed by quantized_linear (native_model.cc:349-362).
- * g4q_weight_create allocates an empty N x K handle (N % 16 == 0, K % 64 == 0; bits 4, group 64).
+ * g4q_weight_create allocates an empty N x K handle. bits 4 / group 64 (N % 16 == 0,
+ * K % 64 == 0) is repacked into the kernel layout and runs every entry point below. The 8-bit
+ * group-64 override the reference's manifest allows per module (model_manifest.cc:146-152), and
+ * groups 32 / 128 at 4 or 8 bits as mlx::core accepts them (any N, K % group == 0), keep MLX's
+ * layout on the device and run g4q_qmm/_ex, g4q_dequantize and export on generic CUDA-core
+ * kernels; the fused LM head and the decode plan return G4Q_ERR_UNSUPPORTED_CONFIG for them. Any other bits/group is G4Q_ERR_UNSUPPORTED_CONFIG.
  * g4q_weight_load copies the window [src_row0, src_row0+n_rows) x [src_k0, src_k0+K) of an
- * MLX-layout matrix (packed uint32 [src_rows, src_cols/8], scales/biases bf16
- * [src_rows, src_cols/64], host or device memory) into rows [dst_row0, dst_row0+n_rows) of the
- * handle, in the kernel layout. One call per matrix uploads it whole; windows give the tensor-
- * parallel column split (rows) and row split (K, group aligned), and several loads into one
- * handle concatenate projections that share an input (q|k|v, gate|up). Dequantised values are
- * preserved exactly (g4q_weight_export inverts the repack). */
+ * MLX-layout matrix (packed uint32 [src_rows, src_cols*bits/32], scales/biases bf16
+ * [src_rows, src_cols/group], host or device memory) into rows [dst_row0, dst_row0+n_rows) of the
+ * handle (4-bit g64: rows in multiples of 16). One call per matrix uploads it whole; windows give
+ * the tensor-parallel column split (rows) and row split (K, group aligned), and several loads into
+ * one handle concatenate projections that share an input (q|k|v, gate|up). Dequantised values
+ * are preserved exactly (g4q_weight_export inverts the repack). */
 G4qStatus g4q_weight_create(int64_t rows, int64_t cols, int32_t bits, int32_t group_size, G4qWeight** out);
 G4qStatus g4q_weight_load(G4qWeight* w, int64_t dst_row0, const uint32_t* packed, const uint16_t* scales,
                           const uint16_t* biases, int64_t src_rows, int64_t src_cols, int64_t src_row0,
                           int64_t src_k0, int64_t n_rows, void* stream);
 G4qStatus g4q_weight_free(G4qWeight* w);
 G4qStatus g4q_weight_info(const G4qWeight* w, G4qWeightInfo* out);
-/* Inverse repack into MLX layout (device pointers: packed [rows, cols/8], scales/biases [rows, cols/64]). */
+/* Inverse repack into MLX layout (device pointers: packed [rows, cols*bits/32], scales/biases
+ * [rows, cols/group]). */
 G4qStatus g4q_weight_export(const G4qWeight* w, uint32_t* packed, uint16_t* scales, uint16_t* biases,
                             void* stream);
 

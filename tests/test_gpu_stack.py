@@ -164,8 +164,10 @@ def test_invalid_calls_return_status(cuda, oracle):
     with pytest.raises(_lib.G4qError) as e:
         Q.QuantizedWeight(60, 256)                       # rows % 16 != 0
     assert e.value.status == _lib.G4Q_ERR_UNSUPPORTED_CONFIG
-    with pytest.raises(_lib.G4qError):
-        Q.QuantizedWeight(64, 256, bits=8)               # 8-bit not in the kernel layout
+    for bits, gs in ((2, 64), (3, 64), (4, 48), (8, 256)):   # specs the manifest never names
+        with pytest.raises(_lib.G4qError) as e:
+            Q.QuantizedWeight(64, 256, bits=bits, group_size=gs)
+        assert e.value.status == _lib.G4Q_ERR_UNSUPPORTED_CONFIG
     q = Q.QuantizedWeight.from_mlx(w, s, b)
     with pytest.raises(ValueError):
         Q.quantized_matmul(torch.zeros((1, 128), dtype=torch.bfloat16, device=cuda), q)   # K mismatch
