@@ -1,23 +1,26 @@
 // g4q_gemv2.cu -- K1 v2: persistent stream-K decode GEMV (M <= 8) fed by per-warp TMA bulk rings.
 //
-// Same product as g4q_gemv.cu (bit-exact R2 dequant in registers, mma.sync bf16 -> fp32), organised
-// for HBM streaming on B200:
+// Same product as g4q_gemv.cu (bit-exact R2 dequant in registers, mma.sync bf16 -> fp32 with the
+// tokens as the n dimension), organised for HBM streaming on B200:
 //  * Work unit = one 64-wide quantization group of a "quad" of four 16-row tiles (64 rows): 2 KB of
 //    packed words (contiguous in layout v1) + 256 B of scale|bias words.
 //  * Persistent grid, one 16-warp CTA per SM. The (quad, group) unit space, quad-major, is cut into
 //    equal contiguous CTA ranges, so every SM streams the same number of bytes whatever N and K are;
-//    inside a CTA, unit cs + w + 16k belongs to warp w (per-warp counts differ by at most one).
+//    inside a CTA each warp owns a contiguous run of units (counts differ by at most one), so a
+//    warp meets at most two quads that other warps share.
 //  * Each warp owns a private ring of 3 unit buffers in shared memory (2 when the tokens' x would not
 //    fit beside 3). Lane 0 refills a buffer with two cp.async.bulk copies (mbarrier completion) as
-//    soon as the warp holds the unit in registers, so 74-110 KB per SM are always in flight.
-//  * x (M <= 8 tokens, full K) is staged once per CTA in B-fragment order while the first weight
-//    copies land; the RMS scale (sum of squares over K) is reduced there too.
-//  * When a warp leaves a quad it parks its fp32 partial in shared memory (double-buffered by quad
-//    parity); the last warp to park a quad sums the partials in warp order, so no CTA-wide barrier
-//    sits in the loop. A quad cut by a CTA-range boundary is finished through global slots: each
-//    CTA stores its partial in its own slot and bumps the quad's counter; the last arriver sums the
-//    slots in CTA order, applies the epilogue and resets the counter to zero. Results are
-//    bit-reproducible.
+//    soon as the warp has read the unit.
+//  * x (M <= 8 tokens, full K) is staged once per CTA, per token in B-fragment order (two 16-byte
+//    loads per lane and unit), while the first weight copies land; the per-token RMS scale (sum of
+//    squares over K) is reduced there too.
+//  * Weights whose |scales| are all < 2^-1 take the raw odd-nibble dequant (the masked bits read as
+//    bf16 are q * 2^-129, times s * 2^129): two operations fewer per packed word.
+//  * A warp parks its fp32 partial of a quad in shared memory when it leaves the quad; the last warp
+//    of a shared quad sums the partials in warp order, so no warp ever waits. A quad cut by a
+//    CTA-range boundary is finished through global slots: each CTA stores its partial in its own
+//    slot and bumps the quad's counter; the last arriver sums the slots in CTA order, applies the
+//    epilogue and resets the counter to zero. Results are bit-reproducible.
 #include "g4q_common.cuh"
 #include "g4q_internal.h"
 
@@ -32,6 +35,9 @@ constexpr uint32_t kUnitSb = 64 * 4;
 constexpr uint32_t kUnitBytes = kUnitPacked + kUnitSb;
 constexpr uint32_t kRedBytesPerTok = 2 * kWarpsV2 * 64 * 4;   // [quad parity][tok][warp][row]
 constexpr long long kWaitLimitCycles2 = 4000000000ll;
+constexpr uint32_t kOddNibbleMask = 0x00F000F0u;  // q at bits 4-7 of each half: bf16 value q * 2^-129
+constexpr uint32_t kPow64x2 = 0x5F805F80u;        // bf16x2 (2^64, 2^64)
+constexpr uint32_t kPow65x2 = 0x60006000u;        // bf16x2 (2^65, 2^65)
 
 struct Gemv2Args {
     const uint32_t* packed;
@@ -100,11 +106,22 @@ __device__ __forceinline__ int cta_of_unit(int u, int U, int C) {
     return c;
 }
 
-// advance a (quad, group) position by kWarpsV2 units
-__device__ __forceinline__ void step(int& q, int& g, int G) {
-    g += kWarpsV2;
-    while (g >= G) {
-        g -= G;
+// Warp w owns the contiguous units [wstart(w), wstart(w + 1)) of its CTA's n units (relative
+// numbering): the first n % kWarpsV2 warps take one unit more, warps past n own none.
+__device__ __forceinline__ int wstart(int w, int n) {
+    const int b = n / kWarpsV2, r = n - b * kWarpsV2;
+    return w * b + min(w, r);
+}
+
+__device__ __forceinline__ int warp_of(int u, int n) {   // owner of relative unit u, 0 <= u < n
+    const int b = n / kWarpsV2, r = n - b * kWarpsV2, big = r * (b + 1);
+    return u < big ? u / (b + 1) : r + (u - big) / b;
+}
+
+// next unit in (quad, group) order
+__device__ __forceinline__ void step1(int& q, int& g, int G) {
+    if (++g == G) {
+        g = 0;
         ++q;
     }
 }
@@ -118,49 +135,46 @@ __device__ __forceinline__ void store_out(const Gemv2Args& a, int q, int row, in
         reinterpret_cast<uint16_t*>(a.y)[idx] = f32_to_bf16_bits(o);
 }
 
-// Shared state of one CTA for the per-quad reduction: partial sums are double-buffered by quad
-// parity; the last warp to park a quad reduces it and frees the buffer.
-struct QuadRed {
-    int cnt[2];
-    int done[2];
-    int last_cta;
-};
+// Shared-memory order of x: inside each 64-wide group, lane t's B-fragment words for the four k16
+// steps (j) sit together: word w = 8j + t + 4hi of the group goes to slot 8t + 2j + hi, so a lane
+// fetches the group's fragments of its token with two 16-byte loads.
+__device__ __forceinline__ int xperm(int w) {
+    const int r = w & 7;
+    return (w & ~31) | ((r & 3) << 3) | (((w >> 3) & 3) << 1) | (r >> 2);
+}
 
-// Park this warp's partial of quad q; the last warp of the quad reduces it (fixed warp order),
-// stores whole quads and finishes cut quads through the global slots.
-__device__ __forceinline__ void park_quad(const Gemv2Args& a, QuadRed& qr, float* red, int q, int cs, int ce, int cta,
-                                          int C, const float (&acc)[4][4], const float* rs) {
+// Park this warp's partial of quad q (the M token columns of its 64 rows). A warp keeps the partial
+// of the first quad of its run in red[warp][0] (earlier warps may share that quad) and any other in
+// red[warp][1] (only its last quad is shared, with later warps, and it comes last), so no warp ever
+// waits. The last contributing warp (arrival counter of the quad's first warp) sums the partials in
+// warp order, then stores a quad whole in this CTA or leaves the CTA's partial in its global slot;
+// the last CTA to arrive at a cut quad sums the slots in CTA order. Results are bit-reproducible.
+__device__ __forceinline__ void park_quad(const Gemv2Args& a, int* qcnt, float* red, int q, int first_q, int cs,
+                                          int ce, int cta, int C, const float (&acc)[4][4], const float* rs) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
-    const int M = a.M, G = a.G;
-    const int b = q & 1;
-    // the buffer was last used by quad q - 2: wait until that quad has been reduced
-    if (*reinterpret_cast<volatile int*>(&qr.done[b]) < q - 2) {
-        const long long t0 = clock64();
-        while (*reinterpret_cast<volatile int*>(&qr.done[b]) < q - 2) {
-            if (clock64() - t0 > kWaitLimitCycles2) {
-                atomicCAS(a.err, 0, 17);
-                break;
-            }
-        }
-    }
-    float* rb = red + (size_t)b * M * kWarpsV2 * 64;
+    const int M = a.M, G = a.G, n = ce - cs;
+    float* rb = red + (size_t)(warp * 2 + (q == first_q ? 0 : 1)) * M * 64;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int tok = 2 * t + (e & 1);
-            if (tok < M) rb[(tok * kWarpsV2 + warp) * 64 + i * 16 + gi + ((e & 2) ? 8 : 0)] = acc[i][e];
+            if (tok < M) rb[tok * 64 + i * 16 + gi + ((e & 2) ? 8 : 0)] = acc[i][e];
         }
     __threadfence_block();
     __syncwarp();
     const int lo = max(cs, q * G), hi = min(ce, (q + 1) * G);
-    const int nw = min(kWarpsV2, hi - lo);          // warps holding a partial of this quad
-    const int w0 = (lo - cs) % kWarpsV2;            // first of them (cyclically)
-    int last = 0;
-    if (lane == 0) last = atomicAdd(&qr.cnt[b], 1) == nw - 1;
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence_block();
+    const int wa = warp_of(lo - cs, n), wb = warp_of(hi - 1 - cs, n);
+    if (wb > wa) {   // shared with other warps: only the last of them goes on
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&qcnt[wa], 1) == wb - wa;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) return;
+        __threadfence_block();
+        if (lane == 0) qcnt[wa] = 0;
+    }
+    // warp wa holds q in slot 0 only if q is also its first quad; the others hold it as their first
+    const int slot_a = (cs + wstart(wa, n)) / G == q ? 0 : 1;
     const bool whole = cs <= q * G && ce >= (q + 1) * G;
     const int nout = 64 * M;
     float* base = a.slots + (size_t)q * 8 * 512;
@@ -171,18 +185,13 @@ __device__ __forceinline__ void park_quad(const Gemv2Args& a, QuadRed& qr, float
     }
     for (int o = lane; o < nout; o += 32) {
         const int tok = o >> 6, row = o & 63;
-        float v = 0.0f;
-        for (int w = 0; w < kWarpsV2; ++w) {
-            const int d = (w - w0 + kWarpsV2) % kWarpsV2;
-            if (d < nw) v += rb[(tok * kWarpsV2 + w) * 64 + row];
-        }
+        float v = red[(size_t)(wa * 2 + slot_a) * M * 64 + o];
+        for (int w = wa + 1; w <= wb; ++w) v += red[(size_t)w * 2 * M * 64 + o];
         if (whole)
             store_out(a, q, row, tok, v, rs[tok]);
         else
             base[(size_t)(cta - cf) * 512 + row * 8 + tok] = v;
     }
-    __syncwarp();
-    if (lane == 0) qr.cnt[b] = 0;
     if (!whole) {
         __threadfence();
         __syncwarp();
@@ -201,64 +210,59 @@ __device__ __forceinline__ void park_quad(const Gemv2Args& a, QuadRed& qr, float
             if (lane == 0) atomicExch(a.counters + q, 0);
         }
     }
-    __threadfence_block();
     __syncwarp();
-    if (lane == 0) *reinterpret_cast<volatile int*>(&qr.done[b]) = q;
 }
 
+// kRaw: every |scale| < 2^-1, so the odd-nibble rows dequantize from the raw masked bits (q * 2^-129
+// read as bf16, times s * 2^129); otherwise all four rows go through the (128 + q) magic.
+template <bool kRaw>
 __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) unsigned long long bars[kWarpsV2][kStages];
     __shared__ float wss[kWarpsV2][8];
     __shared__ float rs[8];
-    __shared__ QuadRed qr;
-    __shared__ uint2 zero_frag;
+    __shared__ int qcnt[kWarpsV2];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
     const int C = gridDim.x, cta = blockIdx.x;
     const int cs = range_start(cta, a.U, C), ce = range_start(cta + 1, a.U, C);
     const int G = a.G, M = a.M;
-    const int q_first = cs / G;
     const int stages = a.stages;
     const size_t ring_bytes = (size_t)stages * kUnitBytes;
     uint8_t* ring = smem + (size_t)warp * ring_bytes;
     const uint32_t ring_s = smem_addr(ring);
     const uint32_t bar0 = smem_addr(&bars[warp][0]);
     float* red = reinterpret_cast<float*>(smem + (size_t)kWarpsV2 * ring_bytes);
-    uint2* xf = reinterpret_cast<uint2*>(smem + (size_t)kWarpsV2 * ring_bytes + (size_t)kRedBytesPerTok * M);
+    uint32_t* xs = reinterpret_cast<uint32_t*>(smem + (size_t)kWarpsV2 * ring_bytes + (size_t)kRedBytesPerTok * M);
 
-    // this warp's units: cs + warp + 16k < ce
-    const int n_units = ce - cs > warp ? (ce - cs - warp + kWarpsV2 - 1) / kWarpsV2 : 0;
-    int pq = (cs + warp) / G, pg = (cs + warp) - pq * G;   // producer position
+    // this warp's run of units
+    const int n = ce - cs;
+    const int u0 = wstart(warp, n);
+    const int n_units = wstart(warp + 1, n) - u0;
+    int pq = (cs + u0) / G, pg = (cs + u0) - pq * G;   // producer position
     if (lane == 0) {
         for (int s = 0; s < stages; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * s));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (threadIdx.x < kWarpsV2) qcnt[threadIdx.x] = 0;
     __syncwarp();
     for (int s = 0; s < stages && s < n_units; ++s) {
         if (lane == 0) issue_unit(a, pq, pg, ring_s + s * kUnitBytes, bar0 + 8 * s);
-        step(pq, pg, G);
-    }
-    if (threadIdx.x == 0) {
-        qr.cnt[0] = qr.cnt[1] = 0;
-        qr.done[q_first & 1] = q_first - 2;
-        qr.done[(q_first + 1) & 1] = q_first - 1;
-        zero_frag = make_uint2(0u, 0u);
+        step1(pq, pg, G);
     }
 
-    // stage x (full K, M <= 8 tokens) into B-fragment order; sums of squares per token
+    // stage x (full K, M <= 8 tokens) into B-fragment order per token; sums of squares per token
     const bool rms = (a.flags & G4Q_QMM_RMS_SCALE) != 0;
-    const int units8 = a.K / 8;
+    const int words = a.K / 2;   // bf16 pairs per token
     for (int m = 0; m < M; ++m) {
         float ss = 0.0f;
-        const uint16_t* xr = a.x + (int64_t)m * a.ldx;
-        for (int u = threadIdx.x; u < units8; u += kThreadsV2) {
-            const uint4 v = *reinterpret_cast<const uint4*>(xr + u * 8);
-            const int kk = u >> 1, h = u & 1;
-            uint32_t* e = reinterpret_cast<uint32_t*>(xf + (kk * M + m) * 4);
-            e[0 + h] = v.x;
-            e[2 + h] = v.y;
-            e[4 + h] = v.z;
-            e[6 + h] = v.w;
+        const uint4* xr = reinterpret_cast<const uint4*>(a.x + (int64_t)m * a.ldx);
+        uint32_t* xm = xs + (size_t)m * words;
+        for (int u = threadIdx.x; u < a.K / 8; u += kThreadsV2) {
+            const uint4 v = xr[u];
+            xm[xperm(4 * u)] = v.x;
+            xm[xperm(4 * u + 1)] = v.y;
+            xm[xperm(4 * u + 2)] = v.z;
+            xm[xperm(4 * u + 3)] = v.w;
             if (rms) {
                 const uint32_t pv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -287,23 +291,22 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
     }
     __syncthreads();
 
-    // B fragments: lanes whose token is >= M read a fixed zero pair
-    const bool tok_ok = gi < M;
-    const uint2* xlane = tok_ok ? xf + gi * 4 + t : &zero_frag;
-    const int kstride = tok_ok ? M * 4 : 0;
-
+    // B fragments: lane (gi, t) reads token gi (token 0 for the columns past M; those outputs are
+    // never stored)
+    const uint4* xt = reinterpret_cast<const uint4*>(xs + (size_t)(gi < M ? gi : 0) * words) + 2 * t;
     float acc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
-    int cq = (cs + warp) / G, cg = (cs + warp) - cq * G;   // consumer position
+    int cq = (cs + u0) / G, cg = (cs + u0) - cq * G;   // consumer position
+    const int first_q = cq;
     int acc_q = cq;
     int stage = 0;
     uint32_t phase = 0;
     for (int k = 0; k < n_units; ++k) {
         if (cq != acc_q) {
-            park_quad(a, qr, red, acc_q, cs, ce, cta, C, acc, rs);
+            park_quad(a, qcnt, red, acc_q, first_q, cs, ce, cta, C, acc, rs);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -312,45 +315,52 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
         }
         wait_parity(bar0 + 8 * stage, phase, a.err);
         const uint8_t* st = ring + stage * kUnitBytes;
-        uint4 wv[4];
-        uint32_t sb0[4], sb1[4];
+        const uint4 xa = xt[cg * 8], xb = xt[cg * 8 + 1];
+        const uint32_t b0[4] = {xa.x, xa.z, xb.x, xb.z}, b1[4] = {xa.y, xa.w, xb.y, xb.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            wv[i] = reinterpret_cast<const uint4*>(st + i * 512)[lane];
+            const uint4 wv = reinterpret_cast<const uint4*>(st + i * 512)[lane];
             const uint32_t* sbw = reinterpret_cast<const uint32_t*>(st + kUnitPacked) + i * 16 + gi;
-            sb0[i] = sbw[0];
-            sb1[i] = sbw[8];
-        }
-        const uint2* xg = xlane + cg * 4 * kstride;
-        uint2 bf[4];
+            const RowConsts c0 = row_consts(sbw[0]);
+            if constexpr (kRaw) {
+                const uint32_t s1 = prmt(sbw[8], 0u, 0x1010u), b1s = prmt(sbw[8], 0u, 0x3232u);
+                const uint32_t s1h = mul_bf16x2(mul_bf16x2(s1, kPow64x2), kPow65x2);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) bf[j] = xg[j * kstride];
-        // the unit is in registers: refill this buffer `stages` units ahead
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t w = j == 0 ? wv.x : j == 1 ? wv.y : j == 2 ? wv.z : wv.w;
+                    const uint32_t w8 = w >> 8;
+                    const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
+                    const uint32_t a1 = add_bf16x2(mul_bf16x2(w & kOddNibbleMask, s1h), b1s);
+                    const uint32_t a2 = deq_r2_fast(lop_nibbles(w8), c0);
+                    const uint32_t a3 = add_bf16x2(mul_bf16x2(w8 & kOddNibbleMask, s1h), b1s);
+                    mma_bf16_16816(acc[i], a0, a1, a2, a3, b0[j], b1[j]);
+                }
+            } else {
+                const RowConsts c1 = row_consts(sbw[8]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t w = j == 0 ? wv.x : j == 1 ? wv.y : j == 2 ? wv.z : wv.w;
+                    const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
+                    const uint32_t a1 = deq_r2_fast(lop_nibbles(w >> 4), c1);
+                    const uint32_t a2 = deq_r2_fast(lop_nibbles(w >> 8), c0);
+                    const uint32_t a3 = deq_r2_fast(lop_nibbles(w >> 12), c1);
+                    mma_bf16_16816(acc[i], a0, a1, a2, a3, b0[j], b1[j]);
+                }
+            }
+        }
+        // the unit has been read: refill this buffer `stages` units ahead
         __syncwarp();
         if (k + stages < n_units) {
             if (lane == 0) issue_unit(a, pq, pg, ring_s + stage * kUnitBytes, bar0 + 8 * stage);
-            step(pq, pg, G);
+            step1(pq, pg, G);
         }
         if (++stage == stages) {
             stage = 0;
             phase ^= 1u;
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const RowConsts c0 = row_consts(sb0[i]), c1 = row_consts(sb1[i]);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint32_t w = j == 0 ? wv[i].x : j == 1 ? wv[i].y : j == 2 ? wv[i].z : wv[i].w;
-                const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
-                const uint32_t a1 = deq_r2_fast(lop_nibbles(w >> 4), c1);
-                const uint32_t a2 = deq_r2_fast(lop_nibbles(w >> 8), c0);
-                const uint32_t a3 = deq_r2_fast(lop_nibbles(w >> 12), c1);
-                mma_bf16_16816(acc[i], a0, a1, a2, a3, bf[j].x, bf[j].y);
-            }
-        }
-        step(cq, cg, G);
+        step1(cq, cg, G);
     }
-    if (n_units > 0) park_quad(a, qr, red, acc_q, cs, ce, cta, C, acc, rs);
+    if (n_units > 0) park_quad(a, qcnt, red, acc_q, first_q, cs, ce, cta, C, acc, rs);
 }
 
 }  // namespace
@@ -392,8 +402,11 @@ void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     static bool attr_set[64] = {false};
     const int dev = current_device();
     if (!attr_set[dev & 63]) {
-        check_cuda(cudaFuncSetAttribute(gemv2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)max_dynamic_smem(reinterpret_cast<const void*>(gemv2_kernel))),
+        check_cuda(cudaFuncSetAttribute(gemv2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)max_dynamic_smem(reinterpret_cast<const void*>(gemv2_kernel<true>))),
+                   "cudaFuncSetAttribute(gemv2)");
+        check_cuda(cudaFuncSetAttribute(gemv2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)max_dynamic_smem(reinterpret_cast<const void*>(gemv2_kernel<false>))),
                    "cudaFuncSetAttribute(gemv2)");
         attr_set[dev & 63] = true;
     }
@@ -424,7 +437,10 @@ void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     a.err = ds.err;
     a.stages = gemv2_stages(a.M, a.K);
     const size_t smem = gemv2_smem(a.stages, a.M, a.K);
-    gemv2_kernel<<<grid, kThreadsV2, smem, st>>>(a);
+    if (w.small_scales)
+        gemv2_kernel<true><<<grid, kThreadsV2, smem, st>>>(a);
+    else
+        gemv2_kernel<false><<<grid, kThreadsV2, smem, st>>>(a);
     check_cuda(cudaGetLastError(), "gemv2 launch");
 }
 
