@@ -249,6 +249,12 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
         if (lane == 0) issue_unit(a, pq, pg, ring_s + s * kUnitBytes, bar0 + 8 * s);
         step1(pq, pg, G);
     }
+    // Launched as a programmatic dependent of the previous kernel in the stream: everything above
+    // touches only this launch's shared memory and the weights (written before any compute call
+    // returns), so it overlaps the previous kernel's tail. x, y and the shared scratch wait for that
+    // kernel to complete; the next launch may start its own prologue as this grid's SMs free up.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     // stage x (full K, M <= 8 tokens) into B-fragment order per token; sums of squares per token
     const bool rms = (a.flags & G4Q_QMM_RMS_SCALE) != 0;
@@ -436,12 +442,17 @@ void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     a.counters = ds.counters;
     a.err = ds.err;
     a.stages = gemv2_stages(a.M, a.K);
-    const size_t smem = gemv2_smem(a.stages, a.M, a.K);
-    if (w.small_scales)
-        gemv2_kernel<true><<<grid, kThreadsV2, smem, st>>>(a);
-    else
-        gemv2_kernel<false><<<grid, kThreadsV2, smem, st>>>(a);
-    check_cuda(cudaGetLastError(), "gemv2 launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreadsV2);
+    cfg.dynamicSmemBytes = gemv2_smem(a.stages, a.M, a.K);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    check_cuda(cudaLaunchKernelEx(&cfg, w.small_scales ? gemv2_kernel<true> : gemv2_kernel<false>, a), "gemv2 launch");
 }
 
 }  // namespace g4q
