@@ -257,7 +257,6 @@ G4qStatus g4q_weight_free(G4qWeight* h) {
         cudaFree(w->argmax_scratch);
         cudaFree(w->mlx_scales);
         cudaFree(w->mlx_biases);
-        direct_release(*w);
         cudaSetDevice(prev);
         delete w;
     });
@@ -355,7 +354,6 @@ G4qStatus g4q_weight_load(G4qWeight* h, int64_t dst_row0, const uint32_t* packed
         check_cuda(cudaMemcpy(&flags, w->d_flags, sizeof(int), cudaMemcpyDeviceToHost), "read handle flags");
         w->fast_ok = (flags & 1) == 0;   // cached so compute calls never read device memory
         w->small_scales = (flags & 4) == 0;
-        direct_prepare(*w);
     });
 }
 
@@ -433,9 +431,7 @@ static void qmm_common(const char* fn, const G4qWeight* h, const uint16_t* x, in
     }
     require(w->fast_ok, G4Q_ERR_UNSUPPORTED_CONFIG,
             "a scale is non-finite or |scale| >= 2^120; use g4q_dequantize for such weights");
-    if (M == 1 && direct_ready(*w, y))
-        launch_direct(*w, x, y, flags, eps, st);   // the persistent decode kernel, one phase
-    else if (M <= 16)
+    if (M <= 16)
         launch_gemv(c, st);
     else
         launch_gemm(c, st);

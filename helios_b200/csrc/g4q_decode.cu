@@ -101,20 +101,7 @@ struct DecodeArgs {
     unsigned long long* keys_out;
     uint16_t* logits;                         // optional bf16 logits of the argmax phase
     int* err;
-    // direct launch of one cached phase (a standalone quantized matmul): x, y and flags of the call
-    int direct;
-    const uint16_t* dx;
-    void* dy;
-    uint32_t dflags;
 };
-
-__device__ __forceinline__ uint32_t phase_flags(const DecodeArgs& a, const PhaseDev& P) {
-    return a.direct ? a.dflags : P.flags;
-}
-__device__ __forceinline__ void* phase_y(const DecodeArgs& a, const PhaseDev& P) { return a.direct ? a.dy : P.y; }
-__device__ __forceinline__ const uint16_t* phase_x(const DecodeArgs& a, const PhaseDev& P) {
-    return a.direct ? a.dx : P.x;
-}
 
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -473,7 +460,7 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
         v[h] = s;
     }
     const bool whole = cs <= q * G && ce >= (q + 1) * G;
-    const uint32_t fl = phase_flags(a, P);
+    const uint32_t fl = P.flags;
     const bool argmax = (fl & G4Q_PHASE_ARGMAX) != 0;
     if (whole && argmax) {
 #pragma unroll
@@ -502,7 +489,7 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
             }
         } else if (whole) {   // an allreduce phase's y needs every rank: written back later
 #pragma unroll
-            for (int h = 0; h < 2; ++h) store_y(phase_y(a, P), fl, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs));
+            for (int h = 0; h < 2; ++h) store_y(P.y, fl, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs));
         } else if (argmax) {   // the logits are needed now: the last contributing CTA finishes the quad
             if (arrive_last(a.qcount + 2 * a.qcount_stride + q, cl - cf)) {
 #pragma unroll
@@ -543,7 +530,7 @@ __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P,
     };
     if (P.src < 0) {
         for (int u = threadIdx.x; u < P.K / 8; u += kThreads) {
-            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(phase_x(a, P)) + u);
+            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(P.x) + u);
             xs[xperm(4 * u)] = v.x;
             xs[xperm(4 * u + 1)] = v.y;
             xs[xperm(4 * u + 2)] = v.z;
@@ -635,7 +622,7 @@ __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P,
 template <bool kTP>
 __device__ __forceinline__ void write_back_warp(const DecodeArgs& a, int pp, int cta, int C, float rs_prev, uint32_t tag0) {
     const PhaseDev& Q = a.ph[pp];
-    const uint32_t fl = phase_flags(a, Q);
+    const uint32_t fl = Q.flags;
     if (fl & G4Q_PHASE_ARGMAX) return;
     const int lane = threadIdx.x & 31;
     const uint32_t tag = phase_tag(tag0, pp);
@@ -652,13 +639,13 @@ __device__ __forceinline__ void write_back_warp(const DecodeArgs& a, int pp, int
             s = sum_slots4(reinterpret_cast<const float*>(a.slots) + slot_f(a, Q, pp, q, 0) + lane * 4, cl - cf + 1);
         const int n = q * 64 + lane * 4;
         if (fl & G4Q_QMM_OUT_F32) {
-            float* y = reinterpret_cast<float*>(phase_y(a, Q)) + n;
+            float* y = reinterpret_cast<float*>(Q.y) + n;
             y[0] = __fmul_rn(s.x, rs_prev);
             y[1] = __fmul_rn(s.y, rs_prev);
             y[2] = __fmul_rn(s.z, rs_prev);
             y[3] = __fmul_rn(s.w, rs_prev);
         } else {
-            *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(phase_y(a, Q)) + n) = finish4(s, rs_prev);
+            *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(Q.y) + n) = finish4(s, rs_prev);
         }
     }
 }
@@ -754,7 +741,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         const float rs_prev = sh.rs_prev;
         const uint32_t tag0 = sh.tag0;
         // ---- stage x (polls the producers' slots) and its RMS scale
-        const bool rms = (phase_flags(a, P) & G4Q_QMM_RMS_SCALE) != 0;
+        const bool rms = (P.flags & G4Q_QMM_RMS_SCALE) != 0;
         float ss = stage_x<kTP>(a, P, xs, sh.cut, C, rs_prev, tag0, rms);
         if (p == 0) {   // first weight loads only now: the x loads above are not queued behind them
             for (int s = 0; s < kStages && pre.p < a.n_phases; ++s) {
@@ -849,7 +836,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             claim = __shfl_sync(0xffffffffu, claim, 0);
             if (claim) write_back_warp<kTP>(a, p - 1, cta, C, rs_prev, tag0);
         }
-        const bool argmax = (phase_flags(a, P) & G4Q_PHASE_ARGMAX) != 0;
+        const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
         if (argmax) {
             unsigned long long kk = best;
 #pragma unroll
@@ -880,7 +867,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     // ---- a plan that ends with a regular phase: once every CTA has left its partials, finish the
     //      quads no single CTA finished
     const int last = a.n_phases - 1;
-    if (!(phase_flags(a, a.ph[last]) & G4Q_PHASE_ARGMAX)) {
+    if (!(a.ph[last].flags & G4Q_PHASE_ARGMAX)) {
         __syncthreads();
         if (threadIdx.x == 0) spin_until(a.done + last, (unsigned)C, a.err);
         __syncthreads();
@@ -893,7 +880,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         if (prev == (unsigned)C - 1) {
             unsigned long long k = atomicExch(a.key, 0ull);
             if constexpr (kTP) k = exchange_keys(a, k, phase_tag(sh.tag0, a.n_phases));
-            if (phase_flags(a, a.ph[last]) & G4Q_PHASE_ARGMAX) {
+            if (a.ph[last].flags & G4Q_PHASE_ARGMAX) {
                 if (a.tokens) a.tokens[0] = (int32_t)key_index(k);
                 if (a.values) a.values[0] = key_value(k);
                 if (a.keys_out) a.keys_out[0] = k;
@@ -1181,7 +1168,7 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     for (int r = 0; r < plan->n_ranks; ++r)
         if (!plan->peer_rp[r] || !plan->peer_xkeys[r])
             throw Error(G4Q_ERR_INVALID_ARGUMENT, "tensor-parallel plan: peer buffers not set");
-    DecodeArgs a{};   // value-initialised: direct = 0, no per-call x / y overrides
+    DecodeArgs a{};
     a.ph = plan->d_ph;
     a.n_phases = plan->n_phases;
     a.eps = eps;
@@ -1220,129 +1207,6 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
         check_cuda(cudaLaunchKernelEx(&cfg, decode_kernel<true>, a), "cudaLaunchKernelEx(decode)");
     else
         check_cuda(cudaLaunchKernelEx(&cfg, decode_kernel<false>, a), "cudaLaunchKernelEx(decode)");
-}
-
-// ---- direct launches: one standalone quantized matmul (M = 1) through the same kernel ----------
-// g4q_qmm / g4q_qmm_ex at M = 1 on a weight that suits the persistent kernel run it as a one-phase
-// plan. The phase descriptor is cached on the weight when it is loaded and the per-device scratch
-// (counters, slots) is sized then, so a call allocates nothing. Calls on one device share that
-// scratch: they run in stream order, like every other call that shares a stream.
-
-namespace {
-struct DirectScratch {
-    unsigned int* done = nullptr;   // [3]: phase counter, exit counter, launch counter
-    unsigned long long* key = nullptr;
-    float* slots = nullptr;
-    int64_t slot_floats = 0;
-    unsigned long long** peers = nullptr;
-};
-std::mutex g_direct_mu;
-DirectScratch g_direct[64];
-
-size_t direct_smem(int64_t K) { return (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4 + (size_t)(K + 8) * 2; }
-}  // namespace
-
-void direct_prepare(Weight& w) {
-    if (w.mlx) return;
-    const int sms = device_sm_count();
-    const int64_t N = w.N, K = w.K;
-    bool ok = w.fast_ok && w.small_scales && N % 64 == 0 && K % 64 == 0;
-    const int64_t Q = N / 64, G = K / 64, U = Q * G;
-    ok = ok && U >= sms && (uint64_t)(U + 1) * (uint64_t)sms < (1ull << 32) &&
-         (uint64_t)N * (uint64_t)K / 2 < (1ull << 32) && (U + sms - 1) / sms + G - 2 < (kMaxCtaQuads - 1) * G &&
-         direct_smem(K) <= max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel<false>));
-    int ks = 1;
-    if (ok)
-        for (int64_t q = 0; q < Q; ++q) {
-            const int64_t cf = (q * G + 1) * sms - 1, cl = ((q + 1) * G) * sms - 1;
-            ks = std::max<int>(ks, (int)(cl / U - cf / U + 1));
-        }
-    ok = ok && ks <= kSlots;
-    if (!ok) {
-        cudaFree(w.d_phase);
-        w.d_phase = nullptr;
-        return;
-    }
-    PhaseDev d{};
-    d.packed = w.packed;
-    d.sb = w.sb;
-    d.N = (int)N;
-    d.K = (int)K;
-    d.R = (int)(N / 16);
-    d.G = (int)G;
-    d.Q = (int)Q;
-    d.U = (int)U;
-    d.src = -1;
-    d.src_ranks = 1;
-    d.ks = ks;
-    d.need_done = 1;
-    if (!w.d_phase) check_cuda(cudaMalloc(&w.d_phase, sizeof(PhaseDev)), "direct phase descriptor");
-    check_cuda(cudaMemcpy(w.d_phase, &d, sizeof(PhaseDev), cudaMemcpyHostToDevice), "direct phase descriptor");
-    std::lock_guard<std::mutex> lock(g_direct_mu);
-    DirectScratch& ds = g_direct[w.device];
-    if (!ds.done) {
-        check_cuda(cudaMalloc(&ds.done, sizeof(unsigned int) * 3), "direct scratch");
-        check_cuda(cudaMemset(ds.done, 0, sizeof(unsigned int) * 3), "direct scratch");
-        check_cuda(cudaMalloc(&ds.key, sizeof(unsigned long long)), "direct scratch");
-        check_cuda(cudaMemset(ds.key, 0, sizeof(unsigned long long)), "direct scratch");
-        check_cuda(cudaMalloc(&ds.peers, sizeof(void*) * 2 * kMaxRanks), "direct scratch");
-        check_cuda(cudaMemset(ds.peers, 0, sizeof(void*) * 2 * kMaxRanks), "direct scratch");
-        check_cuda(cudaFuncSetAttribute(decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel<false>))),
-                   "cudaFuncSetAttribute(decode)");
-    }
-    const int64_t need = Q * ks * 64;
-    if (need > ds.slot_floats) {
-        check_cuda(cudaDeviceSynchronize(), "direct scratch");
-        cudaFree(ds.slots);
-        ds.slots = nullptr;
-        ds.slot_floats = 0;
-        check_cuda(cudaMalloc(&ds.slots, sizeof(float) * (size_t)need), "direct scratch");
-        ds.slot_floats = need;
-    }
-}
-
-void direct_release(Weight& w) {
-    cudaFree(w.d_phase);
-    w.d_phase = nullptr;
-}
-
-bool direct_ready(const Weight& w, const void* y) {
-    return w.d_phase != nullptr && (reinterpret_cast<uintptr_t>(y) & 7u) == 0;
-}
-
-void launch_direct(const Weight& w, const uint16_t* x, void* y, uint32_t flags, float eps, cudaStream_t st) {
-    DirectScratch& ds = g_direct[w.device];
-    DecodeArgs a{};
-    a.ph = static_cast<const PhaseDev*>(w.d_phase);
-    a.n_phases = 1;
-    a.eps = eps;
-    a.done = ds.done;
-    a.exit_count = ds.done + 1;
-    a.run = ds.done + 2;
-    a.key = ds.key;
-    a.slots = reinterpret_cast<unsigned long long*>(ds.slots);
-    a.peer_rp = ds.peers;
-    a.peer_xkeys = ds.peers + kMaxRanks;
-    a.rank = 0;
-    a.n_ranks = 1;
-    a.buf_words = ds.slot_floats / 2;
-    a.err = device_scratch().err;
-    a.direct = 1;
-    a.dx = x;
-    a.dy = y;
-    a.dflags = flags;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(device_sm_count());
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = direct_smem(w.K);
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    check_cuda(cudaLaunchKernelEx(&cfg, decode_kernel<false>, a), "cudaLaunchKernelEx(decode, direct)");
 }
 
 }  // namespace g4q

@@ -31,9 +31,6 @@ struct Weight {
     bool small_scales = true;    // host copy of !(bit2): every |scale| < 2^-1
     // lazily created scratch for the LM-head argmax (keys[16] + counter), zeroed once
     unsigned long long* argmax_scratch = nullptr;
-    // phase descriptor of the persistent decode kernel for direct M = 1 launches (set at load
-    // when the weight suits that kernel, else null)
-    void* d_phase = nullptr;
 };
 
 // Raised inside entry points; converted to a status + last-error message at the C-ABI edge.
@@ -117,11 +114,6 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
 void decode_plan_buffers(void* plan, void** slots, uint64_t* slot_bytes, void** xkeys, uint64_t* xkey_bytes);
 void decode_plan_set_peers(void* plan, void* const* slots, void* const* xkeys);
 void decode_plan_free(void* plan);
-// direct M = 1 launches of the decode kernel (one cached phase per weight)
-void direct_prepare(Weight& w);
-void direct_release(Weight& w);
-bool direct_ready(const Weight& w, const void* y);
-void launch_direct(const Weight& w, const uint16_t* x, void* y, uint32_t flags, float eps, cudaStream_t st);
 void decode_plan_run(void* plan, int M, float eps, float softcap, int64_t row_offset, int32_t* tokens, float* values,
                      uint64_t* keys, uint16_t* logits, int64_t ld_logits, cudaStream_t st);
 
