@@ -685,7 +685,10 @@ template <bool kTP>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ CtaShared sh;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
+    // the warp index through a shuffle from lane 0: provably warp-uniform, so the compiler keeps it
+    // and everything derived from it (ring and barrier addresses, unit cursors) in uniform registers
+    const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0), lane = threadIdx.x & 31, gi = lane >> 2,
+              t = lane & 3;
     const int C = gridDim.x, cta = blockIdx.x;
     uint8_t* ring = smem + (size_t)warp * kRingBytes;
     const uint32_t ring_s = saddr(ring);

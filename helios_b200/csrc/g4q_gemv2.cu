@@ -222,7 +222,10 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
     __shared__ float wss[kWarpsV2][8];
     __shared__ float rs[8];
     __shared__ int qcnt[kWarpsV2];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
+    // the warp index through a shuffle from lane 0: provably warp-uniform, so the compiler keeps it
+    // and everything derived from it (ring and barrier addresses, unit cursors) in uniform registers
+    const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0), lane = threadIdx.x & 31, gi = lane >> 2,
+              t = lane & 3;
     const int C = gridDim.x, cta = blockIdx.x;
     const int cs = range_start(cta, a.U, C), ce = range_start(cta + 1, a.U, C);
     const int G = a.G, M = a.M;
