@@ -57,6 +57,8 @@ class G4qDecodePhase(ctypes.Structure):
                 ("ldy", ctypes.c_int64), ("flags", ctypes.c_uint32)]
 
 
+DTYPE_BF16 = 0
+DTYPE_F32 = 1
 PHASE_ARGMAX = 0x4
 PHASE_ALLREDUCE = 0x8
 IPC_HANDLE_BYTES = 64
@@ -86,6 +88,11 @@ SIGNATURES = {
     "g4q_ipc_handle": [_P, ctypes.POINTER(ctypes.c_uint8)],
     "g4q_ipc_open": [ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(_P)],
     "g4q_ipc_close": [_P],
+    "g4q_comm_create": [_I32, _I32, _I64, ctypes.POINTER(_P)],
+    "g4q_comm_buffer": [_P, ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_uint64)],
+    "g4q_comm_set_peers": [_P, ctypes.POINTER(_P)],
+    "g4q_allreduce": [_P, _P, _I64, _I32, _P],
+    "g4q_comm_free": [_P],
     "g4q_synth_matrix": [_U64, _I64, _I64, _I32, _I32, _P, _P, _P, _P],
     "g4q_synth_normal_bf16": [_U64, _I64, _P, _P],
 }

@@ -518,6 +518,32 @@ G4qStatus g4q_decode_plan_set_peers(G4qDecodePlan* plan, void* const* slots, voi
     return guarded("g4q_decode_plan_set_peers", [&] { decode_plan_set_peers(plan, slots, xkeys); });
 }
 
+G4qStatus g4q_comm_create(int32_t rank, int32_t n_ranks, int64_t max_elems, G4qComm** out) {
+    return guarded("g4q_comm_create", [&] {
+        require(out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null out pointer");
+        *out = nullptr;
+        (void)device_scratch();
+        *out = reinterpret_cast<G4qComm*>(comm_create(rank, n_ranks, max_elems));
+    });
+}
+
+G4qStatus g4q_comm_buffer(const G4qComm* comm, void** buffer, uint64_t* bytes) {
+    return guarded("g4q_comm_buffer", [&] { comm_buffer(comm, buffer, bytes); });
+}
+
+G4qStatus g4q_comm_set_peers(G4qComm* comm, void* const* peer_buffers) {
+    return guarded("g4q_comm_set_peers", [&] { comm_set_peers(comm, peer_buffers); });
+}
+
+G4qStatus g4q_allreduce(G4qComm* comm, void* data, int64_t count, int32_t dtype, void* stream) {
+    return guarded("g4q_allreduce",
+                   [&] { comm_allreduce(comm, data, count, dtype, reinterpret_cast<cudaStream_t>(stream)); });
+}
+
+G4qStatus g4q_comm_free(G4qComm* comm) {
+    return guarded("g4q_comm_free", [&] { comm_free(comm); });
+}
+
 G4qStatus g4q_ipc_handle(const void* device_ptr, uint8_t* handle) {
     return guarded("g4q_ipc_handle", [&] {
         require(device_ptr != nullptr && handle != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires non-null pointers");

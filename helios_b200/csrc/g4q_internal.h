@@ -33,6 +33,13 @@ struct Weight {
     unsigned long long* argmax_scratch = nullptr;
 };
 
+// tensor-parallel allreduce over NVLink peer memory (g4q_comm.cu)
+void* comm_create(int rank, int n_ranks, int64_t max_elems);
+void comm_buffer(const void* h, void** buf, uint64_t* bytes);
+void comm_set_peers(void* h, void* const* peer_bufs);
+void comm_allreduce(void* h, void* data, int64_t count, int dtype, cudaStream_t st);
+void comm_free(void* h);
+
 // Raised inside entry points; converted to a status + last-error message at the C-ABI edge.
 struct Error : std::runtime_error {
     G4qStatus status;

@@ -82,7 +82,8 @@ G4qStatus g4q_get_last_error(char* buffer, size_t buffer_len);
  * group-64 override the reference's manifest allows per module (model_manifest.cc:146-152), and
  * groups 32 / 128 at 4 or 8 bits as mlx::core accepts them (any N, K % group == 0), keep MLX's
  * layout on the device and run g4q_qmm/_ex, g4q_dequantize and export on generic CUDA-core
- * kernels; the fused LM head and the decode plan return G4Q_ERR_UNSUPPORTED_CONFIG for them. Any other bits/group is G4Q_ERR_UNSUPPORTED_CONFIG.
+ * kernels; the fused LM head and the decode plan return G4Q_ERR_UNSUPPORTED_CONFIG for them. Any
+ * other bits/group is G4Q_ERR_UNSUPPORTED_CONFIG.
  * g4q_weight_load copies the window [src_row0, src_row0+n_rows) x [src_k0, src_k0+K) of an
  * MLX-layout matrix (packed uint32 [src_rows, src_cols*bits/32], scales/biases bf16
  * [src_rows, src_cols/group], host or device memory) into rows [dst_row0, dst_row0+n_rows) of the
@@ -223,6 +224,29 @@ G4qStatus g4q_decode_plan_set_peers(G4qDecodePlan* plan, void* const* slots, voi
 G4qStatus g4q_ipc_handle(const void* device_ptr, uint8_t* handle);
 G4qStatus g4q_ipc_open(const uint8_t* handle, void** device_ptr);
 G4qStatus g4q_ipc_close(void* device_ptr);
+
+/* ---- tensor-parallel allreduce -----------------------------------------------------------------
+ * The TP communicator of the boundary: allreduce(sum) of a bf16 or fp32 vector across the ranks of
+ * one node, for the sum after o_proj / down_proj when the linears run sharded outside a decode plan
+ * (prefill chunks, verify blocks). No reference counterpart: the reference runs one process per
+ * model; this replaces the collective of the Megatron split of the same linears. Over NVLink peer
+ * memory (CUDA IPC); no library kernel touches peer memory: one shot (every rank pushes its vector
+ * to every rank) up to 256 KB, two shots (reduce-scatter + all-gather, chunked) above. Sums are fp32
+ * in rank order, so every rank gets the same bits; every wait is bounded (code 40 in the device
+ * error word). Wiring as for the TP decode plan: g4q_comm_create on every rank, export
+ * g4q_comm_buffer with g4q_ipc_handle, exchange the handles on the host, g4q_ipc_open the peers'
+ * and pass them indexed by rank to g4q_comm_set_peers. Collective: every rank calls g4q_allreduce
+ * the same number of times with the same count and dtype; calls on one communicator are serialised
+ * on `stream`. data: device pointer, 16-byte aligned, count * element size a multiple of 16,
+ * count <= max_elems. */
+typedef struct G4qComm G4qComm;
+#define G4Q_DTYPE_BF16 0
+#define G4Q_DTYPE_F32 1
+G4qStatus g4q_comm_create(int32_t rank, int32_t n_ranks, int64_t max_elems, G4qComm** out);
+G4qStatus g4q_comm_buffer(const G4qComm* comm, void** buffer, uint64_t* bytes);
+G4qStatus g4q_comm_set_peers(G4qComm* comm, void* const* peer_buffers);
+G4qStatus g4q_allreduce(G4qComm* comm, void* data, int64_t count, int32_t dtype, void* stream);
+G4qStatus g4q_comm_free(G4qComm* comm);
 
 /* ---- device-side failure detection ----------------------------------------------------------
  * Every wait inside a libg4q kernel is bounded; a wait that gives up records a nonzero code in a

@@ -174,3 +174,80 @@ def test_tensor_parallel_pipelined_prefill_two_gpus(cuda, oracle):
     from helios_b200.stack import decode_keys
     toks, vals = decode_keys(torch.from_numpy(key))
     assert toks[0] == ref_tok or abs(vals[0] - ref_val) <= 0.125
+
+
+def _allreduce_worker(rank, world, port, out_q):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    bad = []
+    try:
+        from helios_b200 import _lib
+        from helios_b200.comm import Comm
+        comm = Comm(rank, world, 2048 * 3840, dist.group.WORLD)
+
+        def inputs(seed, count, dtype):
+            g = torch.Generator().manual_seed(seed)
+            return [torch.randn(count, generator=g).to(dtype) for _ in range(world)]
+
+        def expect(parts):
+            s = torch.zeros(parts[0].shape, dtype=torch.float32)
+            for p in parts:           # fp32, rank order, as the kernel sums
+                s = s + p.float()
+            return s.to(parts[0].dtype)
+
+        # one shot (decode-sized), two shots (prefill-sized, ragged last chunk), fp32; three calls each
+        # so both slot parities and the call counter are exercised
+        for count, dtype in ((3840, torch.bfloat16), (8, torch.bfloat16), (2048 * 3840, torch.bfloat16),
+                             (1000008, torch.float32), (3840 * 4, torch.float32)):
+            for call in range(3):
+                parts = inputs(1000 * count + call, count, dtype)
+                t = parts[rank].cuda()
+                comm.allreduce(t)
+                torch.cuda.synchronize()
+                if not torch.equal(t.cpu(), expect(parts)):
+                    bad.append((count, str(dtype), call))
+        # replays of a captured allreduce: the call counter lives on the device
+        t = torch.empty(3840, dtype=torch.bfloat16, device="cuda")
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            t.copy_(inputs(7, 3840, torch.bfloat16)[rank].cuda())
+            comm.allreduce(t)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                comm.allreduce(t)
+        torch.cuda.synchronize()
+        for rep in range(3):
+            parts = inputs(50 + rep, 3840, torch.bfloat16)
+            t.copy_(parts[rank].cuda())
+            torch.cuda.synchronize()
+            g.replay()
+            torch.cuda.synchronize()
+            if not torch.equal(t.cpu(), expect(parts)):
+                bad.append(("graph", rep))
+        del g
+        code = _lib.device_error()
+        dist.barrier()
+        comm.free()
+        out_q.put((rank, bad, code))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_allreduce_two_gpus():
+    """g4q_allreduce (one shot and two shots, bf16 and fp32, eager and graph-replayed) equals the fp32
+    rank-order sum bit for bit on both ranks, with no in-kernel wait giving up."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    mp.start_processes(_allreduce_worker, args=(2, _free_port(), q), nprocs=2, join=True, start_method="spawn")
+    res = sorted([q.get(), q.get()])
+    for rank, bad, code in res:
+        assert code == 0, f"rank {rank}: device error word {code}"
+        assert not bad, f"rank {rank}: mismatches {bad}"
