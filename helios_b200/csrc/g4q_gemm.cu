@@ -22,6 +22,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "g4q_common.cuh"
@@ -54,6 +55,8 @@ struct GemmParams {
     const float* rms;     // per-row scale or nullptr
     int vec_ok;
     int* err;
+    int splits;           // > 1: split-K; blockIdx.z takes k-blocks [KB*z/splits, KB*(z+1)/splits) and
+    float* part;          //      writes its unscaled fp32 tile to part + z*M*N (row stride N)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -174,6 +177,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    // this CTA's k-blocks (all of them unless split-K); i counts k-steps from kb_begin
+    const int kb_begin = (int)((int64_t)p.KB * blockIdx.z / p.splits);
+    const int nkb = (int)((int64_t)p.KB * (blockIdx.z + 1) / p.splits) - kb_begin;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -197,9 +203,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (warp == 0) {
         // ---------------- TMA producer
         if (lane == 0) {
-            for (int kb = 0; kb < p.KB; ++kb) {
-                const int s = kb % STAGES;
-                if (kb >= STAGES) mbar_wait(empty(s), ((kb / STAGES) - 1) & 1, p.err, 1);
+            for (int i = 0; i < nkb; ++i) {
+                const int kb = kb_begin + i, s = i % STAGES;
+                if (i >= STAGES) mbar_wait(empty(s), ((i / STAGES) - 1) & 1, p.err, 1);
                 mbar_expect_tx(full(s), kXBytes + kPBytes + kSBBytes);
                 tma_load_2d(sX + s * kXBytes, &tm_x, kb * BK, m0, full(s));
                 tma_load_2d(sP + s * kPBytes, &tm_p, 0, (kb * p.R + n0 / 16) * 4, full(s));
@@ -208,9 +214,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer
-        for (int kb = 0; kb < p.KB; ++kb) {
-            const int s = kb % STAGES;
-            const uint32_t ph = (kb / STAGES) & 1;
+        for (int i = 0; i < nkb; ++i) {
+            const int s = i % STAGES;
+            const uint32_t ph = (i / STAGES) & 1;
             mbar_wait(full(s), ph, p.err, 2);
             mbar_wait(bfull(s), ph, p.err, 3);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -221,7 +227,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {   // token rows 0-127 -> columns 0-255, 128-255 -> 256-511
                         const uint64_t ad = umma_desc_sw128(sX + s * kXBytes + h * kXHalf + kk * 32);
-                        umma_bf16(tmem + (uint32_t)(h * BN), ad, bd, (kb | kk) != 0);
+                        umma_bf16(tmem + (uint32_t)(h * BN), ad, bd, (i | kk) != 0);
                     }
                 }
                 umma_commit(empty(s));
@@ -235,9 +241,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int d = threadIdx.x - 64;
         const int rl = (d & 127) >> 3, gi = d & 7, half = d >> 7;   // 16-row tile, row pair, row of the pair
         const int nl = 16 * rl + gi + 8 * half;
-        for (int kb = 0; kb < p.KB; ++kb) {
-            const int s = kb % STAGES;
-            mbar_wait(full(s), (kb / STAGES) & 1, p.err, 4);
+        for (int i = 0; i < nkb; ++i) {
+            const int s = i % STAGES;
+            mbar_wait(full(s), (i / STAGES) & 1, p.err, 4);
             // packed words of lanes 4gi..4gi+3 of block rl: 64 logical bytes at rl*512 + gi*64,
             // stored by the 128B-swizzled TMA as chunk c of row rho at chunk c ^ (rho & 7)
             uint4 wv[4];
@@ -283,7 +289,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tmem_ld_32x32b_x32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(hm * BN + c * 32), v);
             const int ncol = n0 + c * 32;
             if (row >= p.M || ncol >= p.N) continue;
-            if (f32) {
+            if (p.splits > 1) {   // unscaled fp32 partial; the reduction applies the epilogue
+                float* pr = p.part + (int64_t)blockIdx.z * p.M * p.N + (int64_t)row * p.N + ncol;
+                if (ncol + 32 <= p.N) {   // N % 16 == 0 keeps these 16-byte aligned
+                    float4* o = reinterpret_cast<float4*>(pr);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        o[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                           __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+                } else {
+                    for (int i = 0; i < 32; ++i)
+                        if (ncol + i < p.N) pr[i] = __uint_as_float(v[i]);
+                }
+            } else if (f32) {
                 float* yr = reinterpret_cast<float*>(p.y) + (int64_t)row * p.ldy + ncol;
                 for (int i = 0; i < 32; ++i)
                     if (ncol + i < p.N) yr[i] = __fmul_rn(__uint_as_float(v[i]), scale);
@@ -334,6 +352,40 @@ __global__ void rms_rows_kernel(const uint16_t* __restrict__ x, int M, int K, in
     for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
     if (lane == 0) out[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
 }
+
+// Split-K reduction: y[m, n] = (sum over splits, in split order, of part[z][m][n]) * rms[m].
+// One CTA row per output row (blockIdx.y), four columns per thread.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N, const float* rms,
+                                     void* y, int64_t ldy, int f32) {
+    const int m = blockIdx.y;
+    const int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (n >= N) return;
+    const int64_t total = (int64_t)M * N, i = (int64_t)m * N + n;
+    float4 s = __ldcs(reinterpret_cast<const float4*>(part + i));
+    for (int z = 1; z < splits; ++z) {
+        const float4 t = __ldcs(reinterpret_cast<const float4*>(part + (int64_t)z * total + i));
+        s.x += t.x;
+        s.y += t.y;
+        s.z += t.z;
+        s.w += t.w;
+    }
+    const float r = rms ? rms[m] : 1.0f;
+    const float o[4] = {__fmul_rn(s.x, r), __fmul_rn(s.y, r), __fmul_rn(s.z, r), __fmul_rn(s.w, r)};
+    if (f32) {
+        float* yr = reinterpret_cast<float*>(y) + (int64_t)m * ldy + n;
+        for (int e = 0; e < 4; ++e) yr[e] = o[e];
+    } else {
+        uint16_t* yr = reinterpret_cast<uint16_t*>(y) + (int64_t)m * ldy + n;
+        for (int e = 0; e < 4; ++e) yr[e] = f32_to_bf16_bits(o[e]);
+    }
+}
+
+struct SplitScratch {
+    float* part = nullptr;
+    size_t bytes = 0;
+};
+SplitScratch g_split[64];
+std::mutex g_split_mu;
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -406,9 +458,50 @@ void launch_gemm(const QmmCall& c, cudaStream_t st) {
         check_cuda(cudaGetLastError(), "rms launch");
         p.rms = ds.rms;
     }
-    const dim3 grid((unsigned)((c.M + BM - 1) / BM), (unsigned)((w.N + BN - 1) / BN));
+    // Split-K when the tiles fill less than half of the SMs (small N, e.g. q|k|v or k/v shards under
+    // tensor parallelism): up to 8 splits of at least 4 k-blocks, so that tiles x splits <= SMs.
+    const int tiles = (int)(((c.M + BM - 1) / BM) * ((w.N + BN - 1) / BN));
+    const int sms = device_sm_count();
+    int splits = 1;
+    if (2 * tiles <= sms) {
+        splits = sms / tiles;
+        if (splits > 8) splits = 8;
+        if (splits > p.KB / 4) splits = p.KB / 4;
+        if (splits < 1) splits = 1;
+    }
+    p.splits = 1;
+    p.part = nullptr;
+    if (splits > 1) {
+        const size_t need = (size_t)splits * c.M * w.N * sizeof(float);
+        std::lock_guard<std::mutex> lock(g_split_mu);
+        SplitScratch& ss = g_split[dev & 63];
+        if (need > ss.bytes) {
+            // grow only outside a stream capture (no allocation may be captured); else stay unsplit
+            cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+            check_cuda(cudaStreamIsCapturing(st, &cap), "cudaStreamIsCapturing");
+            if (cap == cudaStreamCaptureStatusNone) {
+                check_cuda(cudaStreamSynchronize(st), "split-K scratch");
+                cudaFree(ss.part);
+                ss.part = nullptr;
+                ss.bytes = 0;
+                check_cuda(cudaMalloc(&ss.part, need), "split-K scratch");
+                ss.bytes = need;
+            }
+        }
+        if (need <= ss.bytes) {
+            p.splits = splits;
+            p.part = ss.part;
+        }
+    }
+    const dim3 grid((unsigned)((c.M + BM - 1) / BM), (unsigned)((w.N + BN - 1) / BN), (unsigned)p.splits);
     qgemm_kernel<<<grid, kGemmThreads, kSmemBytes, st>>>(tm_x, tm_p, tm_sb, p);
     check_cuda(cudaGetLastError(), "qgemm launch");
+    if (p.splits > 1) {
+        const dim3 rgrid((unsigned)((w.N / 4 + 255) / 256), (unsigned)c.M);
+        splitk_reduce_kernel<<<rgrid, 256, 0, st>>>(p.part, p.splits, (int)c.M, (int)w.N, p.rms, c.y, c.ldy,
+                                                    (c.flags & G4Q_QMM_OUT_F32) ? 1 : 0);
+        check_cuda(cudaGetLastError(), "split-K reduction launch");
+    }
 }
 
 }  // namespace g4q

@@ -31,6 +31,8 @@ CASES = {
     "down8": dict(N=3840, K=15360, M=8, copies=4),
     "lmhead": dict(N=262144, K=3840, M=1, copies=1),
     "gemm": dict(N=8192, K=3840, M=2048, copies=1),
+    "gemm_kv": dict(N=2048, K=3840, M=2048, copies=1),     # 64 tiles: split-K in two
+    "gemm_tp8": dict(N=1024, K=3840, M=2048, copies=1),    # a q|k|v shard at 8 ranks: split-K in four
     "dequant": dict(N=15360, K=3840, M=0, copies=1),
     "decode": dict(layers=2),
     "decode_lm": dict(layers=0),
@@ -101,7 +103,7 @@ def main():
     wbytes = c["N"] * c["K"] * 9 // 16
     out = {"case": a.case, "us_per_launch": round(us, 3), "weight_bytes": wbytes,
            "weight_GBps": round(wbytes / us / 1e3, 1)}
-    if a.case == "gemm":
+    if a.case.startswith("gemm"):
         out["TFLOPs"] = round(2 * c["M"] * c["N"] * c["K"] / us / 1e6, 1)
     print(json.dumps(out))
 
