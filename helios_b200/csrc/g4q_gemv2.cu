@@ -11,9 +11,10 @@
 //  * Each warp owns a private ring of 3 unit buffers in shared memory (2 when the tokens' x would not
 //    fit beside 3). Lane 0 refills a buffer with two cp.async.bulk copies (mbarrier completion) as
 //    soon as the warp has read the unit.
-//  * x (M <= 8 tokens, full K) is staged once per CTA, per token in B-fragment order (two 16-byte
-//    loads per lane and unit), while the first weight copies land; the per-token RMS scale (sum of
-//    squares over K) is reduced there too.
+//  * x (M <= 8 tokens) is staged once per CTA, per token in B-fragment order (two 16-byte loads per
+//    lane and unit), while the first weight copies land: all of K, or only the window of groups the
+//    CTA's range reads when every range is shorter than a quad row (long K, e.g. down_proj), which
+//    lets more tokens fit; the per-token RMS scale (sum of squares over K) is reduced there too.
 //  * Weights whose |scales| are all < 2^-1 take the raw odd-nibble dequant (the masked bits read as
 //    bf16 are q * 2^-129, times s * 2^129): two operations fewer per packed word.
 //  * A warp parks its fp32 partial of a quad in shared memory when it leaves the quad; the last warp
@@ -54,6 +55,8 @@ struct Gemv2Args {
     int* counters;          // [Q], zero between launches
     int* err;
     int stages;             // ring stages per warp (2 or 3)
+    int xg;                 // 64-wide groups of x staged per token: G, or fewer when every CTA's
+                            // range is shorter than a quad row (the window its units read)
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -259,20 +262,38 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    // stage x (full K, M <= 8 tokens) into B-fragment order per token; sums of squares per token
+    // stage x (M <= 8 tokens) into B-fragment order per token: all K, or, when the CTA's range is
+    // shorter than a quad row, the window of a.xg groups starting at its first unit's group (slot j
+    // holds group (cs + j) mod G, so relative unit u reads slot u); sums of squares per token over K
     const bool rms = (a.flags & G4Q_QMM_RMS_SCALE) != 0;
-    const int words = a.K / 2;   // bf16 pairs per token
+    const bool win = a.xg < G;
+    const int words = a.xg * 32;   // bf16 pairs staged per token
+    const int g0 = win ? cs % G : 0;
     for (int m = 0; m < M; ++m) {
         float ss = 0.0f;
         const uint4* xr = reinterpret_cast<const uint4*>(a.x + (int64_t)m * a.ldx);
         uint32_t* xm = xs + (size_t)m * words;
-        for (int u = threadIdx.x; u < a.K / 8; u += kThreadsV2) {
-            const uint4 v = xr[u];
+        for (int u = threadIdx.x; u < a.xg * 8; u += kThreadsV2) {
+            int g = g0 + (u >> 3);
+            if (g >= G) g -= G;
+            const uint4 v = xr[g * 8 + (u & 7)];
             xm[xperm(4 * u)] = v.x;
             xm[xperm(4 * u + 1)] = v.y;
             xm[xperm(4 * u + 2)] = v.z;
             xm[xperm(4 * u + 3)] = v.w;
-            if (rms) {
+            if (rms && !win) {
+                const uint32_t pv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float lo = bf16_bits_to_f32(pv[i] & 0xffffu), hi = bf16_bits_to_f32(pv[i] >> 16);
+                    ss = __fadd_rn(ss, __fmul_rn(lo, lo));
+                    ss = __fadd_rn(ss, __fmul_rn(hi, hi));
+                }
+            }
+        }
+        if (rms && win) {   // the RMS scale needs all of x
+            for (int u = threadIdx.x; u < a.K / 8; u += kThreadsV2) {
+                const uint4 v = xr[u];
                 const uint32_t pv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -324,7 +345,8 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
         }
         wait_parity(bar0 + 8 * stage, phase, a.err);
         const uint8_t* st = ring + stage * kUnitBytes;
-        const uint4 xa = xt[cg * 8], xb = xt[cg * 8 + 1];
+        const int xj = win ? u0 + k : cg;   // staged slot of this unit's group
+        const uint4 xa = xt[xj * 8], xb = xt[xj * 8 + 1];
         const uint32_t b0[4] = {xa.x, xa.z, xb.x, xb.z}, b1[4] = {xa.y, xa.w, xb.y, xb.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -388,14 +410,20 @@ static int gemv2_grid(int U, int G, int sms) {
     return grid;
 }
 
-static size_t gemv2_smem(int stages, int64_t M, int64_t K) {
-    return (size_t)kWarpsV2 * stages * kUnitBytes + (size_t)kRedBytesPerTok * M + (size_t)K * M * 2;
+static size_t gemv2_smem(int stages, int64_t M, int64_t xg) {
+    return (size_t)kWarpsV2 * stages * kUnitBytes + (size_t)kRedBytesPerTok * M + (size_t)xg * 64 * M * 2;
+}
+
+// groups of x each CTA stages: all G, or the window of its range when every range is shorter
+static int gemv2_xgroups(int U, int G, int grid) {
+    const int nmax = (U + grid - 1) / grid;
+    return nmax < G ? nmax : G;
 }
 
 // 3 ring stages when they fit beside the tokens' x, else 2 (0: does not fit at all)
-static int gemv2_stages(int64_t M, int64_t K) {
+static int gemv2_stages(int64_t M, int64_t xg) {
     for (int s = 3; s >= 2; --s)
-        if (gemv2_smem(s, M, K) <= 220 * 1024) return s;
+        if (gemv2_smem(s, M, xg) <= 220 * 1024) return s;
     return 0;
 }
 
@@ -403,8 +431,10 @@ bool gemv2_supported(const QmmCall& c) {
     if (c.M < 1 || c.M > 8 || c.w->N % 64 != 0) return false;
     const long long units = (c.w->N / 64) * (c.w->K / 64);
     if (units < 1 || units >= (1ll << 31)) return false;
-    if (gemv2_stages(c.M, c.w->K) == 0) return false;
-    return gemv2_grid((int)units, (int)(c.w->K / 64), device_sm_count()) > 0;
+    const int G = (int)(c.w->K / 64);
+    const int grid = gemv2_grid((int)units, G, device_sm_count());
+    if (grid <= 0) return false;
+    return gemv2_stages(c.M, gemv2_xgroups((int)units, G, grid)) != 0;
 }
 
 void launch_gemv2(const QmmCall& c, cudaStream_t st) {
@@ -444,11 +474,13 @@ void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     a.slots = ds.slots;
     a.counters = ds.counters;
     a.err = ds.err;
-    a.stages = gemv2_stages(a.M, a.K);
+    a.xg = gemv2_xgroups(a.U, a.G, grid);
+    a.stages = gemv2_stages(a.M, a.xg);
+    if (a.stages == 0) throw Error(G4Q_ERR_RUNTIME, "gemv2: x does not fit in shared memory");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreadsV2);
-    cfg.dynamicSmemBytes = gemv2_smem(a.stages, a.M, a.K);
+    cfg.dynamicSmemBytes = gemv2_smem(a.stages, a.M, a.xg);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
