@@ -77,6 +77,9 @@ SIGNATURES = {
     "g4q_qmm_ex": [_P, _P, _I64, _I64, _P, _I64, _U32, _F, _P],
     "g4q_lm_head_argmax": [_P, _P, _I64, _I64, _F, _U32, _F, _I64, _P, _I64, _P, _P, _P, _P],
     "g4q_lm_head_argmax_noalloc": [_P, _P, _I64, _I64, _P, _I64, _I64, _F, _U32, _F, _I64, _P, _I64, _P, _P, _P, _P],
+    "g4q_lora_create": [_I64, _I64, _I32, _F, _P, _P, _I32, ctypes.POINTER(_P)],
+    "g4q_lora_apply": [_P, _P, _I64, _I64, _P, _I64, _P],
+    "g4q_lora_free": [_P],
     "g4q_device_error": [ctypes.POINTER(_I32), _I32],
     "g4q_decode_plan_create": [ctypes.POINTER(G4qDecodePhase), _I32, _I32, ctypes.POINTER(_P)],
     "g4q_decode_plan_run": [_P, _I64, _F, _F, _I64, _P, _P, _P, _P, _I64, _P],

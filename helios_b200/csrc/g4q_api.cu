@@ -6,6 +6,7 @@
 // (runtime.cc:41-45, 841-846, 900-912), and no C++ exception crossing the boundary.
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -583,6 +584,106 @@ G4qStatus g4q_decode_plan_run(G4qDecodePlan* plan, int64_t M, float eps, float s
 
 G4qStatus g4q_decode_plan_free(G4qDecodePlan* plan) {
     return guarded("g4q_decode_plan_free", [&] { decode_plan_free(plan); });
+}
+
+static Lora* checked_lora(const G4qLora* h, const char* what) {
+    auto* l = reinterpret_cast<Lora*>(const_cast<G4qLora*>(h));
+    require(l != nullptr, G4Q_ERR_INVALID_ARGUMENT, std::string(what) + " requires a non-null LoRA handle");
+    require(l->magic == kLoraMagic, G4Q_ERR_INVALID_ARGUMENT, std::string(what) + " received an invalid LoRA handle");
+    require(l->device == current_device(), G4Q_ERR_INVALID_ARGUMENT,
+            std::string(what) + ": the current CUDA device is not the handle's device");
+    return l;
+}
+
+// Round-to-nearest-even of a finite float to bf16, returned as a float (model_scalar's bf16 scalar).
+static float round_to_bf16(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, sizeof(u));
+    u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+    std::memcpy(&f, &u, sizeof(f));
+    return f;
+}
+
+G4qStatus g4q_lora_create(int64_t rows, int64_t cols, int32_t rank, float alpha, const float* lora_a,
+                          const float* lora_b, int32_t max_tokens, G4qLora** out) {
+    return guarded("g4q_lora_create", [&] {
+        require(out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "out must be non-null");
+        *out = nullptr;
+        require(rank > 0, G4Q_ERR_INVALID_ARGUMENT, "LoRA rank must be greater than zero");
+        require(alpha > 0.0f && std::isfinite(alpha), G4Q_ERR_INVALID_ARGUMENT, "LoRA alpha must be finite and positive");
+        require(rank <= 256, G4Q_ERR_UNSUPPORTED_CONFIG, "LoRA rank must be <= 256");
+        require(rows > 0 && cols > 0 && cols % 8 == 0, G4Q_ERR_INVALID_ARGUMENT,
+                "rows must be > 0 and cols a positive multiple of 8");
+        require(max_tokens >= 1 && max_tokens <= 65536, G4Q_ERR_INVALID_ARGUMENT, "max_tokens must be in [1, 65536]");
+        require(lora_a != nullptr && lora_b != nullptr, G4Q_ERR_INVALID_ARGUMENT, "lora_a and lora_b must be non-null");
+        auto* l = new (std::nothrow) Lora();
+        require(l != nullptr, G4Q_ERR_MEMORY_GUARD, "host allocation failed");
+        l->N = rows;
+        l->K = cols;
+        l->rank = rank;
+        l->max_tokens = max_tokens;
+        l->alpha = alpha;
+        l->scale_bf16 = round_to_bf16(alpha / static_cast<float>(rank));
+        l->device = current_device();
+        float* b_tmp = nullptr;
+        const size_t ab = (size_t)rank * cols * sizeof(float), bb = (size_t)rank * rows * sizeof(float);
+        cudaError_t e = cudaMalloc(&l->a, ab);
+        if (e == cudaSuccess) e = cudaMalloc(&l->bt, bb);
+        if (e == cudaSuccess) e = cudaMalloc(&l->low, (size_t)max_tokens * rank * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&b_tmp, bb);
+        if (e == cudaSuccess) e = cudaMemcpy(l->a, lora_a, ab, cudaMemcpyDefault);
+        if (e == cudaSuccess) e = cudaMemcpy(b_tmp, lora_b, bb, cudaMemcpyDefault);
+        if (e == cudaSuccess) {
+            try {
+                launch_lora_transpose(b_tmp, rows, rank, l->bt, nullptr);
+            } catch (const Error&) {
+                e = cudaErrorLaunchFailure;
+            }
+        }
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        cudaFree(b_tmp);
+        if (e != cudaSuccess) {
+            cudaFree(l->a);
+            cudaFree(l->bt);
+            cudaFree(l->low);
+            delete l;
+            check_cuda(e, "LoRA upload");
+        }
+        l->magic = kLoraMagic;
+        *out = reinterpret_cast<G4qLora*>(l);
+    });
+}
+
+G4qStatus g4q_lora_apply(const G4qLora* h, const uint16_t* x, int64_t M, int64_t ldx, uint16_t* y, int64_t ldy,
+                         void* stream) {
+    return guarded("g4q_lora_apply", [&] {
+        Lora* l = checked_lora(h, "g4q_lora_apply");
+        require(M >= 0, G4Q_ERR_INVALID_ARGUMENT, "M must be >= 0");
+        if (M == 0) return;
+        require(x != nullptr && y != nullptr, G4Q_ERR_INVALID_ARGUMENT, "x and y must be non-null");
+        require(ldx >= l->K && ldx % 8 == 0, G4Q_ERR_INVALID_ARGUMENT, "ldx must be >= cols and a multiple of 8");
+        require(ldy >= l->N, G4Q_ERR_INVALID_ARGUMENT, "ldy must be >= rows");
+        require_aligned16(x, "x");
+        require((reinterpret_cast<uintptr_t>(y) & 1u) == 0, G4Q_ERR_INVALID_ARGUMENT, "y must be 2-byte aligned");
+        launch_lora_apply(*l, x, M, ldx, y, ldy, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+G4qStatus g4q_lora_free(G4qLora* h) {
+    return guarded("g4q_lora_free", [&] {
+        auto* l = reinterpret_cast<Lora*>(h);
+        require(l != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null LoRA handle");
+        require(l->magic == kLoraMagic, G4Q_ERR_INVALID_ARGUMENT, "received an invalid LoRA handle");
+        l->magic = 0;
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(l->device);
+        cudaFree(l->a);
+        cudaFree(l->bt);
+        cudaFree(l->low);
+        cudaSetDevice(prev);
+        delete l;
+    });
 }
 
 G4qStatus g4q_device_error(int32_t* code, int32_t reset) {

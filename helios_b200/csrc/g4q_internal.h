@@ -33,6 +33,29 @@ struct Weight {
     unsigned long long* argmax_scratch = nullptr;
 };
 
+constexpr uint64_t kLoraMagic = 0x47345141524F4C47ull;    // "G4QLORAG"
+
+// One LoRA adapter module (the reference's NativeLoraAdapter::Impl::Module, native_model.cc:66-73):
+// lora_A kept as [rank][K] fp32, lora_B transposed to [rank][N] fp32, the scale already rounded to
+// bf16 as model_scalar does, and a [max_tokens][rank] fp32 scratch for the low-rank activations.
+struct Lora {
+    uint64_t magic = 0;
+    int64_t N = 0, K = 0;
+    int rank = 0;
+    int max_tokens = 0;
+    float alpha = 0.f;
+    float scale_bf16 = 0.f;     // float value of bf16(alpha / rank)
+    int device = -1;
+    float* a = nullptr;
+    float* bt = nullptr;
+    float* low = nullptr;
+};
+
+// kernels (g4q_lora.cu)
+void launch_lora_transpose(const float* b, int64_t N, int rank, float* bt, cudaStream_t st);
+void launch_lora_apply(const Lora& l, const uint16_t* x, int64_t M, int64_t ldx, uint16_t* y, int64_t ldy,
+                       cudaStream_t st);
+
 // tensor-parallel allreduce over NVLink peer memory (g4q_comm.cu)
 void* comm_create(int rank, int n_ranks, int64_t max_elems);
 void comm_buffer(const void* h, void** buf, uint64_t* bytes);

@@ -27,8 +27,8 @@ from ._lib import (CHAIN_R1, CHAIN_R2, PHASE_ALLREDUCE, PHASE_ARGMAX, QMM_OUT_F3
                    G4qInvalidArgument)
 
 __all__ = [
-    "QuantizedWeight", "quantized_matmul", "dequantize", "lm_head_argmax", "DecodePlan", "synth_matrix",
-    "synth_normal", "CHAIN_R1", "CHAIN_R2", "QMM_RMS_SCALE", "QMM_OUT_F32", "PHASE_ARGMAX", "PHASE_ALLREDUCE", "G4qError",
+    "QuantizedWeight", "quantized_matmul", "quantized_linear", "LoraAdapter", "dequantize", "lm_head_argmax",
+    "DecodePlan", "synth_matrix", "synth_normal", "CHAIN_R1", "CHAIN_R2", "QMM_RMS_SCALE", "QMM_OUT_F32", "PHASE_ARGMAX", "PHASE_ALLREDUCE", "G4qError",
     "G4qInvalidArgument",
 ]
 
@@ -207,6 +207,73 @@ def quantized_matmul(x: torch.Tensor, w, scales: Optional[torch.Tensor] = None,
         raise ValueError("out must be contiguous")
     flags = (QMM_RMS_SCALE if rms_scale else 0) | (QMM_OUT_F32 if out_dtype == torch.float32 else 0)
     _lib.call("g4q_qmm_ex", qw.handle, _ptr(x2), M, x2.stride(0), _ptr(y2), y2.stride(0), flags, eps, _stream())
+    return y
+
+
+class LoraAdapter:
+    """One LoRA adapter module on one GPU (NativeLoraAdapter::Impl::Module, native_model.cc:66-73).
+
+    ``lora_a`` is ``[rank, in_features]`` and ``lora_b`` ``[out_features, rank]`` as the adapter's
+    safetensors store them (``*.lora_A.weight`` / ``*.lora_B.weight``), any float dtype, host or
+    device; they are converted to fp32 as at native_model.cc:3419-3420 and the scale is
+    ``alpha / rank`` (:3378). Validation as in NativeLoraAdapter::load (:3332-3339, :3399-3411):
+    rank > 0, alpha finite and positive, shapes consistent. ``max_tokens`` sizes the low-rank
+    scratch; longer inputs are processed in chunks of it.
+    """
+
+    def __init__(self, lora_a: torch.Tensor, lora_b: torch.Tensor, alpha: float, *, max_tokens: int = 2048):
+        if lora_a.dim() != 2 or lora_b.dim() != 2:
+            raise ValueError("LoRA tensors must be rank-2")
+        rank, cols = lora_a.shape
+        rows = lora_b.shape[0]
+        if lora_b.shape[1] != rank:
+            raise ValueError(f"LoRA shape mismatch: A=[{rank},{cols}] B=[{rows},{lora_b.shape[1]}]")
+        a = lora_a.detach().to(torch.float32).contiguous()
+        b = lora_b.detach().to(torch.float32).contiguous()
+        self._h = ctypes.c_void_p()
+        _lib.call("g4q_lora_create", rows, cols, rank, float(alpha), _ptr(a), _ptr(b), max_tokens,
+                  ctypes.byref(self._h))
+        self.rows, self.cols, self.rank, self.alpha = rows, cols, rank, float(alpha)
+        self.device = torch.cuda.current_device()
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        if not self._h:
+            raise ValueError("LoraAdapter has been freed")
+        return self._h
+
+    def apply(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+        """In place: ``y = bf16(y + bf16((f32(x) @ A.T @ B.T) * bf16(alpha/rank)))`` (native_model.cc:316-328)."""
+        x2 = _rows2d(x, self.cols)
+        if y.dtype != torch.bfloat16 or not y.is_contiguous() or y.shape[-1] != self.rows:
+            raise ValueError("y must be a contiguous bfloat16 tensor with last dimension = out_features")
+        y2 = y.view(-1, self.rows)
+        if y2.shape[0] != x2.shape[0]:
+            raise ValueError("x and y must have the same number of rows")
+        _lib.call("g4q_lora_apply", self.handle, _ptr(x2), x2.shape[0], x2.stride(0), _ptr(y2), y2.stride(0),
+                  _stream())
+        return y
+
+    def free(self) -> None:
+        if self._h:
+            _lib.call("g4q_lora_free", self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def quantized_linear(x: torch.Tensor, w: QuantizedWeight, lora: Optional[LoraAdapter] = None) -> torch.Tensor:
+    """quantized_linear (native_model.cc:349-362): the affine quantized matmul, bf16 output, then the
+    adapter's delta when one is active for this module (add_lora_delta_if_active, :316-328)."""
+    y = quantized_matmul(x, w, group_size=w.group_size, bits=w.bits)
+    if lora is not None:
+        if (lora.rows, lora.cols) != (w.rows, w.cols):
+            raise ValueError("the LoRA module's shape does not match the weight")
+        lora.apply(x, y)
     return y
 
 

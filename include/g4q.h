@@ -166,6 +166,26 @@ G4qStatus g4q_lm_head_argmax_noalloc(const uint32_t* packed, const uint32_t* sb,
                                      float eps, int64_t row_offset, uint16_t* logits, int64_t ld_logits,
                                      int32_t* tokens, float* values, uint64_t* keys, void* stream);
 
+/* ---- LoRA delta on a quantized linear's output -------------------------------------------------
+ * One adapter module as the reference builds it in NativeLoraAdapter::load
+ * (native/gemma4_mlx/src/native_model.cc:3296-3432): lora_A [rank, cols] and lora_B [rows, rank]
+ * converted to fp32 (:3419-3420), scale = alpha / rank (:3378). Validation as there: rank > 0,
+ * alpha finite and > 0. lora_a / lora_b: fp32, row-major, host or device memory (copied; lora_B is
+ * stored transposed). cols % 8 == 0, rank <= 256. max_tokens (1..65536) sizes the handle's fp32
+ * scratch for the low-rank activations; g4q_lora_apply processes larger M in chunks of it, so it
+ * allocates nothing. */
+typedef struct G4qLora G4qLora;
+G4qStatus g4q_lora_create(int64_t rows, int64_t cols, int32_t rank, float alpha, const float* lora_a,
+                          const float* lora_b, int32_t max_tokens, G4qLora** out);
+/* Replaces add_lora_delta_if_active (native_model.cc:316-328), the tail of quantized_linear
+ * (:349-362): in place on y (bf16 [M, ldy], the quantized matmul's bf16 output for the same x),
+ *   y = bf16(y + bf16(fp32(fp32(x) @ lora_A^T @ lora_B^T) * bf16(alpha / rank)))
+ * with fp32 accumulation. x: bf16 [M, ldx], 16-byte aligned, ldx % 8 == 0. Asynchronous on
+ * `stream`; calls on one handle share its scratch, so serialise them. */
+G4qStatus g4q_lora_apply(const G4qLora* lora, const uint16_t* x, int64_t M, int64_t ldx, uint16_t* y, int64_t ldy,
+                         void* stream);
+G4qStatus g4q_lora_free(G4qLora* lora);
+
 /* ---- decode plan: every quantized matmul of one decode step in one persistent kernel ----------
  * Replaces the per-token chain of quantized_linear calls of the decode drivers
  * (native_model.cc:1843-1911 decode_last_logits -> 48 x target_layer_decode_forward :1284-1328 ->

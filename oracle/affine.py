@@ -213,6 +213,31 @@ def qmm_f32(x, w, s, b, group_size: int = 64, chain: int = CHAIN_R2, threads: in
     return y
 
 
+def lora_scale_bf16(alpha: float, rank: int) -> float:
+    """bf16(alpha / rank) as a float: the adapter scale (native_model.cc:3378) as model_scalar
+    rounds it (:342-347), the fp32 quotient first."""
+    q = np.float32(np.float32(alpha) / np.float32(rank))
+    return float(bf16_to_f32(f32_to_bf16(q)))
+
+
+def lora_delta(x, y_base, lora_a, lora_b, alpha: float):
+    """add_lora_delta_if_active (native_model.cc:316-328) on a bf16 base output.
+
+    x: bf16 bits [M, K]; y_base: bf16 bits [M, N]; lora_a: [rank, K]; lora_b: [N, rank] (both
+    converted to fp32 as at :3419-3420). low = f32(x) @ A^T and delta = low @ B^T are accumulated in
+    float64 and rounded once to fp32 (the fp32 matmul results), then delta * bf16(alpha/rank) in
+    fp32, bf16(delta), and the bf16 add bf16(y_base + delta). Returns the bf16 bits [M, N]."""
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    a = np.asarray(lora_a, dtype=np.float32).astype(np.float64)
+    b = np.asarray(lora_b, dtype=np.float32).astype(np.float64)
+    rank = a.shape[0]
+    low = (bf16_to_f32(x).astype(np.float64) @ a.T).astype(np.float32)
+    mm = (low.astype(np.float64) @ b.T).astype(np.float32)
+    delta = f32_to_bf16(mm * np.float32(lora_scale_bf16(alpha, rank)))
+    out = bf16_to_f32(np.asarray(y_base, dtype=np.uint16)) + bf16_to_f32(delta)
+    return f32_to_bf16(out.astype(np.float32))
+
+
 def rms_scale(x_row, eps: float = 1e-6) -> float:
     x_row = np.ascontiguousarray(x_row, dtype=np.uint16)
     return float(lib().g4o_rms_scale(_p(x_row), x_row.size, eps))
