@@ -16,6 +16,9 @@ e2e     = the same metric through the public API with a host hidden state copied
 roofline: the dominant (only) kernel is the persistent decode kernel, one launch per step;
           achieved = the rank's algorithmic bytes per launch (its weight shards + activations) /
           the launch's CUDA-event duration (max over ranks); peak = MEASURED_PEAKS.json hbm_gbs.
+qmatmul: BASELINE configs 1 and 2 on the standalone matmul entry point at N = 1: the up_proj
+          15360 x 3840 at M = 1 and one layer's seven projections at M in {1, 2, 4, 8}, GB/s of
+          algorithmic bytes, launches back to back in a CUDA graph over >= 4x L2 of weight copies.
 cpu_baseline: the CPU oracle (fp32 accumulation, OpenMP on every host core) on a bounded sample
           (layer 0's seven projections at M = 1), rank 0 at N = 1 only.
 --impl reference: MLX (the reference's library) is absent, so the reference arm times the CPU
@@ -51,6 +54,7 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--layers", type=int, default=48)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-qmatmul", action="store_true", help="skip the standalone matmul section (configs 1 and 2)")
     p.add_argument("--prefill-tokens", type=int, default=2048, help="chunk size of the prefill measurement (0: skip)")
     return p.parse_args()
 
@@ -166,6 +170,93 @@ def run_reference(args, rank):
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+LAYER_SHAPES = [("q", 4096, 3840), ("k", 2048, 3840), ("v", 2048, 3840), ("o", 3840, 4096),
+                ("gate", 15360, 3840), ("up", 15360, 3840), ("down", 3840, 15360)]
+
+
+def qmatmul_section(dev, hbm_peak: float) -> dict:
+    """BASELINE configs 1 and 2 on the standalone matmul entry point (the stream-K GEMV): the
+    up_proj 15360x3840 at M = 1, and one layer's seven projections at M in {1, 2, 4, 8}. Launches
+    run back to back in a CUDA graph over enough weight copies that each launch reads its weights
+    from HBM (at least 4x the L2 size in distinct copies). GB/s = algorithmic bytes (0.5625 B per
+    weight + x reads + y writes) / device time per launch."""
+    import torch
+
+    from helios_b200.quantized import QuantizedWeight, quantized_matmul, synth_matrix, synth_normal
+    from helios_b200.stack import activation_seed, matrix_seed
+
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+
+    def alg_bytes(N, K, M):
+        return N * K * 9 // 16 + M * K * 2 + M * N * 2
+
+    def timed(calls, reps=20):
+        # warm, capture the list of launches once, replay `reps` times between two events
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for c in calls:
+                c()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for c in calls:
+                c()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) * 1e3 / (reps * len(calls))   # us per launch
+
+    out = {"method": "CUDA graph of back-to-back g4q_qmm launches (stream-K GEMV, programmatic dependent "
+                     "launch) cycling over >= 4x L2 of distinct weight copies; bf16 out",
+           "peak": hbm_peak}
+    # config 1: up_proj at M = 1
+    N, K = 15360, 3840
+    w, s, b = synth_matrix(matrix_seed(0, "up"), N, K, device=dev)
+    copies = max(4, -(-4 * l2 // alg_bytes(N, K, 0)))
+    ws = [QuantizedWeight.from_mlx(w, s, b) for _ in range(copies)]
+    del w, s, b
+    x = synth_normal(activation_seed(7), (1, K), device=dev)
+    y = torch.empty((1, N), dtype=torch.bfloat16, device=dev)
+    us = timed([lambda qw=qw: quantized_matmul(x, qw, out=y) for qw in ws])
+    gbs = alg_bytes(N, K, 1) / (us * 1e-6) / 1e9
+    out["config1_up_m1"] = {"shape": [N, K], "us": round(us, 2), "gbs": round(gbs, 1),
+                            "frac": round(gbs / hbm_peak, 4), "weight_copies": copies}
+    for qw in ws:
+        qw.free()
+    # config 2: one layer's seven projections at M in {1, 2, 4, 8}
+    layer_bytes = sum(alg_bytes(n, k, 0) for _, n, k in LAYER_SHAPES)
+    ncopy = max(2, -(-4 * l2 // layer_bytes))
+    mats = []
+    for c in range(ncopy):
+        for name, n, k in LAYER_SHAPES:
+            w, s, b = synth_matrix(matrix_seed(c, name), n, k, device=dev)
+            mats.append((QuantizedWeight.from_mlx(w, s, b), n, k))
+            del w, s, b
+    layer = {}
+    for M in (1, 2, 4, 8):
+        xs = {k: synth_normal(activation_seed(M), (M, k), device=dev) for k in {k for _, _, k in LAYER_SHAPES}}
+        ys = {n: torch.empty((M, n), dtype=torch.bfloat16, device=dev) for n in {n for _, n, _ in LAYER_SHAPES}}
+        us = timed([lambda qw=qw, n=n, k=k: quantized_matmul(xs[k], qw, out=ys[n]) for qw, n, k in mats], reps=10)
+        us_layer = us * len(LAYER_SHAPES)
+        by = sum(alg_bytes(n, k, M) for _, n, k in LAYER_SHAPES)
+        gbs = by / (us_layer * 1e-6) / 1e9
+        layer[str(M)] = {"us_per_layer": round(us_layer, 2), "gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4)}
+    out["config2_layer"] = layer
+    out["config2_layer_copies"] = ncopy
+    for qw, _, _ in mats:
+        qw.free()
+    return out
 
 
 def main():
@@ -314,6 +405,10 @@ def main():
     if traffic_file.exists():
         traffic = json.loads(traffic_file.read_text()).get("dram_bytes_per_launch")
 
+    qmm = None
+    if world == 1 and not args.no_qmatmul:
+        qmm = qmatmul_section(dev, hbm_peak)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline()
@@ -345,6 +440,8 @@ def main():
             line["cpu_baseline"] = cpu
         if prefill is not None:
             line["prefill"] = prefill
+        if qmm is not None:
+            line["qmatmul"] = qmm
         print(json.dumps(line), flush=True)
     del graph
     barrier()

@@ -863,7 +863,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
                 __threadfence_block();
                 sh.warps_finished = 0;
                 if (argmax) atomicMax(a.key, sh.best);
-                atom_add_acq_rel(a.done + p, 1u);
+                // a reduction, not an atomic with a result: the warp does not wait for the round
+                // trip to L2 before the next phase's CTA barrier (measured: step 2.70 -> 2.62 ms)
+                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.done + p) : "memory");
             }
         }
     }
