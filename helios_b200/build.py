@@ -18,7 +18,7 @@ LIB = PKG / "libg4q.so"
 OBJDIR = PKG / "_build"
 
 SOURCES = ["g4q_api.cu", "g4q_layout.cu", "g4q_gemv.cu", "g4q_gemv2.cu", "g4q_gemm.cu", "g4q_decode.cu",
-           "g4q_generic.cu", "g4q_comm.cu", "g4q_lora.cu"]
+           "g4q_generic.cu", "g4q_comm.cu", "g4q_lora.cu", "g4q_mlp.cu"]
 HEADERS = ["g4q_common.cuh", "g4q_internal.h"]
 
 NVCC_FLAGS = [

@@ -686,6 +686,39 @@ G4qStatus g4q_lora_free(G4qLora* h) {
     });
 }
 
+G4qStatus g4q_geglu(const uint16_t* gate, int64_t ld_gate, const uint16_t* up, int64_t ld_up, int64_t M, int64_t I,
+                    uint16_t* out, int64_t ld_out, void* stream) {
+    return guarded("g4q_geglu", [&] {
+        require(M >= 0 && I >= 0 && I % 8 == 0, G4Q_ERR_INVALID_ARGUMENT, "M >= 0 and I a multiple of 8 are required");
+        if (M == 0 || I == 0) return;
+        require(gate != nullptr && up != nullptr && out != nullptr, G4Q_ERR_INVALID_ARGUMENT,
+                "gate, up and out must be non-null");
+        require(ld_gate >= I && ld_up >= I && ld_out >= I && ld_gate % 8 == 0 && ld_up % 8 == 0 && ld_out % 8 == 0,
+                G4Q_ERR_INVALID_ARGUMENT, "row strides must be >= I and multiples of 8");
+        require_aligned16(gate, "gate");
+        require_aligned16(up, "up");
+        require_aligned16(out, "out");
+        launch_geglu(gate, ld_gate, up, ld_up, out, ld_out, M, I, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+G4qStatus g4q_rms_norm(const uint16_t* x, int64_t ldx, const uint16_t* weight, int64_t M, int64_t K, float eps,
+                       uint16_t* out, int64_t ld_out, void* stream) {
+    return guarded("g4q_rms_norm", [&] {
+        require(M >= 0 && K > 0 && K % 8 == 0, G4Q_ERR_INVALID_ARGUMENT, "M >= 0 and K a positive multiple of 8 are required");
+        require(M <= 0x7FFFFFFF, G4Q_ERR_INVALID_ARGUMENT, "M must be < 2^31");
+        if (M == 0) return;
+        require(x != nullptr && out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "x and out must be non-null");
+        require(ldx >= K && ld_out >= K && ldx % 8 == 0 && ld_out % 8 == 0, G4Q_ERR_INVALID_ARGUMENT,
+                "row strides must be >= K and multiples of 8");
+        require(eps >= 0.0f && std::isfinite(eps), G4Q_ERR_INVALID_ARGUMENT, "eps must be finite and >= 0");
+        require_aligned16(x, "x");
+        require_aligned16(out, "out");
+        if (weight != nullptr) require_aligned16(weight, "weight");
+        launch_rms_norm(x, ldx, weight, M, K, eps, out, ld_out, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
 G4qStatus g4q_device_error(int32_t* code, int32_t reset) {
     return guarded("g4q_device_error", [&] {
         require(code != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null code pointer");

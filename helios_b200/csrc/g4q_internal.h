@@ -56,6 +56,12 @@ void launch_lora_transpose(const float* b, int64_t N, int rank, float* bt, cudaS
 void launch_lora_apply(const Lora& l, const uint16_t* x, int64_t M, int64_t ldx, uint16_t* y, int64_t ldy,
                        cudaStream_t st);
 
+// kernels (g4q_mlp.cu): the MLP's elementwise neighbours
+void launch_geglu(const uint16_t* gate, int64_t ldg, const uint16_t* up, int64_t ldu, uint16_t* out, int64_t ldo,
+                  int64_t M, int64_t I, cudaStream_t st);
+void launch_rms_norm(const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t M, int64_t K, float eps,
+                     uint16_t* out, int64_t ldo, cudaStream_t st);
+
 // tensor-parallel allreduce over NVLink peer memory (g4q_comm.cu)
 void* comm_create(int rank, int n_ranks, int64_t max_elems);
 void comm_buffer(const void* h, void** buf, uint64_t* bytes);

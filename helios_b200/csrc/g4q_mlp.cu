@@ -1,0 +1,147 @@
+// g4q_mlp.cu -- the elementwise neighbours of the quantized MLP linears (sm_100a).
+//
+// layer_forward (native/gemma4_mlx/src/native_model.cc:899-970) runs, around gate/up/down:
+//   h = bf16(fast::rms_norm(h, pre_feedforward_layernorm.weight, 1e-6))     (:929-932)
+//   act = geglu(gate, up)                                                   (:378-386, :945)
+// MLX evaluates geglu as nine separate bf16 ops (power, two scalar products, an add, tanh, an add,
+// two products and the final product with up), each rounding its fp32 result to bf16. geglu_kernel
+// performs the same nine roundings in registers in one pass over gate and up: one launch instead
+// of nine, and 3 x 2 bytes of HBM per element instead of ~27 x 2. g^3 is computed as g*g*g, which
+// is exact in fp32 for a bf16 g (8-bit significands), so it equals the correctly rounded power.
+//
+// rms_norm_kernel: one CTA per row; fp32 sum of squares, inv = the correctly rounded 1/sqrt of the
+// fp32 mean + eps; the normalized value x * inv is rounded to bf16 (the input dtype) and then
+// multiplied by the bf16 weight with one more rounding, out = bf16(w * bf16(x * inv)), as MLX's
+// fast::rms_norm orders its roundings; the weight may be absent (values norm, :844).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
+#include "g4q_internal.h"
+
+namespace g4q {
+namespace {
+
+__device__ __forceinline__ float bf(uint32_t h) { return __uint_as_float(h << 16); }
+
+// f32 -> bf16 (round to nearest even) -> f32
+__device__ __forceinline__ float rb(float f) { return __bfloat162float(__float2bfloat16_rn(f)); }
+
+__device__ __forceinline__ uint32_t bits(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+
+struct GegluConsts {
+    float cubic, tanh_approx;   // bf16(0.044715), bf16(0.7978845608028654)
+};
+
+__device__ __forceinline__ float geglu1(float g, float u, const GegluConsts& c) {
+    const float g3 = rb(g * g * g);                 // power(gate, 3)
+    const float t1 = rb(c.cubic * g3);              // 0.044715 * gate^3
+    const float t2 = rb(g + t1);                    // gate + ...
+    const float t3 = rb(c.tanh_approx * t2);        // sqrt(2/pi) * (...)
+    const float t4 = rb(tanhf(t3));                 // tanh
+    const float t5 = rb(1.0f + t4);                 // 1 + tanh
+    const float t6 = rb(0.5f * g);                  // 0.5 * gate
+    const float t7 = rb(t6 * t5);                   // gelu
+    return t7 * u;                                  // gelu * up (rounded by the caller)
+}
+
+// out[m, i] for i in [0, I); 8 elements per thread, 16-byte loads and stores (I % 8 == 0).
+__global__ void __launch_bounds__(256) geglu_kernel(const uint16_t* __restrict__ gate, int64_t ldg,
+                                                    const uint16_t* __restrict__ up, int64_t ldu,
+                                                    uint16_t* __restrict__ out, int64_t ldo, int64_t M, int64_t I,
+                                                    GegluConsts c) {
+    const int64_t per_row = I / 8;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= M * per_row) return;
+    const int64_t m = idx / per_row, i = (idx - m * per_row) * 8;
+    const uint4 gv = *reinterpret_cast<const uint4*>(gate + m * ldg + i);
+    const uint4 uv = *reinterpret_cast<const uint4*>(up + m * ldu + i);
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+    uint32_t ow[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float lo = geglu1(bf(gw[j] & 0xFFFFu), bf(uw[j] & 0xFFFFu), c);
+        const float hi = geglu1(bf(gw[j] >> 16), bf(uw[j] >> 16), c);
+        ow[j] = bits(lo) | (bits(hi) << 16);
+    }
+    *reinterpret_cast<uint4*>(out + m * ldo + i) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+}
+
+constexpr int kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const uint16_t* __restrict__ x, int64_t ldx,
+                                                                const uint16_t* __restrict__ w, int64_t K, float eps,
+                                                                uint16_t* __restrict__ out, int64_t ldo) {
+    __shared__ float part[kNormThreads / 32];
+    __shared__ float inv_s;
+    const uint16_t* xr = x + (int64_t)blockIdx.x * ldx;
+    uint16_t* orow = out + (int64_t)blockIdx.x * ldo;
+    float ss = 0.0f;
+    for (int64_t k = (int64_t)threadIdx.x * 8; k < K; k += kNormThreads * 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+        const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float a = bf(vw[j] & 0xFFFFu), b = bf(vw[j] >> 16);
+            ss = fmaf(a, a, ss);
+            ss = fmaf(b, b, ss);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int i = 0; i < kNormThreads / 32; ++i) s += part[i];
+        inv_s = __frsqrt_rn(s / (float)K + eps);
+    }
+    __syncthreads();
+    const float inv = inv_s;
+    for (int64_t k = (int64_t)threadIdx.x * 8; k < K; k += kNormThreads * 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+        uint4 wv = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);   // bf16 1.0 pairs
+        if (w != nullptr) wv = *reinterpret_cast<const uint4*>(w + k);
+        const uint32_t vw[4] = {v.x, v.y, v.z, v.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t ow[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float lo = bf(ww[j] & 0xFFFFu) * rb(bf(vw[j] & 0xFFFFu) * inv);
+            const float hi = bf(ww[j] >> 16) * rb(bf(vw[j] >> 16) * inv);
+            ow[j] = bits(lo) | (bits(hi) << 16);
+        }
+        *reinterpret_cast<uint4*>(orow + k) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+}
+
+float bf16_round_host(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+}  // namespace
+
+void launch_geglu(const uint16_t* gate, int64_t ldg, const uint16_t* up, int64_t ldu, uint16_t* out, int64_t ldo,
+                  int64_t M, int64_t I, cudaStream_t st) {
+    const int64_t total = M * (I / 8);
+    if (total == 0) return;
+    GegluConsts c;
+    c.cubic = bf16_round_host(0.044715f);               // model_scalar(kGeluCubic)
+    c.tanh_approx = bf16_round_host(0.7978845608028654f);   // model_scalar(kTanhApprox)
+    geglu_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(gate, ldg, up, ldu, out, ldo, M, I, c);
+    check_cuda(cudaGetLastError(), "geglu_kernel launch");
+}
+
+void launch_rms_norm(const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t M, int64_t K, float eps,
+                     uint16_t* out, int64_t ldo, cudaStream_t st) {
+    if (M == 0) return;
+    rms_norm_kernel<<<(unsigned)M, kNormThreads, 0, st>>>(x, ldx, w, K, eps, out, ldo);
+    check_cuda(cudaGetLastError(), "rms_norm_kernel launch");
+}
+
+}  // namespace g4q

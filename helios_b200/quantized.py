@@ -27,7 +27,8 @@ from ._lib import (CHAIN_R1, CHAIN_R2, PHASE_ALLREDUCE, PHASE_ARGMAX, QMM_OUT_F3
                    G4qInvalidArgument)
 
 __all__ = [
-    "QuantizedWeight", "quantized_matmul", "quantized_linear", "LoraAdapter", "dequantize", "lm_head_argmax",
+    "QuantizedWeight", "quantized_matmul", "quantized_linear", "LoraAdapter", "geglu", "rms_norm", "dequantize",
+    "lm_head_argmax",
     "DecodePlan", "synth_matrix", "synth_normal", "CHAIN_R1", "CHAIN_R2", "QMM_RMS_SCALE", "QMM_OUT_F32", "PHASE_ARGMAX", "PHASE_ALLREDUCE", "G4qError",
     "G4qInvalidArgument",
 ]
@@ -275,6 +276,56 @@ def quantized_linear(x: torch.Tensor, w: QuantizedWeight, lora: Optional[LoraAda
             raise ValueError("the LoRA module's shape does not match the weight")
         lora.apply(x, y)
     return y
+
+
+def _bf16_rows(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype != torch.bfloat16 or not t.is_cuda:
+        raise ValueError(f"{name} must be a bfloat16 CUDA tensor")
+    t2 = t.reshape(-1, t.shape[-1])
+    if t2.stride(1) != 1 or t2.stride(0) % 8 != 0 or t2.data_ptr() % 16 != 0:
+        t2 = t2.contiguous()
+    return t2
+
+
+def geglu(gate: torch.Tensor, up: torch.Tensor, *, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """geglu (native_model.cc:378-386): bf16 ``0.5*g*(1 + tanh(sqrt(2/pi)*(g + 0.044715*g^3))) * up``
+    with the reference's nine bf16 roundings, in one kernel. ``gate`` and ``up`` may be the two
+    halves of one gate|up matmul output (``y[..., :I]``, ``y[..., I:]``)."""
+    if gate.shape != up.shape:
+        raise ValueError("gate and up must have the same shape")
+    I = gate.shape[-1]
+    if I % 8 != 0:
+        raise ValueError("the last dimension must be a multiple of 8")
+    g2, u2 = _bf16_rows(gate, "gate"), _bf16_rows(up, "up")
+    res = torch.empty(gate.shape, dtype=torch.bfloat16, device=gate.device) if out is None else out
+    o2 = _bf16_rows(res, "out")
+    if o2.data_ptr() != res.data_ptr() or o2.shape != g2.shape:
+        raise ValueError("out must be a contiguous tensor shaped like gate")
+    _lib.call("g4q_geglu", _ptr(g2), g2.stride(0), _ptr(u2), u2.stride(0), g2.shape[0], I, _ptr(o2), o2.stride(0),
+              _stream())
+    return res
+
+
+def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor] = None, eps: float = 1e-6, *,
+             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``model_dtype(mlx::core::fast::rms_norm(x, weight, eps))`` over the last dimension
+    (native_model.cc:910-913 and the other norms of a layer): bf16(weight * bf16(x / rms(x)))."""
+    K = x.shape[-1]
+    if K % 8 != 0:
+        raise ValueError("the last dimension must be a multiple of 8")
+    x2 = _bf16_rows(x, "x")
+    w = None
+    if weight is not None:
+        if weight.shape != (K,):
+            raise ValueError(f"weight must have shape ({K},)")
+        w = _bf16_rows(weight.view(1, K), "weight")
+    res = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device) if out is None else out
+    o2 = _bf16_rows(res, "out")
+    if o2.data_ptr() != res.data_ptr() or o2.shape != x2.shape:
+        raise ValueError("out must be a contiguous tensor shaped like x")
+    _lib.call("g4q_rms_norm", _ptr(x2), x2.stride(0), _ptr(w), x2.shape[0], K, float(eps), _ptr(o2), o2.stride(0),
+              _stream())
+    return res
 
 
 def dequantize(w, scales: Optional[torch.Tensor] = None, biases: Optional[torch.Tensor] = None,

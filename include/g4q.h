@@ -186,6 +186,21 @@ G4qStatus g4q_lora_apply(const G4qLora* lora, const uint16_t* x, int64_t M, int6
                          void* stream);
 G4qStatus g4q_lora_free(G4qLora* lora);
 
+/* ---- the MLP's elementwise neighbours ------------------------------------------------------------
+ * Replaces geglu (native/gemma4_mlx/src/native_model.cc:378-386; called at :945): per element,
+ * bf16 0.5*g*(1 + tanh(sqrt(2/pi)*(g + 0.044715*g^3))) * up with the constants rounded to bf16 and
+ * every one of the nine ops rounded to bf16, as the reference's bf16 MLX ops do, in one launch.
+ * gate / up / out: bf16 [M, I] with row strides ld_* (elements); I, the strides and the pointers
+ * 16-byte multiples (I % 8 == 0). gate and up may be the two halves of one gate|up matmul output. */
+G4qStatus g4q_geglu(const uint16_t* gate, int64_t ld_gate, const uint16_t* up, int64_t ld_up, int64_t M, int64_t I,
+                    uint16_t* out, int64_t ld_out, void* stream);
+/* Replaces model_dtype(fast::rms_norm(x, weight, eps)) (native_model.cc:910-913, 920-923,
+ * 929-932, 954-957; values norm without weight :844): per row, inv = 1/sqrt(mean(x^2) + eps) in
+ * fp32, out = bf16(weight * bf16(x * inv)). weight: bf16 [K] or NULL. x / out: bf16 [M, ld],
+ * K % 8 == 0, 16-byte aligned rows. out may equal x (in place). */
+G4qStatus g4q_rms_norm(const uint16_t* x, int64_t ldx, const uint16_t* weight, int64_t M, int64_t K, float eps,
+                       uint16_t* out, int64_t ld_out, void* stream);
+
 /* ---- decode plan: every quantized matmul of one decode step in one persistent kernel ----------
  * Replaces the per-token chain of quantized_linear calls of the decode drivers
  * (native_model.cc:1843-1911 decode_last_logits -> 48 x target_layer_decode_forward :1284-1328 ->

@@ -238,6 +238,45 @@ def lora_delta(x, y_base, lora_a, lora_b, alpha: float):
     return f32_to_bf16(out.astype(np.float32))
 
 
+def _rb(a) -> np.ndarray:
+    """fp32 -> bf16 (round to nearest even) -> fp32."""
+    return bf16_to_f32(f32_to_bf16(np.asarray(a, dtype=np.float32)))
+
+
+def geglu(gate, up):
+    """geglu (native_model.cc:378-386) on bf16 bits: the nine bf16 ops of the reference, each an
+    fp32 operation on bf16 operands rounded to bf16, with the constants as model_scalar rounds them
+    (bf16(0.044715), bf16(0.7978845608028654), 0.5, 1.0); gate^3 as g*g*g (exact in fp32)."""
+    g = bf16_to_f32(gate)
+    u = bf16_to_f32(up)
+    kc = np.float32(_rb(np.float32(0.044715)))
+    ka = np.float32(_rb(np.float32(0.7978845608028654)))
+    g3 = _rb(g * g * g)
+    t1 = _rb(kc * g3)
+    t2 = _rb(g + t1)
+    t3 = _rb(ka * t2)
+    t4 = _rb(np.tanh(t3))
+    t5 = _rb(np.float32(1.0) + t4)
+    t6 = _rb(np.float32(0.5) * g)
+    t7 = _rb(t6 * t5)
+    return f32_to_bf16(t7 * u)
+
+
+def rms_norm(x, weight=None, eps: float = 1e-6):
+    """model_dtype(fast::rms_norm(x, weight, eps)) on bf16 bits [..., K]: mean(x^2) accumulated in
+    float64 and rounded to fp32, inv = 1/sqrt(mean + eps) correctly rounded to fp32, then
+    bf16(weight * bf16(x * inv)) (the normalized value rounded to the input dtype before the weight
+    product, as MLX's fast::rms_norm does)."""
+    xf = bf16_to_f32(x)
+    m = np.float32((xf.astype(np.float64) ** 2).mean(axis=-1, keepdims=True))
+    v = (m + np.float32(eps)).astype(np.float32)
+    inv = (1.0 / np.sqrt(v.astype(np.float64))).astype(np.float32)
+    y = _rb(xf * inv)
+    if weight is None:
+        return f32_to_bf16(y)
+    return f32_to_bf16(bf16_to_f32(weight) * y)
+
+
 def rms_scale(x_row, eps: float = 1e-6) -> float:
     x_row = np.ascontiguousarray(x_row, dtype=np.uint16)
     return float(lib().g4o_rms_scale(_p(x_row), x_row.size, eps))
