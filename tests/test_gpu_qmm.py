@@ -53,6 +53,67 @@ def test_decode_gemv_odd_widths(cuda, oracle, M):
     qw.free()
 
 
+FULL_ATTENTION = {"q_full": (8192, 3840), "k_full": (512, 3840), "o_full": (3840, 8192)}
+
+
+@pytest.mark.parametrize("proj", list(FULL_ATTENTION))
+@pytest.mark.parametrize("M", [1, 8, 15, 64])
+def test_full_attention_layer_shapes(cuda, oracle, proj, M):
+    """The real model's every-sixth layer (native_model.cc:496-498, 788-897): head_dim 512 and one
+    KV head, so q 8192x3840, k 512x3840 (no v) and o 3840x8192; at decode (1), MTP verify (8, 15:
+    decode_block_logits, :2006) and a prefill width (64)."""
+    from helios_b200 import quantized as Q
+    N, K = FULL_ATTENTION[proj]
+    qw, x, (ow, os_, ob) = make(oracle, Q, "q" if proj != "o_full" else "o", N, K, M, layer=5, chunk=200 + M)
+    ye, yb = oracle.qmm(u16(x), ow, os_, ob)
+    y = Q.quantized_matmul(x, qw)
+    assert_qmm_close(oracle.bf16_to_f32(u16(y)), ye, bf16_out=True)
+    assert (u16(y) == yb).mean() > 0.99
+    qw.free()
+
+
+# The 12B MTP assistant (config checked at native/gemma4_mlx/src/model_manifest.cc:265-272: hidden
+# 1024, intermediate 8192, 16 heads of 256, head_dim 512 on its full-attention layer 3, no k/v
+# projections) and its linears (native_model.cc:2134-2243): pre_projection over the concatenated
+# token embedding and target hidden (3840 + 3840 -> 1024), post_projection back to 3840.
+ASSISTANT = {"pre_projection": (1024, 7680), "q": (4096, 1024), "q_full": (8192, 1024), "o": (1024, 4096),
+             "o_full": (1024, 8192), "gate_up": (8192, 1024), "down": (1024, 8192), "post_projection": (3840, 1024)}
+
+
+@pytest.mark.parametrize("name", list(ASSISTANT))
+@pytest.mark.parametrize("M", [1, 4])
+def test_mtp_assistant_shapes(cuda, oracle, name, M):
+    from helios_b200 import quantized as Q
+    N, K = ASSISTANT[name]
+    qw, x, (ow, os_, ob) = make(oracle, Q, "up", N, K, M, layer=40, chunk=300 + M)
+    ye, yb = oracle.qmm(u16(x), ow, os_, ob)
+    y = Q.quantized_matmul(x, qw)
+    assert_qmm_close(oracle.bf16_to_f32(u16(y)), ye, bf16_out=True)
+    assert (u16(y) == yb).mean() > 0.99
+    qw.free()
+
+
+def test_mtp_assistant_lm_head_without_softcap(cuda, oracle):
+    """assistant_logits (native_model.cc:2103-2116): the assistant's tied 262144 x 1024 head, bf16
+    logits with no softcap, then a greedy argmax (:2227)."""
+    from helios_b200 import quantized as Q
+    N, K = 262144, 1024
+    seed = oracle.matrix_seed(41, 7)
+    w, s, b = Q.synth_matrix(seed, N, K)
+    qw = Q.QuantizedWeight.from_mlx(w, s, b)
+    x = Q.synth_normal(oracle.activation_seed(41), (1, K))
+    logits = torch.empty((1, N), dtype=torch.bfloat16, device=cuda)
+    tok, val, _ = Q.lm_head_argmax(x, qw, softcap=0.0, logits=logits)
+    ow, os_, ob = oracle.synth_matrix(seed, N, K)
+    ye, yb = oracle.qmm(u16(x), ow, os_, ob)
+    assert_qmm_close(oracle.bf16_to_f32(u16(logits)), ye, bf16_out=True)
+    t_self, v_self = oracle.softcap_argmax(u16(logits[0]), 0.0)
+    assert int(tok[0]) == t_self and float(val[0]) == v_self
+    t_ref, v_ref = oracle.softcap_argmax(yb[0], 0.0)
+    assert int(tok[0]) == t_ref or abs(v_self - v_ref) <= 0.125
+    qw.free()
+
+
 @pytest.mark.parametrize("N,K", [(16, 64), (48, 192), (80, 1024), (272, 640), (128, 768), (320, 192),
                                  (1088, 512)])
 @pytest.mark.parametrize("M", [1, 7, 16])
