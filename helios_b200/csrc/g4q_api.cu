@@ -448,6 +448,40 @@ G4qStatus g4q_qmm_ex(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t l
     return guarded("g4q_qmm_ex", [&] { qmm_common("g4q_qmm_ex", h, x, M, ldx, y, ldy, flags, eps, stream); });
 }
 
+G4qStatus g4q_qmm_norm(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t ldx, const uint16_t* weight,
+                       float eps, uint16_t* xn, int64_t ldxn, uint16_t* y, int64_t ldy, void* stream) {
+    return guarded("g4q_qmm_norm", [&] {
+        Weight* w = checked(h, "g4q_qmm_norm");
+        require(M >= 0, G4Q_ERR_INVALID_ARGUMENT, "M must be >= 0");
+        if (M == 0) return;
+        require(x != nullptr && y != nullptr && weight != nullptr, G4Q_ERR_INVALID_ARGUMENT,
+                "x, weight and y must be non-null");
+        require(ldx >= w->K && ldx % 8 == 0, G4Q_ERR_INVALID_ARGUMENT, "ldx must be >= cols and a multiple of 8");
+        require(ldy >= w->N, G4Q_ERR_INVALID_ARGUMENT, "ldy must be >= rows");
+        require(w->K % 8 == 0, G4Q_ERR_UNSUPPORTED_CONFIG, "cols must be a multiple of 8");
+        require(eps >= 0.0f && std::isfinite(eps), G4Q_ERR_INVALID_ARGUMENT, "eps must be finite and >= 0");
+        require_aligned16(x, "x");
+        require_aligned16(weight, "weight");
+        if (xn != nullptr) {
+            require(ldxn >= w->K && ldxn % 8 == 0, G4Q_ERR_INVALID_ARGUMENT, "ldxn must be >= cols and a multiple of 8");
+            require_aligned16(xn, "xn");
+        }
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        QmmCall c{w, x, M, ldx, y, ldy, 0u, eps};
+        c.norm_w = weight;
+        c.xn = xn;
+        c.ldxn = ldxn;
+        if (!w->mlx && w->fast_ok && M <= 8 && gemv2_supported(c)) {
+            launch_gemv2(c, st);   // the norm fused into the GEMV's x staging
+            return;
+        }
+        require(xn != nullptr, G4Q_ERR_INVALID_ARGUMENT,
+                "xn is required unless M <= 8 on a 4-bit group-64 weight the fused GEMV takes");
+        launch_rms_norm(x, ldx, weight, M, w->K, eps, xn, ldxn, st);
+        qmm_common("g4q_qmm_norm", h, xn, M, ldxn, y, ldy, 0u, eps, stream);
+    });
+}
+
 G4qStatus g4q_lm_head_argmax(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t ldx, float softcap,
                              uint32_t flags, float eps, int64_t row_offset, uint16_t* logits, int64_t ld_logits,
                              int32_t* tokens, float* values, uint64_t* keys, void* stream) {

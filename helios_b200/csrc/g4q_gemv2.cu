@@ -57,7 +57,25 @@ struct Gemv2Args {
     int stages;             // ring stages per warp (2 or 3)
     int xg;                 // 64-wide groups of x staged per token: G, or fewer when every CTA's
                             // range is shorter than a quad row (the window its units read)
+    const uint16_t* norm_w; // non-null: fused RMSNorm of x with this bf16 [K] weight (no output scale)
+    uint16_t* xn;           // non-null (norm only): CTA 0 also writes the normalized rows here
+    int64_t ldxn;
 };
+
+// One bf16 pair of the fused RMSNorm: bf16(w * bf16(x * inv)) per half, the rounding order of
+// fast::rms_norm (the normalized value in the input dtype, then the weight product).
+__device__ __forceinline__ uint32_t norm_pair(uint32_t xv, uint32_t wv, float inv) {
+    const float lo = __fmul_rn(bf16_bits_to_f32(wv & 0xffffu),
+                               bf16_bits_to_f32(f32_to_bf16_bits(__fmul_rn(bf16_bits_to_f32(xv & 0xffffu), inv))));
+    const float hi = __fmul_rn(bf16_bits_to_f32(wv >> 16),
+                               bf16_bits_to_f32(f32_to_bf16_bits(__fmul_rn(bf16_bits_to_f32(xv >> 16), inv))));
+    return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+}
+
+__device__ __forceinline__ uint4 norm_vec(uint4 v, uint4 w, float inv) {
+    return make_uint4(norm_pair(v.x, w.x, inv), norm_pair(v.y, w.y, inv), norm_pair(v.z, w.z, inv),
+                      norm_pair(v.w, w.w, inv));
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -224,6 +242,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
     __shared__ __align__(8) unsigned long long bars[kWarpsV2][kStages];
     __shared__ float wss[kWarpsV2][8];
     __shared__ float rs[8];
+    __shared__ float ninv[8];   // fused RMSNorm: per-token inverse RMS
     __shared__ int qcnt[kWarpsV2];
     // the warp index through a shuffle from lane 0: provably warp-uniform, so the compiler keeps it
     // and everything derived from it (ring and barrier addresses, unit cursors) in uniform registers
@@ -269,6 +288,43 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
     const bool win = a.xg < G;
     const int words = a.xg * 32;   // bf16 pairs staged per token
     const int g0 = win ? cs % G : 0;
+    const bool norm = a.norm_w != nullptr;
+    if (norm) {
+        // fused RMSNorm: the per-token inverse RMS over all of K first (every CTA reduces in the same
+        // order, so every CTA stages the same bits), then x is normalized as it is staged
+        for (int m = 0; m < M; ++m) {
+            float ss = 0.0f;
+            const uint4* xr = reinterpret_cast<const uint4*>(a.x + (int64_t)m * a.ldx);
+            for (int u = threadIdx.x; u < a.K / 8; u += kThreadsV2) {
+                const uint4 v = xr[u];
+                const uint32_t pv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float lo = bf16_bits_to_f32(pv[i] & 0xffffu), hi = bf16_bits_to_f32(pv[i] >> 16);
+                    ss = __fadd_rn(ss, __fmul_rn(lo, lo));
+                    ss = __fadd_rn(ss, __fmul_rn(hi, hi));
+                }
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+            if (lane == 0) wss[warp][m] = ss;
+        }
+        __syncthreads();
+        if (threadIdx.x < M) {
+            float s = 0.0f;
+            for (int w = 0; w < kWarpsV2; ++w) s = __fadd_rn(s, wss[w][threadIdx.x]);
+            ninv[threadIdx.x] = __frsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)a.K), a.eps));
+        }
+        __syncthreads();
+        if (a.xn != nullptr && cta == 0) {   // the normalized rows, for callers that need them too
+            for (int m = 0; m < M; ++m) {
+                const uint4* xr = reinterpret_cast<const uint4*>(a.x + (int64_t)m * a.ldx);
+                const uint4* wr = reinterpret_cast<const uint4*>(a.norm_w);
+                uint4* outr = reinterpret_cast<uint4*>(a.xn + (int64_t)m * a.ldxn);
+                for (int u = threadIdx.x; u < a.K / 8; u += kThreadsV2) outr[u] = norm_vec(xr[u], wr[u], ninv[m]);
+            }
+        }
+    }
     for (int m = 0; m < M; ++m) {
         float ss = 0.0f;
         const uint4* xr = reinterpret_cast<const uint4*>(a.x + (int64_t)m * a.ldx);
@@ -276,7 +332,8 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
         for (int u = threadIdx.x; u < a.xg * 8; u += kThreadsV2) {
             int g = g0 + (u >> 3);
             if (g >= G) g -= G;
-            const uint4 v = xr[g * 8 + (u & 7)];
+            uint4 v = xr[g * 8 + (u & 7)];
+            if (norm) v = norm_vec(v, reinterpret_cast<const uint4*>(a.norm_w)[g * 8 + (u & 7)], ninv[m]);
             xm[xperm(4 * u)] = v.x;
             xm[xperm(4 * u + 1)] = v.y;
             xm[xperm(4 * u + 2)] = v.z;
@@ -474,6 +531,9 @@ void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     a.slots = ds.slots;
     a.counters = ds.counters;
     a.err = ds.err;
+    a.norm_w = c.norm_w;
+    a.xn = c.norm_w != nullptr ? c.xn : nullptr;
+    a.ldxn = c.ldxn;
     a.xg = gemv2_xgroups(a.U, a.G, grid);
     a.stages = gemv2_stages(a.M, a.xg);
     if (a.stages == 0) throw Error(G4Q_ERR_RUNTIME, "gemv2: x does not fit in shared memory");

@@ -131,6 +131,11 @@ struct QmmCall {
     int64_t ldy;
     uint32_t flags;
     float eps;
+    // fused RMSNorm prologue (stream-K GEMV only): x is replaced by bf16(norm_w * bf16(x * inv)),
+    // inv = 1/sqrt(mean(x^2) + eps); the normalized rows also go to xn when it is non-null
+    const uint16_t* norm_w = nullptr;
+    uint16_t* xn = nullptr;
+    int64_t ldxn = 0;
 };
 void launch_qmm_mlx(const QmmCall& c, cudaStream_t st);
 

@@ -27,10 +27,9 @@ from ._lib import (CHAIN_R1, CHAIN_R2, PHASE_ALLREDUCE, PHASE_ARGMAX, QMM_OUT_F3
                    G4qInvalidArgument)
 
 __all__ = [
-    "QuantizedWeight", "quantized_matmul", "quantized_linear", "LoraAdapter", "geglu", "rms_norm", "dequantize",
-    "lm_head_argmax",
-    "DecodePlan", "synth_matrix", "synth_normal", "CHAIN_R1", "CHAIN_R2", "QMM_RMS_SCALE", "QMM_OUT_F32", "PHASE_ARGMAX", "PHASE_ALLREDUCE", "G4qError",
-    "G4qInvalidArgument",
+    "QuantizedWeight", "quantized_matmul", "quantized_linear", "norm_quantized_matmul", "LoraAdapter", "geglu",
+    "rms_norm", "dequantize", "lm_head_argmax", "DecodePlan", "synth_matrix", "synth_normal", "CHAIN_R1",
+    "CHAIN_R2", "QMM_RMS_SCALE", "QMM_OUT_F32", "PHASE_ARGMAX", "PHASE_ALLREDUCE", "G4qError", "G4qInvalidArgument",
 ]
 
 
@@ -326,6 +325,32 @@ def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor] = None, eps: float 
     _lib.call("g4q_rms_norm", _ptr(x2), x2.stride(0), _ptr(w), x2.shape[0], K, float(eps), _ptr(o2), o2.stride(0),
               _stream())
     return res
+
+
+def norm_quantized_matmul(x: torch.Tensor, norm_weight: torch.Tensor, w: QuantizedWeight, *, eps: float = 1e-6,
+                          xn: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``quantized_matmul(rms_norm(x, norm_weight, eps), w)`` -- the norm -> linear pair of
+    layer_forward (native_model.cc:910-913, 929-932). At M <= 8 the norm is fused into the decode
+    GEMV's staging of x (one launch); ``xn``, if given, also receives the normalized rows. Larger M
+    needs ``xn`` (bf16, shaped like x): the normalized rows are written there, then multiplied."""
+    x2 = _rows2d(x, w.cols)
+    M = x2.shape[0]
+    if norm_weight.shape != (w.cols,) or norm_weight.dtype != torch.bfloat16:
+        raise ValueError(f"norm_weight must be bf16 of shape ({w.cols},)")
+    nw = norm_weight.contiguous()
+    xn2 = None
+    if xn is not None:
+        if xn.dtype != torch.bfloat16 or not xn.is_contiguous() or xn.numel() != M * w.cols:
+            raise ValueError("xn must be a contiguous bf16 tensor shaped like x")
+        xn2 = xn.view(M, w.cols)
+    shape = tuple(x.shape[:-1]) + (w.rows,)
+    y = torch.empty(shape, dtype=torch.bfloat16, device=x.device) if out is None else out
+    if y.dtype != torch.bfloat16 or not y.is_contiguous() or y.shape[-1] != w.rows:
+        raise ValueError("out must be a contiguous bf16 tensor with last dimension = rows")
+    y2 = y.view(-1, w.rows)
+    _lib.call("g4q_qmm_norm", w.handle, _ptr(x2), M, x2.stride(0), _ptr(nw), float(eps), _ptr(xn2),
+              0 if xn2 is None else xn2.stride(0), _ptr(y2), y2.stride(0), _stream())
+    return y
 
 
 def dequantize(w, scales: Optional[torch.Tensor] = None, biases: Optional[torch.Tensor] = None,

@@ -131,6 +131,17 @@ G4qStatus g4q_qmm(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t ldx,
 G4qStatus g4q_qmm_ex(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t ldx, void* y, int64_t ldy,
                      uint32_t flags, float eps, void* stream);
 
+/* Replaces the pair model_dtype(fast::rms_norm(h, weight, eps)) -> quantized_linear of
+ * layer_forward (native_model.cc:910-913 -> q/k/v, 929-932 -> gate/up; the decode twins
+ * :993-1018, :1318-1321): y = qmm(bf16(weight * bf16(x * inv))) with inv = 1/sqrt(mean(x^2) + eps)
+ * per row. At M <= 8 on a 4-bit group-64 weight the norm is fused into the stream-K GEMV's x
+ * staging (one launch, x read twice from L2, no normalized copy in HBM); xn may be NULL there, and
+ * when given it also receives the normalized rows. Otherwise xn (bf16 [M, ldxn], 16-byte aligned)
+ * is required: the normalized rows are written there first and the matmul reads them. weight:
+ * bf16 [cols], 16-byte aligned. */
+G4qStatus g4q_qmm_norm(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t ldx, const uint16_t* weight,
+                       float eps, uint16_t* xn, int64_t ldxn, uint16_t* y, int64_t ldy, void* stream);
+
 /* ---- tied LM head with fused softcap + greedy argmax ----------------------------------------
  * Replaces target_logits_for_hidden (native_model.cc:1782-1795: quantized_matmul against
  * embed_tokens, bf16, tanh(l/30)*30 in bf16) and the greedy argmax of its callers (:3825,

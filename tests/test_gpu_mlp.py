@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import dev_u16, u16, u32
+from gpu_util import assert_qmm_close, dev_u16, u16, u32
 
 pytestmark = pytest.mark.gpu
 
@@ -99,3 +99,64 @@ def test_real_mlp_block(cuda, oracle):
     assert (u16(act) == act_ref).mean() >= 0.99
     gate_up.free()
     down.free()
+
+
+@pytest.mark.parametrize("proj,N,K", [("gate_up", 30720, 3840), ("down", 3840, 15360), ("qkv", 8192, 3840)])
+@pytest.mark.parametrize("M", [1, 2, 4, 8])
+def test_norm_fused_into_decode_gemv(cuda, oracle, proj, N, K, M):
+    """rms_norm -> quantized matmul as one stream-K GEMV launch (the norm applied while x is staged;
+    down_proj's K = 15360 exercises the staged window of x) against the oracle's two steps."""
+    from helios_b200 import quantized as Q
+    seed = oracle.matrix_seed(7, oracle.PROJ_IDS["up" if proj != "down" else "down"])
+    w, s, b = Q.synth_matrix(seed, N, K)
+    qw = Q.QuantizedWeight.from_mlx(w, s, b)
+    g = torch.Generator().manual_seed(M + K)
+    x = (2.0 * torch.randn(M, K, generator=g)).to(torch.bfloat16).to(cuda)
+    nw = (1.0 + 0.2 * torch.randn(K, generator=g)).to(torch.bfloat16).to(cuda)
+    xn = torch.empty_like(x)
+    y = Q.norm_quantized_matmul(x, nw, qw, eps=1e-6, xn=xn)
+    fused = not (proj == "down" and M == 8)   # 8 tokens of a 15360-wide x do not fit beside the rings
+    if fused:
+        y2 = Q.norm_quantized_matmul(x, nw, qw, eps=1e-6)      # without the normalized-rows output
+    else:
+        from helios_b200 import _lib
+        with pytest.raises(_lib.G4qInvalidArgument):           # the unfused path needs xn
+            Q.norm_quantized_matmul(x, nw, qw, eps=1e-6)
+        y2 = y
+    torch.cuda.synchronize()
+    xn_ref = oracle.rms_norm(u16(x), u16(nw), 1e-6)
+    assert (u16(xn) == xn_ref).mean() >= 0.99 and ulps_apart(oracle, u16(xn), xn_ref).max() <= 1.0
+    ow, os_, ob = u32(w), u16(s), u16(b)
+    # the matmul consumed exactly the normalized rows it wrote out
+    ye, yb = oracle.qmm(u16(xn), ow, os_, ob)
+    assert_qmm_close(oracle.bf16_to_f32(u16(y)), ye, bf16_out=True)
+    assert (u16(y) == yb).mean() > 0.99
+    assert (u16(y2) == u16(y)).all()
+    # and the whole pair is within the matmul tolerance of the oracle's rms_norm -> qmm
+    ye2, _ = oracle.qmm(xn_ref, ow, os_, ob)
+    assert_qmm_close(oracle.bf16_to_f32(u16(y)), ye2, bf16_out=True)
+    qw.free()
+
+
+@pytest.mark.parametrize("M", [12, 64])
+def test_norm_matmul_outside_the_fused_widths(cuda, oracle, M):
+    """M > 8: the normalized rows go through xn (required) and the regular matmul path."""
+    from helios_b200 import _lib
+    from helios_b200 import quantized as Q
+    N, K = 2048, 3840
+    seed = oracle.matrix_seed(8, oracle.PROJ_IDS["k"])
+    w, s, b = Q.synth_matrix(seed, N, K)
+    qw = Q.QuantizedWeight.from_mlx(w, s, b)
+    g = torch.Generator().manual_seed(M)
+    x = (2.0 * torch.randn(M, K, generator=g)).to(torch.bfloat16).to(cuda)
+    nw = (1.0 + 0.2 * torch.randn(K, generator=g)).to(torch.bfloat16).to(cuda)
+    with pytest.raises(_lib.G4qInvalidArgument):
+        Q.norm_quantized_matmul(x, nw, qw)
+    xn = torch.empty_like(x)
+    y = Q.norm_quantized_matmul(x, nw, qw, xn=xn)
+    torch.cuda.synchronize()
+    xn_ref = oracle.rms_norm(u16(x), u16(nw), 1e-6)
+    assert (u16(xn) == xn_ref).mean() >= 0.99
+    ye, _ = oracle.qmm(xn_ref, u32(w), u16(s), u16(b))
+    assert_qmm_close(oracle.bf16_to_f32(u16(y)), ye, bf16_out=True)
+    qw.free()
