@@ -482,6 +482,43 @@ G4qStatus g4q_qmm_norm(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t
     });
 }
 
+G4qStatus g4q_qmm_geglu(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t ldx, uint32_t flags, float eps,
+                        uint16_t* y, uint16_t* act, int64_t ld_act, void* stream) {
+    return guarded("g4q_qmm_geglu", [&] {
+        Weight* w = checked(h, "g4q_qmm_geglu");
+        require(!w->mlx, G4Q_ERR_UNSUPPORTED_CONFIG, "the fused GeGLU takes a 4-bit group-64 weight");
+        require(w->N % 64 == 0, G4Q_ERR_INVALID_ARGUMENT, "a paired gate|up weight has rows in multiples of 64");
+        require(M >= 0, G4Q_ERR_INVALID_ARGUMENT, "M must be >= 0");
+        if (M == 0) return;
+        require(x != nullptr && act != nullptr, G4Q_ERR_INVALID_ARGUMENT, "x and act must be non-null");
+        require((flags & ~G4Q_QMM_RMS_SCALE) == 0, G4Q_ERR_INVALID_ARGUMENT, "only G4Q_QMM_RMS_SCALE is accepted");
+        require(ldx >= w->K && ldx % 8 == 0, G4Q_ERR_INVALID_ARGUMENT, "ldx must be >= cols and a multiple of 8");
+        require(ld_act >= w->N / 2 && ld_act % 8 == 0, G4Q_ERR_INVALID_ARGUMENT,
+                "ld_act must be >= rows/2 and a multiple of 8");
+        require_aligned16(x, "x");
+        require_aligned16(act, "act");
+        require(w->fast_ok, G4Q_ERR_UNSUPPORTED_CONFIG, "a scale is non-finite or |scale| >= 2^120");
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        QmmCall c{w, x, M, ldx, act, ld_act, flags, eps};
+        c.geglu = true;
+        if (M <= 8 && gemv2_supported(c)) {
+            launch_gemv2(c, st);   // the GeGLU in the GEMV's epilogue
+            return;
+        }
+        require(y != nullptr, G4Q_ERR_INVALID_ARGUMENT,
+                "y is required unless M <= 8 on a shape the fused GEMV takes");
+        require_aligned16(y, "y");
+        qmm_common("g4q_qmm_geglu", h, x, M, ldx, y, w->N, flags, eps, stream);
+        // the pairs: per token, N/64 rows of 32 gate values followed by the 32 matching up values
+        if (ld_act == w->N / 2) {
+            launch_geglu(y, 64, y + 32, 64, act, 32, M * (w->N / 64), 32, st);
+        } else {
+            for (int64_t m = 0; m < M; ++m)
+                launch_geglu(y + m * w->N, 64, y + m * w->N + 32, 64, act + m * ld_act, 32, w->N / 64, 32, st);
+        }
+    });
+}
+
 G4qStatus g4q_lm_head_argmax(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t ldx, float softcap,
                              uint32_t flags, float eps, int64_t row_offset, uint16_t* logits, int64_t ld_logits,
                              int32_t* tokens, float* values, uint64_t* keys, void* stream) {

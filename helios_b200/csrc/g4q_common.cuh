@@ -117,6 +117,22 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 
+// geglu (native_model.cc:378-386) of one bf16 pair (g, u), each of the reference's nine bf16 ops
+// rounded to bf16: cubic = bf16(0.044715), tanh_approx = bf16(0.7978845608028654) as model_scalar
+// rounds them; g^3 = g*g*g is exact in fp32 for a bf16 g. Returns the bf16 bits.
+__device__ __forceinline__ uint16_t geglu_bf16(float g, float u, float cubic, float tanh_approx) {
+    const auto rb = [](float f) { return __bfloat162float(__float2bfloat16_rn(f)); };
+    const float g3 = rb(g * g * g);              // power(gate, 3)
+    const float t1 = rb(cubic * g3);             // 0.044715 * gate^3
+    const float t2 = rb(g + t1);                 // gate + ...
+    const float t3 = rb(tanh_approx * t2);       // sqrt(2/pi) * (...)
+    const float t4 = rb(tanhf(t3));              // tanh
+    const float t5 = rb(1.0f + t4);              // 1 + tanh
+    const float t6 = rb(0.5f * g);               // 0.5 * gate
+    const float t7 = rb(t6 * t5);                // gelu
+    return f32_to_bf16_bits(t7 * u);             // gelu * up
+}
+
 // Order-preserving key of (value, index): max key = max value, ties -> smallest index.
 // NaN maps to 0 so it is never selected over a number.
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {

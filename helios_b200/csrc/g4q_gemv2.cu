@@ -60,6 +60,8 @@ struct Gemv2Args {
     const uint16_t* norm_w; // non-null: fused RMSNorm of x with this bf16 [K] weight (no output scale)
     uint16_t* xn;           // non-null (norm only): CTA 0 also writes the normalized rows here
     int64_t ldxn;
+    int geglu;              // 1: paired gate|up quads, y = geglu(gate, up) bf16 [M, N/2]
+    float gk_cubic, gk_tanh;   // the GeGLU constants rounded to bf16
 };
 
 // One bf16 pair of the fused RMSNorm: bf16(w * bf16(x * inv)) per half, the rounding order of
@@ -156,6 +158,14 @@ __device__ __forceinline__ void store_out(const Gemv2Args& a, int q, int row, in
         reinterpret_cast<uint16_t*>(a.y)[idx] = f32_to_bf16_bits(o);
 }
 
+// GeGLU epilogue of a paired quad q: rows r and r + 32 are gate and up of output feature 32q + r;
+// each is scaled and rounded to bf16 as the matmul's own output would be, then geglu'd.
+__device__ __forceinline__ void store_act(const Gemv2Args& a, int q, int r, int tok, float vg, float vu, float rs) {
+    const float g = bf16_bits_to_f32(f32_to_bf16_bits(__fmul_rn(vg, rs)));
+    const float u = bf16_bits_to_f32(f32_to_bf16_bits(__fmul_rn(vu, rs)));
+    reinterpret_cast<uint16_t*>(a.y)[(int64_t)tok * a.ldy + q * 32 + r] = geglu_bf16(g, u, a.gk_cubic, a.gk_tanh);
+}
+
 // Shared-memory order of x: inside each 64-wide group, lane t's B-fragment words for the four k16
 // steps (j) sit together: word w = 8j + t + 4hi of the group goes to slot 8t + 2j + hi, so a lane
 // fetches the group's fragments of its token with two 16-byte loads.
@@ -204,14 +214,27 @@ __device__ __forceinline__ void park_quad(const Gemv2Args& a, int* qcnt, float* 
         cf = cta_of_unit(q * G, a.U, C);
         nc = cta_of_unit((q + 1) * G - 1, a.U, C) - cf + 1;
     }
-    for (int o = lane; o < nout; o += 32) {
-        const int tok = o >> 6, row = o & 63;
-        float v = red[(size_t)(wa * 2 + slot_a) * M * 64 + o];
-        for (int w = wa + 1; w <= wb; ++w) v += red[(size_t)w * 2 * M * 64 + o];
-        if (whole)
-            store_out(a, q, row, tok, v, rs[tok]);
-        else
-            base[(size_t)(cta - cf) * 512 + row * 8 + tok] = v;
+    if (whole && a.geglu) {   // both rows of each gate/up pair, summed exactly as below
+        for (int o2 = lane; o2 < 32 * M; o2 += 32) {
+            const int tok = o2 >> 5, r = o2 & 31, og = tok * 64 + r, ou = og + 32;
+            float vg = red[(size_t)(wa * 2 + slot_a) * M * 64 + og];
+            float vu = red[(size_t)(wa * 2 + slot_a) * M * 64 + ou];
+            for (int w = wa + 1; w <= wb; ++w) {
+                vg += red[(size_t)w * 2 * M * 64 + og];
+                vu += red[(size_t)w * 2 * M * 64 + ou];
+            }
+            store_act(a, q, r, tok, vg, vu, rs[tok]);
+        }
+    } else {
+        for (int o = lane; o < nout; o += 32) {
+            const int tok = o >> 6, row = o & 63;
+            float v = red[(size_t)(wa * 2 + slot_a) * M * 64 + o];
+            for (int w = wa + 1; w <= wb; ++w) v += red[(size_t)w * 2 * M * 64 + o];
+            if (whole)
+                store_out(a, q, row, tok, v, rs[tok]);
+            else
+                base[(size_t)(cta - cf) * 512 + row * 8 + tok] = v;
+        }
     }
     if (!whole) {
         __threadfence();
@@ -221,11 +244,23 @@ __device__ __forceinline__ void park_quad(const Gemv2Args& a, int* qcnt, float* 
         lastc = __shfl_sync(0xffffffffu, lastc, 0);
         if (lastc) {
             __threadfence();
-            for (int o = lane; o < nout; o += 32) {
-                const int tok = o >> 6, row = o & 63;
-                float s = 0.0f;
-                for (int c = 0; c < nc; ++c) s += __ldcg(base + (size_t)c * 512 + row * 8 + tok);
-                store_out(a, q, row, tok, s, rs[tok]);
+            if (a.geglu) {
+                for (int o2 = lane; o2 < 32 * M; o2 += 32) {
+                    const int tok = o2 >> 5, r = o2 & 31;
+                    float sg = 0.0f, su = 0.0f;
+                    for (int c = 0; c < nc; ++c) {
+                        sg += __ldcg(base + (size_t)c * 512 + r * 8 + tok);
+                        su += __ldcg(base + (size_t)c * 512 + (r + 32) * 8 + tok);
+                    }
+                    store_act(a, q, r, tok, sg, su, rs[tok]);
+                }
+            } else {
+                for (int o = lane; o < nout; o += 32) {
+                    const int tok = o >> 6, row = o & 63;
+                    float s = 0.0f;
+                    for (int c = 0; c < nc; ++c) s += __ldcg(base + (size_t)c * 512 + row * 8 + tok);
+                    store_out(a, q, row, tok, s, rs[tok]);
+                }
             }
             __syncwarp();
             if (lane == 0) atomicExch(a.counters + q, 0);
@@ -531,6 +566,9 @@ void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     a.slots = ds.slots;
     a.counters = ds.counters;
     a.err = ds.err;
+    a.geglu = c.geglu ? 1 : 0;
+    a.gk_cubic = bf16_round_host(0.044715f);
+    a.gk_tanh = bf16_round_host(0.7978845608028654f);
     a.norm_w = c.norm_w;
     a.xn = c.norm_w != nullptr ? c.xn : nullptr;
     a.ldxn = c.ldxn;

@@ -56,6 +56,9 @@ void launch_lora_transpose(const float* b, int64_t N, int rank, float* bt, cudaS
 void launch_lora_apply(const Lora& l, const uint16_t* x, int64_t M, int64_t ldx, uint16_t* y, int64_t ldy,
                        cudaStream_t st);
 
+// round-to-nearest-even of a float to bf16, as a float (host side)
+float bf16_round_host(float f);
+
 // kernels (g4q_mlp.cu): the MLP's elementwise neighbours
 void launch_geglu(const uint16_t* gate, int64_t ldg, const uint16_t* up, int64_t ldu, uint16_t* out, int64_t ldo,
                   int64_t M, int64_t I, cudaStream_t st);
@@ -136,6 +139,9 @@ struct QmmCall {
     const uint16_t* norm_w = nullptr;
     uint16_t* xn = nullptr;
     int64_t ldxn = 0;
+    // fused GeGLU epilogue (stream-K GEMV only): the weight's 64-row quads pair 32 gate rows with the
+    // matching 32 up rows; y receives geglu(gate, up) = bf16 [M, N/2] with row stride ldy
+    bool geglu = false;
 };
 void launch_qmm_mlx(const QmmCall& c, cudaStream_t st);
 

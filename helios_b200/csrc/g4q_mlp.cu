@@ -19,6 +19,7 @@
 #include <cstdint>
 #include <cstring>
 
+#include "g4q_common.cuh"
 #include "g4q_internal.h"
 
 namespace g4q {
@@ -35,18 +36,6 @@ struct GegluConsts {
     float cubic, tanh_approx;   // bf16(0.044715), bf16(0.7978845608028654)
 };
 
-__device__ __forceinline__ float geglu1(float g, float u, const GegluConsts& c) {
-    const float g3 = rb(g * g * g);                 // power(gate, 3)
-    const float t1 = rb(c.cubic * g3);              // 0.044715 * gate^3
-    const float t2 = rb(g + t1);                    // gate + ...
-    const float t3 = rb(c.tanh_approx * t2);        // sqrt(2/pi) * (...)
-    const float t4 = rb(tanhf(t3));                 // tanh
-    const float t5 = rb(1.0f + t4);                 // 1 + tanh
-    const float t6 = rb(0.5f * g);                  // 0.5 * gate
-    const float t7 = rb(t6 * t5);                   // gelu
-    return t7 * u;                                  // gelu * up (rounded by the caller)
-}
-
 // out[m, i] for i in [0, I); 8 elements per thread, 16-byte loads and stores (I % 8 == 0).
 __global__ void __launch_bounds__(256) geglu_kernel(const uint16_t* __restrict__ gate, int64_t ldg,
                                                     const uint16_t* __restrict__ up, int64_t ldu,
@@ -62,9 +51,9 @@ __global__ void __launch_bounds__(256) geglu_kernel(const uint16_t* __restrict__
     uint32_t ow[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const float lo = geglu1(bf(gw[j] & 0xFFFFu), bf(uw[j] & 0xFFFFu), c);
-        const float hi = geglu1(bf(gw[j] >> 16), bf(uw[j] >> 16), c);
-        ow[j] = bits(lo) | (bits(hi) << 16);
+        const uint32_t lo = geglu_bf16(bf(gw[j] & 0xFFFFu), bf(uw[j] & 0xFFFFu), c.cubic, c.tanh_approx);
+        const uint32_t hi = geglu_bf16(bf(gw[j] >> 16), bf(uw[j] >> 16), c.cubic, c.tanh_approx);
+        ow[j] = lo | (hi << 16);
     }
     *reinterpret_cast<uint4*>(out + m * ldo + i) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
 }
@@ -116,6 +105,8 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const uint16_t* 
     }
 }
 
+}  // namespace
+
 float bf16_round_host(float f) {
     uint32_t u;
     memcpy(&u, &f, 4);
@@ -123,8 +114,6 @@ float bf16_round_host(float f) {
     memcpy(&f, &u, 4);
     return f;
 }
-
-}  // namespace
 
 void launch_geglu(const uint16_t* gate, int64_t ldg, const uint16_t* up, int64_t ldu, uint16_t* out, int64_t ldo,
                   int64_t M, int64_t I, cudaStream_t st) {

@@ -27,7 +27,8 @@ from ._lib import (CHAIN_R1, CHAIN_R2, PHASE_ALLREDUCE, PHASE_ARGMAX, QMM_OUT_F3
                    G4qInvalidArgument)
 
 __all__ = [
-    "QuantizedWeight", "quantized_matmul", "quantized_linear", "norm_quantized_matmul", "LoraAdapter", "geglu",
+    "QuantizedWeight", "quantized_matmul", "quantized_linear", "norm_quantized_matmul", "quantized_matmul_geglu",
+    "LoraAdapter", "geglu",
     "rms_norm", "dequantize", "lm_head_argmax", "DecodePlan", "synth_matrix", "synth_normal", "CHAIN_R1",
     "CHAIN_R2", "QMM_RMS_SCALE", "QMM_OUT_F32", "PHASE_ARGMAX", "PHASE_ALLREDUCE", "G4qError", "G4qInvalidArgument",
 ]
@@ -131,6 +132,20 @@ class QuantizedWeight:
             q.load(p[0], p[1], p[2], dst_row=dst, src_row=r0, n_rows=r1 - r0)
             dst += r1 - r0
         return q
+
+    @classmethod
+    def geglu_pair(cls, gate, up) -> "QuantizedWeight":
+        """A paired gate|up weight for :func:`quantized_matmul_geglu`: gate and up are MLX-layout
+        (w, scales, biases) triples of the same [I, K] shape (I % 32 == 0); the upload interleaves
+        them in 32-row slices, so each 64-row quad holds 32 gate rows and the same 32 up rows."""
+        parts = []
+        for a, b in zip(gate, up):
+            if a.shape != b.shape or a.shape[0] % 32 != 0:
+                raise ValueError("gate and up must have the same shape with rows a multiple of 32")
+            n = a.shape[0]
+            parts.append(torch.stack([a.reshape(n // 32, 32, -1), b.reshape(n // 32, 32, -1)], dim=1)
+                         .reshape(2 * n, -1))
+        return cls.from_mlx(*parts)
 
     def info(self) -> dict:
         info = _lib.G4qWeightInfo()
@@ -351,6 +366,26 @@ def norm_quantized_matmul(x: torch.Tensor, norm_weight: torch.Tensor, w: Quantiz
     _lib.call("g4q_qmm_norm", w.handle, _ptr(x2), M, x2.stride(0), _ptr(nw), float(eps), _ptr(xn2),
               0 if xn2 is None else xn2.stride(0), _ptr(y2), y2.stride(0), _stream())
     return y
+
+
+def quantized_matmul_geglu(x: torch.Tensor, w: QuantizedWeight, *, rms_scale: bool = False, eps: float = 1e-6,
+                           y: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``geglu(x @ gate.T, x @ up.T)`` for a paired gate|up weight (:meth:`QuantizedWeight.geglu_pair`):
+    the gate/up projections and the GeGLU of layer_forward (native_model.cc:934-945). At M <= 8 the
+    GeGLU runs in the decode GEMV's epilogue; larger M needs ``y`` (bf16 [..., rows]) for the paired
+    matmul output. Returns bf16 [..., rows / 2]."""
+    x2 = _rows2d(x, w.cols)
+    M = x2.shape[0]
+    I = w.rows // 2
+    shape = tuple(x.shape[:-1]) + (I,)
+    act = torch.empty(shape, dtype=torch.bfloat16, device=x.device) if out is None else out
+    if act.dtype != torch.bfloat16 or not act.is_contiguous() or act.shape[-1] != I:
+        raise ValueError("out must be a contiguous bf16 tensor with last dimension rows / 2")
+    if y is not None and (y.dtype != torch.bfloat16 or not y.is_contiguous() or y.numel() != M * w.rows):
+        raise ValueError("y must be a contiguous bf16 tensor of M x rows elements")
+    _lib.call("g4q_qmm_geglu", w.handle, _ptr(x2), M, x2.stride(0), QMM_RMS_SCALE if rms_scale else 0, eps,
+              _ptr(y), _ptr(act), I, _stream())
+    return act
 
 
 def dequantize(w, scales: Optional[torch.Tensor] = None, biases: Optional[torch.Tensor] = None,

@@ -142,6 +142,18 @@ G4qStatus g4q_qmm_ex(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t l
 G4qStatus g4q_qmm_norm(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t ldx, const uint16_t* weight,
                        float eps, uint16_t* xn, int64_t ldxn, uint16_t* y, int64_t ldy, void* stream);
 
+/* Replaces gate = quantized_linear(h, gate_proj), up = quantized_linear(h, up_proj),
+ * act = geglu(gate, up) of layer_forward (native_model.cc:934-945; decode twin :1318-1321):
+ * act = bf16 [M, rows/2] (row stride ld_act) of the GeGLU of the two bf16 matmul outputs. w is a
+ * PAIRED gate|up weight: rows [64j, 64j+32) hold gate rows [32j, 32j+32) and rows [64j+32, 64j+64)
+ * the same up rows (load each 32-row slice with g4q_weight_load; I = rows/2 must be a multiple of
+ * 32). flags: 0 or G4Q_QMM_RMS_SCALE. At M <= 8 the GeGLU runs in the stream-K GEMV's epilogue
+ * (one launch; gate and up never reach HBM) and y may be NULL. Otherwise y (bf16 [M, rows],
+ * contiguous) is required and receives the paired matmul output before the GeGLU pass. Bit-identical
+ * either way to g4q_qmm followed by g4q_geglu on the pairs. */
+G4qStatus g4q_qmm_geglu(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t ldx, uint32_t flags, float eps,
+                        uint16_t* y, uint16_t* act, int64_t ld_act, void* stream);
+
 /* ---- tied LM head with fused softcap + greedy argmax ----------------------------------------
  * Replaces target_logits_for_hidden (native_model.cc:1782-1795: quantized_matmul against
  * embed_tokens, bf16, tanh(l/30)*30 in bf16) and the greedy argmax of its callers (:3825,

@@ -160,3 +160,53 @@ def test_norm_matmul_outside_the_fused_widths(cuda, oracle, M):
     ye, _ = oracle.qmm(xn_ref, u32(w), u16(s), u16(b))
     assert_qmm_close(oracle.bf16_to_f32(u16(y)), ye, bf16_out=True)
     qw.free()
+
+
+def _pair_case(oracle, cuda, M, I=15360, K=3840, layer=9):
+    from helios_b200 import quantized as Q
+    gw = Q.synth_matrix(oracle.matrix_seed(layer, oracle.PROJ_IDS["gate"]), I, K, device=cuda)
+    uw = Q.synth_matrix(oracle.matrix_seed(layer, oracle.PROJ_IDS["up"]), I, K, device=cuda)
+    pair = Q.QuantizedWeight.geglu_pair(gw, uw)
+    x = Q.synth_normal(oracle.activation_seed(60 + M), (M, K), device=cuda)
+    return Q, gw, uw, pair, x
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8])
+@pytest.mark.parametrize("rms", [False, True])
+def test_geglu_fused_into_decode_gemv(cuda, oracle, M, rms):
+    """gate|up matmul + GeGLU as one stream-K GEMV launch: bit-identical to the paired matmul followed
+    by the GeGLU kernel, and within the matmul tolerance of the oracle's gate, up and geglu."""
+    Q, gw, uw, pair, x = _pair_case(oracle, cuda, M)
+    I = gw[0].shape[0]
+    act = Q.quantized_matmul_geglu(x, pair, rms_scale=rms)
+    y = Q.quantized_matmul(x, pair, rms_scale=rms)                   # [M, 2I], paired order
+    yp = y.view(M * I // 32, 64)
+    act2 = Q.geglu(yp[:, :32], yp[:, 32:]).view(M, I)
+    torch.cuda.synchronize()
+    assert (u16(act) == u16(act2)).all()
+    if not rms:
+        _, gate_ref = oracle.qmm(u16(x), u32(gw[0]), u16(gw[1]), u16(gw[2]))
+        _, up_ref = oracle.qmm(u16(x), u32(uw[0]), u16(uw[1]), u16(uw[2]))
+        ref = oracle.geglu(gate_ref, up_ref)
+        got = u16(act)
+        assert (got == ref).mean() > 0.99
+        gf, rf = oracle.bf16_to_f32(got).astype(np.float64), oracle.bf16_to_f32(ref).astype(np.float64)
+        assert np.abs(gf - rf).max() <= 1e-2 * float(np.sqrt(np.mean(rf ** 2))) + np.abs(rf).max() * 2.0 ** -8
+    pair.free()
+
+
+@pytest.mark.parametrize("M", [12, 40])
+def test_geglu_pair_outside_the_fused_widths(cuda, oracle, M):
+    from helios_b200 import _lib
+    Q, gw, uw, pair, x = _pair_case(oracle, cuda, M, I=2048, K=1024, layer=10)
+    I = 2048
+    with pytest.raises(_lib.G4qInvalidArgument):
+        Q.quantized_matmul_geglu(x, pair)
+    y = torch.empty((M, 2 * I), dtype=torch.bfloat16, device=cuda)
+    act = Q.quantized_matmul_geglu(x, pair, y=y)
+    yref = Q.quantized_matmul(x, pair)
+    yp = yref.view(M * I // 32, 64)
+    act2 = Q.geglu(yp[:, :32], yp[:, 32:]).view(M, I)
+    torch.cuda.synchronize()
+    assert (u16(y) == u16(yref)).all() and (u16(act) == u16(act2)).all()
+    pair.free()
