@@ -76,7 +76,7 @@ SIGNATURES = {
     "g4q_qmm": [_P, _P, _I64, _I64, _P, _I64, _P],
     "g4q_qmm_ex": [_P, _P, _I64, _I64, _P, _I64, _U32, _F, _P],
     "g4q_qmm_norm": [_P, _P, _I64, _I64, _P, _F, _P, _I64, _P, _I64, _P],
-    "g4q_qmm_geglu": [_P, _P, _I64, _I64, _U32, _F, _P, _P, _I64, _P],
+    "g4q_qmm_geglu": [_P, _P, _I64, _I64, _P, _U32, _F, _P, _P, _I64, _P],
     "g4q_lm_head_argmax": [_P, _P, _I64, _I64, _F, _U32, _F, _I64, _P, _I64, _P, _P, _P, _P],
     "g4q_lm_head_argmax_noalloc": [_P, _P, _I64, _I64, _P, _I64, _I64, _F, _U32, _F, _I64, _P, _I64, _P, _P, _P, _P],
     "g4q_lora_create": [_I64, _I64, _I32, _F, _P, _P, _I32, ctypes.POINTER(_P)],

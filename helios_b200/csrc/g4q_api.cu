@@ -482,8 +482,8 @@ G4qStatus g4q_qmm_norm(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t
     });
 }
 
-G4qStatus g4q_qmm_geglu(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t ldx, uint32_t flags, float eps,
-                        uint16_t* y, uint16_t* act, int64_t ld_act, void* stream) {
+G4qStatus g4q_qmm_geglu(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t ldx, const uint16_t* norm_weight,
+                        uint32_t flags, float eps, uint16_t* y, uint16_t* act, int64_t ld_act, void* stream) {
     return guarded("g4q_qmm_geglu", [&] {
         Weight* w = checked(h, "g4q_qmm_geglu");
         require(!w->mlx, G4Q_ERR_UNSUPPORTED_CONFIG, "the fused GeGLU takes a 4-bit group-64 weight");
@@ -501,10 +501,19 @@ G4qStatus g4q_qmm_geglu(const G4qWeight* h, const uint16_t* x, int64_t M, int64_
         cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
         QmmCall c{w, x, M, ldx, act, ld_act, flags, eps};
         c.geglu = true;
+        if (norm_weight != nullptr) {
+            require(flags == 0, G4Q_ERR_INVALID_ARGUMENT, "a norm weight and G4Q_QMM_RMS_SCALE exclude each other");
+            require(eps >= 0.0f && std::isfinite(eps), G4Q_ERR_INVALID_ARGUMENT, "eps must be finite and >= 0");
+            require(w->K % 8 == 0, G4Q_ERR_UNSUPPORTED_CONFIG, "cols must be a multiple of 8");
+            require_aligned16(norm_weight, "norm_weight");
+            c.norm_w = norm_weight;
+        }
         if (M <= 8 && gemv2_supported(c)) {
-            launch_gemv2(c, st);   // the GeGLU in the GEMV's epilogue
+            launch_gemv2(c, st);   // the GeGLU in the GEMV's epilogue (and the norm in its staging)
             return;
         }
+        require(norm_weight == nullptr, G4Q_ERR_INVALID_ARGUMENT,
+                "a norm weight is taken only where the fused GEMV runs (M <= 8); normalize with g4q_rms_norm first");
         require(y != nullptr, G4Q_ERR_INVALID_ARGUMENT,
                 "y is required unless M <= 8 on a shape the fused GEMV takes");
         require_aligned16(y, "y");

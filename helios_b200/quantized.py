@@ -368,12 +368,19 @@ def norm_quantized_matmul(x: torch.Tensor, norm_weight: torch.Tensor, w: Quantiz
     return y
 
 
-def quantized_matmul_geglu(x: torch.Tensor, w: QuantizedWeight, *, rms_scale: bool = False, eps: float = 1e-6,
-                           y: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+def quantized_matmul_geglu(x: torch.Tensor, w: QuantizedWeight, *, norm_weight: Optional[torch.Tensor] = None,
+                           rms_scale: bool = False, eps: float = 1e-6, y: Optional[torch.Tensor] = None,
+                           out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``geglu(x @ gate.T, x @ up.T)`` for a paired gate|up weight (:meth:`QuantizedWeight.geglu_pair`):
     the gate/up projections and the GeGLU of layer_forward (native_model.cc:934-945). At M <= 8 the
     GeGLU runs in the decode GEMV's epilogue; larger M needs ``y`` (bf16 [..., rows]) for the paired
-    matmul output. Returns bf16 [..., rows / 2]."""
+    matmul output. ``norm_weight`` (M <= 8 only) first applies the pre-feed-forward RMSNorm
+    (:929-932) in the same launch. Returns bf16 [..., rows / 2]."""
+    nw = None
+    if norm_weight is not None:
+        if norm_weight.shape != (w.cols,) or norm_weight.dtype != torch.bfloat16:
+            raise ValueError(f"norm_weight must be bf16 of shape ({w.cols},)")
+        nw = norm_weight.contiguous()
     x2 = _rows2d(x, w.cols)
     M = x2.shape[0]
     I = w.rows // 2
@@ -383,8 +390,8 @@ def quantized_matmul_geglu(x: torch.Tensor, w: QuantizedWeight, *, rms_scale: bo
         raise ValueError("out must be a contiguous bf16 tensor with last dimension rows / 2")
     if y is not None and (y.dtype != torch.bfloat16 or not y.is_contiguous() or y.numel() != M * w.rows):
         raise ValueError("y must be a contiguous bf16 tensor of M x rows elements")
-    _lib.call("g4q_qmm_geglu", w.handle, _ptr(x2), M, x2.stride(0), QMM_RMS_SCALE if rms_scale else 0, eps,
-              _ptr(y), _ptr(act), I, _stream())
+    _lib.call("g4q_qmm_geglu", w.handle, _ptr(x2), M, x2.stride(0), _ptr(nw), QMM_RMS_SCALE if rms_scale else 0,
+              eps, _ptr(y), _ptr(act), I, _stream())
     return act
 
 

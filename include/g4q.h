@@ -150,9 +150,12 @@ G4qStatus g4q_qmm_norm(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t
  * 32). flags: 0 or G4Q_QMM_RMS_SCALE. At M <= 8 the GeGLU runs in the stream-K GEMV's epilogue
  * (one launch; gate and up never reach HBM) and y may be NULL. Otherwise y (bf16 [M, rows],
  * contiguous) is required and receives the paired matmul output before the GeGLU pass. Bit-identical
- * either way to g4q_qmm followed by g4q_geglu on the pairs. */
-G4qStatus g4q_qmm_geglu(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t ldx, uint32_t flags, float eps,
-                        uint16_t* y, uint16_t* act, int64_t ld_act, void* stream);
+ * either way to g4q_qmm followed by g4q_geglu on the pairs. norm_weight (bf16 [cols], or NULL):
+ * x is first normalized as by g4q_qmm_norm (pre_feedforward_layernorm, :929-932), so the norm,
+ * both projections and the GeGLU are one launch; only on the fused path (M <= 8, flags 0): other
+ * calls with a norm weight are rejected, normalize with g4q_rms_norm first there. */
+G4qStatus g4q_qmm_geglu(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t ldx, const uint16_t* norm_weight,
+                        uint32_t flags, float eps, uint16_t* y, uint16_t* act, int64_t ld_act, void* stream);
 
 /* ---- tied LM head with fused softcap + greedy argmax ----------------------------------------
  * Replaces target_logits_for_hidden (native_model.cc:1782-1795: quantized_matmul against

@@ -210,3 +210,23 @@ def test_geglu_pair_outside_the_fused_widths(cuda, oracle, M):
     torch.cuda.synchronize()
     assert (u16(y) == u16(yref)).all() and (u16(act) == u16(act2)).all()
     pair.free()
+
+
+@pytest.mark.parametrize("M", [1, 4, 8])
+def test_norm_gate_up_geglu_in_one_launch(cuda, oracle, M):
+    """pre_feedforward_layernorm -> gate|up -> geglu (native_model.cc:929-945) as one GEMV launch:
+    bit-identical to norm_quantized_matmul (the same fused norm) followed by the GeGLU kernel."""
+    from helios_b200 import _lib
+    Q, gw, uw, pair, x = _pair_case(oracle, cuda, M, layer=11)
+    I, K = gw[0].shape[0], x.shape[1]
+    g = torch.Generator().manual_seed(70 + M)
+    nw = (1.0 + 0.2 * torch.randn(K, generator=g)).to(torch.bfloat16).to(cuda)
+    act = Q.quantized_matmul_geglu(x, pair, norm_weight=nw)
+    y = Q.norm_quantized_matmul(x, nw, pair)
+    yp = y.view(M * I // 32, 64)
+    act2 = Q.geglu(yp[:, :32], yp[:, 32:]).view(M, I)
+    torch.cuda.synchronize()
+    assert (u16(act) == u16(act2)).all()
+    with pytest.raises(_lib.G4qInvalidArgument):
+        Q.quantized_matmul_geglu(x, pair, norm_weight=nw, rms_scale=True)
+    pair.free()

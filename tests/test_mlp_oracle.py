@@ -63,3 +63,16 @@ def test_mlp_entry_points_reject_bad_arguments_without_gpu():
     assert L.g4q_rms_norm(p, 8, None, 1, 8, float("nan"), p, 8, None) == _lib.G4Q_ERR_INVALID_ARGUMENT
     assert "eps" in _lib.last_error()
     assert L.g4q_rms_norm(None, 8, None, 1, 8, 1e-6, p, 8, None) == _lib.G4Q_ERR_INVALID_ARGUMENT
+
+
+def test_fused_matmul_entry_points_reject_bad_arguments_without_gpu():
+    from helios_b200 import _lib
+    L = _lib.load()
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    assert L.g4q_qmm_norm(None, p, 1, 8, p, 1e-6, None, 0, p, 8, None) == _lib.G4Q_ERR_INVALID_ARGUMENT
+    assert "weight handle" in _lib.last_error()
+    assert L.g4q_qmm_geglu(None, p, 1, 8, None, 0, 1e-6, None, p, 8, None) == _lib.G4Q_ERR_INVALID_ARGUMENT
+    assert "weight handle" in _lib.last_error()
+    assert L.g4q_qmm_geglu(p, p, 1, 8, None, 0, 1e-6, None, p, 8, None) == _lib.G4Q_ERR_INVALID_ARGUMENT
+    assert "invalid weight handle" in _lib.last_error()
