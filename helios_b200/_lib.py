@@ -84,6 +84,7 @@ SIGNATURES = {
     "g4q_lora_free": [_P],
     "g4q_geglu": [_P, _I64, _P, _I64, _I64, _I64, _P, _I64, _P],
     "g4q_rms_norm": [_P, _I64, _P, _I64, _I64, _F, _P, _I64, _P],
+    "g4q_rms_norm_residual": [_P, _I64, _P, _I64, _I64, _F, _P, _I64, _P, _P, _I64, _P],
     "g4q_device_error": [ctypes.POINTER(_I32), _I32],
     "g4q_decode_plan_create": [ctypes.POINTER(G4qDecodePhase), _I32, _I32, ctypes.POINTER(_P)],
     "g4q_decode_plan_run": [_P, _I64, _F, _F, _I64, _P, _P, _P, _P, _I64, _P],

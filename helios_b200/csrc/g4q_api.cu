@@ -799,6 +799,27 @@ G4qStatus g4q_rms_norm(const uint16_t* x, int64_t ldx, const uint16_t* weight, i
     });
 }
 
+G4qStatus g4q_rms_norm_residual(const uint16_t* x, int64_t ldx, const uint16_t* weight, int64_t M, int64_t K,
+                                float eps, const uint16_t* residual, int64_t ld_res, const uint16_t* layer_scalar,
+                                uint16_t* out, int64_t ld_out, void* stream) {
+    return guarded("g4q_rms_norm_residual", [&] {
+        require(M >= 0 && K > 0 && K % 8 == 0, G4Q_ERR_INVALID_ARGUMENT, "M >= 0 and K a positive multiple of 8 are required");
+        require(M <= 0x7FFFFFFF, G4Q_ERR_INVALID_ARGUMENT, "M must be < 2^31");
+        if (M == 0) return;
+        require(x != nullptr && residual != nullptr && out != nullptr, G4Q_ERR_INVALID_ARGUMENT,
+                "x, residual and out must be non-null");
+        require(ldx >= K && ld_res >= K && ld_out >= K && ldx % 8 == 0 && ld_res % 8 == 0 && ld_out % 8 == 0,
+                G4Q_ERR_INVALID_ARGUMENT, "row strides must be >= K and multiples of 8");
+        require(eps >= 0.0f && std::isfinite(eps), G4Q_ERR_INVALID_ARGUMENT, "eps must be finite and >= 0");
+        require_aligned16(x, "x");
+        require_aligned16(residual, "residual");
+        require_aligned16(out, "out");
+        if (weight != nullptr) require_aligned16(weight, "weight");
+        launch_rms_norm(x, ldx, weight, M, K, eps, out, ld_out, reinterpret_cast<cudaStream_t>(stream), residual, ld_res,
+                        layer_scalar);
+    });
+}
+
 G4qStatus g4q_device_error(int32_t* code, int32_t reset) {
     return guarded("g4q_device_error", [&] {
         require(code != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null code pointer");

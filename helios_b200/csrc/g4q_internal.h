@@ -63,7 +63,8 @@ float bf16_round_host(float f);
 void launch_geglu(const uint16_t* gate, int64_t ldg, const uint16_t* up, int64_t ldu, uint16_t* out, int64_t ldo,
                   int64_t M, int64_t I, cudaStream_t st);
 void launch_rms_norm(const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t M, int64_t K, float eps,
-                     uint16_t* out, int64_t ldo, cudaStream_t st);
+                     uint16_t* out, int64_t ldo, cudaStream_t st, const uint16_t* res = nullptr, int64_t ldr = 0,
+                     const uint16_t* scale = nullptr);
 
 // tensor-parallel allreduce over NVLink peer memory (g4q_comm.cu)
 void* comm_create(int rank, int n_ranks, int64_t max_elems);

@@ -60,9 +60,14 @@ __global__ void __launch_bounds__(256) geglu_kernel(const uint16_t* __restrict__
 
 constexpr int kNormThreads = 256;
 
-__global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const uint16_t* __restrict__ x, int64_t ldx,
+// res / scale (optional): the tail of a layer's sub-block, out = bf16(bf16(res + norm) * scale)
+// (native_model.cc:954-968: post_feedforward_layernorm, the residual add, layer_scalar; :920-926:
+// post_attention_layernorm and its residual add, no scale). scale is a bf16 scalar in device memory.
+__global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const uint16_t* x, int64_t ldx,
                                                                 const uint16_t* __restrict__ w, int64_t K, float eps,
-                                                                uint16_t* __restrict__ out, int64_t ldo) {
+                                                                uint16_t* out, int64_t ldo,
+                                                                const uint16_t* res, int64_t ldr,
+                                                                const uint16_t* __restrict__ scale) {
     __shared__ float part[kNormThreads / 32];
     __shared__ float inv_s;
     const uint16_t* xr = x + (int64_t)blockIdx.x * ldx;
@@ -89,16 +94,28 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const uint16_t* 
     }
     __syncthreads();
     const float inv = inv_s;
+    const uint16_t* rrow = res != nullptr ? res + (int64_t)blockIdx.x * ldr : nullptr;
+    const float sc = scale != nullptr ? bf(*scale) : 1.0f;
     for (int64_t k = (int64_t)threadIdx.x * 8; k < K; k += kNormThreads * 8) {
         const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
         uint4 wv = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);   // bf16 1.0 pairs
         if (w != nullptr) wv = *reinterpret_cast<const uint4*>(w + k);
-        const uint32_t vw[4] = {v.x, v.y, v.z, v.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint4 rv = make_uint4(0u, 0u, 0u, 0u);
+        if (rrow != nullptr) rv = *reinterpret_cast<const uint4*>(rrow + k);
+        const uint32_t vw[4] = {v.x, v.y, v.z, v.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w}, rw[4] = {rv.x, rv.y, rv.z, rv.w};
         uint32_t ow[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const float lo = bf(ww[j] & 0xFFFFu) * rb(bf(vw[j] & 0xFFFFu) * inv);
-            const float hi = bf(ww[j] >> 16) * rb(bf(vw[j] >> 16) * inv);
+            float lo = rb(bf(ww[j] & 0xFFFFu) * rb(bf(vw[j] & 0xFFFFu) * inv));
+            float hi = rb(bf(ww[j] >> 16) * rb(bf(vw[j] >> 16) * inv));
+            if (rrow != nullptr) {   // the residual add, then the layer scalar, each rounded to bf16
+                lo = rb(bf(rw[j] & 0xFFFFu) + lo);
+                hi = rb(bf(rw[j] >> 16) + hi);
+                if (scale != nullptr) {
+                    lo = lo * sc;
+                    hi = hi * sc;
+                }
+            }
             ow[j] = bits(lo) | (bits(hi) << 16);
         }
         *reinterpret_cast<uint4*>(orow + k) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
@@ -127,9 +144,10 @@ void launch_geglu(const uint16_t* gate, int64_t ldg, const uint16_t* up, int64_t
 }
 
 void launch_rms_norm(const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t M, int64_t K, float eps,
-                     uint16_t* out, int64_t ldo, cudaStream_t st) {
+                     uint16_t* out, int64_t ldo, cudaStream_t st, const uint16_t* res, int64_t ldr,
+                     const uint16_t* scale) {
     if (M == 0) return;
-    rms_norm_kernel<<<(unsigned)M, kNormThreads, 0, st>>>(x, ldx, w, K, eps, out, ldo);
+    rms_norm_kernel<<<(unsigned)M, kNormThreads, 0, st>>>(x, ldx, w, K, eps, out, ldo, res, ldr, scale);
     check_cuda(cudaGetLastError(), "rms_norm_kernel launch");
 }
 

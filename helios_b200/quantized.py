@@ -28,9 +28,9 @@ from ._lib import (CHAIN_R1, CHAIN_R2, PHASE_ALLREDUCE, PHASE_ARGMAX, QMM_OUT_F3
 
 __all__ = [
     "QuantizedWeight", "quantized_matmul", "quantized_linear", "norm_quantized_matmul", "quantized_matmul_geglu",
-    "LoraAdapter", "geglu",
-    "rms_norm", "dequantize", "lm_head_argmax", "DecodePlan", "synth_matrix", "synth_normal", "CHAIN_R1",
-    "CHAIN_R2", "QMM_RMS_SCALE", "QMM_OUT_F32", "PHASE_ARGMAX", "PHASE_ALLREDUCE", "G4qError", "G4qInvalidArgument",
+    "LoraAdapter", "geglu", "rms_norm", "rms_norm_residual", "dequantize", "lm_head_argmax", "DecodePlan",
+    "synth_matrix", "synth_normal", "CHAIN_R1", "CHAIN_R2", "QMM_RMS_SCALE", "QMM_OUT_F32", "PHASE_ARGMAX",
+    "PHASE_ALLREDUCE", "G4qError", "G4qInvalidArgument",
 ]
 
 
@@ -339,6 +339,36 @@ def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor] = None, eps: float 
         raise ValueError("out must be a contiguous tensor shaped like x")
     _lib.call("g4q_rms_norm", _ptr(x2), x2.stride(0), _ptr(w), x2.shape[0], K, float(eps), _ptr(o2), o2.stride(0),
               _stream())
+    return res
+
+
+def rms_norm_residual(x: torch.Tensor, weight: Optional[torch.Tensor], residual: torch.Tensor,
+                      layer_scalar: Optional[torch.Tensor] = None, eps: float = 1e-6, *,
+                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The tail of a layer's sub-block (native_model.cc:954-968 / :920-926) in one kernel:
+    ``bf16(bf16(residual + rms_norm(x, weight, eps)) * layer_scalar)`` (no scalar when None)."""
+    K = x.shape[-1]
+    if K % 8 != 0:
+        raise ValueError("the last dimension must be a multiple of 8")
+    if residual.shape != x.shape:
+        raise ValueError("residual must be shaped like x")
+    x2, r2 = _bf16_rows(x, "x"), _bf16_rows(residual, "residual")
+    w = None
+    if weight is not None:
+        if weight.shape != (K,):
+            raise ValueError(f"weight must have shape ({K},)")
+        w = _bf16_rows(weight.view(1, K), "weight")
+    sc = None
+    if layer_scalar is not None:
+        if layer_scalar.numel() != 1 or layer_scalar.dtype != torch.bfloat16 or not layer_scalar.is_cuda:
+            raise ValueError("layer_scalar must be one bf16 value on the GPU")
+        sc = layer_scalar.reshape(1)
+    res = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device) if out is None else out
+    o2 = _bf16_rows(res, "out")
+    if o2.data_ptr() != res.data_ptr() or o2.shape != x2.shape:
+        raise ValueError("out must be a contiguous tensor shaped like x")
+    _lib.call("g4q_rms_norm_residual", _ptr(x2), x2.stride(0), _ptr(w), x2.shape[0], K, float(eps), _ptr(r2),
+              r2.stride(0), _ptr(sc), _ptr(o2), o2.stride(0), _stream())
     return res
 
 

@@ -227,6 +227,16 @@ G4qStatus g4q_geglu(const uint16_t* gate, int64_t ld_gate, const uint16_t* up, i
 G4qStatus g4q_rms_norm(const uint16_t* x, int64_t ldx, const uint16_t* weight, int64_t M, int64_t K, float eps,
                        uint16_t* out, int64_t ld_out, void* stream);
 
+/* The tail of each sub-block of layer_forward in one pass: out = bf16(bf16(residual + norm) * scale)
+ * with norm = model_dtype(fast::rms_norm(x, weight, eps)) as g4q_rms_norm computes it
+ * (native_model.cc:954-968: post_feedforward_layernorm, the MLP residual add, layer_scalar; :920-926:
+ * post_attention_layernorm and the attention residual add, layer_scalar NULL). layer_scalar: one bf16
+ * value in device memory (the checkpoint's `.layer_scalar`), or NULL. residual / out: bf16 [M, ld],
+ * 16-byte aligned rows; out may equal x or residual. */
+G4qStatus g4q_rms_norm_residual(const uint16_t* x, int64_t ldx, const uint16_t* weight, int64_t M, int64_t K,
+                                float eps, const uint16_t* residual, int64_t ld_res, const uint16_t* layer_scalar,
+                                uint16_t* out, int64_t ld_out, void* stream);
+
 /* ---- decode plan: every quantized matmul of one decode step in one persistent kernel ----------
  * Replaces the per-token chain of quantized_linear calls of the decode drivers
  * (native_model.cc:1843-1911 decode_last_logits -> 48 x target_layer_decode_forward :1284-1328 ->

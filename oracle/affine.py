@@ -277,6 +277,16 @@ def rms_norm(x, weight=None, eps: float = 1e-6):
     return f32_to_bf16(bf16_to_f32(weight) * y)
 
 
+def rms_norm_residual(x, weight, residual, layer_scalar=None, eps: float = 1e-6):
+    """native_model.cc:954-968 on bf16 bits: n = rms_norm(x, weight); h = bf16(residual + n); then
+    bf16(h * layer_scalar) when a scalar (bf16 bits) is given -- each op one bf16 rounding."""
+    n = bf16_to_f32(rms_norm(x, weight, eps))
+    h = _rb(bf16_to_f32(residual) + n)
+    if layer_scalar is None:
+        return f32_to_bf16(h)
+    return f32_to_bf16(h * np.float32(bf16_to_f32(np.asarray([layer_scalar], np.uint16))[0]))
+
+
 def rms_scale(x_row, eps: float = 1e-6) -> float:
     x_row = np.ascontiguousarray(x_row, dtype=np.uint16)
     return float(lib().g4o_rms_scale(_p(x_row), x_row.size, eps))

@@ -230,3 +230,23 @@ def test_norm_gate_up_geglu_in_one_launch(cuda, oracle, M):
     with pytest.raises(_lib.G4qInvalidArgument):
         Q.quantized_matmul_geglu(x, pair, norm_weight=nw, rms_scale=True)
     pair.free()
+
+
+@pytest.mark.parametrize("with_scalar", [True, False])
+def test_rms_norm_residual_layer_scalar(cuda, oracle, with_scalar):
+    """post_feedforward_layernorm -> residual add -> layer_scalar (native_model.cc:954-968) in one
+    kernel, in place on the residual stream, against the oracle's three rounded steps."""
+    from helios_b200 import quantized as Q
+    M, K = 5, 3840
+    g = torch.Generator().manual_seed(80)
+    x = (3.0 * torch.randn(M, K, generator=g)).to(torch.bfloat16).to(cuda)
+    w = (1.0 + 0.2 * torch.randn(K, generator=g)).to(torch.bfloat16).to(cuda)
+    res = (4.0 * torch.randn(M, K, generator=g)).to(torch.bfloat16).to(cuda)
+    sc = torch.tensor([0.71875], dtype=torch.bfloat16, device=cuda) if with_scalar else None
+    r0 = u16(res).copy()
+    Q.rms_norm_residual(x, w, res, sc, 1e-6, out=res)
+    torch.cuda.synchronize()
+    ref = oracle.rms_norm_residual(u16(x), u16(w), r0, None if sc is None else int(u16(sc)[0]), 1e-6)
+    got = u16(res)
+    assert (got == ref).mean() >= 0.99, (got == ref).mean()
+    assert ulps_apart(oracle, got, ref).max() <= 1.0

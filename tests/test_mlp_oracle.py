@@ -76,3 +76,15 @@ def test_fused_matmul_entry_points_reject_bad_arguments_without_gpu():
     assert "weight handle" in _lib.last_error()
     assert L.g4q_qmm_geglu(p, p, 1, 8, None, 0, 1e-6, None, p, 8, None) == _lib.G4Q_ERR_INVALID_ARGUMENT
     assert "invalid weight handle" in _lib.last_error()
+
+
+def test_rms_norm_residual_known_answer(oracle):
+    # the norm of [2]*8 with weight 2 and eps 0 is 2; residual 256 + 2 = 258 (exact in bf16);
+    # x 1.5 = 387 lies halfway between the bf16 neighbours 386 and 388: ties to even -> 388
+    x = b16(oracle, [[2] * 8])
+    w = b16(oracle, [2] * 8)
+    r = b16(oracle, [[256] * 8])
+    out = oracle.rms_norm_residual(x, w, r, int(b16(oracle, [1.5])[0]), eps=0.0)
+    assert oracle.bf16_to_f32(out)[0].tolist() == [388.0] * 8
+    # without a scalar: 256 + 2 = 258 (exact in bf16)
+    assert oracle.bf16_to_f32(oracle.rms_norm_residual(x, w, r, None, eps=0.0))[0].tolist() == [258.0] * 8
