@@ -71,6 +71,8 @@ SIGNATURES = {
     "g4q_weight_free": [_P],
     "g4q_weight_info": [_P, ctypes.POINTER(G4qWeightInfo)],
     "g4q_weight_export": [_P, _P, _P, _P, _P],
+    "g4q_weight_save": [_P, ctypes.c_char_p],
+    "g4q_weight_open": [ctypes.c_char_p, ctypes.POINTER(_P)],
     "g4q_dequantize": [_P, _P, _I64, _P, _I32, _P],
     "g4q_dequantize_mlx": [_P, _P, _P, _I64, _I64, _I32, _I32, _I32, _P, _P],
     "g4q_qmm": [_P, _P, _I64, _I64, _P, _I64, _P],

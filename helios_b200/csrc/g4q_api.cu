@@ -263,6 +263,99 @@ G4qStatus g4q_weight_free(G4qWeight* h) {
     });
 }
 
+// Repacked-weight cache file: header, then packed words, then scale|bias words.
+struct CacheHeader {
+    char magic[8];            // "G4QWCACH"
+    uint32_t version;         // 1
+    uint32_t layout;          // 1: kernel layout v1
+    int64_t rows, cols;
+    int32_t bits, group_size;
+    uint64_t packed_bytes, sb_bytes;
+    uint64_t checksum;        // FNV-1a 64 over the payload
+};
+static_assert(sizeof(CacheHeader) == 64, "cache header is 64 bytes");
+static const char kCacheMagic[8] = {'G', '4', 'Q', 'W', 'C', 'A', 'C', 'H'};
+
+static uint64_t fnv1a(const unsigned char* p, size_t n, uint64_t h = 0xcbf29ce484222325ull) {
+    for (size_t i = 0; i < n; ++i) h = (h ^ p[i]) * 0x100000001b3ull;
+    return h;
+}
+
+G4qStatus g4q_weight_save(const G4qWeight* h, const char* path) {
+    return guarded("g4q_weight_save", [&] {
+        Weight* w = checked(h, "g4q_weight_save");
+        require(path != nullptr, G4Q_ERR_INVALID_ARGUMENT, "path must be non-null");
+        require(!w->mlx, G4Q_ERR_UNSUPPORTED_CONFIG, "the cache holds 4-bit group-64 handles only");
+        CacheHeader hd{};
+        std::memcpy(hd.magic, kCacheMagic, 8);
+        hd.version = 1;
+        hd.layout = 1;
+        hd.rows = w->N;
+        hd.cols = w->K;
+        hd.bits = 4;
+        hd.group_size = 64;
+        hd.packed_bytes = (uint64_t)w->N * w->K / 2;
+        hd.sb_bytes = (uint64_t)w->N * (w->K / 64) * 4;
+        std::string buf(hd.packed_bytes + hd.sb_bytes, '\0');
+        check_cuda(cudaMemcpy(&buf[0], w->packed, hd.packed_bytes, cudaMemcpyDeviceToHost), "read packed words");
+        check_cuda(cudaMemcpy(&buf[hd.packed_bytes], w->sb, hd.sb_bytes, cudaMemcpyDeviceToHost), "read scale words");
+        hd.checksum = fnv1a(reinterpret_cast<const unsigned char*>(buf.data()), buf.size());
+        FILE* f = std::fopen(path, "wb");
+        require(f != nullptr, G4Q_ERR_RUNTIME, std::string("cannot open ") + path + " for writing");
+        const bool okw = std::fwrite(&hd, sizeof(hd), 1, f) == 1 && std::fwrite(buf.data(), 1, buf.size(), f) == buf.size();
+        const bool okc = std::fclose(f) == 0;
+        require(okw && okc, G4Q_ERR_RUNTIME, std::string("writing ") + path + " failed");
+    });
+}
+
+G4qStatus g4q_weight_open(const char* path, G4qWeight** out) {
+    return guarded("g4q_weight_open", [&] {
+        require(out != nullptr && path != nullptr, G4Q_ERR_INVALID_ARGUMENT, "path and out must be non-null");
+        *out = nullptr;
+        FILE* f = std::fopen(path, "rb");
+        require(f != nullptr, G4Q_ERR_MODEL_LOAD, std::string("cannot open ") + path);
+        CacheHeader hd{};
+        const bool got = std::fread(&hd, sizeof(hd), 1, f) == 1;
+        std::string buf;
+        bool ok_hdr = got && std::memcmp(hd.magic, kCacheMagic, 8) == 0 && hd.version == 1 && hd.layout == 1 &&
+                      hd.bits == 4 && hd.group_size == 64 && hd.rows > 0 && hd.cols > 0 && hd.rows % 16 == 0 &&
+                      hd.cols % 64 == 0 && hd.rows <= (int64_t)1 << 31 && hd.cols <= (int64_t)1 << 31 &&
+                      hd.packed_bytes == (uint64_t)hd.rows * hd.cols / 2 &&
+                      hd.sb_bytes == (uint64_t)hd.rows * (hd.cols / 64) * 4;
+        bool ok_payload = false;
+        if (ok_hdr) {
+            buf.resize(hd.packed_bytes + hd.sb_bytes);
+            ok_payload = std::fread(&buf[0], 1, buf.size(), f) == buf.size() && std::fgetc(f) == EOF &&
+                         fnv1a(reinterpret_cast<const unsigned char*>(buf.data()), buf.size()) == hd.checksum;
+        }
+        std::fclose(f);
+        require(ok_hdr, G4Q_ERR_MODEL_LOAD, std::string(path) + " is not a version-1 g4q weight cache file");
+        require(ok_payload, G4Q_ERR_MODEL_LOAD, std::string(path) + ": payload size or checksum mismatch");
+        G4qWeight* hw = nullptr;
+        const G4qStatus st = g4q_weight_create(hd.rows, hd.cols, 4, 64, &hw);
+        if (st != G4Q_OK) throw Error(st, "creating the handle failed");
+        Weight* w = reinterpret_cast<Weight*>(hw);
+        cudaError_t e = cudaMemcpy(w->packed, buf.data(), hd.packed_bytes, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(w->sb, buf.data() + hd.packed_bytes, hd.sb_bytes, cudaMemcpyHostToDevice);
+        int flags = 0;
+        if (e == cudaSuccess) {
+            try {
+                launch_sb_flags(*w, nullptr);
+            } catch (...) {
+                e = cudaErrorLaunchFailure;
+            }
+        }
+        if (e == cudaSuccess) e = cudaMemcpy(&flags, w->d_flags, sizeof(int), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) {
+            g4q_weight_free(hw);
+            check_cuda(e, "uploading the cached buffers");
+        }
+        w->fast_ok = (flags & 1) == 0;
+        w->small_scales = (flags & 4) == 0;
+        *out = hw;
+    });
+}
+
 G4qStatus g4q_weight_info(const G4qWeight* h, G4qWeightInfo* out) {
     return guarded("g4q_weight_info", [&] {
         Weight* w = checked(h, "g4q_weight_info");

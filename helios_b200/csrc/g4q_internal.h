@@ -118,6 +118,7 @@ void launch_repack(const uint32_t* src_w, const uint16_t* src_s, const uint16_t*
                    int64_t src_ld_groups, int64_t src_row0, int64_t src_k0, int64_t n_rows, Weight& w,
                    int64_t dst_row0, cudaStream_t st);
 void launch_export(const Weight& w, uint32_t* dst_w, uint16_t* dst_s, uint16_t* dst_b, cudaStream_t st);
+void launch_sb_flags(const Weight& w, cudaStream_t st);
 // kernels (g4q_generic.cu): weights kept in MLX's layout (specs other than 4-bit / group 64)
 void launch_dequantize_mlx_rows(const Weight& w, const int32_t* ids, int64_t n_ids, uint16_t* out, int chain,
                                 cudaStream_t st);

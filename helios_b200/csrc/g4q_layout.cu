@@ -104,6 +104,16 @@ __global__ void repack_sb_kernel(const uint16_t* __restrict__ s, const uint16_t*
     }
 }
 
+// The scale flags of repack_sb_kernel, recomputed over a whole sb array (weights opened from a
+// cache file skip the repack).
+__global__ void sb_flags_kernel(const uint32_t* __restrict__ sb, int64_t count, int* flags) {
+    for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < count;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const uint32_t e = (sb[idx] >> 7) & 0xFFu;
+        if (e >= 126u) atomicOr(flags, e >= 247u ? 5 : 4);
+    }
+}
+
 __global__ void export_words_kernel(const uint32_t* __restrict__ packed, int64_t N, int64_t K,
                                     uint32_t* __restrict__ dst) {
     const int64_t R = N / 16, words = N * (K / 8);
@@ -281,6 +291,12 @@ void launch_repack(const uint32_t* src_w, const uint16_t* src_s, const uint16_t*
     repack_sb_kernel<<<grid_for(G * n_rows), 256, 0, st>>>(src_s, src_b, src_ld_groups, src_row0, src_k0 / 64, n_rows,
                                                            G, w.N, dst_row0, w.sb, w.d_flags);
     check_cuda(cudaGetLastError(), "repack launch");
+}
+
+void launch_sb_flags(const Weight& w, cudaStream_t st) {
+    const int64_t count = (w.K / 64) * w.N;
+    sb_flags_kernel<<<grid_for(count), 256, 0, st>>>(w.sb, count, w.d_flags);
+    check_cuda(cudaGetLastError(), "sb flags launch");
 }
 
 void launch_export(const Weight& w, uint32_t* dst_w, uint16_t* dst_s, uint16_t* dst_b, cudaStream_t st) {

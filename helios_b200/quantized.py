@@ -147,6 +147,22 @@ class QuantizedWeight:
                          .reshape(2 * n, -1))
         return cls.from_mlx(*parts)
 
+    def save(self, path) -> None:
+        """Write the repacked buffers to a versioned cache file (g4q_weight_save)."""
+        _lib.call("g4q_weight_save", self.handle, str(path).encode())
+
+    @classmethod
+    def open(cls, path) -> "QuantizedWeight":
+        """A handle on the current GPU from a cache file written by :meth:`save`, without a repack."""
+        q = cls.__new__(cls)
+        q._h = ctypes.c_void_p()
+        _lib.call("g4q_weight_open", str(path).encode(), ctypes.byref(q._h))
+        info = _lib.G4qWeightInfo()
+        _lib.call("g4q_weight_info", q._h, ctypes.byref(info))
+        q.rows, q.cols, q.bits, q.group_size = info.rows, info.cols, info.bits, info.group_size
+        q.device = torch.cuda.current_device()
+        return q
+
     def info(self) -> dict:
         info = _lib.G4qWeightInfo()
         _lib.call("g4q_weight_info", self.handle, ctypes.byref(info))

@@ -102,6 +102,18 @@ G4qStatus g4q_weight_info(const G4qWeight* w, G4qWeightInfo* out);
 G4qStatus g4q_weight_export(const G4qWeight* w, uint32_t* packed, uint16_t* scales, uint16_t* biases,
                             void* stream);
 
+/* ---- repacked-weight cache ------------------------------------------------------------------
+ * A versioned file of a handle's kernel-layout buffers, so a later load skips the repack (the
+ * reference re-reads and re-evaluates the MLX safetensors at every NativeTextModel::load,
+ * native_model.cc:3506-3590). File: a 64-byte header (magic "G4QWCACH", format version 1, kernel
+ * layout 1, rows, cols, bits 4, group 64, the two payload sizes, an FNV-1a 64-bit checksum of the
+ * payload), then the packed words and the scale|bias words, little-endian. 4-bit group-64 handles
+ * only (G4Q_ERR_UNSUPPORTED_CONFIG otherwise). g4q_weight_open checks the header, the file size
+ * and the checksum on the host before it touches the GPU (G4Q_ERR_MODEL_LOAD on any mismatch),
+ * then creates a handle on the current device and uploads the buffers as they are. */
+G4qStatus g4q_weight_save(const G4qWeight* w, const char* path);
+G4qStatus g4q_weight_open(const char* path, G4qWeight** out);
+
 /* ---- dequantize --------------------------------------------------------------------------
  * Replaces mlx::core::dequantize(..., "affine") -> bf16: the embedding gather of
  * quantized_embedding (native_model.cc:364-376: take rows, then dequantize) when row_ids is
