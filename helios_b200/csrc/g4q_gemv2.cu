@@ -237,13 +237,20 @@ __device__ __forceinline__ void park_quad(const Gemv2Args& a, int* qcnt, float* 
         }
     }
     if (!whole) {
-        __threadfence();
+        // arrival: the warp barrier orders the lanes' slot stores before lane 0's gpu-scope release
+        // on the counter, and the last arriver's acquire makes every CTA's slots visible to its lanes
+        // (one acq_rel atomic instead of a fence on each side of a relaxed one: measured 14.9 -> 14.1 us
+        // for up_proj at M = 1, together with the plain-store reset below)
         __syncwarp();
         int lastc = 0;
-        if (lane == 0) lastc = atomicAdd(a.counters + q, 1) == nc - 1;
+        if (lane == 0) {
+            unsigned int old;
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + q) : "memory");
+            lastc = old == (unsigned)(nc - 1);
+        }
         lastc = __shfl_sync(0xffffffffu, lastc, 0);
+        __syncwarp();
         if (lastc) {
-            __threadfence();
             if (a.geglu) {
                 for (int o2 = lane; o2 < 32 * M; o2 += 32) {
                     const int tok = o2 >> 5, r = o2 & 31;
@@ -263,7 +270,9 @@ __device__ __forceinline__ void park_quad(const Gemv2Args& a, int* qcnt, float* 
                 }
             }
             __syncwarp();
-            if (lane == 0) atomicExch(a.counters + q, 0);
+            // nothing else touches this counter in this launch and the next launch reads it only after
+            // this grid completes, so a plain store resets it (no round trip on the kernel's tail)
+            if (lane == 0) asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a.counters + q), "r"(0u) : "memory");
         }
     }
     __syncwarp();
