@@ -61,6 +61,10 @@ DTYPE_BF16 = 0
 DTYPE_F32 = 1
 PHASE_ARGMAX = 0x4
 PHASE_ALLREDUCE = 0x8
+PATH_GEMV_STREAMK = 1
+PATH_GEMV_CLUSTER = 2
+PATH_GEMM = 3
+PATH_GENERIC = 4
 IPC_HANDLE_BYTES = 64
 
 SIGNATURES = {
@@ -77,6 +81,7 @@ SIGNATURES = {
     "g4q_dequantize_mlx": [_P, _P, _P, _I64, _I64, _I32, _I32, _I32, _P, _P],
     "g4q_qmm": [_P, _P, _I64, _I64, _P, _I64, _P],
     "g4q_qmm_ex": [_P, _P, _I64, _I64, _P, _I64, _U32, _F, _P],
+    "g4q_qmm_path": [_P, _I64, ctypes.POINTER(_I32), ctypes.POINTER(_I32)],
     "g4q_qmm_norm": [_P, _P, _I64, _I64, _P, _F, _P, _I64, _P, _I64, _P],
     "g4q_qmm_geglu": [_P, _P, _I64, _I64, _P, _U32, _F, _P, _P, _I64, _P],
     "g4q_lm_head_argmax": [_P, _P, _I64, _I64, _F, _U32, _F, _I64, _P, _I64, _P, _P, _P, _P],
@@ -91,6 +96,7 @@ SIGNATURES = {
     "g4q_decode_plan_create": [ctypes.POINTER(G4qDecodePhase), _I32, _I32, ctypes.POINTER(_P)],
     "g4q_decode_plan_run": [_P, _I64, _F, _F, _I64, _P, _P, _P, _P, _I64, _P],
     "g4q_decode_plan_free": [_P],
+    "g4q_decode_plan_trace": [_P, _P, ctypes.POINTER(_I64)],
     "g4q_decode_plan_create_tp": [ctypes.POINTER(G4qDecodePhase), _I32, _I32, _I32, _I32, ctypes.POINTER(_P)],
     "g4q_decode_plan_buffers": [_P, ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_P),
                                 ctypes.POINTER(ctypes.c_uint64)],

@@ -47,15 +47,22 @@ def build(verbose: bool = False, force: bool = False) -> Path:
     OBJDIR.mkdir(exist_ok=True)
     nvcc = _nvcc()
     common_deps = [CSRC / h for h in HEADERS] + [INCLUDE / "g4q.h"]
-    objs = []
+    objs, cmds = [], []
     for src in SOURCES:
         obj = OBJDIR / (src + ".o")
         objs.append(obj)
         if force or _stale(obj, [CSRC / src] + common_deps):
-            cmd = [nvcc, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-c", str(CSRC / src), "-o", str(obj)]
-            if verbose:
-                print(" ".join(cmd), flush=True)
-            subprocess.run(cmd, check=True)
+            cmds.append([nvcc, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC), "-c", str(CSRC / src), "-o", str(obj)])
+    # translation units compile independently: one nvcc per source, a few at a time
+    from concurrent.futures import ThreadPoolExecutor
+
+    def compile_one(cmd):
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+
+    with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
+        list(ex.map(compile_one, cmds))
     if force or _stale(LIB, objs):
         cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", str(LIB), *map(str, objs),
                "-lcudart", "-Xlinker", "-z,defs"]

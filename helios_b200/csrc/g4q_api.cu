@@ -58,11 +58,19 @@ size_t max_dynamic_smem(const void* kernel) {
 
 static std::mutex g_scratch_mu;
 
-DeviceScratch& device_scratch() {
-    static DeviceScratch per_dev[64];
+static DeviceScratch g_per_dev[64];
+
+DeviceScratch* device_scratch_if_created() {
     const int d = current_device();
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    DeviceScratch& s = per_dev[d & 63];
+    DeviceScratch& s = g_per_dev[d & 63];
+    return s.err != nullptr ? &s : nullptr;
+}
+
+DeviceScratch& device_scratch() {
+    const int d = current_device();
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    DeviceScratch& s = g_per_dev[d & 63];
     if (s.err == nullptr) {
         constexpr int64_t kRows = 65536, kQuads = 65536;
         int* err = nullptr;
@@ -94,11 +102,12 @@ void reserve_gemv_scratch(int64_t N, int64_t K) {
     const size_t need = gemv2_slots_bytes(N, K, device_sm_count());
     std::lock_guard<std::mutex> lock(g_scratch_mu);
     if (need <= s.slots_bytes) return;
-    // cudaFree/cudaMalloc synchronise with the device, so no kernel is still using the old slots
-    cudaFree(s.slots);
-    s.slots = nullptr;
-    s.slots_bytes = 0;
-    check_cuda(cudaMalloc(&s.slots, need), "cudaMalloc(gemv slots)");
+    // The old slots are never freed: a CUDA graph captured earlier with g4q_qmm has their address
+    // baked into its kernel arguments and may still be replayed. They stay allocated until the
+    // process exits (the sizes only grow, so the retired buffers add up to less than the new one).
+    float* grown = nullptr;
+    check_cuda(cudaMalloc(&grown, need), "cudaMalloc(gemv slots)");
+    s.slots = grown;
     s.slots_bytes = need;
 }
 
@@ -541,6 +550,26 @@ G4qStatus g4q_qmm_ex(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t l
     return guarded("g4q_qmm_ex", [&] { qmm_common("g4q_qmm_ex", h, x, M, ldx, y, ldy, flags, eps, stream); });
 }
 
+G4qStatus g4q_qmm_path(const G4qWeight* h, int64_t M, int32_t* kernel, int32_t* splits) {
+    return guarded("g4q_qmm_path", [&] {
+        Weight* w = checked(h, "g4q_qmm_path");
+        require(M >= 1, G4Q_ERR_INVALID_ARGUMENT, "M must be >= 1");
+        require(kernel != nullptr && splits != nullptr, G4Q_ERR_INVALID_ARGUMENT, "kernel and splits must be non-null");
+        *splits = 0;
+        if (w->mlx) {
+            *kernel = G4Q_PATH_GENERIC;
+            return;
+        }
+        QmmCall c{w, nullptr, M, w->K, nullptr, w->N, 0u, 1e-6f};
+        if (M <= 16) {
+            *kernel = gemv2_supported(c) ? G4Q_PATH_GEMV_STREAMK : G4Q_PATH_GEMV_CLUSTER;
+            return;
+        }
+        *kernel = G4Q_PATH_GEMM;
+        *splits = gemm_splits(M, w->N, w->K);
+    });
+}
+
 G4qStatus g4q_qmm_norm(const G4qWeight* h, const uint16_t* x, int64_t M, int64_t ldx, const uint16_t* weight,
                        float eps, uint16_t* xn, int64_t ldxn, uint16_t* y, int64_t ldy, void* stream) {
     return guarded("g4q_qmm_norm", [&] {
@@ -679,6 +708,15 @@ G4qStatus g4q_decode_plan_create_tp(const G4qDecodePhase* phases, int32_t n_phas
         require(out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null out pointer");
         *out = nullptr;
         *out = reinterpret_cast<G4qDecodePlan*>(decode_plan_create(phases, n_phases, max_tokens, rank, n_ranks));
+    });
+}
+
+G4qStatus g4q_decode_plan_trace(G4qDecodePlan* plan, uint64_t* buffer, int64_t* words) {
+    return guarded("g4q_decode_plan_trace", [&] {
+        require(words != nullptr, G4Q_ERR_INVALID_ARGUMENT, "words must be non-null");
+        const int64_t need = decode_plan_trace_words(plan);
+        decode_plan_set_trace(plan, buffer, need);
+        *words = need;
     });
 }
 
@@ -916,11 +954,15 @@ G4qStatus g4q_rms_norm_residual(const uint16_t* x, int64_t ldx, const uint16_t* 
 G4qStatus g4q_device_error(int32_t* code, int32_t reset) {
     return guarded("g4q_device_error", [&] {
         require(code != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null code pointer");
-        DeviceScratch& ds = device_scratch();
+        // nothing is allocated here: a device on which only the allocation-free entry point ran
+        // has no library scratch yet, and its error word is the entry point's static one
         int v = 0;
-        check_cuda(cudaMemcpy(&v, ds.err, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
-        if (reset && v != 0) check_cuda(cudaMemset(ds.err, 0, sizeof(int)), "reset device error word");
-        *code = v;
+        if (DeviceScratch* ds = device_scratch_if_created()) {
+            check_cuda(cudaMemcpy(&v, ds->err, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
+            if (reset && v != 0) check_cuda(cudaMemset(ds->err, 0, sizeof(int)), "reset device error word");
+        }
+        const int v2 = noalloc_error(reset != 0);
+        *code = v != 0 ? v : v2;
     });
 }
 

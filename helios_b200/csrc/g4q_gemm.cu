@@ -420,6 +420,21 @@ void make_map(CUtensorMap* m, CUtensorMapDataType dt, void* base, uint64_t d0, u
 
 bool gemm_supported(const QmmCall& c) { return c.w->K % BK == 0; }
 
+// Split-K when the tiles fill less than half of the SMs (small N, e.g. q|k|v or k/v shards under
+// tensor parallelism): up to 8 splits of at least 4 k-blocks, so that tiles x splits <= SMs.
+int gemm_splits(int64_t M, int64_t N, int64_t K) {
+    const int tiles = (int)(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
+    const int sms = device_sm_count();
+    int splits = 1;
+    if (2 * tiles <= sms) {
+        splits = sms / tiles;
+        if (splits > 8) splits = 8;
+        if (splits > (int)(K / BK) / 4) splits = (int)(K / BK) / 4;
+        if (splits < 1) splits = 1;
+    }
+    return splits;
+}
+
 void launch_gemm(const QmmCall& c, cudaStream_t st) {
     static bool attr_set[64] = {false};
     const int dev = current_device();
@@ -458,17 +473,7 @@ void launch_gemm(const QmmCall& c, cudaStream_t st) {
         check_cuda(cudaGetLastError(), "rms launch");
         p.rms = ds.rms;
     }
-    // Split-K when the tiles fill less than half of the SMs (small N, e.g. q|k|v or k/v shards under
-    // tensor parallelism): up to 8 splits of at least 4 k-blocks, so that tiles x splits <= SMs.
-    const int tiles = (int)(((c.M + BM - 1) / BM) * ((w.N + BN - 1) / BN));
-    const int sms = device_sm_count();
-    int splits = 1;
-    if (2 * tiles <= sms) {
-        splits = sms / tiles;
-        if (splits > 8) splits = 8;
-        if (splits > p.KB / 4) splits = p.KB / 4;
-        if (splits < 1) splits = 1;
-    }
+    const int splits = gemm_splits(c.M, w.N, w.K);
     p.splits = 1;
     p.part = nullptr;
     if (splits > 1) {
@@ -480,11 +485,11 @@ void launch_gemm(const QmmCall& c, cudaStream_t st) {
             cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
             check_cuda(cudaStreamIsCapturing(st, &cap), "cudaStreamIsCapturing");
             if (cap == cudaStreamCaptureStatusNone) {
-                check_cuda(cudaStreamSynchronize(st), "split-K scratch");
-                cudaFree(ss.part);
-                ss.part = nullptr;
-                ss.bytes = 0;
-                check_cuda(cudaMalloc(&ss.part, need), "split-K scratch");
+                // the smaller buffer is retired, not freed: a graph captured earlier may still
+                // replay a split-K launch that writes it (it stays allocated until exit)
+                float* grown = nullptr;
+                check_cuda(cudaMalloc(&grown, need), "split-K scratch");
+                ss.part = grown;
                 ss.bytes = need;
             }
         }

@@ -34,6 +34,7 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxTokens = 16;
 constexpr int kPrefetch = 4;  // groups of weights in flight per warp
+constexpr uint32_t kFastScaleLimit = 247u << 7;   // bf16 |scale| >= 2^120 (exponent 127 + 120), inf, NaN
 
 struct GemvArgs {
     const uint4* packed;
@@ -93,10 +94,12 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, int g0, int ng, uint2
     __syncthreads();
 }
 
-// One warp: acc += W[16r.., 64*g0 .. 64*(g0+ng)) . x^T for its 16-row tile r.
-template <int MT>
+// One warp: acc += W[16r.., 64*g0 .. 64*(g0+ng)) . x^T for its 16-row tile r. kScan: also keep in
+// scale_max the largest exponent-and-mantissa field (bits 7..14 | 0..6) of the scales it reads, so a
+// caller whose weight has not been scanned at load time can tell whether every |scale| < 2^120.
+template <int MT, bool kScan = false>
 __device__ __forceinline__ void warp_tile(const GemvArgs& a, int r, int g0, int ng, const uint2* xf,
-                                          float (&out)[MT][4]) {
+                                          float (&out)[MT][4], uint32_t* scale_max = nullptr) {
     const int lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
     float acc[2][MT][4];
 #pragma unroll
@@ -129,6 +132,7 @@ __device__ __forceinline__ void warp_tile(const GemvArgs& a, int r, int g0, int 
             if (gl < ng) {
                 const uint4 w = wq[i];
                 const RowConsts c0 = row_consts(s0[i]), c1 = row_consts(s1[i]);
+                if constexpr (kScan) *scale_max = max(*scale_max, max(s0[i] & 0x7FFFu, s1[i] & 0x7FFFu));
                 if (gl + kPrefetch < ng) {
                     wq[i] = ldg_stream(wp + (gl + kPrefetch) * wstride);
                     s0[i] = ldg_u32(sp + (gl + kPrefetch) * sstride);
@@ -245,11 +249,15 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(GemvArgs a) {
 // argmax key; CTA-level reduction, one 64-bit atomicMax per token into the handle's scratch,
 // and the last CTA to finish (ticket counter) publishes tokens/values/keys and resets the
 // scratch to zero for the next call.
-template <int MT>
+// kScan (the allocation-free entry point, whose caller-owned weight was never scanned at load):
+// any scale that is non-finite or has |scale| >= 2^120 -- outside what the fast dequantisation
+// handles -- records code 50 in the device error word (the results are then invalid).
+template <int MT, bool kScan = false>
 __global__ void __launch_bounds__(kThreads) lm_head_kernel(GemvArgs a, float cap, int64_t row_offset,
                                                            uint16_t* logits, int64_t ldl,
                                                            unsigned long long* scratch, int32_t* tokens,
-                                                           float* values, unsigned long long* keys_out) {
+                                                           float* values, unsigned long long* keys_out,
+                                                           int* err) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ unsigned long long wbest[kWarps][kMaxTokens];
     __shared__ int is_last;
@@ -264,9 +272,10 @@ __global__ void __launch_bounds__(kThreads) lm_head_kernel(GemvArgs a, float cap
 #pragma unroll
     for (int nt = 0; nt < MT; ++nt) best[nt][0] = best[nt][1] = 0ull;
 
+    uint32_t scale_max = 0u;
     for (int r = blockIdx.x * kWarps + warp; r < a.R; r += gridDim.x * kWarps) {
         float out[MT][4];
-        warp_tile<MT>(a, r, 0, a.G, xf, out);
+        warp_tile<MT, kScan>(a, r, 0, a.G, xf, out, &scale_max);
 #pragma unroll
         for (int nt = 0; nt < MT; ++nt)
 #pragma unroll
@@ -284,6 +293,9 @@ __global__ void __launch_bounds__(kThreads) lm_head_kernel(GemvArgs a, float cap
                     if (key > best[nt][i & 1]) best[nt][i & 1] = key;
                 }
             }
+    }
+    if constexpr (kScan) {
+        if (__any_sync(0xffffffffu, scale_max >= kFastScaleLimit) && lane == 0) atomicCAS(err, 0, 50);
     }
     // lanes sharing t hold the same tokens: reduce over gi (lane bits 2..4)
 #pragma unroll
@@ -419,25 +431,26 @@ void launch_gemv_t(GemvArgs a, cudaStream_t st) {
     check_cuda(cudaGetLastError(), "gemv launch");
 }
 
-template <int MT>
+template <int MT, bool kScan = false>
 void launch_lm_t(GemvArgs a, float cap, int64_t row_offset, uint16_t* logits, int64_t ldl,
-                 unsigned long long* scratch, int32_t* tokens, float* values, unsigned long long* keys,
+                 unsigned long long* scratch, int32_t* tokens, float* values, unsigned long long* keys, int* err,
                  cudaStream_t st) {
     static bool attr_set[64] = {false};
     const int dev = current_device();
     if (!attr_set[dev & 63]) {
-        set_max_smem(lm_head_kernel<MT>);
+        set_max_smem(lm_head_kernel<MT, kScan>);
         attr_set[dev & 63] = true;
     }
     a.gps = a.G;
     const size_t smem = gemv_smem_bytes(a.G, a.M, MT);
-    if (smem > max_dynamic_smem(reinterpret_cast<const void*>(lm_head_kernel<MT>)))
+    if (smem > max_dynamic_smem(reinterpret_cast<const void*>(lm_head_kernel<MT, kScan>)))
         throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "lm_head: activations do not fit in shared memory");
     const int chunks = (a.R + kWarps - 1) / kWarps;
-    int grid = occupancy(lm_head_kernel<MT>, smem) * device_sm_count();
+    int grid = occupancy(lm_head_kernel<MT, kScan>, smem) * device_sm_count();
     if (grid < 1) grid = 1;
     if (grid > chunks) grid = chunks;
-    lm_head_kernel<MT><<<grid, kThreads, smem, st>>>(a, cap, row_offset, logits, ldl, scratch, tokens, values, keys);
+    lm_head_kernel<MT, kScan><<<grid, kThreads, smem, st>>>(a, cap, row_offset, logits, ldl, scratch, tokens, values,
+                                                           keys, err);
     check_cuda(cudaGetLastError(), "lm_head launch");
 }
 
@@ -462,8 +475,11 @@ void launch_gemv(const QmmCall& c, cudaStream_t st) {
 // running keys + a ticket counter) lives in this static array instead of handle-owned memory.
 // Every GPU that loads the library holds these 136 bytes until the process exits; all calls on a
 // device share them, so calls that overlap on the GPU race and must be serialised by the caller.
+// Word kMaxTokens + 1 is this entry point's own error word: the scale check below records code 50
+// there (g4q_device_error reads it beside the library's error word), and the per-call clearing of
+// the keys and the ticket leaves it alone.
 constexpr int kNoAllocScratchWords = kMaxTokens + 1;
-static __device__ __align__(256) unsigned long long g_noalloc_scratch[kNoAllocScratchWords];
+static __device__ __align__(256) unsigned long long g_noalloc_scratch[kNoAllocScratchWords + 1];
 
 static unsigned long long* noalloc_scratch_ptr() {
     // The symbol's host-side name is only a stand-in: its device address is looked up once per
@@ -497,10 +513,25 @@ void launch_lm_head_noalloc(const uint32_t* packed, const uint32_t* sb, int64_t 
     w.packed = const_cast<uint32_t*>(packed);
     w.sb = const_cast<uint32_t*>(sb);
     GemvArgs a = make_args(w, x, M, ldx, nullptr, 0, flags, eps);
+    // the caller's weight was never scanned at load time: the kernel checks the scales it reads
+    int* err = reinterpret_cast<int*>(scratch + kNoAllocScratchWords);
     if (M <= 8)
-        launch_lm_t<1>(a, softcap, row_offset, logits, ld_logits, scratch, tokens, values, keys, st);
+        launch_lm_t<1, true>(a, softcap, row_offset, logits, ld_logits, scratch, tokens, values, keys, err, st);
     else
-        launch_lm_t<2>(a, softcap, row_offset, logits, ld_logits, scratch, tokens, values, keys, st);
+        launch_lm_t<2, true>(a, softcap, row_offset, logits, ld_logits, scratch, tokens, values, keys, err, st);
+}
+
+int noalloc_error(bool reset) {
+    int v = 0;
+    check_cuda(cudaMemcpyFromSymbol(&v, g_noalloc_scratch, sizeof(int), sizeof(unsigned long long) * kNoAllocScratchWords),
+               "read the allocation-free LM head's error word");
+    if (reset && v != 0) {
+        const unsigned long long zero = 0ull;
+        check_cuda(cudaMemcpyToSymbol(g_noalloc_scratch, &zero, sizeof(zero),
+                                      sizeof(unsigned long long) * kNoAllocScratchWords),
+                   "reset the allocation-free LM head's error word");
+    }
+    return v;
 }
 
 void launch_lm_head(const Weight& w, const uint16_t* x, int64_t M, int64_t ldx, float softcap, uint32_t flags,
@@ -508,9 +539,9 @@ void launch_lm_head(const Weight& w, const uint16_t* x, int64_t M, int64_t ldx, 
                     float* values, unsigned long long* keys, cudaStream_t st) {
     GemvArgs a = make_args(w, x, M, ldx, nullptr, 0, flags, eps);
     if (M <= 8)
-        launch_lm_t<1>(a, softcap, row_offset, logits, ld_logits, w.argmax_scratch, tokens, values, keys, st);
+        launch_lm_t<1>(a, softcap, row_offset, logits, ld_logits, w.argmax_scratch, tokens, values, keys, nullptr, st);
     else
-        launch_lm_t<2>(a, softcap, row_offset, logits, ld_logits, w.argmax_scratch, tokens, values, keys, st);
+        launch_lm_t<2>(a, softcap, row_offset, logits, ld_logits, w.argmax_scratch, tokens, values, keys, nullptr, st);
 }
 
 }  // namespace g4q

@@ -104,6 +104,8 @@ struct DeviceScratch {
     int64_t counters_n = 0;
 };
 DeviceScratch& device_scratch();
+// the current device's scratch if a call has created it already, else nullptr (allocates nothing)
+DeviceScratch* device_scratch_if_created();
 // Grows the GEMV partial-sum slots to cover an N x K weight (called by g4q_weight_create).
 void reserve_gemv_scratch(int64_t N, int64_t K);
 
@@ -154,6 +156,9 @@ void launch_lm_head_noalloc(const uint32_t* packed, const uint32_t* sb, int64_t 
                             int64_t M, int64_t ldx, float softcap, uint32_t flags, float eps, int64_t row_offset,
                             uint16_t* logits, int64_t ld_logits, int32_t* tokens, float* values,
                             unsigned long long* keys, cudaStream_t st);
+// the allocation-free LM head's own error word (code 50: a scale outside the fast dequantisation's
+// range); read, and optionally cleared, without allocating
+int noalloc_error(bool reset);
 void launch_lm_head(const Weight& w, const uint16_t* x, int64_t M, int64_t ldx, float softcap, uint32_t flags,
                     float eps, int64_t row_offset, uint16_t* logits, int64_t ld_logits, int32_t* tokens,
                     float* values, unsigned long long* keys, cudaStream_t st);
@@ -163,11 +168,16 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
 void decode_plan_buffers(void* plan, void** slots, uint64_t* slot_bytes, void** xkeys, uint64_t* xkey_bytes);
 void decode_plan_set_peers(void* plan, void* const* slots, void* const* xkeys);
 void decode_plan_free(void* plan);
+int64_t decode_plan_trace_words(void* plan);
+void decode_plan_set_trace(void* plan, uint64_t* buffer, int64_t words);
 void decode_plan_run(void* plan, int M, float eps, float softcap, int64_t row_offset, int32_t* tokens, float* values,
                      uint64_t* keys, uint16_t* logits, int64_t ld_logits, cudaStream_t st);
 
 // kernels (g4q_gemm.cu): tcgen05 dequant-GEMM for M > 16
 void launch_gemm(const QmmCall& c, cudaStream_t st);
 bool gemm_supported(const QmmCall& c);
+// k-block splits the GEMM uses for an M x N x K call (1: unsplit; a larger count also needs the
+// split-K scratch, which is grown outside stream captures only)
+int gemm_splits(int64_t M, int64_t N, int64_t K);
 
 }  // namespace g4q

@@ -17,6 +17,16 @@
  *   - Element types: bf16 values travel as uint16_t bit patterns; packed weights as uint32_t.
  *   - A handle or a stream is not safe for concurrent use by two host threads (the
  *     reference's single scheduler thread owns a target: crates/gemma4d-server/src/http.rs:421-470).
+ *   - Compute calls on one device share library scratch: the stream-K GEMV's partial sums and
+ *     arrival counters, the prefill GEMM's row scales and split-K partials. Calls that overlap on
+ *     the GPU race on it, even on different streams or handles, so issue a device's compute calls
+ *     on one stream or order them with events (as the reference's single scheduler thread issues
+ *     its matmuls one after another). Decode plans, LoRA handles and the allreduce communicator own
+ *     their scratch; the LM head's lives in its weight handle.
+ *   - That scratch is never freed while the process runs: it grows at g4q_weight_create (GEMV
+ *     slots) or at the first GEMM launch outside a stream capture that needs more (split-K
+ *     partials), and a grown buffer replaces the old one without freeing it. A CUDA graph captured
+ *     with any compute call therefore stays valid when larger weights are created later.
  */
 #ifndef G4Q_H
 #define G4Q_H
@@ -143,6 +153,18 @@ G4qStatus g4q_qmm(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t ldx,
 G4qStatus g4q_qmm_ex(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t ldx, void* y, int64_t ldy,
                      uint32_t flags, float eps, void* stream);
 
+/* Which kernel g4q_qmm / g4q_qmm_ex runs for this weight at M rows, without launching anything (no
+ * reference counterpart: MLX picks its kernels internally). kernel: G4Q_PATH_GEMV_STREAMK (the
+ * stream-K decode GEMV, M <= 8), G4Q_PATH_GEMV_CLUSTER (cluster split-K GEMV for the other M <= 16
+ * shapes), G4Q_PATH_GEMM (the tcgen05 dequant-GEMM, M > 16) or G4Q_PATH_GENERIC (8-bit / group
+ * 32, 128 weights). splits: the GEMM's k-block split count (1 = every CTA owns whole tiles; a split
+ * launch inside a stream capture whose split scratch is too small runs unsplit), 0 otherwise. */
+#define G4Q_PATH_GEMV_STREAMK 1
+#define G4Q_PATH_GEMV_CLUSTER 2
+#define G4Q_PATH_GEMM 3
+#define G4Q_PATH_GENERIC 4
+G4qStatus g4q_qmm_path(const G4qWeight* w, int64_t M, int32_t* kernel, int32_t* splits);
+
 /* Replaces the pair model_dtype(fast::rms_norm(h, weight, eps)) -> quantized_linear of
  * layer_forward (native_model.cc:910-913 -> q/k/v, 929-932 -> gate/up; the decode twins
  * :993-1018, :1318-1321): y = qmm(bf16(weight * bf16(x * inv))) with inv = 1/sqrt(mean(x^2) + eps)
@@ -192,13 +214,17 @@ G4qStatus g4q_lm_head_argmax(const G4qWeight* w, const uint16_t* x, int64_t M, i
  * weight handle: the caller passes the weight in kernel layout v1 in memory it owns (packed:
  * (cols/64) x (rows/16) blocks of 128 uint32, block (g, r) at word (g*rows/16 + r)*128; sb:
  * (cols/64) x rows words scale | bias << 16 -- the layout g4q_weight_load builds, documented with
- * the oracle's g4o_repack), plus x and the outputs. Its scratch (16 argmax keys and a ticket
- * counter, 136 bytes) is a static array inside the library: every GPU that loads libg4q holds it
- * until the process exits, so M is limited to 16 rows (larger M is rejected with
- * G4Q_ERR_INVALID_ARGUMENT). Each call clears the scratch on `stream` before its kernel. All calls
- * on one device share that scratch, so calls that overlap on the GPU race: serialise them. The
- * first call on a device looks up the scratch's device address (cudaGetSymbolAddress) with that
- * device current; make that first call before any stream capture. */
+ * the oracle's g4o_repack), plus x and the outputs. Its scratch (16 argmax keys, a ticket
+ * counter and an error word, 144 bytes) is a static array inside the library: every GPU that loads
+ * libg4q holds it until the process exits, so M is limited to 16 rows (larger M is rejected with
+ * G4Q_ERR_INVALID_ARGUMENT). Each call clears the keys and the ticket on `stream` before its
+ * kernel. All calls on one device share that scratch, so calls that overlap on the GPU race:
+ * serialise them. The first call on a device looks up the scratch's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before any stream capture.
+ * Precondition, as for a handle (G4qWeightInfo.fast_path_ok): every scale finite with
+ * |scale| < 2^120. A handle's scales are scanned at load time; caller-owned memory is not, so the
+ * kernel checks the scales it reads, and a violation records code 50 in the error word that
+ * g4q_device_error reports (tokens, values, keys and logits of that call are then invalid). */
 G4qStatus g4q_lm_head_argmax_noalloc(const uint32_t* packed, const uint32_t* sb, int64_t rows, int64_t cols,
                                      const uint16_t* x, int64_t M, int64_t ldx, float softcap, uint32_t flags,
                                      float eps, int64_t row_offset, uint16_t* logits, int64_t ld_logits,
@@ -282,6 +308,13 @@ G4qStatus g4q_decode_plan_run(G4qDecodePlan* plan, int64_t M, float eps, float s
                               int32_t* tokens, float* values, uint64_t* keys, uint16_t* logits, int64_t ld_logits,
                               void* stream);
 G4qStatus g4q_decode_plan_free(G4qDecodePlan* plan);
+/* Per-phase timeline of a plan's runs, a profiling aid (no reference counterpart; the reference
+ * profiles its own phases separately, gemma4_mlx.h:141). *words receives the size of a trace in
+ * 64-bit words: grid CTAs x phases x (3 + 20) globaltimer stamps (ns), per CTA and phase: entry,
+ * x's producers done, x staged with its RMS scale, then the end of each of the 20 warps' units.
+ * With a device buffer of at least that many words set, later runs launch the tracing build of the
+ * kernel and overwrite the buffer; NULL switches back to the regular build. */
+G4qStatus g4q_decode_plan_trace(G4qDecodePlan* plan, uint64_t* buffer, int64_t* words);
 
 /* ---- tensor-parallel decode plans (one process per GPU) ---------------------------------------
  * Replaces the per-rank linears plus the NCCL allreduce after o_proj / down_proj and the vocab-shard
@@ -334,7 +367,8 @@ G4qStatus g4q_comm_free(G4qComm* comm);
 /* ---- device-side failure detection ----------------------------------------------------------
  * Every wait inside a libg4q kernel is bounded; a wait that gives up records a nonzero code in a
  * per-device error word and the kernel runs to its end (its results are then invalid). This
- * reads the word for the current device (synchronising it) and optionally clears it. No
+ * reads the word for the current device (synchronising it) and optionally clears it; it also
+ * reports (and clears) code 50 of g4q_lm_head_argmax_noalloc, and allocates nothing. No
  * reference counterpart: the reference's MLX graph has no device-side waits. */
 G4qStatus g4q_device_error(int32_t* code, int32_t reset);
 

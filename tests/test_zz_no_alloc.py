@@ -69,3 +69,35 @@ def test_noalloc_rejects_sizes_beyond_the_scratch(cuda):
     with pytest.raises(_lib.G4qInvalidArgument, match="static scratch holds 16 keys"):
         _lib.call("g4q_lm_head_argmax_noalloc", _p(d), _p(d), 64, 64, _p(x), 17, 64, 30.0, 0, 1e-6, 0, None, 0,
                   None, None, None, None)
+
+
+def test_noalloc_reports_an_out_of_range_scale(cuda, oracle):
+    """A caller-owned weight is never scanned at load time, so the kernel checks the scales it reads:
+    one scale of 2^121 (beyond the fast dequantisation's |scale| < 2^120) records code 50 in the
+    error word g4q_device_error reports; reading it with reset clears it, and a clean weight then
+    leaves it at zero."""
+    from helios_b200 import _lib
+    from helios_b200 import quantized as Q
+    N, K = 4096, 256
+    w, s, b = oracle.synth_matrix(oracle.matrix_seed(3, 7), N, K)
+    x = Q.synth_normal(oracle.activation_seed(90), (1, K))
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    tok = torch.empty((1,), dtype=torch.int32, device=cuda)
+
+    def run(scales):
+        packed, sb = oracle.repack(w, scales, b)
+        d_packed = torch.from_numpy(packed.view(np.int32)).to(cuda)
+        d_sb = torch.from_numpy(sb.view(np.int32)).to(cuda)
+        _lib.call("g4q_lm_head_argmax_noalloc", _p(d_packed), _p(d_sb), N, K, _p(x), 1, K, 30.0, 0, 1e-6, 0, None,
+                  0, _p(tok), None, None, stream)
+        torch.cuda.synchronize()
+
+    assert _lib.device_error() == 0
+    bad = s.copy()
+    bad[1234, 2] = 0x7C00            # bf16 2^121
+    run(bad)
+    assert _lib.device_error(reset=False) == 50
+    assert _lib.device_error(reset=True) == 50
+    assert _lib.device_error() == 0
+    run(s)
+    assert _lib.device_error() == 0
