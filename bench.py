@@ -21,9 +21,22 @@ qmatmul: BASELINE configs 1 and 2 on the standalone matmul entry point at N = 1:
           algorithmic bytes, launches back to back in a CUDA graph over >= 4x L2 of weight copies.
 cpu_baseline: the CPU oracle (fp32 accumulation, OpenMP on every host core) on a bounded sample
           (layer 0's seven projections at M = 1), rank 0 at N = 1 only.
+prefill: BASELINE config 5 -- a 16384-token prompt as 8 chunks of 2048 tokens through all 48
+          layers on the tcgen05 GEMM, then the LM head on the final row (each chunk its own seeded
+          input); total ms and whole-job TFLOP/s, max over ranks; at N > 1 also the time of the
+          chunk's 96 o/down allreduces run alone (same sizes, same collective), for the split of a
+          chunk into GEMM and allreduce time.
+parity: after every timed region, one decode step of a plan with per-layer output buffers (the
+          same kernel and dataflow) is checked phase by phase against the CPU oracle on the GPU's
+          own inputs (max excess over the bf16 rounding <= 1e-2 * rms for all 193 phases; the
+          token is the argmax of the kernel's own softcapped logits and the oracle's up to a tie),
+          plus the divergence of the oracle's own chained step. The oracle is only the checker
+          here (tests/stack_parity.py); nothing it computes is timed or reported as a speed.
 --impl reference: MLX (the reference's library) is absent, so the reference arm times the CPU
           restatement of the reference's CPU quantized_matmul (oracle/, kind "port") on the same
           metric with all host threads; ranks other than 0 exit without work.
+--case NAME: one small kernel case for an ncu capture (one GPU, a few GB at most; see CASES),
+          printing its CUDA-event time per launch.
 """
 from __future__ import annotations
 
@@ -46,6 +59,91 @@ WORKLOAD = ("decode step, batch 1: 48 layers x {q|k|v, o, gate|up, down} 4-bit g
             "262144x3840 with softcap+argmax (BASELINE config 4)")
 
 
+# Small self-contained cases for ncu captures (one GPU, a few GB at most): seeded weights (several
+# copies where one matrix is smaller than L2, so consecutive launches read cold data), a few warm-up
+# launches, then --launches timed ones; prints the CUDA-event time per launch.
+CASES = {
+    "gemv": dict(N=30720, K=3840, M=1, copies=4),      # fused gate|up decode GEMV, M = 1
+    "gemv2": dict(N=30720, K=3840, M=2, copies=4),
+    "gemv4": dict(N=30720, K=3840, M=4, copies=4),
+    "gemv8": dict(N=30720, K=3840, M=8, copies=4),     # MTP verify width
+    "up1": dict(N=15360, K=3840, M=1, copies=8),
+    "down8": dict(N=3840, K=15360, M=8, copies=4),
+    "lmhead": dict(N=262144, K=3840, M=1, copies=1),   # LM head + softcap + argmax
+    "gemm": dict(N=8192, K=3840, M=2048, copies=1),    # prefill GEMM, q|k|v at 2048 tokens
+    "gemm_kv": dict(N=2048, K=3840, M=2048, copies=1),     # 64 tiles: split-K in two
+    "gemm_tp8": dict(N=1024, K=3840, M=2048, copies=1),    # a q|k|v shard at 8 ranks: split-K in four
+    "dequant": dict(N=15360, K=3840, M=0, copies=1),   # bit-exact dequantize
+    "decode": dict(layers=2),                          # persistent decode step, 2 full layers + LM head
+    "decode_lm": dict(layers=0),                       # the same kernel, LM-head phase alone
+}
+
+
+def profile_case(a):
+    import torch
+
+    from helios_b200 import _lib
+    from helios_b200.quantized import (QuantizedWeight, dequantize, lm_head_argmax, quantized_matmul, synth_matrix,
+                                       synth_normal)
+    from helios_b200.stack import StackConfig, SyntheticStack, activation_seed, matrix_seed
+    _lib.load()
+    torch.cuda.set_device(0)
+    c = CASES[a.case]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if a.case.startswith("decode"):
+        cfg = StackConfig(layers=c["layers"])
+        st = SyntheticStack(cfg, max_tokens=1)
+        st.build_plan(1)
+        h = synth_normal(activation_seed(0), (1, cfg.hidden))
+        for _ in range(a.warmup):
+            st.decode(h)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(a.launches):
+            st.decode(h)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / a.launches
+        wbytes = cfg.weight_bytes()
+        print(json.dumps({"case": a.case, "us_per_launch": round(us, 3), "weight_bytes": wbytes,
+                          "weight_GBps": round(wbytes / us / 1e3, 1)}))
+        st.free()
+        return
+    ws = []
+    for i in range(c["copies"]):
+        w, s, b = synth_matrix(matrix_seed(i, "gate"), c["N"], c["K"])
+        ws.append(QuantizedWeight.from_mlx(w, s, b))
+        del w, s, b
+    M = max(c["M"], 1)
+    x = synth_normal(activation_seed(0), (M, c["K"]))
+    y = torch.empty((M, c["N"]), dtype=torch.bfloat16, device="cuda")
+
+    def run(i):
+        q = ws[i % len(ws)]
+        if a.case == "lmhead":
+            lm_head_argmax(x, q, softcap=30.0, rms_scale=True)
+        elif a.case == "dequant":
+            dequantize(q)
+        else:
+            quantized_matmul(x, q, rms_scale=True, out=y)
+
+    for i in range(a.warmup):
+        run(i)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(a.launches):
+        run(i)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / a.launches
+    wbytes = c["N"] * c["K"] * 9 // 16
+    out = {"case": a.case, "us_per_launch": round(us, 3), "weight_bytes": wbytes,
+           "weight_GBps": round(wbytes / us / 1e3, 1)}
+    if a.case.startswith("gemm"):
+        out["TFLOPs"] = round(2 * c["M"] * c["N"] * c["K"] / us / 1e6, 1)
+    print(json.dumps(out))
+
+
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -56,6 +154,10 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-qmatmul", action="store_true", help="skip the standalone matmul section (configs 1 and 2)")
     p.add_argument("--prefill-tokens", type=int, default=2048, help="chunk size of the prefill measurement (0: skip)")
+    p.add_argument("--prefill-chunks", type=int, default=8, help="chunks of the long prompt (config 5: 8 x 2048)")
+    p.add_argument("--no-parity", action="store_true", help="skip the per-phase oracle check after timing")
+    p.add_argument("--case", choices=sorted(CASES), help="run one small ncu case instead of the benchmark")
+    p.add_argument("--launches", type=int, default=6, help="timed launches of --case")
     return p.parse_args()
 
 
@@ -261,6 +363,9 @@ def qmatmul_section(dev, hbm_peak: float) -> dict:
 
 def main():
     args = parse()
+    if args.case:
+        profile_case(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -315,12 +420,13 @@ def main():
         graph.replay()
     torch.cuda.synchronize()
 
-    def max_over_ranks(v: float) -> float:
+    def over_ranks(v: float):
+        """(max, min) of a per-rank value over the ranks."""
         if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
+            return v, v
+        t = torch.tensor([v, -v], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return float(t[0].item()), -float(t[1].item())
 
     clocks = Clocks(local)
     if rank == 0:
@@ -335,64 +441,107 @@ def main():
     e1.record()
     torch.cuda.synchronize()
     barrier()
-    ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
-    # ---- end to end through the public API: host hidden in, token out, every step
+    ms_max, ms_min = over_ranks(e0.elapsed_time(e1) / args.steps)
+    ms = ms_max
+    # ---- end to end through the public API, every step: the pinned host hidden state copied in,
+    #      one g4q_decode_plan_run call (SyntheticStack.decode), the token key read back to the host
     barrier()
     torch.cuda.synchronize()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record()
     for _ in range(args.steps):
         h_static.copy_(h_host, non_blocking=True)
-        graph.replay()
-        key_host.copy_(keys[:1], non_blocking=True)
+        k_dev, _ = st.decode(h_static)
+        key_host.copy_(k_dev[:1], non_blocking=True)
     e3.record()
     torch.cuda.synchronize()
     barrier()
-    ms_e2e = max_over_ranks(e2.elapsed_time(e3)) / args.steps
+    ms_e2e = over_ranks(e2.elapsed_time(e3) / args.steps)[0]
     clk = clocks.stop() if rank == 0 else None
     tok, _ = decode_keys(key_host)
+    del graph
 
-    # ---- chunked prefill (BASELINE config 5 chunk): P tokens through all layers on the tcgen05
-    #      GEMM path, then the LM head on the last row; captured once in a CUDA graph (with the
-    #      NCCL allreduces at N > 1) and replayed; whole-job TFLOP/s, max over ranks
+    # ---- chunked prefill: a 16384-token prompt as 8 chunks of 2048 tokens, each
+    #      chunk through all layers on the tcgen05 GEMM path; the LM head on the final chunk's last
+    #      row only. One chunk is captured in a CUDA graph (with the NCCL allreduces at N > 1) and
+    #      replayed per chunk after a device copy of that chunk's seeded input; whole-job TFLOP/s.
     prefill = None
-    if args.prefill_tokens > 0:
-        P = args.prefill_tokens
-        hp = synth_normal(activation_seed(1), (P, cfg.hidden), device=dev)
+    if args.prefill_tokens > 0 and args.prefill_chunks > 0:
+        P, C = args.prefill_tokens, args.prefill_chunks
+        inputs = [synth_normal(activation_seed(1 + c), (P, cfg.hidden), device=dev) for c in range(C)]
+        hp = torch.empty((P, cfg.hidden), dtype=torch.bfloat16, device=dev)
+        hp.copy_(inputs[0])
         ps = torch.cuda.Stream()
         ps.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(ps):
-            st.prefill(hp)
+            _, hlast = st.prefill(hp, head=False)
+            st.head(hlast[P - 1:P])
         torch.cuda.current_stream().wait_stream(ps)
         torch.cuda.synchronize()
-        pgraph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(pgraph):
-            st.prefill(hp)
-        pgraph.replay()
+        g_chunk, g_head = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_chunk):
+            _, hlast = st.prefill(hp, head=False)
+        with torch.cuda.graph(g_head):
+            pkey, _ = st.head(hlast[P - 1:P])
+
+        def prompt():
+            for c in range(C):
+                hp.copy_(inputs[c])
+                g_chunk.replay()
+            g_head.replay()
+
+        prompt()   # warm-up run
         torch.cuda.synchronize()
         barrier()
-        reps = 3
+        reps = 2
         p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         p0.record()
         for _ in range(reps):
-            pgraph.replay()
+            prompt()
         p1.record()
         torch.cuda.synchronize()
         barrier()
-        pms = max_over_ranks(p0.elapsed_time(p1)) / reps
-        del pgraph
+        total_ms = over_ranks(p0.elapsed_time(p1) / reps)[0]
+        del g_chunk, g_head
         _, tf_burst, _ = measured_peaks()
         tf_sus = sustained_tflops()
-        tflops = st.prefill_flops(P) / (pms * 1e-3) / 1e12
-        # whole-job TFLOP/s against the whole job's peak (per-GPU measured peak x GPUs)
-        prefill = {"tokens": P, "layers": cfg.layers, "ms_per_chunk": round(pms, 3), "tflops": round(tflops, 1),
+        flops = st.cfg.flops_per_token() * P * C + 2 * cfg.vocab * cfg.hidden
+        tflops = flops / (total_ms * 1e-3) / 1e12
+        prefill = {"tokens": P * C, "chunk_tokens": P, "chunks": C, "layers": cfg.layers, "total_ms": round(total_ms, 3),
+                   "ms_per_chunk": round(total_ms / C, 3), "flops": flops, "tflops": round(tflops, 1),
                    "unit": "TFLOP/s", "peak_sustained": round(tf_sus * world, 1),
                    "frac_of_sustained": round(tflops / (tf_sus * world), 4),
                    "peak_burst": round(tf_burst * world, 1), "frac_of_burst": round(tflops / (tf_burst * world), 4),
-                   "path": "CUDA graph of the chunk: tcgen05 dequant-GEMM for every projection"
+                   "timing": f"{reps} runs of the whole prompt after one warm-up run, CUDA events, max over ranks",
+                   "path": "per chunk a CUDA graph: tcgen05 dequant-GEMM for every projection"
                            + (", NCCL allreduce of fp32 partials after o/down" if world > 1 else "")
-                           + ", LM head on the last row",
-                   "gpu_launches_per_chunk": 6 * cfg.layers + 1}   # q|k|v, gate|up: RMS rows + GEMM
+                           + "; the LM head on the final row",
+                   "gpu_launches_per_chunk": 6 * cfg.layers}   # q|k|v, gate|up: RMS rows + GEMM
+        if world > 1:
+            # the chunk's 96 o/down allreduces alone: same sizes, same collective, captured the same way
+            part = torch.zeros((P, cfg.hidden), dtype=torch.float32, device=dev)
+            ps.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(ps):
+                dist.all_reduce(part, group=group)
+            torch.cuda.current_stream().wait_stream(ps)
+            torch.cuda.synchronize()
+            g_ar = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_ar):
+                for _ in range(2 * cfg.layers):
+                    dist.all_reduce(part, group=group)
+            g_ar.replay()
+            torch.cuda.synchronize()
+            barrier()
+            p0.record()
+            g_ar.replay()
+            p1.record()
+            torch.cuda.synchronize()
+            barrier()
+            ar_ms = over_ranks(p0.elapsed_time(p1))[0]
+            del g_ar
+            prefill["allreduce_ms_per_chunk_alone"] = round(ar_ms, 3)
+            prefill["allreduce_bytes_each"] = P * cfg.hidden * 4
+        del inputs, hp
 
     hbm_peak, tf_peak, peak_kind = measured_peaks()
     # the dominant (only) kernel is the persistent decode kernel: one launch per step per rank
@@ -413,6 +562,31 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline()
 
+    # ---- parity (after every timed region): one step of a plan with per-layer outputs, every phase
+    #      checked on its own GPU input against the CPU oracle on rank 0
+    parity = None
+    if not args.no_parity:
+        st.build_plan(1, keep_layers=True)
+        logits = torch.empty((1, st.v_rows[1] - st.v_rows[0]), dtype=torch.bfloat16, device=dev)
+        pk, _ = st.decode(h_static, logits=logits)
+        torch.cuda.synchronize()
+        perr = _lib.device_error()
+        outs, lg = st.gather_layer_outputs(1, logits)
+        if rank == 0:
+            sys.path.insert(0, str(ROOT / "tests"))
+            from oracle import affine as A
+            from stack_parity import check_decode_step
+            t_p, v_p = decode_keys(pk)
+            h0 = h_static.view(torch.int16).cpu().numpy().view("uint16")
+            t0 = time.perf_counter()
+            parity = check_decode_step(A.stack_shapes(cfg.hidden, cfg.q_out, cfg.kv_out, cfg.inter, cfg.vocab),
+                                       cfg.layers, h0, outs, t_p, v_p, logits=lg, softcap=cfg.softcap, eps=cfg.eps)
+            parity["device_error"] = perr
+            parity["token_equals_timed_step"] = t_p[0] == tok[0]
+            parity["checker"] = (f"tests/stack_parity.py on the CPU oracle, {time.perf_counter() - t0:.1f} s, "
+                                 "after the timed regions")
+        barrier()
+
     wbytes = cfg.weight_bytes()
     gbs = wbytes / (ms * 1e-3) / 1e9
     gbs_e2e = wbytes / (ms_e2e * 1e-3) / 1e9
@@ -426,8 +600,11 @@ def main():
                        "l2": "inputs larger than L2: 6.6 GB of weights streamed per step, no flush"},
             "decode_tok_s": round(1e3 / ms, 2),
             "decode_tok_s_e2e": round(1e3 / ms_e2e, 2),
+            "ms_per_step_over_ranks": {"max": round(ms_max, 5), "min": round(ms_min, 5)},
             "e2e": {"value": round(gbs_e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": cfg.hidden * 2,
-                    "d2h_bytes_per_step": 8, "path": "pinned host hidden -> CUDA graph of the step -> token key"},
+                    "d2h_bytes_per_step": 8,
+                    "path": "per step: pinned host hidden -> device, g4q_decode_plan_run (one C-ABI call), "
+                            "token key -> pinned host"},
             "roofline": {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1),
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                          "peak_kind": f"{peak_kind} hbm_gbs", "traffic": traffic,
@@ -436,6 +613,8 @@ def main():
             "clocks": clk,
             "last_token": tok[0],
         }
+        if parity is not None:
+            line["parity"] = parity
         if cpu is not None:
             line["cpu_baseline"] = cpu
         if prefill is not None:
@@ -443,8 +622,8 @@ def main():
         if qmm is not None:
             line["qmatmul"] = qmm
         print(json.dumps(line), flush=True)
-    del graph
     barrier()
+    st.free()
     if world > 1:
         dist.destroy_process_group()
 

@@ -101,7 +101,19 @@ struct DecodeArgs {
     unsigned long long* keys_out;
     uint16_t* logits;                         // optional bf16 logits of the argmax phase
     int* err;
+    unsigned long long* trace;                // kTrace: [C][n_phases][kTraceWords] globaltimer stamps
 };
+
+// Per-phase timeline of one CTA (tracing instantiation only): word 0 phase entry, 1 producers of x
+// done (every wait before staging met), 2 x staged and its RMS scale known, 3 + w the end of warp w's
+// units (after its last park).
+constexpr int kTraceWords = 3 + kWarps;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -680,8 +692,9 @@ __device__ __forceinline__ unsigned long long exchange_keys(const DecodeArgs& a,
 }
 
 // kTP: tensor-parallel instantiation (allreduce phases, key exchange); the single-GPU one has none
-// of that code.
-template <bool kTP>
+// of that code. kTrace: also stamps each CTA's per-phase timeline into a.trace (a profiling build
+// selected at run time; the default instantiations have no trace code).
+template <bool kTP, bool kTrace = false>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ CtaShared sh;
@@ -726,6 +739,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         // ---- phase entry: the CTA's warps are done with the previous phase (x buffer reuse). While
         //      the previous phase finishes elsewhere, tabulate where x's producer partials live.
         __syncthreads();
+        unsigned long long* tr = nullptr;
+        if constexpr (kTrace) {
+            tr = a.trace + ((size_t)cta * a.n_phases + p) * kTraceWords;
+            if (threadIdx.x == 0) tr[0] = global_ns();
+        }
         if (P.src >= 0) {
             const PhaseDev& S = a.ph[P.src];
             for (int j = threadIdx.x; j < P.K / 64; j += kThreads) {
@@ -739,6 +757,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             if (P.sync_before) spin_until(a.done + (p - 1), (unsigned)C, a.err);
             sh.rs_prev = sh.rs;
             sh.wb_claim = 0;
+            if constexpr (kTrace) tr[1] = global_ns();
         }
         __syncthreads();
         const float rs_prev = sh.rs_prev;
@@ -766,6 +785,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
                 r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)P.K), a.eps)));
             }
             sh.rs = r;
+            if constexpr (kTrace) tr[2] = global_ns();
         }
         __syncthreads();
 
@@ -832,6 +852,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             }
         }
         if (n_units > 0) park<kTP>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
+        if constexpr (kTrace) {
+            if (lane == 0) tr[3 + warp] = global_ns();
+        }
         // ---- the first warp of the CTA to run out of units writes phase p-1's unfinished quads to y
         if (p > 0) {
             int claim = 0;
@@ -919,6 +942,7 @@ struct DecodePlan {
     unsigned long long** d_peers = nullptr;   // [2][kMaxRanks]: slot buffers, key arrays of every rank
     unsigned long long* peer_rp[kMaxRanks] = {};
     unsigned long long* peer_xkeys[kMaxRanks] = {};
+    unsigned long long* trace = nullptr;      // caller's buffer: runs use the tracing kernel while set
 };
 
 constexpr uint64_t kPlanMagic = 0x4734514445434f44ull;
@@ -1084,6 +1108,8 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     plan->smem = (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4 + (size_t)(kmax + 8) * 2;
     const void* kfn = n_ranks > 1 ? reinterpret_cast<const void*>(decode_kernel<true>)
                                   : reinterpret_cast<const void*>(decode_kernel<false>);
+    const void* kfn_trace = n_ranks > 1 ? reinterpret_cast<const void*>(decode_kernel<true, true>)
+                                        : reinterpret_cast<const void*>(decode_kernel<false, true>);
     if (plan->smem > max_dynamic_smem(kfn)) {
         delete plan;
         throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: K too large for shared memory");
@@ -1115,6 +1141,9 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     upload_peers(plan);
     check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_dynamic_smem(kfn)),
                "cudaFuncSetAttribute(decode)");
+    check_cuda(cudaFuncSetAttribute(kfn_trace, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)max_dynamic_smem(kfn_trace)),
+               "cudaFuncSetAttribute(decode, tracing)");
     int per_sm = 0;
     check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kThreads, plan->smem),
                "occupancy(decode)");
@@ -1208,10 +1237,26 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    a.trace = plan->trace;
     if (plan->n_ranks > 1)
-        check_cuda(cudaLaunchKernelEx(&cfg, decode_kernel<true>, a), "cudaLaunchKernelEx(decode)");
+        check_cuda(cudaLaunchKernelEx(&cfg, plan->trace ? decode_kernel<true, true> : decode_kernel<true>, a),
+                   "cudaLaunchKernelEx(decode)");
     else
-        check_cuda(cudaLaunchKernelEx(&cfg, decode_kernel<false>, a), "cudaLaunchKernelEx(decode)");
+        check_cuda(cudaLaunchKernelEx(&cfg, plan->trace ? decode_kernel<false, true> : decode_kernel<false>, a),
+                   "cudaLaunchKernelEx(decode)");
+}
+
+int64_t decode_plan_trace_words(void* h) {
+    DecodePlan* plan = checked_plan(h);
+    return (int64_t)plan->grid * plan->n_phases * kTraceWords;
+}
+
+void decode_plan_set_trace(void* h, uint64_t* buffer, int64_t words) {
+    DecodePlan* plan = checked_plan(h);
+    if (buffer != nullptr && words < decode_plan_trace_words(h))
+        throw Error(G4Q_ERR_INVALID_ARGUMENT, "trace buffer needs " + std::to_string(decode_plan_trace_words(h)) +
+                                                  " 64-bit words");
+    plan->trace = reinterpret_cast<unsigned long long*>(buffer);
 }
 
 }  // namespace g4q

@@ -168,6 +168,13 @@ class QuantizedWeight:
         _lib.call("g4q_weight_info", self.handle, ctypes.byref(info))
         return {f: getattr(info, f) for f, _ in info._fields_}
 
+    def qmm_path(self, M: int) -> Tuple[int, int]:
+        """(kernel, splits) that quantized_matmul takes at M rows (``_lib.PATH_*``; splits is the
+        GEMM's k-block split count, 0 for the other kernels). Launches nothing."""
+        kernel, splits = ctypes.c_int32(0), ctypes.c_int32(0)
+        _lib.call("g4q_qmm_path", self.handle, M, ctypes.byref(kernel), ctypes.byref(splits))
+        return kernel.value, splits.value
+
     def export(self) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """Inverse repack: MLX-layout (w uint32, scales bf16, biases bf16) on this GPU."""
         dev = torch.device("cuda", self.device)
@@ -573,6 +580,21 @@ class DecodePlan:
         ld = 0 if logits is None else logits.stride(0)
         _lib.call("g4q_decode_plan_run", self._h, M, eps, softcap, row_offset, _ptr(tokens), _ptr(values), _ptr(keys),
                   _ptr(logits), ld, _stream())
+
+    def trace(self, enable: bool = True) -> Optional[torch.Tensor]:
+        """Per-phase timeline of the following runs (profiling aid): returns the int64 device buffer
+        [CTAs, phases, 23] of globaltimer stamps (ns) the tracing build of the kernel fills (entry,
+        x's producers done, x staged, then each of the 20 warps' end of units), or None after
+        switching back to the regular build."""
+        words = ctypes.c_int64(0)
+        _lib.call("g4q_decode_plan_trace", self._h, None, ctypes.byref(words))
+        if not enable:
+            self._trace = None
+            return None
+        buf = torch.zeros(words.value, dtype=torch.int64, device="cuda")
+        _lib.call("g4q_decode_plan_trace", self._h, _ptr(buf), ctypes.byref(words))
+        self._trace = buf
+        return buf
 
     def free(self):
         for p in getattr(self, "_opened", []):

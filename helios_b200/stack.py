@@ -164,7 +164,7 @@ class SyntheticStack:
             x = self._row_parallel(L["down"], gu[:, self.ni:], self.h_out[:M])
         return self.head(x)
 
-    def prefill(self, h: torch.Tensor, sub_chunks: int = 1):
+    def prefill(self, h: torch.Tensor, sub_chunks: int = 1, head: bool = True):
         """One chunked-prefill chunk: M tokens through every layer's quantized
         linears on the tcgen05 GEMM (M > 16), then the LM head on the chunk's last row only.
         Uses its own activation buffers (the decode buffers stay baked into the plan).
@@ -174,7 +174,9 @@ class SyntheticStack:
         run (the rows are independent; results are bit-identical to ``sub_chunks`` = 1). Measured
         on B200 at 2 GPUs it is slower (41.3 vs 33.8 ms per 2048-token chunk): the GEMM keeps one
         CTA on every SM, so the NCCL kernels wait for SMs instead of overlapping, and the half-height
-        GEMMs lose tile efficiency. Off by default. Returns (key of the last row, h)."""
+        GEMMs lose tile efficiency. Off by default. ``head`` False skips the LM head (the chunks
+        before the last one of a long prompt, as prefill_chunked_last_logits computes logits for the
+        final chunk only). Returns (key of the last row or None, h)."""
         M = h.shape[0]
         c, dev = self.cfg, self.device
         pb = getattr(self, "_pre", None)
@@ -194,7 +196,7 @@ class SyntheticStack:
                 o = self._row_parallel(L["o"], qkv[:, : self.nq], pb["o"][:M], part=pb["part"])
                 gu = quantized_matmul(o, L["gu"], rms_scale=True, eps=c.eps, out=pb["gu"][:M])
                 x = self._row_parallel(L["down"], gu[:, self.ni:], pb["h"][:M], part=pb["part"])
-            key, _ = self.head(x[M - 1:M])
+            key = self.head(x[M - 1:M])[0] if head else None
             return key, x
         # row blocks on 256-row boundaries (the GEMM's token tile)
         step = -(-M // sub_chunks)
@@ -236,40 +238,93 @@ class SyntheticStack:
         for ev in h_ready:
             comp.wait_event(ev)
         x = pb["h"][:M]
-        key, _ = self.head(x[M - 1:M])
+        key = self.head(x[M - 1:M])[0] if head else None
         return key, x
 
     def prefill_flops(self, M: int) -> int:
         """Whole-job FLOPs of one prefill chunk of M tokens (all ranks; LM head on one row)."""
         return self.cfg.flops_per_token() * M + 2 * self.cfg.vocab * self.cfg.hidden
 
-    def build_plan(self, max_tokens: int = 1) -> DecodePlan:
+    def build_plan(self, max_tokens: int = 1, keep_layers: bool = False) -> DecodePlan:
         """The whole decode step (48 x 4 matmuls + LM head argmax) as one persistent-kernel plan.
 
         Tensor parallel (``tp_size`` > 1, collective over the group): o and down are ALLREDUCE phases,
         their partial sums cross NVLink inside the kernel, and the LM-head keys are combined there too,
-        so one step is one launch per GPU with no NCCL call."""
+        so one step is one launch per GPU with no NCCL call.
+
+        ``keep_layers``: every layer writes its own output buffers (``self.layer_outs[l]`` with
+        ``qkv``, ``o``, ``gu``, ``h``) instead of reusing one set, so each phase's input and output
+        stay readable after the step (the per-phase parity check). The kernel's work and dataflow
+        are the same: each phase still reads the previous phase's output."""
         c = self.cfg
+        if getattr(self, "plan", None) is not None:
+            self.plan.free()
         self.h_in = torch.zeros((max(max_tokens, 1), c.hidden), dtype=torch.bfloat16, device=self.device)
         ar = PHASE_ALLREDUCE if self.size > 1 else 0
         phases, x = [], self.h_in
+        self.layer_outs = []
         for L in self.layers:
-            phases.append((L["qkv"], x, self.qkv_out, QMM_RMS_SCALE))
-            phases.append((L["o"], self.qkv_out[:, : self.nq], self.o_out, ar))
-            phases.append((L["gu"], self.o_out, self.gu_out, QMM_RMS_SCALE))
-            phases.append((L["down"], self.gu_out[:, self.ni:], self.h_out, ar))
-            x = self.h_out
+            if keep_layers:
+                M, dev = self.max_tokens, self.device
+                bufs = {"qkv": torch.empty((M, self.nq + 2 * self.nkv), dtype=torch.bfloat16, device=dev),
+                        "o": torch.empty((M, c.hidden), dtype=torch.bfloat16, device=dev),
+                        "gu": torch.empty((M, 2 * self.ni), dtype=torch.bfloat16, device=dev),
+                        "h": torch.empty((M, c.hidden), dtype=torch.bfloat16, device=dev)}
+                self.layer_outs.append(bufs)
+            else:
+                bufs = {"qkv": self.qkv_out, "o": self.o_out, "gu": self.gu_out, "h": self.h_out}
+            phases.append((L["qkv"], x, bufs["qkv"], QMM_RMS_SCALE))
+            phases.append((L["o"], bufs["qkv"][:, : self.nq], bufs["o"], ar))
+            phases.append((L["gu"], bufs["o"], bufs["gu"], QMM_RMS_SCALE))
+            phases.append((L["down"], bufs["gu"][:, self.ni:], bufs["h"], ar))
+            x = bufs["h"]
+        self.h_last = x
         phases.append((self.lm, x, None, QMM_RMS_SCALE | PHASE_ARGMAX))
         self.plan = DecodePlan(phases, max_tokens, rank=self.rank, n_ranks=self.size, group=self.group)
         return self.plan
 
-    def decode(self, h: torch.Tensor):
-        """One decode step through the single-launch plan: h [M, hidden] -> (keys, final hidden)."""
+    def decode(self, h: torch.Tensor, logits: Optional[torch.Tensor] = None):
+        """One decode step through the single-launch plan: h [M, hidden] -> (keys, final hidden).
+        ``logits`` (bf16 [M, vocab shard]) also receives the LM head's pre-softcap logits."""
         M = h.shape[0]
         self.h_in[:M].copy_(h)
         self.plan.run(M, eps=self.cfg.eps, softcap=self.cfg.softcap, row_offset=self.v_rows[0],
-                      tokens=self.tokens[:M], values=self.values[:M], keys=self.keys[:M])
-        return self.keys[:M], self.h_out[:M]
+                      tokens=self.tokens[:M], values=self.values[:M], keys=self.keys[:M], logits=logits)
+        return self.keys[:M], self.h_last[:M]
+
+    def gather_layer_outputs(self, M: int = 1, logits: Optional[torch.Tensor] = None):
+        """The per-layer outputs of the last step of a ``keep_layers`` plan at full width, as bf16 bit
+        patterns (numpy uint16) on rank 0: a list of dicts qkv (q|k|v), o, gu (gate|up), h, and the
+        logits when given (the rank's vocabulary shard [M, rows]). Column-parallel shards are
+        gathered over the group (a collective: every rank calls it); other ranks get None."""
+        def bits(t):
+            return t.contiguous().view(torch.int16).cpu().numpy().view("uint16")
+
+        def gather(t):
+            if self.size == 1:
+                return [t]
+            parts = [torch.empty_like(t) for _ in range(self.size)]
+            torch.distributed.all_gather(parts, t.contiguous(), group=self.group)
+            return parts
+
+        outs = []
+        for bufs in self.layer_outs:
+            qkv = gather(bufs["qkv"][:M])
+            gu = gather(bufs["gu"][:M])
+            if self.rank == 0:
+                q = [p[:, : self.nq] for p in qkv]
+                k = [p[:, self.nq: self.nq + self.nkv] for p in qkv]
+                v = [p[:, self.nq + self.nkv:] for p in qkv]
+                g = [p[:, : self.ni] for p in gu]
+                u = [p[:, self.ni:] for p in gu]
+                outs.append({"qkv": bits(torch.cat(q + k + v, dim=1)), "o": bits(bufs["o"][:M]),
+                             "gu": bits(torch.cat(g + u, dim=1)), "h": bits(bufs["h"][:M])})
+        full_logits = None
+        if logits is not None:
+            lg = gather(logits[:M])
+            if self.rank == 0:
+                full_logits = bits(torch.cat(lg, dim=1))
+        return (outs, full_logits) if self.rank == 0 else (None, None)
 
     def local_weight_bytes(self) -> int:
         """Packed + scale/bias bytes of this rank's shards (0.5625 B per weight)."""

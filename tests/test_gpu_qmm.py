@@ -203,6 +203,87 @@ def test_prefill_chunk_2048(cuda, oracle):
     qw.free()
 
 
+def test_prefill_gemm_unsplit_up_slice_2048(cuda, oracle):
+    """The GEMM path the prefill benchmark times: 2048 tokens on 2560 rows of up_proj gives 80 tiles,
+    more than half of the SMs, so every CTA owns whole 256 x 256 tiles (no split-K) and writes its
+    two 128-token MMA halves straight from TMEM. Every row of both halves is checked, with the RMS
+    row scale, in bf16 and fp32."""
+    from helios_b200 import _lib
+    from helios_b200 import quantized as Q
+    seed = oracle.matrix_seed(0, 5)
+    w, s, b = Q.synth_matrix(seed, 15360, 3840)
+    qw = Q.QuantizedWeight.from_mlx(w, s, b, rows=(1280, 3840))
+    assert qw.qmm_path(2048) == (_lib.PATH_GEMM, 1)
+    x = Q.synth_normal(oracle.activation_seed(2), (2048, 3840))
+    xn = u16(x)
+    ow, os_, ob = oracle.synth_matrix(seed, 15360, 3840)
+    r = np.array([oracle.rms_scale(xn[m]) for m in range(2048)], dtype=np.float32)
+    ye, _ = oracle.qmm(xn, ow[1280:3840], os_[1280:3840], ob[1280:3840], row_scale=r)
+    yb = Q.quantized_matmul(x, qw, rms_scale=True)
+    yg = oracle.bf16_to_f32(u16(yb))
+    for h0 in (0, 128):        # token rows of each MMA half of every 256-token tile, separately
+        rows = np.concatenate([np.arange(t + h0, t + h0 + 128) for t in range(0, 2048, 256)])
+        assert_qmm_close(yg[rows], ye[rows], bf16_out=True)
+    yf = Q.quantized_matmul(x, qw, rms_scale=True, out_dtype=torch.float32).cpu().numpy()
+    assert_qmm_close(yf, ye, bf16_out=False)
+    assert _lib.device_error() == 0
+    qw.free()
+
+
+def test_prefill_gemm_unsplit_full_qkv_2048(cuda, oracle):
+    """The full q|k|v projection of one layer (8192 x 3840: q, k and v concatenated as the stack
+    uploads them) at 2048 tokens with the RMS row scale: 256 tiles, unsplit."""
+    from helios_b200 import _lib
+    from helios_b200 import quantized as Q
+    mats = [oracle.synth_matrix(oracle.matrix_seed(0, oracle.PROJ_IDS[p]), n, 3840)
+            for p, n in (("q", 4096), ("k", 2048), ("v", 2048))]
+    dev = [Q.synth_matrix(oracle.matrix_seed(0, oracle.PROJ_IDS[p]), n, 3840) for p, n in (("q", 4096), ("k", 2048),
+                                                                                           ("v", 2048))]
+    qw = Q.QuantizedWeight.concat([(w, s, b, (0, w.shape[0])) for w, s, b in dev])
+    assert qw.rows == 8192 and qw.qmm_path(2048) == (_lib.PATH_GEMM, 1)
+    x = Q.synth_normal(oracle.activation_seed(3), (2048, 3840))
+    xn = u16(x)
+    r = np.array([oracle.rms_scale(xn[m]) for m in range(2048)], dtype=np.float32)
+    ow = np.concatenate([m[0] for m in mats])
+    os_ = np.concatenate([m[1] for m in mats])
+    ob = np.concatenate([m[2] for m in mats])
+    ye, _ = oracle.qmm(xn, ow, os_, ob, row_scale=r)
+    yb = Q.quantized_matmul(x, qw, rms_scale=True)
+    assert_qmm_close(oracle.bf16_to_f32(u16(yb)), ye, bf16_out=True)
+    assert _lib.device_error() == 0
+    qw.free()
+
+
+def test_captured_graph_survives_scratch_growth(cuda, oracle):
+    """A CUDA graph captured with a decode-width matmul keeps the library scratch it was captured
+    with: creating a much larger weight afterwards grows the scratch without freeing the old one,
+    so replaying the graph still gives the eager result bit for bit."""
+    from helios_b200 import quantized as Q
+    N, K = 4096, 3840
+    w, s, b = Q.synth_matrix(oracle.matrix_seed(9, 0), N, K)
+    qw = Q.QuantizedWeight.from_mlx(w, s, b)
+    x = Q.synth_normal(oracle.activation_seed(61), (1, K))
+    y = torch.empty((1, N), dtype=torch.bfloat16, device=cuda)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        Q.quantized_matmul(x, qw, out=y)
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        Q.quantized_matmul(x, qw, out=y)
+    # 1,048,576 rows: more stream-K quads than any other weight of the test session
+    big = Q.QuantizedWeight.from_mlx(*Q.synth_matrix(oracle.matrix_seed(9, 1), 1 << 20, 64))
+    x.copy_(Q.synth_normal(oracle.activation_seed(62), (1, K)))
+    g.replay()
+    torch.cuda.synchronize()
+    eager = Q.quantized_matmul(x, qw)
+    assert torch.equal(y, eager)
+    del g
+    big.free()
+    qw.free()
+
+
 @pytest.mark.parametrize("M", [1, 4])
 def test_lm_head_softcap_argmax_full_vocab(cuda, oracle, M):
     from helios_b200 import quantized as Q

@@ -121,6 +121,65 @@ def test_tensor_parallel_decode_plan_two_gpus(cuda, oracle):
     assert toks[0] == ref["tokens"][0] or abs(vals[0] - ref["values"][0]) <= 0.125
 
 
+def _full_plan_worker(rank, world, port, out_q):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from helios_b200 import _lib
+        from helios_b200.quantized import synth_normal
+        from helios_b200.stack import StackConfig, SyntheticStack, activation_seed, decode_keys
+        cfg = StackConfig(layers=4)
+        st = SyntheticStack(cfg, rank, world, dist.group.WORLD, max_tokens=1)
+        st.build_plan(1, keep_layers=True)
+        h0 = synth_normal(activation_seed(0), (1, cfg.hidden))
+        logits = torch.empty((1, st.v_rows[1] - st.v_rows[0]), dtype=torch.bfloat16, device="cuda")
+        keys, _ = st.decode(h0, logits=logits)
+        torch.cuda.synchronize()
+        err = _lib.device_error()
+        all_keys = [torch.empty_like(keys) for _ in range(world)]
+        dist.all_gather(all_keys, keys)
+        outs, lg = st.gather_layer_outputs(1, logits)
+        if rank == 0:
+            # checked in this process: the per-layer outputs are too large for the result pipe while
+            # the parent is still joining the ranks
+            from oracle import affine as oracle
+            from stack_parity import check_decode_step
+            toks, vals = decode_keys(keys)
+            h0n = h0.view(torch.int16).cpu().numpy().view(np.uint16)
+            rep = check_decode_step(oracle.stack_shapes(), cfg.layers, h0n, outs, toks, vals, logits=lg,
+                                    softcap=cfg.softcap, eps=cfg.eps)
+            same = all(torch.equal(k, all_keys[0]) for k in all_keys)
+            out_q.put((rep, same, err))
+        else:
+            out_q.put((None, None, err))
+        dist.barrier()
+        st.free()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_full_width_plan_every_phase(cuda, oracle):
+    """The tensor-parallel decode plan at the benchmark's full width (4 layers + the 262144-row LM head
+    over 2 GPUs): every phase, the allreduced o/down outputs included, against the oracle on its own
+    gathered GPU input, and the same key on both ranks."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    mp.start_processes(_full_plan_worker, args=(2, _free_port(), q), nprocs=2, join=True, start_method="spawn")
+    res = [q.get(), q.get()]
+    rep, same, _ = next(r for r in res if r[0] is not None)
+    assert all(r[2] == 0 for r in res)
+    assert same
+    assert rep["pass"], rep
+
+
 def _prefill_worker(rank, world, port, out_q):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
