@@ -514,21 +514,24 @@ def main():
                    "peak_burst": round(tf_burst * world, 1), "frac_of_burst": round(tflops / (tf_burst * world), 4),
                    "timing": f"{reps} runs of the whole prompt after one warm-up run, CUDA events, max over ranks",
                    "path": "per chunk a CUDA graph: tcgen05 dequant-GEMM for every projection"
-                           + (", NCCL allreduce of fp32 partials after o/down" if world > 1 else "")
+                           + (", after o/down the NCCL reduce-scatter (fp32) + all-gather (bf16) of the partial "
+                              "sums" if world > 1 else "")
                            + "; the LM head on the final row",
                    "gpu_launches_per_chunk": 6 * cfg.layers}   # q|k|v, gate|up: RMS rows + GEMM
         if world > 1:
-            # the chunk's 96 o/down allreduces alone: same sizes, same collective, captured the same way
+            # the chunk's 96 o/down collectives alone (fp32 partials -> summed bf16 rows on every rank):
+            # same sizes, same calls, captured the same way
             part = torch.zeros((P, cfg.hidden), dtype=torch.float32, device=dev)
+            summed = torch.empty((P, cfg.hidden), dtype=torch.bfloat16, device=dev)
             ps.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(ps):
-                dist.all_reduce(part, group=group)
+                st.sum_partials(part, summed)
             torch.cuda.current_stream().wait_stream(ps)
             torch.cuda.synchronize()
             g_ar = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g_ar):
                 for _ in range(2 * cfg.layers):
-                    dist.all_reduce(part, group=group)
+                    st.sum_partials(part, summed)
             g_ar.replay()
             torch.cuda.synchronize()
             barrier()
@@ -541,6 +544,8 @@ def main():
             del g_ar
             prefill["allreduce_ms_per_chunk_alone"] = round(ar_ms, 3)
             prefill["allreduce_bytes_each"] = P * cfg.hidden * 4
+            prefill["allreduce"] = ("NCCL reduce-scatter of the fp32 partials, bf16 rounding of each rank's block "
+                                    "of rows, NCCL all-gather of the bf16 rows")
         del inputs, hp
 
     hbm_peak, tf_peak, peak_kind = measured_peaks()

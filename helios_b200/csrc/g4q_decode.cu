@@ -14,23 +14,25 @@
 //    phase boundaries, so the next phase's weights land while the grid finishes the current one;
 //  * the units of a phase are cut into equal contiguous CTA ranges (quad-major) and each CTA range
 //    into contiguous warp runs; a quad's warp partials are reduced in shared memory, wait-free;
-//  * dataflow instead of grid barriers: every CTA stores its unscaled fp32 partial of each quad it
-//    touched into a slot as one 64-bit word (value | phase tag). A CTA consuming the phase output
-//    polls the slots of the quads it needs and sums them in a fixed (rank, CTA) order while
-//    staging its x, so a phase starts on an SM as soon as its inputs exist and no SM ever waits
-//    for a whole-grid barrier. Tags are unique per (launch, phase); slot buffers rotate over three
-//    phases, which the host proves safe (or falls back to a barrier) when the plan is made;
+//  * dataflow instead of grid barriers or arrival counters: every output quad has ONE finisher. A
+//    quad whole in one CTA is finished by that CTA; a quad cut between CTA ranges is finished by the
+//    first of its CTAs (whose part of the quad comes last in its range), which polls the others'
+//    fp32 partials -- stored as 64-bit words (value | phase tag) -- and sums them in CTA order. The
+//    finisher writes y and, for the phase that reads it, the final bf16 values as tagged words of an
+//    exchange buffer; a consumer CTA polls those words while it stages its x. So a phase starts on an
+//    SM as soon as its inputs exist, and no store needs a fence: each word carries its own tag. Tags
+//    are unique per (launch, phase); exchange and slot buffers rotate over three phases, which the
+//    host proves safe when the plan is made (or places a grid barrier);
 //  * tensor parallel plans (one process per GPU): after a row-parallel phase (G4Q_PHASE_ALLREDUCE)
-//    each rank sums its CTAs' partials of a quad once (the CTA that owns the quad's write-back) and
-//    stores that rank partial, tagged, into every rank's rank-partial buffer over NVLink (peer
-//    stores); consumers on every rank poll the tags and add the ranks' partials in rank order, so
-//    the allreduce after o/down needs no separate collective and every rank sees the same bits.
-//    The LM-head keys are exchanged the same way at the end of the step;
+//    each CTA stores its tagged partial of every quad it touched into the rank-partial buffer of
+//    every rank over NVLink (peer stores); the finisher of the quad on each rank polls all ranks'
+//    partials and adds them in rank-then-CTA order, so the allreduce after o/down needs no separate
+//    collective and every rank sees the same bits. The LM-head keys are exchanged the same way at
+//    the end of the step;
 //  * the argmax phase keeps 64-bit keys (order-preserving logit bits | ~row); its cut quads are
-//    finished by the last contributing CTA (slot + arrival counter), and the last CTA to finish
-//    publishes tokens/values/keys. The last CTA to leave resets the counters and advances the
-//    launch counter (the tag base), so a plan is ready for the next launch and for CUDA-graph
-//    replay without a memset.
+//    finished like any other, and the last CTA to finish publishes tokens/values/keys. The last CTA
+//    to leave resets the counters and advances the launch counter (the tag base), so a plan is ready
+//    for the next launch and for CUDA-graph replay without a memset.
 // Every wait is bounded (about two seconds of clocks); a wait that gives up records an error code
 // in the per-device error word and the kernel runs to its end.
 #include <algorithm>
@@ -52,7 +54,7 @@ constexpr uint32_t kUnitSb = 64 * 4;
 constexpr uint32_t kUnitBytes = kUnitPacked + kUnitSb;
 constexpr uint32_t kRingBytes = kStages * kUnitBytes;
 constexpr int kSlots = 16;                        // CTA ranges one 64-row quad may be cut into
-constexpr int kSlotBufs = 3;                      // slot buffers rotate over three phases
+constexpr int kBufs = 3;                          // exchange / slot buffers rotate over three phases
 constexpr int kMaxCtaQuads = 64;                  // quads one CTA range may touch in a phase
 constexpr int kMaxRanks = 8;
 constexpr int kMaxXQuads = 256;                   // 64-wide groups of x a phase may read (K <= 16384)
@@ -75,6 +77,7 @@ struct PhaseDev {
     int ks;           // slot rows per (quad, rank): the most CTA ranges one quad meets
     int sync_before;  // wait for every CTA to finish the previous phase before staging x
     int need_done;    // count finished CTAs of this phase (a later barrier or the argmax publish)
+    int xout;         // the next phase stages this phase's output from the exchange buffer
 };
 
 struct DecodeArgs {
@@ -86,16 +89,15 @@ struct DecodeArgs {
     unsigned int* exit_count;                 // [1]
     unsigned int* run;                        // [1] launches so far (tag base)
     unsigned long long* key;                  // running argmax key of this rank
-    unsigned long long* slots;                // this rank's slot buffers (fp32 partials of its CTAs)
+    unsigned long long* slots;                // [kBufs][buf_words] tagged fp32 partials of cut quads
+    unsigned long long* xbuf;                 // [kBufs][xbuf_words] tagged bf16 pairs of finished outputs
     unsigned long long* rp;                   // this rank's rank-partial buffers (tagged, written by all ranks)
     unsigned long long* const* peer_rp;       // [n_ranks] rank-partial buffers of every rank (device array)
     unsigned long long* const* peer_xkeys;    // [n_ranks] key exchange arrays ([n_ranks][2]) of every rank
     int rank, n_ranks;
-    int64_t qcount_stride;                    // counters per region of qcount
     int64_t buf_words;                        // words per slot buffer
+    int64_t xbuf_words;                       // words per exchange buffer
     int64_t rp_words;                         // words per rank-partial buffer
-    int* qcount;                              // [3][max quads] arrival counters of cut quads: allreduce
-                                              // phases by ordinal parity, then the argmax phase
     int32_t* tokens;
     float* values;
     unsigned long long* keys_out;
@@ -166,17 +168,22 @@ __device__ __forceinline__ uint32_t phase_tag(uint32_t tag0, int p) {
     return t + 1u;
 }
 
-// Slots of a phase live in buffer p mod 3: plain fp32 partials, float index of (quad q, source
-// CTA c, row 0).
-__device__ __forceinline__ int64_t slot_f(const DecodeArgs& a, const PhaseDev& P, int p, int q, int c) {
-    return (int64_t)(p % kSlotBufs) * a.buf_words * 2 + (int64_t)q * P.ks * 64 + (int64_t)c * 64;
+// Slots of a phase live in buffer p mod 3: tagged fp32 partials, word index of (quad q, source CTA
+// offset c = cta - cf, row 0).
+__device__ __forceinline__ int64_t slot_w(const DecodeArgs& a, const PhaseDev& P, int p, int q, int c) {
+    return (int64_t)(p % kBufs) * a.buf_words + ((int64_t)q * P.ks + c) * 64;
 }
 
-// Rank partials of the allreduce phase with ordinal ar: word index of (quad q, rank r, row 0). The
-// buffers rotate over allreduce ordinals: a rank writes buffer j mod 3 again only after every rank
-// has sent allreduce j+2, i.e. after every rank has finished reading allreduce j.
-__device__ __forceinline__ int64_t rp_word(const DecodeArgs& a, int ar, int q, int r) {
-    return (int64_t)(ar % kSlotBufs) * a.rp_words + ((int64_t)q * a.n_ranks + r) * 64;
+// Finished bf16 outputs of phase p in exchange buffer p mod 3: word of (output pair n/2).
+__device__ __forceinline__ int64_t xbuf_w(const DecodeArgs& a, int p, int n) {
+    return (int64_t)(p % kBufs) * a.xbuf_words + (n >> 1);
+}
+
+// Rank partials of the allreduce phase with ordinal ar: word index of (quad q, rank r, source CTA
+// offset c, row 0). The buffers rotate over allreduce ordinals: a rank writes buffer j mod 3 again
+// only after every rank has sent allreduce j+2, i.e. after every rank has finished reading allreduce j.
+__device__ __forceinline__ int64_t rp_word(const DecodeArgs& a, const PhaseDev& P, int ar, int q, int r, int c) {
+    return (int64_t)(ar % kBufs) * a.rp_words + (((int64_t)q * a.n_ranks + r) * P.ks + c) * 64;
 }
 
 // Warp w owns the contiguous units [wstart(w), wstart(w + 1)) of its CTA's n units of a phase
@@ -250,12 +257,10 @@ struct Pre {
 struct CtaShared {
     unsigned long long bars[kWarps][kStages];
     float wss[kWarps];
-    float rs, rs_prev;
+    float rs;
     uint32_t tag0;
     int qcnt[kMaxCtaQuads];   // arrivals per quad of the CTA's range (reset by the last arriver)
-    int2 cut[kMaxXQuads];     // per producer quad of x: (first slot float, slot count)
     int warps_finished;
-    int wb_claim;
     unsigned long long best;
 };
 
@@ -283,120 +288,77 @@ __device__ __forceinline__ void spin_until(const unsigned int* ctr, unsigned int
     }
 }
 
-// Arrival of this CTA's finishing warp at a quad cut between CTAs (its slot row already stored):
-// the warp sync orders the lanes' slot stores before lane 0's gpu-scope release on the counter;
-// the last arriver's acquire makes every other CTA's slot rows visible to its lanes.
-__device__ __forceinline__ bool arrive_last(int* cnt, int last_value) {
-    __syncwarp();
-    int last = 0;
-    if ((threadIdx.x & 31) == 0)
-        last = atom_add_acq_rel(reinterpret_cast<unsigned int*>(cnt), 1u) == (unsigned int)last_value;
-    last = __shfl_sync(0xffffffffu, last, 0);
-    __syncwarp();
-    return last != 0;
-}
-
-__device__ __forceinline__ void ld_slot2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+__device__ __forceinline__ void ld_relaxed2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
     asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
-// Sums of 4 rows of a quad over its slots, s = slot[0] + slot[1] + ... in source order; every
-// reader of a quad (x staging in every CTA, the write-back to y) goes through the same function,
-// so all of them see the same bits. Single-rank phases: plain fp32 slots (complete once the
-// phase's completion counter says so), up to four in flight.
-__device__ __forceinline__ float4 sum_slots4(const float* base, int nc) {
-    float4 s = __ldcg(reinterpret_cast<const float4*>(base));
-    for (int c = 1; c < nc; c += 4) {
-        float4 t[4];
+__device__ __forceinline__ unsigned long long ld_relaxed(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_relaxed(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long tagged(float v, uint32_t tag) {
+    return (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
+}
+
+// The finisher's sum over n tagged source rows of a quad (rows lane and lane + 32 of each, row
+// stride 64 words), in source order after `init` (when has_init), polling until every word carries
+// `tag`: the sources are other CTAs' (and ranks') partials, stored on their own schedule. Bounded:
+// a wait that gives up records code 35 and returns what it has.
+__device__ __noinline__ float2 poll_sum(const unsigned long long* base, int n, uint32_t tag, float2 init,
+                                        bool has_init, int* err) {
+    const int lane = threadIdx.x & 31;
+    float2 s = init;
+    bool have = has_init;
+    const long long t0 = clock64();
+    for (int i0 = 0; i0 < n; i0 += 4) {
+        unsigned long long w[4][2];
+        for (;;) {
+            bool ok = true;
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-            t[e] = c + e < nc ? __ldcg(reinterpret_cast<const float4*>(base + (size_t)(c + e) * 64))
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-            if (c + e < nc) {
-                s.x += t[e].x;
-                s.y += t[e].y;
-                s.z += t[e].z;
-                s.w += t[e].w;
+            for (int e = 0; e < 4; ++e) {
+                if (i0 + e < n) {
+                    const unsigned long long* src = base + (int64_t)(i0 + e) * 64;
+                    w[e][0] = ld_relaxed(src + lane);
+                    w[e][1] = ld_relaxed(src + lane + 32);
+                    ok &= (uint32_t)(w[e][0] >> 32) == tag && (uint32_t)(w[e][1] >> 32) == tag;
+                }
             }
+            if (__all_sync(0xffffffffu, ok)) break;
+            if (*reinterpret_cast<volatile int*>(err) != 0) return s;
+            if (clock64() - t0 > kSpinLimit) {
+                atomicCAS(err, 0, 35);
+                return s;
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            if (i0 + e < n) {
+                const float v0 = __uint_as_float((uint32_t)w[e][0]), v1 = __uint_as_float((uint32_t)w[e][1]);
+                if (have) {
+                    s.x += v0;
+                    s.y += v1;
+                } else {
+                    s = make_float2(v0, v1);
+                    have = true;
+                }
+            }
+        }
     }
     return s;
 }
 
-// Allreduce phases: tagged words from every rank, rank-major then CTA order; polls until every
-// source word carries `tag` (bounded), since a peer's partials arrive on their own schedule.
-__device__ __noinline__ float4 sum_tagged4(const unsigned long long* q0, int ranks, int ks, int nc, uint32_t tag,
-                                           int* err) {
-    const int n = ranks * nc;
-    const long long t0 = clock64();
-    for (;;) {
-        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-        bool ok = true;
-        for (int i0 = 0; i0 < n; i0 += 4) {
-            unsigned long long w[4][4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int i = i0 + e;
-                if (i < n) {
-                    const int r = i / nc, c = i - r * nc;
-                    const unsigned long long* src = q0 + ((int64_t)r * ks + c) * 64;
-                    ld_slot2(src, w[e][0], w[e][1]);
-                    ld_slot2(src + 2, w[e][2], w[e][3]);
-                }
-            }
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int i = i0 + e;
-                if (i < n) {
-                    ok &= (uint32_t)(w[e][0] >> 32) == tag && (uint32_t)(w[e][1] >> 32) == tag &&
-                          (uint32_t)(w[e][2] >> 32) == tag && (uint32_t)(w[e][3] >> 32) == tag;
-                    const float v0 = __uint_as_float((uint32_t)w[e][0]), v1 = __uint_as_float((uint32_t)w[e][1]);
-                    const float v2 = __uint_as_float((uint32_t)w[e][2]), v3 = __uint_as_float((uint32_t)w[e][3]);
-                    if (i == 0) {
-                        s = make_float4(v0, v1, v2, v3);
-                    } else {
-                        s.x += v0;
-                        s.y += v1;
-                        s.z += v2;
-                        s.w += v3;
-                    }
-                }
-            }
-        }
-        if (ok) return s;
-        if (*reinterpret_cast<volatile int*>(err) != 0) return s;
-        if (clock64() - t0 > kSpinLimit) {
-            atomicCAS(err, 0, 35);
-            return s;
-        }
-        __nanosleep(32);
-    }
-}
-
-// After an allreduce phase: this rank's partial of quad q (its CTAs' slots summed in CTA order,
-// four rows per lane of 16 lanes) stored, tagged, into the rank-partial buffer of every rank.
-__device__ __noinline__ void send_rank_partial(unsigned long long* const* peers, int n_ranks, int64_t w0,
-                                               const float* slots, int nc, uint32_t tag) {
+// A CTA's partial of a quad of an allreduce phase, tagged, into its slot row of every rank's
+// rank-partial buffer (NVLink peer stores for the other ranks).
+__device__ __forceinline__ void send_partial(unsigned long long* const* peers, int n_ranks, int64_t w0, float v0,
+                                             float v1, uint32_t tag) {
     const int lane = threadIdx.x & 31;
-    if (lane >= 16) return;
-    const float4 s = sum_slots4(slots + lane * 4, nc);
-    const unsigned long long t = (unsigned long long)tag << 32;
-    const unsigned long long e0 = __float_as_uint(s.x) | t, e1 = __float_as_uint(s.y) | t;
-    const unsigned long long e2 = __float_as_uint(s.z) | t, e3 = __float_as_uint(s.w) | t;
-    for (int r = 0; r < n_ranks; ++r) {
-        unsigned long long* dst = peers[r] + w0 + lane * 4;
-        asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(e0), "l"(e1) : "memory");
-        asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + 2), "l"(e2), "l"(e3) : "memory");
-    }
-}
-
-// The same for a quad that one CTA covers whole: its partial is in registers, rows lane, lane + 32.
-__device__ __noinline__ void send_rank_partial_regs(unsigned long long* const* peers, int n_ranks, int64_t w0,
-                                                    float v0, float v1, uint32_t tag) {
-    const int lane = threadIdx.x & 31;
-    const unsigned long long t = (unsigned long long)tag << 32;
-    const unsigned long long e0 = __float_as_uint(v0) | t, e1 = __float_as_uint(v1) | t;
+    const unsigned long long e0 = tagged(v0, tag), e1 = tagged(v1, tag);
     for (int r = 0; r < n_ranks; ++r) {
         unsigned long long* dst = peers[r] + w0;
         asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + lane), "l"(e0) : "memory");
@@ -404,16 +366,32 @@ __device__ __noinline__ void send_rank_partial_regs(unsigned long long* const* p
     }
 }
 
-__device__ __forceinline__ uint2 finish4(float4 s, float rs) {
-    return make_uint2((uint32_t)f32_to_bf16_bits(__fmul_rn(s.x, rs)) | ((uint32_t)f32_to_bf16_bits(__fmul_rn(s.y, rs)) << 16),
-                      (uint32_t)f32_to_bf16_bits(__fmul_rn(s.z, rs)) | ((uint32_t)f32_to_bf16_bits(__fmul_rn(s.w, rs)) << 16));
-}
-
-__device__ __forceinline__ void store_y(void* y, uint32_t flags, int n, float v) {
-    if (flags & G4Q_QMM_OUT_F32)
-        reinterpret_cast<float*>(y)[n] = v;
-    else
-        reinterpret_cast<uint16_t*>(y)[n] = f32_to_bf16_bits(v);
+// Finished rows lane and lane + 32 of quad q of phase p (unscaled sums v0, v1): y = v * rs, and for a
+// phase the next one reads, the bf16 values as tagged pairs in the exchange buffer (even lanes store
+// the pairs (lane, lane + 1) and (lane + 32, lane + 33)).
+__device__ __forceinline__ void publish(const DecodeArgs& a, const PhaseDev& P, int p, int q, float v0, float v1,
+                                        float rs, uint32_t tag) {
+    const int lane = threadIdx.x & 31;
+    const float f0 = __fmul_rn(v0, rs), f1 = __fmul_rn(v1, rs);
+    if (P.flags & G4Q_QMM_OUT_F32) {
+        float* y = reinterpret_cast<float*>(P.y) + (int64_t)q * 64;
+        y[lane] = f0;
+        y[lane + 32] = f1;
+        return;
+    }
+    const uint32_t b0 = f32_to_bf16_bits(f0), b1 = f32_to_bf16_bits(f1);
+    uint16_t* y = reinterpret_cast<uint16_t*>(P.y) + (int64_t)q * 64;
+    y[lane] = (uint16_t)b0;
+    y[lane + 32] = (uint16_t)b1;
+    if (P.xout) {
+        const uint32_t n0 = __shfl_down_sync(0xffffffffu, b0, 1), n1 = __shfl_down_sync(0xffffffffu, b1, 1);
+        if ((lane & 1) == 0) {
+            const unsigned long long t = (unsigned long long)tag << 32;
+            unsigned long long* xw = a.xbuf + xbuf_w(a, p, q * 64);
+            st_relaxed(xw + (lane >> 1), (unsigned long long)(b0 | (n0 << 16)) | t);
+            st_relaxed(xw + 16 + (lane >> 1), (unsigned long long)(b1 | (n1 << 16)) | t);
+        }
+    }
 }
 
 // argmax phase: fold one finished output into the running key
@@ -430,10 +408,14 @@ __device__ __forceinline__ unsigned long long fold_logit(uint16_t* logits, float
 // Park this warp's partial of quad q. A warp keeps the partial of the first quad of its range in
 // red[warp][0] (the previous warp may need it) and everything else in red[warp][1] (only the last
 // quad of the range is read by another warp, and it comes last). The last contributing warp sums
-// the partials in warp order, then: argmax phase, whole quad: folds the logits into the running
-// key; otherwise leaves the CTA's unscaled partial in its slot (tagged, on every rank, for an
-// allreduce phase) and, for a whole single-rank quad, stores the finished values to y. No warp
-// ever waits.
+// the partials in warp order, which gives the CTA's partial of the quad, and then:
+//  * allreduce phase: stores it, tagged, into every rank's rank-partial buffer; the quad's finisher
+//    CTA (the first CTA of the quad) then sums all ranks' partials and publishes the quad;
+//  * a quad whole in this CTA: publishes it (argmax phase: folds the logits into the running key);
+//  * a cut quad: a CTA other than the quad's first stores its tagged partial in its slot; the first
+//    CTA, whose share of the quad is the last of its range, polls the others' slots, sums them in CTA
+//    order after its own and publishes (or folds) the quad.
+// No warp waits here except a finisher, for partials that are (or are about to be) stored.
 template <bool kTP>
 __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int p, CtaShared& sh, float* red, int q,
                                      int first_q, int cs, int ce, int cta, int C, const float (&acc)[4][4],
@@ -472,51 +454,32 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
         v[h] = s;
     }
     const bool whole = cs <= q * G && ce >= (q + 1) * G;
-    const uint32_t fl = P.flags;
-    const bool argmax = (fl & G4Q_PHASE_ARGMAX) != 0;
-    if (whole && argmax) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-            best = fold_logit(a.logits, a.softcap, a.row_offset, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs), best);
-    } else {
-        int cf, cl;
-        quad_ctas(P, q, C, cf, cl);
-        float* base = reinterpret_cast<float*>(a.slots) + slot_f(a, P, p, q, 0);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) base[(size_t)(cta - cf) * 64 + lane + 32 * h] = v[h];
-        if (kTP && P.src_ranks > 1) {
-            // allreduce phase: once this rank's partial of the quad is complete, send it to every rank
-            // (a whole quad straight from registers; a cut one by the last of its CTAs to arrive)
-            const uint32_t tag = phase_tag(sh.tag0, p);
-            const int64_t w0 = rp_word(a, P.ar, q, a.rank);
-            if (cf == cl) {
-                send_rank_partial_regs(a.peer_rp, a.n_ranks, w0, v[0], v[1], tag);
-            } else {
-                int* cnt = a.qcount + (int64_t)(P.ar & 1) * a.qcount_stride + q;
-                if (arrive_last(cnt, cl - cf)) {
-                    send_rank_partial(a.peer_rp, a.n_ranks, w0, base, cl - cf + 1, tag);
-                    __syncwarp();
-                    if (lane == 0) atomicExch(cnt, 0);
-                }
-            }
-        } else if (whole) {   // an allreduce phase's y needs every rank: written back later
-#pragma unroll
-            for (int h = 0; h < 2; ++h) store_y(P.y, fl, q * 64 + lane + 32 * h, __fmul_rn(v[h], sh.rs));
-        } else if (argmax) {   // the logits are needed now: the last contributing CTA finishes the quad
-            if (arrive_last(a.qcount + 2 * a.qcount_stride + q, cl - cf)) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    float s = __ldcg(base + lane + 32 * h);
-                    for (int c = 1; c <= cl - cf; ++c) s += __ldcg(base + (size_t)c * 64 + lane + 32 * h);
-                    best = fold_logit(a.logits, a.softcap, a.row_offset, q * 64 + lane + 32 * h,
-                                      __fmul_rn(s, sh.rs), best);
-                }
-                __syncwarp();
-                if (lane == 0) atomicExch(a.qcount + 2 * a.qcount_stride + q, 0);
-            }
+    const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
+    const uint32_t tag = phase_tag(sh.tag0, p);
+    int cf, cl;
+    quad_ctas(P, q, C, cf, cl);
+    float2 f = make_float2(v[0], v[1]);
+    if (kTP && P.src_ranks > 1) {
+        send_partial(a.peer_rp, a.n_ranks, rp_word(a, P, P.ar, q, a.rank, cta - cf), v[0], v[1], tag);
+        if (cta != cf) return;
+        const int nc = cl - cf + 1;
+        for (int r = 0; r < a.n_ranks; ++r)   // rank-major, then CTA order: the same bits on every rank
+            f = poll_sum(a.rp + rp_word(a, P, P.ar, q, r, 0), nc, tag, f, r > 0, a.err);
+    } else if (!whole) {
+        if (cta != cf) {
+            unsigned long long* sl = a.slots + slot_w(a, P, p, q, cta - cf);
+            st_relaxed(sl + lane, tagged(v[0], tag));
+            st_relaxed(sl + lane + 32, tagged(v[1], tag));
+            return;
         }
+        f = poll_sum(a.slots + slot_w(a, P, p, q, 1), cl - cf, tag, f, true, a.err);
     }
-    __syncwarp();
+    if (argmax) {
+        best = fold_logit(a.logits, a.softcap, a.row_offset, q * 64 + lane, __fmul_rn(f.x, sh.rs), best);
+        best = fold_logit(a.logits, a.softcap, a.row_offset, q * 64 + lane + 32, __fmul_rn(f.y, sh.rs), best);
+    } else {
+        publish(a, P, p, q, f.x, f.y, sh.rs, tag);
+    }
 }
 
 // Shared-memory order of x: inside each 64-wide group, lane t's B-fragment words for the four k16
@@ -527,13 +490,18 @@ __device__ __forceinline__ int xperm(int w) {
     return (w & ~31) | ((r & 3) << 3) | (((w >> 3) & 3) << 1) | (r >> 2);
 }
 
-// Stage the x of phase P (K bf16 values) into shared memory; returns this thread's sum of squares.
-// From an external input: plain 16-byte copies. From the previous phase's output: every thread
-// owns 4-row cells (16 per producer quad) and sums the cell's tagged slots (polling until the
-// producers have written them); two cells are in flight per thread.
-template <bool kTP>
-__device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P, uint32_t* xs, const int2* cut, int C,
-                                         float rs_prev, uint32_t tag0, bool rms) {
+// Stage the x of phase P (K bf16 values) into shared memory; returns this thread's sum of squares
+// (every CTA maps values to threads the same way, so every CTA derives the same RMS scale).
+// From an external input: plain 16-byte copies. From the previous phase's output: the finished
+// bf16 pairs of its exchange buffer, polled until they carry that phase's tag; every load of a
+// thread is in flight at once, and only words still missing are loaded again.
+constexpr int kMaxStageLoads = 8;   // 16-byte exchange loads per thread: K <= 4 * 8 * 640 = 20480
+
+__device__ __noinline__ float stage_xbuf(const unsigned long long* src, int K, uint32_t tag, uint32_t* xs, bool rms,
+                                         int* err);
+
+__device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P, uint32_t* xs, uint32_t tag0,
+                                         bool rms) {
     float ss = 0.0f;
     auto acc_sq = [&](uint32_t w) {
         const float lo = bf16_bits_to_f32(w & 0xffffu), hi = bf16_bits_to_f32(w >> 16);
@@ -556,110 +524,67 @@ __device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P,
         }
         return ss;
     }
-    const PhaseDev& S = a.ph[P.src];
-    const int q0 = P.src_col >> 6;
-    const int cells = P.K / 4;
-    (void)q0;
-    auto put = [&](int idx, float4 s) {
-        const uint2 w = finish4(s, rs_prev);
-        xs[xperm(2 * idx)] = w.x;
-        xs[xperm(2 * idx + 1)] = w.y;
-        if (rms) {
-            acc_sq(w.x);
-            acc_sq(w.y);
-        }
+    return stage_xbuf(a.xbuf + xbuf_w(a, P.src, P.src_col), P.K, phase_tag(tag0, P.src), xs, rms, a.err);
+}
+
+// Staging from the exchange buffer (out of line: its loads in flight need registers the streaming
+// loop does not have to keep free).
+__device__ __noinline__ float stage_xbuf(const unsigned long long* src, int K, uint32_t tag, uint32_t* xs, bool rms,
+                                         int* err) {
+    float ss = 0.0f;
+    auto acc_sq = [&](uint32_t w) {
+        const float lo = bf16_bits_to_f32(w & 0xffffu), hi = bf16_bits_to_f32(w >> 16);
+        ss = __fadd_rn(ss, __fmul_rn(lo, lo));
+        ss = __fadd_rn(ss, __fmul_rn(hi, hi));
     };
-    if constexpr (kTP) {
-        if (S.src_ranks > 1) {   // rank partials of every rank, tagged: poll until all have arrived
-            const uint32_t tag = phase_tag(tag0, P.src);
-            for (int idx = threadIdx.x; idx < cells; idx += kThreads) {
-                const int q = q0 + (idx >> 4);
-                put(idx, sum_tagged4(a.rp + rp_word(a, S.ar, q, 0) + (idx & 15) * 4, a.n_ranks, 1, 1, tag, a.err));
-            }
-            return ss;
+    const int nl = K / 4;   // 16-byte loads: two tagged words, four values
+    uint32_t w[kMaxStageLoads][2];   // the value halves of the words (the tags are checked on arrival)
+    uint32_t missing = 0;
+#pragma unroll
+    for (int j = 0; j < kMaxStageLoads; ++j) {
+        const int i = threadIdx.x + j * kThreads;
+        if (i < nl) {
+            unsigned long long u0, u1;
+            ld_relaxed2(src + 2 * i, u0, u1);
+            w[j][0] = (uint32_t)u0;
+            w[j][1] = (uint32_t)u1;
+            if ((uint32_t)(u0 >> 32) != tag || (uint32_t)(u1 >> 32) != tag) missing |= 1u << j;
         }
     }
-    // single-rank partials: two cells per thread with up to four slots each in flight at once,
-    // summed in slot order exactly as sum_slots4 does
-    const float* sl = reinterpret_cast<const float*>(a.slots);
-    constexpr int kB = 2;
-    for (int e0 = threadIdx.x; e0 < cells; e0 += kB * kThreads) {
-        const float* base[kB];
-        int nc[kB];
+    if (missing) {
+        const long long t0 = clock64();
+        while (missing) {
 #pragma unroll
-        for (int h = 0; h < kB; ++h) {
-            const int idx = e0 + h * kThreads;
-            nc[h] = 0;
-            base[h] = sl;
-            if (idx < cells) {
-                const int2 ct = cut[idx >> 4];
-                nc[h] = ct.y;
-                base[h] = sl + ct.x + (idx & 15) * 4;
+            for (int j = 0; j < kMaxStageLoads; ++j) {
+                if (missing & (1u << j)) {
+                    const int i = threadIdx.x + j * kThreads;
+                    unsigned long long u0, u1;
+                    ld_relaxed2(src + 2 * i, u0, u1);
+                    w[j][0] = (uint32_t)u0;
+                    w[j][1] = (uint32_t)u1;
+                    if ((uint32_t)(u0 >> 32) == tag && (uint32_t)(u1 >> 32) == tag) missing &= ~(1u << j);
+                }
+            }
+            if (missing && (*reinterpret_cast<volatile int*>(err) != 0 || clock64() - t0 > kSpinLimit)) {
+                atomicCAS(err, 0, 37);
+                break;
             }
         }
-        float4 l[kB][4];
+    }
 #pragma unroll
-        for (int h = 0; h < kB; ++h)
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-                l[h][c] = c < nc[h] ? __ldcg(reinterpret_cast<const float4*>(base[h] + c * 64))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int h = 0; h < kB; ++h) {
-            if (nc[h] == 0) continue;
-            float4 t = l[h][0];
-#pragma unroll
-            for (int c = 1; c < 4; ++c)
-                if (c < nc[h]) {
-                    t.x += l[h][c].x;
-                    t.y += l[h][c].y;
-                    t.z += l[h][c].z;
-                    t.w += l[h][c].w;
-                }
-            for (int c = 4; c < nc[h]; ++c) {
-                const float4 u = __ldcg(reinterpret_cast<const float4*>(base[h] + c * 64));
-                t.x += u.x;
-                t.y += u.y;
-                t.z += u.z;
-                t.w += u.w;
+    for (int j = 0; j < kMaxStageLoads; ++j) {
+        const int i = threadIdx.x + j * kThreads;
+        if (i < nl) {
+            const uint32_t lo = w[j][0], hi = w[j][1];
+            xs[xperm(2 * i)] = lo;
+            xs[xperm(2 * i + 1)] = hi;
+            if (rms) {
+                acc_sq(lo);
+                acc_sq(hi);
             }
-            put(e0 + h * kThreads, t);
         }
     }
     return ss;
-}
-
-// One warp writes the quads of phase pp that no single CTA finished (cut across CTAs, or summed
-// over ranks) back to y; quad q goes to CTA q mod C.
-template <bool kTP>
-__device__ __forceinline__ void write_back_warp(const DecodeArgs& a, int pp, int cta, int C, float rs_prev, uint32_t tag0) {
-    const PhaseDev& Q = a.ph[pp];
-    const uint32_t fl = Q.flags;
-    if (fl & G4Q_PHASE_ARGMAX) return;
-    const int lane = threadIdx.x & 31;
-    const uint32_t tag = phase_tag(tag0, pp);
-    for (int q = cta; q < Q.Q; q += C) {
-        int cf, cl;
-        quad_ctas(Q, q, C, cf, cl);
-        if ((cf == cl && Q.src_ranks == 1) || lane >= 16) continue;
-        float4 s;
-        if constexpr (kTP) {
-            if (Q.src_ranks > 1)
-                s = sum_tagged4(a.rp + rp_word(a, Q.ar, q, 0) + lane * 4, a.n_ranks, 1, 1, tag, a.err);
-        }
-        if (!kTP || Q.src_ranks == 1)
-            s = sum_slots4(reinterpret_cast<const float*>(a.slots) + slot_f(a, Q, pp, q, 0) + lane * 4, cl - cf + 1);
-        const int n = q * 64 + lane * 4;
-        if (fl & G4Q_QMM_OUT_F32) {
-            float* y = reinterpret_cast<float*>(Q.y) + n;
-            y[0] = __fmul_rn(s.x, rs_prev);
-            y[1] = __fmul_rn(s.y, rs_prev);
-            y[2] = __fmul_rn(s.z, rs_prev);
-            y[3] = __fmul_rn(s.w, rs_prev);
-        } else {
-            *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(Q.y) + n) = finish4(s, rs_prev);
-        }
-    }
 }
 
 // End of a step on a tensor-parallel plan: every rank's last CTA posts its argmax key to every
@@ -716,7 +641,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     if (threadIdx.x == 0) {
         for (int i = 0; i < kMaxCtaQuads; ++i) sh.qcnt[i] = 0;
         sh.warps_finished = 0;
-        sh.wb_claim = 0;
         sh.best = 0ull;
         sh.rs = 1.0f;
         const unsigned long long e = (unsigned long long)*reinterpret_cast<volatile unsigned int*>(a.run) *
@@ -744,27 +668,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             tr = a.trace + ((size_t)cta * a.n_phases + p) * kTraceWords;
             if (threadIdx.x == 0) tr[0] = global_ns();
         }
-        if (P.src >= 0) {
-            const PhaseDev& S = a.ph[P.src];
-            for (int j = threadIdx.x; j < P.K / 64; j += kThreads) {
-                const int q = (P.src_col >> 6) + j;
-                int cf, cl;
-                quad_ctas(S, q, C, cf, cl);
-                sh.cut[j] = make_int2((int)slot_f(a, S, P.src, q, 0), cl - cf + 1);
-            }
+        if (P.sync_before) {   // x is not the previous phase's output: a grid barrier first
+            if (threadIdx.x == 0) spin_until(a.done + (p - 1), (unsigned)C, a.err);
+            __syncthreads();
         }
-        if (threadIdx.x == 0) {
-            if (P.sync_before) spin_until(a.done + (p - 1), (unsigned)C, a.err);
-            sh.rs_prev = sh.rs;
-            sh.wb_claim = 0;
-            if constexpr (kTrace) tr[1] = global_ns();
+        if constexpr (kTrace) {
+            if (threadIdx.x == 0) tr[1] = global_ns();
         }
-        __syncthreads();
-        const float rs_prev = sh.rs_prev;
         const uint32_t tag0 = sh.tag0;
-        // ---- stage x (polls the producers' slots) and its RMS scale
+        // ---- stage x (polls the producer's exchange words) and its RMS scale
         const bool rms = (P.flags & G4Q_QMM_RMS_SCALE) != 0;
-        float ss = stage_x<kTP>(a, P, xs, sh.cut, C, rs_prev, tag0, rms);
+        float ss = stage_x(a, P, xs, tag0, rms);
         if (p == 0) {   // first weight loads only now: the x loads above are not queued behind them
             for (int s = 0; s < kStages && pre.p < a.n_phases; ++s) {
                 if (lane == 0) pre.issue(ring_s + s * kUnitBytes, bar0 + 8 * s);
@@ -855,13 +769,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         if constexpr (kTrace) {
             if (lane == 0) tr[3 + warp] = global_ns();
         }
-        // ---- the first warp of the CTA to run out of units writes phase p-1's unfinished quads to y
-        if (p > 0) {
-            int claim = 0;
-            if (lane == 0) claim = atomicAdd(&sh.wb_claim, 1) == 0;
-            claim = __shfl_sync(0xffffffffu, claim, 0);
-            if (claim) write_back_warp<kTP>(a, p - 1, cta, C, rs_prev, tag0);
-        }
         const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
         if (argmax) {
             unsigned long long kk = best;
@@ -892,16 +799,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             }
         }
     }
-    // ---- a plan that ends with a regular phase: once every CTA has left its partials, finish the
-    //      quads no single CTA finished
-    const int last = a.n_phases - 1;
-    if (!(a.ph[last].flags & G4Q_PHASE_ARGMAX)) {
-        __syncthreads();
-        if (threadIdx.x == 0) spin_until(a.done + last, (unsigned)C, a.err);
-        __syncthreads();
-        if (threadIdx.x < 32) write_back_warp<kTP>(a, last, cta, C, sh.rs, sh.tag0);
-    }
     // ---- the last CTA out publishes the step's key, resets the counters and advances the tag base
+    const int last = a.n_phases - 1;
     __syncthreads();
     if (threadIdx.x == 0) {
         const unsigned int prev = atom_add_acq_rel(a.exit_count, 1u);
@@ -937,8 +836,8 @@ struct DecodePlan {
     unsigned long long* d_rp = nullptr;      // rank partials (tensor parallel), written by every rank
     int64_t rp_words = 0;
     unsigned long long* d_xkeys = nullptr;   // [kMaxRanks][2]
-    int* d_qcount = nullptr;
-    int64_t max_q = 0;
+    unsigned long long* d_xbuf = nullptr;    // [kBufs][xbuf_words] exchange buffers
+    int64_t xbuf_words = 0;
     unsigned long long** d_peers = nullptr;   // [2][kMaxRanks]: slot buffers, key arrays of every rank
     unsigned long long* peer_rp[kMaxRanks] = {};
     unsigned long long* peer_xkeys[kMaxRanks] = {};
@@ -954,7 +853,7 @@ static void free_plan_memory(DecodePlan* plan) {
     cudaFree(plan->d_slots);
     cudaFree(plan->d_rp);
     cudaFree(plan->d_xkeys);
-    cudaFree(plan->d_qcount);
+    cudaFree(plan->d_xbuf);
     cudaFree(plan->d_peers);
 }
 
@@ -978,7 +877,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     const int sms = device_sm_count();
     std::vector<PhaseDev> ph(n);
     std::vector<std::vector<char>> producers(n);   // which producer CTAs each phase's x window needs
-    int kmax = 0, max_q = 0;
+    int kmax = 0;
     for (int i = 0; i < n; ++i) {
         const Weight* w = reinterpret_cast<const Weight*>(phases[i].weight);
         const std::string tag = "phase " + std::to_string(i) + ": ";
@@ -1018,6 +917,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
         d.ar = -1;
         d.sync_before = 0;
         d.need_done = (fl & G4Q_PHASE_ARGMAX) ? 1 : 0;
+        d.xout = 0;
         if (d.U < sms) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "too small for a full-grid decode plan");
         if (d.G > kMaxXQuads) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "K above 16384");
         if ((uint64_t)(d.U + 1) * (uint64_t)sms >= (1ull << 32) || (uint64_t)w->N * (uint64_t)w->K / 2 >= (1ull << 32))
@@ -1054,29 +954,36 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
             for (int64_t c = cf; c <= cl && c < sms; ++c) producers[i][c] = 1;
         }
         if (d.K > kmax) kmax = d.K;
-        if (d.Q > max_q) max_q = d.Q;
     }
-    // Every phase waits until every CTA of this rank has finished the previous one (one acquire
-    // poll of a counter that each CTA bumps with a release atomic); on one GPU that makes the slot
-    // tags redundant, across ranks they are what says a peer's partials have arrived. Slot buffers
-    // rotate over three phases so that a rank running one phase ahead of another never overwrites
-    // slots the other still reads.
+    // Dataflow: a phase that reads the previous phase's output polls that phase's exchange words (its
+    // finished, tagged bf16 values) and needs no barrier. A phase whose x is anything else (an external
+    // input or an older output) waits for every CTA of this rank to finish the previous phase first.
     auto full = [&](int i) {
         for (int c = 0; c < sms; ++c)
             if (!producers[i][c]) return false;
         return true;
     };
-    // On one GPU every phase waits for the previous one. In a tensor-parallel plan a phase reading an
-    // allreduce output waits for nothing: its x is the rank partials, which carry their phase tag.
     int n_ar = 0;
     for (int i = 0; i < n; ++i)
         if (ph[i].src_ranks > 1) ph[i].ar = n_ar++;
-    for (int i = 1; i < n; ++i)
-        ph[i].sync_before = (n_ranks > 1 && ph[i].src >= 0 && ph[ph[i].src].src_ranks > 1) ? 0 : 1;
-    // local slots of phase i are read until the end of phase i+1 and rewritten by phase i+3: some CTA
-    // barrier must sit at phase i+2 or i+3
-    for (int i = 0; i + 3 < n; ++i)
-        if (!ph[i + 2].sync_before && !ph[i + 3].sync_before) ph[i + 3].sync_before = 1;
+    for (int i = 1; i < n; ++i) {
+        if (ph[i].src >= 0)
+            ph[i - 1].xout = 1;
+        else
+            ph[i].sync_before = 1;
+    }
+    // Buffer rotation: phase i's slots and exchange words (buffer i mod 3) are read during phase i (by
+    // finishers) and while phase i+1 stages x; phase i+3 writes the same buffer. A CTA can only stage
+    // x of a phase j that reads ALL of phase j-1's output after every CTA has finished its share of
+    // phase j-1 (every CTA owns units in every phase), and so after every CTA has staged phase j-1.
+    // So the buffer is free once such a phase j <= i+3 (with j >= i+2) has been staged, or a barrier
+    // sits at i+2 or i+3; otherwise a barrier is placed at phase i+3.
+    for (int i = 0; i + 3 < n; ++i) {
+        bool safe = false;
+        for (int j = i + 2; j <= i + 3; ++j)
+            safe |= ph[j].sync_before || (ph[j].src == j - 1 && full(j));
+        if (!safe) ph[i + 3].sync_before = 1;
+    }
     // Across ranks there is no barrier at all: a rank can only run ahead into the next phase that
     // reads an allreduce phase's output, which needs every rank's partials. So every allreduce phase
     // must feed the phase after it whole, and the step ends with the key exchange.
@@ -1087,15 +994,15 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
                             "phase " + std::to_string(i) + ": the next phase must read all of an allreduce output");
     for (int i = 1; i < n; ++i)
         if (ph[i].sync_before) ph[i - 1].need_done = 1;
-    ph[n - 1].need_done = 1;   // the final write-back (or the argmax publish) waits for the last phase
-    int64_t buf_words = 0;
-    for (int i = 0; i < n; ++i)
-        buf_words = std::max<int64_t>(buf_words, (int64_t)ph[i].Q * ph[i].ks * 32);
-    int64_t rp_words = 1;
-    for (int i = 0; i < n; ++i)
-        if (ph[i].src_ranks > 1) rp_words = std::max<int64_t>(rp_words, (int64_t)ph[i].Q * n_ranks * 64);
-    if ((int64_t)kSlotBufs * buf_words * 2 >= (1ll << 31))
-        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: slot buffers above 2^31 floats");
+    ph[n - 1].need_done = 1;   // the argmax publish (or the plan's end) counts the last phase
+    int64_t buf_words = 64, xbuf_words = 32, rp_words = 64;
+    for (int i = 0; i < n; ++i) {
+        buf_words = std::max<int64_t>(buf_words, (int64_t)ph[i].Q * ph[i].ks * 64);
+        if (ph[i].xout) xbuf_words = std::max<int64_t>(xbuf_words, (int64_t)ph[i].N / 2);
+        if (ph[i].src_ranks > 1) rp_words = std::max<int64_t>(rp_words, (int64_t)ph[i].Q * n_ranks * ph[i].ks * 64);
+    }
+    if ((int64_t)kBufs * std::max(buf_words, rp_words) >= (1ll << 31))
+        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: slot buffers above 2^31 words");
     auto* plan = new DecodePlan();
     plan->device = dev;
     plan->n_phases = n;
@@ -1104,7 +1011,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     plan->n_ranks = n_ranks;
     plan->buf_words = buf_words;
     plan->rp_words = rp_words;
-    plan->max_q = max_q;
+    plan->xbuf_words = xbuf_words;
     plan->smem = (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4 + (size_t)(kmax + 8) * 2;
     const void* kfn = n_ranks > 1 ? reinterpret_cast<const void*>(decode_kernel<true>)
                                   : reinterpret_cast<const void*>(decode_kernel<false>);
@@ -1114,22 +1021,22 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
         delete plan;
         throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: K too large for shared memory");
     }
-    const size_t slot_bytes = sizeof(unsigned long long) * kSlotBufs * (size_t)buf_words;
+    const size_t slot_bytes = sizeof(unsigned long long) * kBufs * (size_t)buf_words;
     cudaError_t e = cudaMalloc(&plan->d_ph, sizeof(PhaseDev) * n);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_done, sizeof(unsigned int) * (n + 2));
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_key, sizeof(unsigned long long));
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_slots, slot_bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&plan->d_rp, sizeof(unsigned long long) * kSlotBufs * (size_t)rp_words);
-    if (e == cudaSuccess) e = cudaMemset(plan->d_rp, 0, sizeof(unsigned long long) * kSlotBufs * (size_t)rp_words);
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_rp, sizeof(unsigned long long) * kBufs * (size_t)rp_words);
+    if (e == cudaSuccess) e = cudaMemset(plan->d_rp, 0, sizeof(unsigned long long) * kBufs * (size_t)rp_words);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_xkeys, sizeof(unsigned long long) * 2 * kMaxRanks);
-    if (e == cudaSuccess) e = cudaMalloc(&plan->d_qcount, sizeof(int) * 3 * (size_t)max_q);
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_xbuf, sizeof(unsigned long long) * kBufs * (size_t)xbuf_words);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_peers, sizeof(void*) * 2 * kMaxRanks);
     if (e == cudaSuccess) e = cudaMemcpy(plan->d_ph, ph.data(), sizeof(PhaseDev) * n, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(plan->d_done, 0, sizeof(unsigned int) * (n + 2));
     if (e == cudaSuccess) e = cudaMemset(plan->d_key, 0, sizeof(unsigned long long));
     if (e == cudaSuccess) e = cudaMemset(plan->d_slots, 0, slot_bytes);
     if (e == cudaSuccess) e = cudaMemset(plan->d_xkeys, 0, sizeof(unsigned long long) * 2 * kMaxRanks);
-    if (e == cudaSuccess) e = cudaMemset(plan->d_qcount, 0, sizeof(int) * 3 * (size_t)max_q);
+    if (e == cudaSuccess) e = cudaMemset(plan->d_xbuf, 0, sizeof(unsigned long long) * kBufs * (size_t)xbuf_words);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         free_plan_memory(plan);
@@ -1161,7 +1068,7 @@ static DecodePlan* checked_plan(void* h) {
 void decode_plan_buffers(void* h, void** slots, uint64_t* slot_bytes, void** xkeys, uint64_t* xkey_bytes) {
     DecodePlan* plan = checked_plan(h);
     if (slots) *slots = plan->d_rp;
-    if (slot_bytes) *slot_bytes = sizeof(unsigned long long) * kSlotBufs * (uint64_t)plan->rp_words;
+    if (slot_bytes) *slot_bytes = sizeof(unsigned long long) * kBufs * (uint64_t)plan->rp_words;
     if (xkeys) *xkeys = plan->d_xkeys;
     if (xkey_bytes) *xkey_bytes = sizeof(unsigned long long) * 2 * kMaxRanks;
 }
@@ -1220,8 +1127,8 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     a.rank = plan->rank;
     a.n_ranks = plan->n_ranks;
     a.buf_words = plan->buf_words;
-    a.qcount = plan->d_qcount;
-    a.qcount_stride = plan->max_q;
+    a.xbuf = plan->d_xbuf;
+    a.xbuf_words = plan->xbuf_words;
     a.tokens = tokens;
     a.values = values;
     a.keys_out = reinterpret_cast<unsigned long long*>(keys);

@@ -55,6 +55,8 @@ def lib():
         L = ctypes.CDLL(str(LIB_PATH))
         P = ctypes.c_void_p
         i64, i32, u64 = ctypes.c_int64, ctypes.c_int, ctypes.c_uint64
+        L.g4o_set_threads.restype = None
+        L.g4o_set_threads.argtypes = [i32]
         L.g4o_rand.restype = u64
         L.g4o_rand.argtypes = [u64, u64]
         L.g4o_matrix_seed.restype = u64
@@ -201,6 +203,11 @@ def qmm(x, w, s, b, bits: int = 4, group_size: int = 64, chain: int = CHAIN_R2, 
     _check(lib().g4o_qmm(_p(x), M, _p(w), _p(s), _p(b), N, K, bits, group_size, chain,
                          None if rs is None else _p(rs), _p(ye), _p(yb)), "qmm")
     return ye, yb
+
+
+def set_threads(n: int) -> None:
+    """OpenMP threads of the oracle's loops (n <= 0: the runtime's default)."""
+    lib().g4o_set_threads(int(n))
 
 
 def qmm_f32(x, w, s, b, group_size: int = 64, chain: int = CHAIN_R2, threads: int = 0):

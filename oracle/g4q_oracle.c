@@ -216,6 +216,16 @@ int g4o_qmm(const uint16_t* x, int64_t M, const uint32_t* w, const uint16_t* sca
     return G4O_OK;
 }
 
+/* Threads of the OpenMP loops below (the checker's own setting; a launcher such as torchrun may
+ * have set OMP_NUM_THREADS=1 for the process). n <= 0 keeps the runtime's default. */
+void g4o_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 int g4o_qmm_f32(const uint16_t* x, int64_t M, const uint32_t* w, const uint16_t* scales,
                 const uint16_t* biases, int64_t N, int64_t K, int group_size, int chain,
                 int threads, uint16_t* y_bf16) {

@@ -80,6 +80,7 @@ int g4o_qmm(const uint16_t* x, int64_t M, const uint32_t* w, const uint16_t* sca
 
 /* CPU baseline: the same product with fp32 accumulation (vectorisable), bf16 out,
  * `threads` OpenMP threads (<=0: all). This is the timed stand-in for MLX's CPU path. */
+void g4o_set_threads(int n);                     /* OpenMP threads of the oracle's loops */
 int g4o_qmm_f32(const uint16_t* x, int64_t M, const uint32_t* w, const uint16_t* scales,
                 const uint16_t* biases, int64_t N, int64_t K, int group_size, int chain,
                 int threads, uint16_t* y_bf16);

@@ -19,6 +19,8 @@ stack_forward (oracle/affine.py); shapes are full width by default.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 
 from oracle import affine as A
@@ -47,6 +49,7 @@ def check_decode_step(shapes: dict, n_layers: int, h0: np.ndarray, layer_outs: l
     bf16 bits qkv [M, q+2kv] (q|k|v), o [M, hidden], gu [M, 2*inter] (gate|up), h [M, hidden];
     token/value: the step's results per row; logits: the GPU's bf16 logits [M, vocab] or None."""
     M = h0.shape[0]
+    A.set_threads(len(os.sched_getaffinity(0)))   # torchrun starts ranks with OMP_NUM_THREADS=1
     nq, nkv, ni = shapes["q"][0], shapes["k"][0], shapes["gate"][0]
     worst, worst_at = 0.0, ""
     per_kind = {"qkv": 0.0, "o": 0.0, "gu": 0.0, "down": 0.0}
