@@ -514,8 +514,7 @@ def main():
                    "peak_burst": round(tf_burst * world, 1), "frac_of_burst": round(tflops / (tf_burst * world), 4),
                    "timing": f"{reps} runs of the whole prompt after one warm-up run, CUDA events, max over ranks",
                    "path": "per chunk a CUDA graph: tcgen05 dequant-GEMM for every projection"
-                           + (", after o/down the NCCL reduce-scatter (fp32) + all-gather (bf16) of the partial "
-                              "sums" if world > 1 else "")
+                           + (", NCCL allreduce of fp32 partials after o/down" if world > 1 else "")
                            + "; the LM head on the final row",
                    "gpu_launches_per_chunk": 6 * cfg.layers}   # q|k|v, gate|up: RMS rows + GEMM
         if world > 1:
@@ -544,8 +543,7 @@ def main():
             del g_ar
             prefill["allreduce_ms_per_chunk_alone"] = round(ar_ms, 3)
             prefill["allreduce_bytes_each"] = P * cfg.hidden * 4
-            prefill["allreduce"] = ("NCCL reduce-scatter of the fp32 partials, bf16 rounding of each rank's block "
-                                    "of rows, NCCL all-gather of the bf16 rows")
+            prefill["allreduce"] = "NCCL allreduce of the fp32 partials, then a cast to bf16"
         del inputs, hp
 
     hbm_peak, tf_peak, peak_kind = measured_peaks()

@@ -141,11 +141,7 @@ class SyntheticStack:
         self.keys = torch.empty(M, dtype=torch.int64, device=dev)
 
     def _row_parallel(self, w: QuantizedWeight, x: torch.Tensor, out: torch.Tensor, part=None) -> torch.Tensor:
-        """Row-parallel linear + the allreduce after it. When the rows (tokens) split evenly over the
-        ranks, the fp32 partial sums are reduce-scattered (each rank sums one block of rows in fp32),
-        the block is rounded to bf16 once -- the output's own rounding -- and all-gathered into
-        ``out``: the same sum as an fp32 allreduce plus a cast, with 3/4 of its NVLink bytes and no
-        full-size cast. Other row counts (decode steps) allreduce the fp32 partials."""
+        """Row-parallel linear + the allreduce after it (fp32 partial sums, then one bf16 rounding)."""
         if self.size == 1:
             return quantized_matmul(x, w, out=out)
         part = self.part if part is None else part
@@ -154,25 +150,13 @@ class SyntheticStack:
         return self.sum_partials(part[:M], out)
 
     def sum_partials(self, p: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-        """The collective of a row-parallel linear: out (bf16) = sum over ranks of p (fp32 [M, cols])."""
-        M = p.shape[0]
-        if M % self.size == 0 and out.is_contiguous():
-            rows = M // self.size
-            shard = self._rs_shard(rows, out.shape[1])
-            torch.distributed.reduce_scatter_tensor(shard, p, group=self.group)
-            mine = out[self.rank * rows:(self.rank + 1) * rows]
-            mine.copy_(shard)
-            torch.distributed.all_gather_into_tensor(out, mine, group=self.group)
-            return out
+        """The collective of a row-parallel linear: out (bf16) = sum over ranks of p (fp32 [M, cols]),
+        as an NCCL allreduce of the fp32 partials and a cast. (A reduce-scatter of the fp32 partials
+        followed by an all-gather of bf16 rows moves 3/4 of the bytes but measured slower at 2 GPUs for
+        2048 x 3840 partials: 114 vs 89 us per sum, two collectives' latency instead of one.)"""
         torch.distributed.all_reduce(p, group=self.group)
         out.copy_(p)
         return out
-
-    def _rs_shard(self, rows: int, cols: int) -> torch.Tensor:
-        buf = getattr(self, "_rs_buf", None)
-        if buf is None or buf.numel() < rows * cols:
-            buf = self._rs_buf = torch.empty(rows * cols, dtype=torch.float32, device=self.device)
-        return buf[: rows * cols].view(rows, cols)
 
     def forward(self, h: torch.Tensor):
         """One decode step (M <= max_tokens rows) or one prefill chunk; returns (tokens, values, h)."""

@@ -139,38 +139,3 @@ def test_lost_rank_is_detected_not_hung():
         p.join(timeout=120)
         assert not p.is_alive(), "a rank hung instead of failing"
     assert q.get().startswith("error")
-
-
-def _sum_partials_worker(rank, world, port, out_q):
-    sys.path.insert(0, ROOT)
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
-    try:
-        from types import SimpleNamespace
-
-        from helios_b200.stack import SyntheticStack
-        # the stack's collective on CPU tensors: only its rank, size, group and device are used
-        me = SimpleNamespace(rank=rank, size=world, group=dist.group.WORLD, device=torch.device("cpu"))
-        me._rs_shard = lambda rows, cols: SyntheticStack._rs_shard(me, rows, cols)
-        res = []
-        for M in (8, 3):      # even rows: reduce-scatter + all-gather; odd rows: allreduce
-            g = torch.Generator().manual_seed(100 + M)
-            parts = [torch.randn(M, 16, generator=g) for _ in range(world)]
-            out = torch.empty(M, 16, dtype=torch.bfloat16)
-            SyntheticStack.sum_partials(me, parts[rank].clone(), out)
-            ref = (parts[0] + parts[1]).to(torch.bfloat16)     # fp32 sum, one bf16 rounding
-            res.append(bool(torch.equal(out, ref)))
-        out_q.put((rank, res))
-    finally:
-        dist.destroy_process_group()
-
-
-def test_row_parallel_sum_of_partials_gloo():
-    """The row-parallel collective (fp32 partials -> bf16 sum on every rank): reduce-scatter + bf16
-    all-gather when the rows split over the ranks, an fp32 allreduce otherwise; both equal the fp32
-    sum rounded once to bf16."""
-    ctx = mp.get_context("spawn")
-    q = ctx.SimpleQueue()
-    mp.start_processes(_sum_partials_worker, args=(2, _free_port(), q), nprocs=2, join=True, start_method="spawn")
-    for rank, res in sorted([q.get(), q.get()]):
-        assert res == [True, True], (rank, res)
