@@ -636,8 +636,12 @@ G4qStatus g4q_qmm_geglu(const G4qWeight* h, const uint16_t* x, int64_t M, int64_
         }
         require(norm_weight == nullptr, G4Q_ERR_INVALID_ARGUMENT,
                 "a norm weight is taken only where the fused GEMV runs (M <= 8); normalize with g4q_rms_norm first");
+        if (M > 16) {
+            launch_gemm(c, st);    // the GeGLU in the tcgen05 GEMM's epilogue (or its split-K reduction)
+            return;
+        }
         require(y != nullptr, G4Q_ERR_INVALID_ARGUMENT,
-                "y is required unless M <= 8 on a shape the fused GEMV takes");
+                "y is required for 9 <= M <= 16 and for M <= 8 on a shape the fused GEMV does not take");
         require_aligned16(y, "y");
         qmm_common("g4q_qmm_geglu", h, x, M, ldx, y, w->N, flags, eps, stream);
         // the pairs: per token, N/64 rows of 32 gate values followed by the 32 matching up values

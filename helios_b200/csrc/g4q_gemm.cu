@@ -57,6 +57,8 @@ struct GemmParams {
     int* err;
     int splits;           // > 1: split-K; blockIdx.z takes k-blocks [KB*z/splits, KB*(z+1)/splits) and
     float* part;          //      writes its unscaled fp32 tile to part + z*M*N (row stride N)
+    int geglu;            // paired gate|up weight: y = geglu(gate, up), bf16 [M, N/2] (row stride ldy)
+    float gk_cubic, gk_tanh;   // the GeGLU constants rounded to bf16
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -141,6 +143,15 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)
           "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
           "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
           "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -283,6 +294,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int row = m0 + hm * 128 + quarter * 32 + lane;
         const bool f32 = (p.flags & G4Q_QMM_OUT_F32) != 0;
         const float scale = (p.rms != nullptr && row < p.M) ? p.rms[row] : 1.0f;
+        if (p.geglu && p.splits == 1) {
+            // paired gate|up tile: quad j of the tile holds 32 gate rows (columns 64j..64j+31) and the
+            // same 32 up rows (64j+32..64j+63); each output is geglu of the two bf16 matmul outputs,
+            // rounded exactly as the unfused matmul followed by g4q_geglu rounds them
+#pragma unroll 1
+            for (int j = 0; j < BN / 64; ++j) {
+#pragma unroll 1
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t g[16], u[16];
+                    const uint32_t col = (uint32_t)(hm * BN + 64 * j + 16 * h);
+                    tmem_ld_32x32b_x16(tmem + ((uint32_t)(quarter * 32) << 16) + col, g);
+                    tmem_ld_32x32b_x16(tmem + ((uint32_t)(quarter * 32) << 16) + col + 32, u);
+                    if (row >= p.M || n0 + 64 * j >= p.N) continue;
+                    uint32_t pk[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        uint32_t o2[2];
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const float gv = bf16_bits_to_f32(f32_to_bf16_bits(__fmul_rn(__uint_as_float(g[2 * i + e]), scale)));
+                            const float uv = bf16_bits_to_f32(f32_to_bf16_bits(__fmul_rn(__uint_as_float(u[2 * i + e]), scale)));
+                            o2[e] = geglu_bf16(gv, uv, p.gk_cubic, p.gk_tanh);
+                        }
+                        pk[i] = o2[0] | (o2[1] << 16);
+                    }
+                    uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.y) + (int64_t)row * p.ldy +
+                                                        (n0 / 2 + 32 * j + 16 * h));
+                    o[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    o[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                }
+            }
+        } else
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
             uint32_t v[32];
@@ -351,6 +394,39 @@ __global__ void rms_rows_kernel(const uint16_t* __restrict__ x, int M, int K, in
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
     if (lane == 0) out[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
+}
+
+// Split-K reduction of a paired gate|up weight with the GeGLU epilogue: output o = 32j + i of row m is
+// geglu(bf16(gate), bf16(up)) of columns 64j + i and 64j + 32 + i, each summed in split order and
+// scaled by rms[m] exactly as the unsplit epilogue does. Four outputs per thread.
+__global__ void splitk_reduce_geglu_kernel(const float* __restrict__ part, int splits, int M, int N, const float* rms,
+                                           uint16_t* y, int64_t ldy, float cubic, float tanh_c) {
+    const int m = blockIdx.y;
+    const int o = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (o >= N / 2) return;
+    const int j = o >> 5, i = o & 31;
+    const int64_t total = (int64_t)M * N, ig = (int64_t)m * N + 64 * j + i, iu = ig + 32;
+    float4 g = __ldcs(reinterpret_cast<const float4*>(part + ig)), u = __ldcs(reinterpret_cast<const float4*>(part + iu));
+    for (int z = 1; z < splits; ++z) {
+        const float4 tg = __ldcs(reinterpret_cast<const float4*>(part + (int64_t)z * total + ig));
+        const float4 tu = __ldcs(reinterpret_cast<const float4*>(part + (int64_t)z * total + iu));
+        g.x += tg.x;
+        g.y += tg.y;
+        g.z += tg.z;
+        g.w += tg.w;
+        u.x += tu.x;
+        u.y += tu.y;
+        u.z += tu.z;
+        u.w += tu.w;
+    }
+    const float r = rms ? rms[m] : 1.0f;
+    const float gs[4] = {g.x, g.y, g.z, g.w}, us[4] = {u.x, u.y, u.z, u.w};
+    uint16_t* yr = y + (int64_t)m * ldy + o;
+    for (int e = 0; e < 4; ++e) {
+        const float gv = bf16_bits_to_f32(f32_to_bf16_bits(__fmul_rn(gs[e], r)));
+        const float uv = bf16_bits_to_f32(f32_to_bf16_bits(__fmul_rn(us[e], r)));
+        yr[e] = geglu_bf16(gv, uv, cubic, tanh_c);
+    }
 }
 
 // Split-K reduction: y[m, n] = (sum over splits, in split order, of part[z][m][n]) * rms[m].
@@ -476,6 +552,12 @@ void launch_gemm(const QmmCall& c, cudaStream_t st) {
     const int splits = gemm_splits(c.M, w.N, w.K);
     p.splits = 1;
     p.part = nullptr;
+    p.geglu = c.geglu ? 1 : 0;
+    p.gk_cubic = bf16_round_host(0.044715f);
+    p.gk_tanh = bf16_round_host(0.7978845608028654f);
+    if (c.geglu && (w.N % 64 != 0 || (c.flags & G4Q_QMM_OUT_F32) || (reinterpret_cast<uintptr_t>(c.y) & 15u) ||
+                    c.ldy % 8 != 0))
+        throw Error(G4Q_ERR_INVALID_ARGUMENT, "GeGLU epilogue: rows % 64, bf16 out, 16-byte aligned rows");
     if (splits > 1) {
         const size_t need = (size_t)splits * c.M * w.N * sizeof(float);
         std::lock_guard<std::mutex> lock(g_split_mu);
@@ -501,7 +583,12 @@ void launch_gemm(const QmmCall& c, cudaStream_t st) {
     const dim3 grid((unsigned)((c.M + BM - 1) / BM), (unsigned)((w.N + BN - 1) / BN), (unsigned)p.splits);
     qgemm_kernel<<<grid, kGemmThreads, kSmemBytes, st>>>(tm_x, tm_p, tm_sb, p);
     check_cuda(cudaGetLastError(), "qgemm launch");
-    if (p.splits > 1) {
+    if (p.splits > 1 && p.geglu) {
+        const dim3 rgrid((unsigned)((w.N / 8 + 255) / 256), (unsigned)c.M);
+        splitk_reduce_geglu_kernel<<<rgrid, 256, 0, st>>>(p.part, p.splits, (int)c.M, (int)w.N, p.rms,
+                                                          static_cast<uint16_t*>(c.y), c.ldy, p.gk_cubic, p.gk_tanh);
+        check_cuda(cudaGetLastError(), "split-K GeGLU reduction launch");
+    } else if (p.splits > 1) {
         const dim3 rgrid((unsigned)((w.N / 4 + 255) / 256), (unsigned)c.M);
         splitk_reduce_kernel<<<rgrid, 256, 0, st>>>(p.part, p.splits, (int)c.M, (int)w.N, p.rms, c.y, c.ldy,
                                                     (c.flags & G4Q_QMM_OUT_F32) ? 1 : 0);

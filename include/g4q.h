@@ -181,10 +181,11 @@ G4qStatus g4q_qmm_norm(const G4qWeight* w, const uint16_t* x, int64_t M, int64_t
  * act = bf16 [M, rows/2] (row stride ld_act) of the GeGLU of the two bf16 matmul outputs. w is a
  * PAIRED gate|up weight: rows [64j, 64j+32) hold gate rows [32j, 32j+32) and rows [64j+32, 64j+64)
  * the same up rows (load each 32-row slice with g4q_weight_load; I = rows/2 must be a multiple of
- * 32). flags: 0 or G4Q_QMM_RMS_SCALE. At M <= 8 the GeGLU runs in the stream-K GEMV's epilogue
- * (one launch; gate and up never reach HBM) and y may be NULL. Otherwise y (bf16 [M, rows],
- * contiguous) is required and receives the paired matmul output before the GeGLU pass. Bit-identical
- * either way to g4q_qmm followed by g4q_geglu on the pairs. norm_weight (bf16 [cols], or NULL):
+ * 32). flags: 0 or G4Q_QMM_RMS_SCALE. At M <= 8 the GeGLU runs in the stream-K GEMV's epilogue and
+ * at M > 16 in the tcgen05 GEMM's epilogue (or its split-K reduction): one launch, gate and up never
+ * reach HBM, and y may be NULL. For 9 <= M <= 16 y (bf16 [M, rows], contiguous) is required and
+ * receives the paired matmul output before the GeGLU pass. Bit-identical either way to g4q_qmm
+ * followed by g4q_geglu on the pairs. norm_weight (bf16 [cols], or NULL):
  * x is first normalized as by g4q_qmm_norm (pre_feedforward_layernorm, :929-932), so the norm,
  * both projections and the GeGLU are one launch; only on the fused path (M <= 8, flags 0): other
  * calls with a norm weight are rejected, normalize with g4q_rms_norm first there. */

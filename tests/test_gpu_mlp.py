@@ -195,8 +195,45 @@ def test_geglu_fused_into_decode_gemv(cuda, oracle, M, rms):
     pair.free()
 
 
-@pytest.mark.parametrize("M", [12, 40])
+@pytest.mark.parametrize("M,I,K,splits", [(40, 2048, 1024, 4), (2048, 15360, 3840, 1), (2048, 256, 3840, 8),
+                                          (300, 7680, 3840, 1)])
+@pytest.mark.parametrize("rms", [False, True])
+def test_geglu_fused_into_prefill_gemm(cuda, oracle, M, I, K, splits, rms):
+    """gate|up matmul + GeGLU at prefill widths in the tcgen05 GEMM's epilogue (unsplit tiles) or in its
+    split-K reduction (small I): bit-identical to the paired matmul followed by the GeGLU kernel, and
+    within the matmul tolerance of the oracle's gate, up and geglu (checked without the RMS scale)."""
+    from helios_b200 import _lib
+    Q, gw, uw, pair, x = _pair_case(oracle, cuda, M, I=I, K=K, layer=12)
+    assert pair.qmm_path(M) == (_lib.PATH_GEMM, splits)
+    act = Q.quantized_matmul_geglu(x, pair, rms_scale=rms)
+    y = Q.quantized_matmul(x, pair, rms_scale=rms)
+    yp = y.view(M * I // 32, 64)
+    act2 = Q.geglu(yp[:, :32], yp[:, 32:]).view(M, I)
+    torch.cuda.synchronize()
+    assert (u16(act) == u16(act2)).all()
+    assert _lib.device_error() == 0
+    if not rms and M <= 300:
+        # gate and up within the matmul tolerance of the oracle's exact products, and the GeGLU the
+        # oracle's nine bf16 steps on exactly those gate / up values (a one-ulp flip of gate or up is
+        # within the matmul tolerance but moves gelu * up by an ulp of the product, so the GeGLU is
+        # compared on the GPU's own gate and up)
+        yg = u16(y).reshape(M, I // 32, 64)
+        gate_gpu = np.ascontiguousarray(yg[:, :, :32].reshape(M, I))
+        up_gpu = np.ascontiguousarray(yg[:, :, 32:].reshape(M, I))
+        ge, _ = oracle.qmm(u16(x), u32(gw[0]), u16(gw[1]), u16(gw[2]))
+        ue, _ = oracle.qmm(u16(x), u32(uw[0]), u16(uw[1]), u16(uw[2]))
+        assert_qmm_close(oracle.bf16_to_f32(gate_gpu), ge, bf16_out=True)
+        assert_qmm_close(oracle.bf16_to_f32(up_gpu), ue, bf16_out=True)
+        ref = oracle.geglu(gate_gpu, up_gpu)
+        got = u16(act)
+        assert (got == ref).mean() > 0.999 and ulps_apart(oracle, got, ref).max() <= 1.0
+    pair.free()
+
+
+@pytest.mark.parametrize("M", [12, 16])
 def test_geglu_pair_outside_the_fused_widths(cuda, oracle, M):
+    """9 <= M <= 16 (the cluster GEMV): the paired matmul output goes through y (required), then the
+    GeGLU kernel."""
     from helios_b200 import _lib
     Q, gw, uw, pair, x = _pair_case(oracle, cuda, M, I=2048, K=1024, layer=10)
     I = 2048
