@@ -361,6 +361,7 @@ G4qStatus g4q_weight_open(const char* path, G4qWeight** out) {
         }
         w->fast_ok = (flags & 1) == 0;
         w->small_scales = (flags & 4) == 0;
+        w->subnormal_scales = (flags & 8) != 0;
         *out = hw;
     });
 }
@@ -457,6 +458,7 @@ G4qStatus g4q_weight_load(G4qWeight* h, int64_t dst_row0, const uint32_t* packed
         check_cuda(cudaMemcpy(&flags, w->d_flags, sizeof(int), cudaMemcpyDeviceToHost), "read handle flags");
         w->fast_ok = (flags & 1) == 0;   // cached so compute calls never read device memory
         w->small_scales = (flags & 4) == 0;
+        w->subnormal_scales = (flags & 8) != 0;
     });
 }
 

@@ -48,11 +48,18 @@ namespace {
 
 constexpr int kWarps = 20;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 3;
+constexpr int kMaxStages = 3;
 constexpr uint32_t kUnitPacked = 4 * 512;
 constexpr uint32_t kUnitSb = 64 * 4;
 constexpr uint32_t kUnitBytes = kUnitPacked + kUnitSb;
-constexpr uint32_t kRingBytes = kStages * kUnitBytes;
+constexpr int kMaxPlanTokens = 4;                 // tokens per step (M): 1, 2 or 4
+constexpr int kXKeyStride = 8;                    // key-exchange words per rank: keys[0..M), tag at [7]
+
+// Ring stages per warp at M tokens: three at M <= 2; two at M = 4, which leaves shared memory for
+// the four tokens' x and partial sums (46 KB of weights in flight per SM is still well above what
+// the HBM latency needs).
+template <int kM>
+constexpr int ring_stages() { return kM <= 2 ? 3 : 2; }
 constexpr int kSlots = 16;                        // CTA ranges one 64-row quad may be cut into
 constexpr int kBufs = 3;                          // exchange / slot buffers rotate over three phases
 constexpr int kMaxCtaQuads = 64;                  // quads one CTA range may touch in a phase
@@ -60,8 +67,6 @@ constexpr int kMaxRanks = 8;
 constexpr int kMaxXQuads = 256;                   // 64-wide groups of x a phase may read (K <= 16384)
 constexpr long long kSpinLimit = 4000000000ll;    // ~2 s of SM clocks
 constexpr uint32_t kOddNibbleMask = 0x00F000F0u;  // q at bits 4-7 of each half: bf16 value q * 2^-129
-constexpr uint32_t kPow64x2 = 0x5F805F80u;        // bf16x2 (2^64, 2^64)
-constexpr uint32_t kPow65x2 = 0x60006000u;        // bf16x2 (2^65, 2^65)
 
 struct PhaseDev {
     const uint32_t* packed;
@@ -78,6 +83,10 @@ struct PhaseDev {
     int sync_before;  // wait for every CTA to finish the previous phase before staging x
     int need_done;    // count finished CTAs of this phase (a later barrier or the argmax publish)
     int xout;         // the next phase stages this phase's output from the exchange buffer
+    int64_t ldx, ldy; // row strides of x and y (elements), one row per token
+    int xwin;         // 0: every CTA stages all of x (slot = group); 1: only the groups of its own range
+                      // (slot = unit index relative to the range start; the range is shorter than G)
+    int xslots;       // 64-wide slots of x staged per token
 };
 
 struct DecodeArgs {
@@ -88,15 +97,17 @@ struct DecodeArgs {
     unsigned int* done;                       // [n_phases] CTAs that finished each phase
     unsigned int* exit_count;                 // [1]
     unsigned int* run;                        // [1] launches so far (tag base)
-    unsigned long long* key;                  // running argmax key of this rank
+    unsigned long long* key;                  // [M] running argmax keys of this rank
     unsigned long long* slots;                // [kBufs][buf_words] tagged fp32 partials of cut quads
     unsigned long long* xbuf;                 // [kBufs][xbuf_words] tagged bf16 pairs of finished outputs
     unsigned long long* rp;                   // this rank's rank-partial buffers (tagged, written by all ranks)
     unsigned long long* const* peer_rp;       // [n_ranks] rank-partial buffers of every rank (device array)
-    unsigned long long* const* peer_xkeys;    // [n_ranks] key exchange arrays ([n_ranks][2]) of every rank
+    unsigned long long* const* peer_xkeys;    // [n_ranks] key exchange arrays ([n_ranks][8]) of every rank
     int rank, n_ranks;
     int64_t buf_words;                        // words per slot buffer
     int64_t xbuf_words;                       // words per exchange buffer
+    int64_t xbuf_tok;                         // words per token inside an exchange buffer
+    int64_t ld_logits;                        // row stride of the optional logits (elements)
     int64_t rp_words;                         // words per rank-partial buffer
     int32_t* tokens;
     float* values;
@@ -169,21 +180,25 @@ __device__ __forceinline__ uint32_t phase_tag(uint32_t tag0, int p) {
 }
 
 // Slots of a phase live in buffer p mod 3: tagged fp32 partials, word index of (quad q, source CTA
-// offset c = cta - cf, row 0).
-__device__ __forceinline__ int64_t slot_w(const DecodeArgs& a, const PhaseDev& P, int p, int q, int c) {
-    return (int64_t)(p % kBufs) * a.buf_words + ((int64_t)q * P.ks + c) * 64;
+// offset c = cta - cf, token tok, row 0).
+template <int kM>
+__device__ __forceinline__ int64_t slot_w(const DecodeArgs& a, const PhaseDev& P, int p, int q, int c, int tok) {
+    return (int64_t)(p % kBufs) * a.buf_words + (((int64_t)q * P.ks + c) * kM + tok) * 64;
 }
 
-// Finished bf16 outputs of phase p in exchange buffer p mod 3: word of (output pair n/2).
-__device__ __forceinline__ int64_t xbuf_w(const DecodeArgs& a, int p, int n) {
-    return (int64_t)(p % kBufs) * a.xbuf_words + (n >> 1);
+// Finished bf16 outputs of phase p in exchange buffer p mod 3: word of (token, output pair n/2).
+__device__ __forceinline__ int64_t xbuf_w(const DecodeArgs& a, int p, int tok, int n) {
+    return (int64_t)(p % kBufs) * a.xbuf_words + (int64_t)tok * a.xbuf_tok + (n >> 1);
 }
 
 // Rank partials of the allreduce phase with ordinal ar: word index of (quad q, rank r, source CTA
-// offset c, row 0). The buffers rotate over allreduce ordinals: a rank writes buffer j mod 3 again
-// only after every rank has sent allreduce j+2, i.e. after every rank has finished reading allreduce j.
-__device__ __forceinline__ int64_t rp_word(const DecodeArgs& a, const PhaseDev& P, int ar, int q, int r, int c) {
-    return (int64_t)(ar % kBufs) * a.rp_words + (((int64_t)q * a.n_ranks + r) * P.ks + c) * 64;
+// offset c, token tok, row 0). The buffers rotate over allreduce ordinals: a rank writes buffer j mod 3
+// again only after every rank has sent allreduce j+2, i.e. after every rank has finished reading
+// allreduce j.
+template <int kM>
+__device__ __forceinline__ int64_t rp_word(const DecodeArgs& a, const PhaseDev& P, int ar, int q, int r, int c,
+                                           int tok) {
+    return (int64_t)(ar % kBufs) * a.rp_words + (((((int64_t)q * a.n_ranks + r) * P.ks + c) * kM + tok) * 64);
 }
 
 // Warp w owns the contiguous units [wstart(w), wstart(w + 1)) of its CTA's n units of a phase
@@ -254,14 +269,15 @@ struct Pre {
     }
 };
 
+template <int kM>
 struct CtaShared {
-    unsigned long long bars[kWarps][kStages];
-    float wss[kWarps];
-    float rs;
+    unsigned long long bars[kWarps][kMaxStages];
+    float wss[kWarps][kM];
+    float rs[kM];
     uint32_t tag0;
     int qcnt[kMaxCtaQuads];   // arrivals per quad of the CTA's range (reset by the last arriver)
     int warps_finished;
-    unsigned long long best;
+    unsigned long long best[kM];
 };
 
 __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
@@ -306,11 +322,12 @@ __device__ __forceinline__ unsigned long long tagged(float v, uint32_t tag) {
     return (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
 }
 
-// The finisher's sum over n tagged source rows of a quad (rows lane and lane + 32 of each, row
-// stride 64 words), in source order after `init` (when has_init), polling until every word carries
-// `tag`: the sources are other CTAs' (and ranks') partials, stored on their own schedule. Bounded:
-// a wait that gives up records code 35 and returns what it has.
-__device__ __noinline__ float2 poll_sum(const unsigned long long* base, int n, uint32_t tag, float2 init,
+// The finisher's sum over n tagged source rows of a quad (rows lane and lane + 32 of each, source
+// stride `stride` words), in source order after `init` (when has_init), polling until every word
+// carries `tag`: the sources are other CTAs' (and ranks') partials, stored on their own schedule; a
+// short sleep between polls leaves the issue slots to the warps still streaming. Bounded: a wait that
+// gives up records code 35 and returns what it has.
+__device__ __noinline__ float2 poll_sum(const unsigned long long* base, int n, int stride, uint32_t tag, float2 init,
                                         bool has_init, int* err) {
     const int lane = threadIdx.x & 31;
     float2 s = init;
@@ -323,7 +340,7 @@ __device__ __noinline__ float2 poll_sum(const unsigned long long* base, int n, u
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 if (i0 + e < n) {
-                    const unsigned long long* src = base + (int64_t)(i0 + e) * 64;
+                    const unsigned long long* src = base + (int64_t)(i0 + e) * stride;
                     w[e][0] = ld_relaxed(src + lane);
                     w[e][1] = ld_relaxed(src + lane + 32);
                     ok &= (uint32_t)(w[e][0] >> 32) == tag && (uint32_t)(w[e][1] >> 32) == tag;
@@ -335,6 +352,7 @@ __device__ __noinline__ float2 poll_sum(const unsigned long long* base, int n, u
                 atomicCAS(err, 0, 35);
                 return s;
             }
+            __nanosleep(20);
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -366,28 +384,29 @@ __device__ __forceinline__ void send_partial(unsigned long long* const* peers, i
     }
 }
 
-// Finished rows lane and lane + 32 of quad q of phase p (unscaled sums v0, v1): y = v * rs, and for a
-// phase the next one reads, the bf16 values as tagged pairs in the exchange buffer (even lanes store
-// the pairs (lane, lane + 1) and (lane + 32, lane + 33)).
-__device__ __forceinline__ void publish(const DecodeArgs& a, const PhaseDev& P, int p, int q, float v0, float v1,
-                                        float rs, uint32_t tag) {
+// Finished rows lane and lane + 32 of quad q of phase p for one token (unscaled sums v0, v1):
+// y = v * rs, and for a phase the next one reads, the bf16 values as tagged pairs in the exchange
+// buffer (even lanes store the pairs (lane, lane + 1) and (lane + 32, lane + 33)).
+__device__ __forceinline__ void publish(const DecodeArgs& a, const PhaseDev& P, int p, int q, int tok, float v0,
+                                        float v1, float rs, uint32_t tag) {
     const int lane = threadIdx.x & 31;
     const float f0 = __fmul_rn(v0, rs), f1 = __fmul_rn(v1, rs);
+    const int64_t yo = (int64_t)tok * P.ldy + (int64_t)q * 64;
     if (P.flags & G4Q_QMM_OUT_F32) {
-        float* y = reinterpret_cast<float*>(P.y) + (int64_t)q * 64;
+        float* y = reinterpret_cast<float*>(P.y) + yo;
         y[lane] = f0;
         y[lane + 32] = f1;
         return;
     }
     const uint32_t b0 = f32_to_bf16_bits(f0), b1 = f32_to_bf16_bits(f1);
-    uint16_t* y = reinterpret_cast<uint16_t*>(P.y) + (int64_t)q * 64;
+    uint16_t* y = reinterpret_cast<uint16_t*>(P.y) + yo;
     y[lane] = (uint16_t)b0;
     y[lane + 32] = (uint16_t)b1;
     if (P.xout) {
         const uint32_t n0 = __shfl_down_sync(0xffffffffu, b0, 1), n1 = __shfl_down_sync(0xffffffffu, b1, 1);
         if ((lane & 1) == 0) {
             const unsigned long long t = (unsigned long long)tag << 32;
-            unsigned long long* xw = a.xbuf + xbuf_w(a, p, q * 64);
+            unsigned long long* xw = a.xbuf + xbuf_w(a, p, tok, q * 64);
             st_relaxed(xw + (lane >> 1), (unsigned long long)(b0 | (n0 << 16)) | t);
             st_relaxed(xw + 16 + (lane >> 1), (unsigned long long)(b1 | (n1 << 16)) | t);
         }
@@ -405,10 +424,11 @@ __device__ __forceinline__ unsigned long long fold_logit(uint16_t* logits, float
     return key > best ? key : best;
 }
 
-// Park this warp's partial of quad q. A warp keeps the partial of the first quad of its range in
-// red[warp][0] (the previous warp may need it) and everything else in red[warp][1] (only the last
-// quad of the range is read by another warp, and it comes last). The last contributing warp sums
-// the partials in warp order, which gives the CTA's partial of the quad, and then:
+// Park this warp's partial of quad q (its 64 rows for each of the M tokens). A warp keeps the partial
+// of the first quad of its range in red[warp][0] (the previous warp may need it) and everything else
+// in red[warp][1] (only the last quad of the range is read by another warp, and it comes last). The
+// last contributing warp sums the partials in warp order, which gives the CTA's partial of the quad,
+// and then, per token:
 //  * allreduce phase: stores it, tagged, into every rank's rank-partial buffer; the quad's finisher
 //    CTA (the first CTA of the quad) then sums all ranks' partials and publishes the quad;
 //  * a quad whole in this CTA: publishes it (argmax phase: folds the logits into the running key);
@@ -416,20 +436,21 @@ __device__ __forceinline__ unsigned long long fold_logit(uint16_t* logits, float
 //    CTA, whose share of the quad is the last of its range, polls the others' slots, sums them in CTA
 //    order after its own and publishes (or folds) the quad.
 // No warp waits here except a finisher, for partials that are (or are about to be) stored.
-template <bool kTP>
-__device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int p, CtaShared& sh, float* red, int q,
-                                     int first_q, int cs, int ce, int cta, int C, const float (&acc)[4][4],
-                                     unsigned long long& best) {
+template <bool kTP, int kM>
+__device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int p, CtaShared<kM>& sh, float* red,
+                                     int q, int first_q, int cs, int ce, int cta, int C, const float (&acc)[4][4],
+                                     unsigned long long (&best)[kM]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
     const int G = P.G, n = ce - cs;
-    float* rb = red + (size_t)(warp * 2 + (q == first_q ? 0 : 1)) * 64;
-    if (t == 0) {   // token 0 lives in the t == 0 lanes (C fragment column 0)
+    float* rb = red + (size_t)(warp * 2 + (q == first_q ? 0 : 1)) * kM * 64;
+    // C fragment: lane (gi, t) holds rows gi, gi + 8 of each tile for tokens 2t, 2t + 1
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            rb[i * 16 + gi] = acc[i][0];
-            rb[i * 16 + gi + 8] = acc[i][2];
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int tok = 2 * t + (e & 1);
+            if (tok < kM) rb[tok * 64 + i * 16 + gi + ((e & 2) ? 8 : 0)] = acc[i][e];
         }
-    }
     __threadfence_block();
     __syncwarp();
     const int lo = max(cs, q * G), hi = min(ce, (q + 1) * G);
@@ -445,40 +466,59 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
     }
     // warp wa holds q in slot 0 only if q is also its first quad; the others hold it as their first
     const int slot_a = (cs + wstart(wa, n)) / G == q ? 0 : 1;
-    float v[2];
+    float2 f[kM];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int row = lane + 32 * h;
-        float s = red[(wa * 2 + slot_a) * 64 + row];
-        for (int w = wa + 1; w <= wb; ++w) s += red[w * 2 * 64 + row];
-        v[h] = s;
+    for (int tok = 0; tok < kM; ++tok) {
+        float v[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int row = tok * 64 + lane + 32 * h;
+            float s = red[(wa * 2 + slot_a) * kM * 64 + row];
+            for (int w = wa + 1; w <= wb; ++w) s += red[w * 2 * kM * 64 + row];
+            v[h] = s;
+        }
+        f[tok] = make_float2(v[0], v[1]);
     }
     const bool whole = cs <= q * G && ce >= (q + 1) * G;
     const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
     const uint32_t tag = phase_tag(sh.tag0, p);
     int cf, cl;
     quad_ctas(P, q, C, cf, cl);
-    float2 f = make_float2(v[0], v[1]);
     if (kTP && P.src_ranks > 1) {
-        send_partial(a.peer_rp, a.n_ranks, rp_word(a, P, P.ar, q, a.rank, cta - cf), v[0], v[1], tag);
+#pragma unroll
+        for (int tok = 0; tok < kM; ++tok)
+            send_partial(a.peer_rp, a.n_ranks, rp_word<kM>(a, P, P.ar, q, a.rank, cta - cf, tok), f[tok].x, f[tok].y,
+                         tag);
         if (cta != cf) return;
         const int nc = cl - cf + 1;
-        for (int r = 0; r < a.n_ranks; ++r)   // rank-major, then CTA order: the same bits on every rank
-            f = poll_sum(a.rp + rp_word(a, P, P.ar, q, r, 0), nc, tag, f, r > 0, a.err);
+#pragma unroll
+        for (int tok = 0; tok < kM; ++tok)
+            for (int r = 0; r < a.n_ranks; ++r)   // rank-major, then CTA order: the same bits on every rank
+                f[tok] = poll_sum(a.rp + rp_word<kM>(a, P, P.ar, q, r, 0, tok), nc, kM * 64, tag, f[tok], r > 0, a.err);
     } else if (!whole) {
         if (cta != cf) {
-            unsigned long long* sl = a.slots + slot_w(a, P, p, q, cta - cf);
-            st_relaxed(sl + lane, tagged(v[0], tag));
-            st_relaxed(sl + lane + 32, tagged(v[1], tag));
+#pragma unroll
+            for (int tok = 0; tok < kM; ++tok) {
+                unsigned long long* sl = a.slots + slot_w<kM>(a, P, p, q, cta - cf, tok);
+                st_relaxed(sl + lane, tagged(f[tok].x, tag));
+                st_relaxed(sl + lane + 32, tagged(f[tok].y, tag));
+            }
             return;
         }
-        f = poll_sum(a.slots + slot_w(a, P, p, q, 1), cl - cf, tag, f, true, a.err);
+#pragma unroll
+        for (int tok = 0; tok < kM; ++tok)
+            f[tok] = poll_sum(a.slots + slot_w<kM>(a, P, p, q, 1, tok), cl - cf, kM * 64, tag, f[tok], true, a.err);
     }
-    if (argmax) {
-        best = fold_logit(a.logits, a.softcap, a.row_offset, q * 64 + lane, __fmul_rn(f.x, sh.rs), best);
-        best = fold_logit(a.logits, a.softcap, a.row_offset, q * 64 + lane + 32, __fmul_rn(f.y, sh.rs), best);
-    } else {
-        publish(a, P, p, q, f.x, f.y, sh.rs, tag);
+#pragma unroll
+    for (int tok = 0; tok < kM; ++tok) {
+        if (argmax) {
+            uint16_t* lg = a.logits ? a.logits + (int64_t)tok * a.ld_logits : nullptr;
+            best[tok] = fold_logit(lg, a.softcap, a.row_offset, q * 64 + lane, __fmul_rn(f[tok].x, sh.rs[tok]), best[tok]);
+            best[tok] = fold_logit(lg, a.softcap, a.row_offset, q * 64 + lane + 32, __fmul_rn(f[tok].y, sh.rs[tok]),
+                                   best[tok]);
+        } else {
+            publish(a, P, p, q, tok, f[tok].x, f[tok].y, sh.rs[tok], tag);
+        }
     }
 }
 
@@ -490,54 +530,36 @@ __device__ __forceinline__ int xperm(int w) {
     return (w & ~31) | ((r & 3) << 3) | (((w >> 3) & 3) << 1) | (r >> 2);
 }
 
-// Stage the x of phase P (K bf16 values) into shared memory; returns this thread's sum of squares
-// (every CTA maps values to threads the same way, so every CTA derives the same RMS scale).
-// From an external input: plain 16-byte copies. From the previous phase's output: the finished
-// bf16 pairs of its exchange buffer, polled until they carry that phase's tag; every load of a
-// thread is in flight at once, and only words still missing are loaded again.
-constexpr int kMaxStageLoads = 8;   // 16-byte exchange loads per thread: K <= 4 * 8 * 640 = 20480
-
-__device__ __noinline__ float stage_xbuf(const unsigned long long* src, int K, uint32_t tag, uint32_t* xs, bool rms,
-                                         int* err);
-
-__device__ __forceinline__ float stage_x(const DecodeArgs& a, const PhaseDev& P, uint32_t* xs, uint32_t tag0,
-                                         bool rms) {
-    float ss = 0.0f;
-    auto acc_sq = [&](uint32_t w) {
-        const float lo = bf16_bits_to_f32(w & 0xffffu), hi = bf16_bits_to_f32(w >> 16);
-        ss = __fadd_rn(ss, __fmul_rn(lo, lo));
-        ss = __fadd_rn(ss, __fmul_rn(hi, hi));
-    };
-    if (P.src < 0) {
-        for (int u = threadIdx.x; u < P.K / 8; u += kThreads) {
-            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(P.x) + u);
-            xs[xperm(4 * u)] = v.x;
-            xs[xperm(4 * u + 1)] = v.y;
-            xs[xperm(4 * u + 2)] = v.z;
-            xs[xperm(4 * u + 3)] = v.w;
-            if (rms) {
-                acc_sq(v.x);
-                acc_sq(v.y);
-                acc_sq(v.z);
-                acc_sq(v.w);
-            }
-        }
-        return ss;
-    }
-    return stage_xbuf(a.xbuf + xbuf_w(a, P.src, P.src_col), P.K, phase_tag(tag0, P.src), xs, rms, a.err);
+// The 64-wide group of x that staging slot j of a CTA range starting at unit cs holds.
+__device__ __forceinline__ int slot_group(const PhaseDev& P, int cs, int j) {
+    return P.xwin ? (cs + j) % P.G : j;
 }
 
-// Staging from the exchange buffer (out of line: its loads in flight need registers the streaming
-// loop does not have to keep free).
-__device__ __noinline__ float stage_xbuf(const unsigned long long* src, int K, uint32_t tag, uint32_t* xs, bool rms,
-                                         int* err) {
+constexpr int kMaxStageLoads = 8;   // 16-byte exchange loads per thread and token: 4 * 8 * 640 values
+
+// Staging of one token's x from the exchange buffer (out of line: its loads in flight need registers
+// the streaming loop does not have to keep free): the finished bf16 pairs of the producer phase,
+// polled until they carry that phase's tag; every load of a thread is in flight at once, and only
+// words still missing are loaded again. src points at the token's word of x's first column.
+// kWin: the CTA's window (slot j holds group (cs + j) mod G); otherwise slot j holds group j. The
+// phase's numbers come by value: loads through the phase record would be repeated after every
+// polling load (each is a memory clobber).
+template <bool kWin>
+__device__ __noinline__ float stage_xbuf(const unsigned long long* src, int nslots, int cs, int G, uint32_t tag,
+                                         uint32_t* xs, bool rms, int* err) {
     float ss = 0.0f;
     auto acc_sq = [&](uint32_t w) {
         const float lo = bf16_bits_to_f32(w & 0xffffu), hi = bf16_bits_to_f32(w >> 16);
         ss = __fadd_rn(ss, __fmul_rn(lo, lo));
         ss = __fadd_rn(ss, __fmul_rn(hi, hi));
     };
-    const int nl = K / 4;   // 16-byte loads: two tagged words, four values
+    const int nl = nslots * 16;   // 16-byte loads: two tagged words, four values; 16 per slot
+    auto word_of = [&](int i) -> int64_t {
+        if constexpr (kWin)
+            return (int64_t)((cs + (i >> 4)) % G) * 32 + 2 * (i & 15);
+        else
+            return (int64_t)2 * i;
+    };
     uint32_t w[kMaxStageLoads][2];   // the value halves of the words (the tags are checked on arrival)
     uint32_t missing = 0;
 #pragma unroll
@@ -545,7 +567,7 @@ __device__ __noinline__ float stage_xbuf(const unsigned long long* src, int K, u
         const int i = threadIdx.x + j * kThreads;
         if (i < nl) {
             unsigned long long u0, u1;
-            ld_relaxed2(src + 2 * i, u0, u1);
+            ld_relaxed2(src + word_of(i), u0, u1);
             w[j][0] = (uint32_t)u0;
             w[j][1] = (uint32_t)u1;
             if ((uint32_t)(u0 >> 32) != tag || (uint32_t)(u1 >> 32) != tag) missing |= 1u << j;
@@ -559,7 +581,7 @@ __device__ __noinline__ float stage_xbuf(const unsigned long long* src, int K, u
                 if (missing & (1u << j)) {
                     const int i = threadIdx.x + j * kThreads;
                     unsigned long long u0, u1;
-                    ld_relaxed2(src + 2 * i, u0, u1);
+                    ld_relaxed2(src + word_of(i), u0, u1);
                     w[j][0] = (uint32_t)u0;
                     w[j][1] = (uint32_t)u1;
                     if ((uint32_t)(u0 >> 32) == tag && (uint32_t)(u1 >> 32) == tag) missing &= ~(1u << j);
@@ -587,62 +609,118 @@ __device__ __noinline__ float stage_xbuf(const unsigned long long* src, int K, u
     return ss;
 }
 
-// End of a step on a tensor-parallel plan: every rank's last CTA posts its argmax key to every
-// rank (key word, then the tag with release semantics) and waits for all of them; the maximum is
-// the step's key on every rank. Also keeps the ranks within one step of each other.
-__device__ __forceinline__ unsigned long long exchange_keys(const DecodeArgs& a, unsigned long long key, uint32_t tag) {
-    for (int r = 0; r < a.n_ranks; ++r) {
-        unsigned long long* dst = a.peer_xkeys[r] + 2 * a.rank;
-        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(key) : "memory");
-        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(dst + 1), "l"((unsigned long long)tag) : "memory");
+// Stage the x of phase P (per token: K bf16 values, or the CTA's window of groups) into shared memory,
+// token tok at xs + tok * xslots * 32 words; ss[tok] receives this thread's sum of squares (every CTA
+// maps values to threads the same way, so every CTA derives the same RMS scale). From an external
+// input: plain 16-byte copies; from the previous phase's output: its exchange words.
+template <int kM>
+__device__ __forceinline__ void stage_x(const DecodeArgs& a, const PhaseDev& P, uint32_t* xs, int cs, uint32_t tag0,
+                                        bool rms, float (&ss)[kM]) {
+#pragma unroll
+    for (int tok = 0; tok < kM; ++tok) {
+        uint32_t* xt = xs + (size_t)tok * P.xslots * 32;
+        float s = 0.0f;
+        if (P.src < 0) {
+            for (int u = threadIdx.x; u < P.xslots * 8; u += kThreads) {
+                const int g = slot_group(P, cs, u >> 3);
+                const uint4 v = __ldcg(reinterpret_cast<const uint4*>(P.x + (int64_t)tok * P.ldx + (int64_t)g * 64) + (u & 7));
+                xt[xperm(4 * u)] = v.x;
+                xt[xperm(4 * u + 1)] = v.y;
+                xt[xperm(4 * u + 2)] = v.z;
+                xt[xperm(4 * u + 3)] = v.w;
+                if (rms) {
+                    const uint32_t pv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float lo = bf16_bits_to_f32(pv[e] & 0xffffu), hi = bf16_bits_to_f32(pv[e] >> 16);
+                        s = __fadd_rn(s, __fmul_rn(lo, lo));
+                        s = __fadd_rn(s, __fmul_rn(hi, hi));
+                    }
+                }
+            }
+        } else {
+            const unsigned long long* src = a.xbuf + xbuf_w(a, P.src, tok, P.src_col);
+            if (kM > 1 && P.xwin)
+                s = stage_xbuf<kM != 1>(src, P.xslots, cs, P.G, phase_tag(tag0, P.src), xt, rms, a.err);
+            else
+                s = stage_xbuf<false>(src, P.xslots, cs, P.G, phase_tag(tag0, P.src), xt, rms, a.err);
+        }
+        ss[tok] = s;
     }
-    unsigned long long best = 0ull;
+}
+
+// End of a step on a tensor-parallel plan: every rank's last CTA posts its argmax keys to every rank
+// (key words, then the tag with release semantics) and waits for all of them; the maximum per token
+// is the step's key on every rank. Also keeps the ranks within one step of each other.
+template <int kM>
+__device__ __forceinline__ void exchange_keys(const DecodeArgs& a, unsigned long long (&key)[kM], uint32_t tag) {
+    for (int r = 0; r < a.n_ranks; ++r) {
+        unsigned long long* dst = a.peer_xkeys[r] + kXKeyStride * a.rank;
+#pragma unroll
+        for (int tok = 0; tok < kM; ++tok)
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + tok), "l"(key[tok]) : "memory");
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(dst + kXKeyStride - 1), "l"((unsigned long long)tag)
+                     : "memory");
+    }
+    unsigned long long best[kM];
+#pragma unroll
+    for (int tok = 0; tok < kM; ++tok) best[tok] = 0ull;
     const long long t0 = clock64();
     for (int r = 0; r < a.n_ranks; ++r) {
-        const unsigned long long* src = a.peer_xkeys[a.rank] + 2 * r;
+        const unsigned long long* src = a.peer_xkeys[a.rank] + kXKeyStride * r;
         for (;;) {
             unsigned long long t;
-            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(t) : "l"(src + 1) : "memory");
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(t) : "l"(src + kXKeyStride - 1) : "memory");
             if ((uint32_t)t == tag) break;
             if (clock64() - t0 > kSpinLimit) {
                 atomicCAS(a.err, 0, 36);
-                return key;
+                return;
             }
         }
-        unsigned long long k;
-        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(src) : "memory");
-        best = k > best ? k : best;
+#pragma unroll
+        for (int tok = 0; tok < kM; ++tok) {
+            unsigned long long k;
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(src + tok) : "memory");
+            best[tok] = k > best[tok] ? k : best[tok];
+        }
     }
-    return best;
+#pragma unroll
+    for (int tok = 0; tok < kM; ++tok) key[tok] = best[tok];
 }
 
 // kTP: tensor-parallel instantiation (allreduce phases, key exchange); the single-GPU one has none
-// of that code. kTrace: also stamps each CTA's per-phase timeline into a.trace (a profiling build
-// selected at run time; the default instantiations have no trace code).
-template <bool kTP, bool kTrace = false>
+// of that code. kM: tokens per step (the MMA's n dimension holds them). kTrace: also stamps each
+// CTA's per-phase timeline into a.trace (a profiling build selected at run time; the default
+// instantiations have no trace code).
+template <bool kTP, int kM, bool kTrace = false>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
+    constexpr int kS = ring_stages<kM>();
+    constexpr uint32_t kRing = kS * kUnitBytes;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ CtaShared sh;
+    __shared__ CtaShared<kM> sh;
     // the warp index through a shuffle from lane 0: provably warp-uniform, so the compiler keeps it
     // and everything derived from it (ring and barrier addresses, unit cursors) in uniform registers
     const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0), lane = threadIdx.x & 31, gi = lane >> 2,
               t = lane & 3;
     const int C = gridDim.x, cta = blockIdx.x;
-    uint8_t* ring = smem + (size_t)warp * kRingBytes;
+    uint8_t* ring = smem + (size_t)warp * kRing;
     const uint32_t ring_s = saddr(ring);
-    float* red = reinterpret_cast<float*>(smem + (size_t)kWarps * kRingBytes);
-    uint32_t* xs = reinterpret_cast<uint32_t*>(smem + (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4);
+    float* red = reinterpret_cast<float*>(smem + (size_t)kWarps * kRing);
+    uint32_t* xs = reinterpret_cast<uint32_t*>(smem + (size_t)kWarps * kRing + (size_t)2 * kWarps * kM * 64 * 4);
     const uint32_t bar0 = saddr(&sh.bars[warp][0]);
 
     if (lane == 0) {
-        for (int s = 0; s < kStages; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * s));
+        for (int s = 0; s < kS; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * s));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (threadIdx.x == 0) {
         for (int i = 0; i < kMaxCtaQuads; ++i) sh.qcnt[i] = 0;
         sh.warps_finished = 0;
-        sh.best = 0ull;
-        sh.rs = 1.0f;
+#pragma unroll
+        for (int tok = 0; tok < kM; ++tok) {
+            sh.best[tok] = 0ull;
+            sh.rs[tok] = 1.0f;
+        }
         const unsigned long long e = (unsigned long long)*reinterpret_cast<volatile unsigned int*>(a.run) *
                                      (unsigned)(a.n_phases + 1);
         sh.tag0 = (uint32_t)(e % 0xFFFFFFFFull);
@@ -654,14 +732,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
 
     int stage = 0;
     uint32_t phase_bit = 0;
-    unsigned long long best = 0ull;
+    unsigned long long best[kM];
+#pragma unroll
+    for (int tok = 0; tok < kM; ++tok) best[tok] = 0ull;
+    // the token whose x this lane's B fragment carries (column gi of the MMA's n dimension); columns
+    // past the M tokens repeat token 0 and their accumulators are never read
+    const int xtok = gi < kM ? gi : 0;
 
     for (int p = 0; p < a.n_phases; ++p) {
         const PhaseDev& P = a.ph[p];
         const int cs = range_start(cta, P.U, C), ce = range_start(cta + 1, P.U, C);
         const int G = P.G;
-        // ---- phase entry: the CTA's warps are done with the previous phase (x buffer reuse). While
-        //      the previous phase finishes elsewhere, tabulate where x's producer partials live.
+        // ---- phase entry: the CTA's warps are done with the previous phase (x buffer reuse)
         __syncthreads();
         unsigned long long* tr = nullptr;
         if constexpr (kTrace) {
@@ -676,29 +758,37 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             if (threadIdx.x == 0) tr[1] = global_ns();
         }
         const uint32_t tag0 = sh.tag0;
-        // ---- stage x (polls the producer's exchange words) and its RMS scale
+        // ---- stage x (polls the producer's exchange words) and its RMS scale per token
         const bool rms = (P.flags & G4Q_QMM_RMS_SCALE) != 0;
-        float ss = stage_x(a, P, xs, tag0, rms);
+        float ss[kM];
+        stage_x<kM>(a, P, xs, cs, tag0, rms, ss);
         if (p == 0) {   // first weight loads only now: the x loads above are not queued behind them
-            for (int s = 0; s < kStages && pre.p < a.n_phases; ++s) {
+            for (int s = 0; s < kS && pre.p < a.n_phases; ++s) {
                 if (lane == 0) pre.issue(ring_s + s * kUnitBytes, bar0 + 8 * s);
                 pre.next(a, cta, C, warp);
             }
         }
         if (rms) {
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
-            if (lane == 0) sh.wss[warp] = ss;
+            for (int tok = 0; tok < kM; ++tok) {
+                float v = ss[tok];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+                if (lane == 0) sh.wss[warp][tok] = v;
+            }
         }
         __syncthreads();
         if (threadIdx.x == 0) {
-            float r = 1.0f;
-            if (rms) {
-                float s = 0.0f;
-                for (int w = 0; w < kWarps; ++w) s = __fadd_rn(s, sh.wss[w]);
-                r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)P.K), a.eps)));
+#pragma unroll
+            for (int tok = 0; tok < kM; ++tok) {
+                float r = 1.0f;
+                if (rms) {
+                    float s = 0.0f;
+                    for (int w = 0; w < kWarps; ++w) s = __fadd_rn(s, sh.wss[w][tok]);
+                    r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)P.K), a.eps)));
+                }
+                sh.rs[tok] = r;
             }
-            sh.rs = r;
             if constexpr (kTrace) tr[2] = global_ns();
         }
         __syncthreads();
@@ -706,9 +796,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         // ---- this warp's units of phase p
         const int u0 = wstart(warp, ce - cs);
         const int n_units = wstart(warp + 1, ce - cs) - u0;
-        // every lane loads the token's x: all eight B columns hold token 0 (reads broadcast, no
-        // bank conflicts), and column 0 of the accumulators is the one kept
-        const uint4* xt = reinterpret_cast<const uint4*>(xs) + 2 * t;
+        // B fragments: this lane's token, two 16-byte loads per unit from the unit's x slot
+        const uint4* xt = reinterpret_cast<const uint4*>(xs) + (size_t)xtok * P.xslots * 8 + 2 * t;
         float acc[4][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
@@ -718,7 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         const int first_q = cq;
         for (int k = 0; k < n_units; ++k) {
             if (cq != acc_q) {
-                park<kTP>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
+                park<kTP, kM>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -727,7 +816,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             }
             wait_parity(bar0 + 8 * stage, phase_bit, a.err);
             const uint8_t* st = ring + stage * kUnitBytes;
-            const uint4 xa = xt[cg * 8], xb = xt[cg * 8 + 1];
+            int xslot = cg;
+            if constexpr (kM > 1) {
+                if (P.xwin) xslot = u0 + k;
+            }
+            const uint4 xa = xt[xslot * 8], xb = xt[xslot * 8 + 1];
             const uint32_t b0[4] = {xa.x, xa.z, xb.x, xb.z}, b1[4] = {xa.y, xa.w, xb.y, xb.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -736,9 +829,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
                 // row n0 (nibbles at bits 0-3 / 8-11): (128 + q) magic, RN(q*s) = fma((128+q), s, -128 s);
                 // row n1 (bits 4-7 / 12-15): the masked bits read as bf16 are exactly q * 2^-129, so
                 // RN(q*s) = RN((q * 2^-129) * (s * 2^129)) with s * 2^129 exact for |s| < 2^-1
+                // s * 2^129 is an exponent add (the host refuses weights with subnormal scales)
                 const RowConsts c0 = row_consts(sbw[0]);
-                const uint32_t s1 = prmt(sbw[8], 0u, 0x1010u), b1s = prmt(sbw[8], 0u, 0x3232u);
-                const uint32_t s1h = mul_bf16x2(mul_bf16x2(s1, kPow64x2), kPow65x2);
+                const uint32_t b1s = bcast_hi(sbw[8]);
+                const uint32_t s1h = bcast_lo(sbw[8]) + kExp129x2;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const uint32_t w = j == 0 ? wv.x : j == 1 ? wv.y : j == 2 ? wv.z : wv.w;
@@ -756,7 +850,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
                 if (lane == 0) pre.issue(ring_s + stage * kUnitBytes, bar0 + 8 * stage);
                 pre.next(a, cta, C, warp);
             }
-            if (++stage == kStages) {
+            if (++stage == kS) {
                 stage = 0;
                 phase_bit ^= 1u;
             }
@@ -765,19 +859,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
                 ++cq;
             }
         }
-        if (n_units > 0) park<kTP>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
+        if (n_units > 0) park<kTP, kM>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
         if constexpr (kTrace) {
             if (lane == 0) tr[3 + warp] = global_ns();
         }
         const bool argmax = (P.flags & G4Q_PHASE_ARGMAX) != 0;
         if (argmax) {
-            unsigned long long kk = best;
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) {
-                const unsigned long long o = __shfl_xor_sync(0xffffffffu, kk, off);
-                kk = o > kk ? o : kk;
+            for (int tok = 0; tok < kM; ++tok) {
+                unsigned long long kk = best[tok];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    const unsigned long long o = __shfl_xor_sync(0xffffffffu, kk, off);
+                    kk = o > kk ? o : kk;
+                }
+                if (lane == 0) atomicMax(&sh.best[tok], kk);
             }
-            if (lane == 0) atomicMax(&sh.best, kk);
         }
         // ---- completion count, only where a later barrier or the argmax publish needs it: the warps
         //      meet on a shared counter (CTA scope), the last one publishes with a gpu-scope release
@@ -792,25 +889,33 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             if (last_warp && lane == 0) {
                 __threadfence_block();
                 sh.warps_finished = 0;
-                if (argmax) atomicMax(a.key, sh.best);
+                if (argmax) {
+#pragma unroll
+                    for (int tok = 0; tok < kM; ++tok) atomicMax(a.key + tok, sh.best[tok]);
+                }
                 // a reduction, not an atomic with a result: the warp does not wait for the round
                 // trip to L2 before the next phase's CTA barrier (measured: step 2.70 -> 2.62 ms)
                 asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.done + p) : "memory");
             }
         }
     }
-    // ---- the last CTA out publishes the step's key, resets the counters and advances the tag base
+    // ---- the last CTA out publishes the step's keys, resets the counters and advances the tag base
     const int last = a.n_phases - 1;
     __syncthreads();
     if (threadIdx.x == 0) {
         const unsigned int prev = atom_add_acq_rel(a.exit_count, 1u);
         if (prev == (unsigned)C - 1) {
-            unsigned long long k = atomicExch(a.key, 0ull);
-            if constexpr (kTP) k = exchange_keys(a, k, phase_tag(sh.tag0, a.n_phases));
+            unsigned long long k[kM];
+#pragma unroll
+            for (int tok = 0; tok < kM; ++tok) k[tok] = atomicExch(a.key + tok, 0ull);
+            if constexpr (kTP) exchange_keys<kM>(a, k, phase_tag(sh.tag0, a.n_phases));
             if (a.ph[last].flags & G4Q_PHASE_ARGMAX) {
-                if (a.tokens) a.tokens[0] = (int32_t)key_index(k);
-                if (a.values) a.values[0] = key_value(k);
-                if (a.keys_out) a.keys_out[0] = k;
+#pragma unroll
+                for (int tok = 0; tok < kM; ++tok) {
+                    if (a.tokens) a.tokens[tok] = (int32_t)key_index(k[tok]);
+                    if (a.values) a.values[tok] = key_value(k[tok]);
+                    if (a.keys_out) a.keys_out[tok] = k[tok];
+                }
             }
             for (int p = 0; p < a.n_phases; ++p) a.done[p] = 0u;
             atomicAdd(a.run, 1u);
@@ -820,12 +925,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     }
 }
 
+// The instantiation a plan launches: tensor parallel or not, tokens per step, tracing (M = 1 only).
+const void* decode_kernel_for(bool tp, int tokens, bool trace) {
+    if (trace) return tp ? reinterpret_cast<const void*>(decode_kernel<true, 1, true>)
+                         : reinterpret_cast<const void*>(decode_kernel<false, 1, true>);
+    switch (tokens) {
+        case 2:
+            return tp ? reinterpret_cast<const void*>(decode_kernel<true, 2>)
+                      : reinterpret_cast<const void*>(decode_kernel<false, 2>);
+        case 4:
+            return tp ? reinterpret_cast<const void*>(decode_kernel<true, 4>)
+                      : reinterpret_cast<const void*>(decode_kernel<false, 4>);
+        default:
+            return tp ? reinterpret_cast<const void*>(decode_kernel<true, 1>)
+                      : reinterpret_cast<const void*>(decode_kernel<false, 1>);
+    }
+}
+
+size_t ring_bytes_for(int tokens) {
+    return (size_t)kWarps * (tokens <= 2 ? 3 : 2) * kUnitBytes;
+}
+
 }  // namespace
 
 struct DecodePlan {
     uint64_t magic = 0;
     int device = -1;
     int n_phases = 0, grid = 0;
+    int tokens = 1;                    // M per step
     int rank = 0, n_ranks = 1;
     size_t smem = 0;
     int64_t buf_words = 0;
@@ -835,9 +962,9 @@ struct DecodePlan {
     unsigned long long* d_slots = nullptr;
     unsigned long long* d_rp = nullptr;      // rank partials (tensor parallel), written by every rank
     int64_t rp_words = 0;
-    unsigned long long* d_xkeys = nullptr;   // [kMaxRanks][2]
+    unsigned long long* d_xkeys = nullptr;   // [kMaxRanks][kXKeyStride]
     unsigned long long* d_xbuf = nullptr;    // [kBufs][xbuf_words] exchange buffers
-    int64_t xbuf_words = 0;
+    int64_t xbuf_words = 0, xbuf_tok = 0;
     unsigned long long** d_peers = nullptr;   // [2][kMaxRanks]: slot buffers, key arrays of every rank
     unsigned long long* peer_rp[kMaxRanks] = {};
     unsigned long long* peer_xkeys[kMaxRanks] = {};
@@ -868,8 +995,9 @@ static void upload_peers(DecodePlan* plan) {
 
 void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, int rank, int n_ranks) {
     if (n <= 0 || phases == nullptr) throw Error(G4Q_ERR_INVALID_ARGUMENT, "a plan needs at least one phase");
-    if (max_tokens != 1)
-        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "the decode plan runs one token per step (max_tokens = 1)");
+    if (max_tokens != 1 && max_tokens != 2 && max_tokens != 4)
+        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "the decode plan runs 1, 2 or 4 tokens per step (max_tokens)");
+    const int kM = max_tokens;
     if (n_ranks < 1 || n_ranks > kMaxRanks || rank < 0 || rank >= n_ranks)
         throw Error(G4Q_ERR_INVALID_ARGUMENT, "rank must be in [0, n_ranks) with 1 <= n_ranks <= 8");
     if (n > 60000) throw Error(G4Q_ERR_INVALID_ARGUMENT, "too many phases");
@@ -884,8 +1012,9 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
         if (!w || w->magic != kWeightMagic) throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "invalid weight");
         if (w->device != dev) throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "weight lives on another device");
         if (w->mlx) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "the decode plan takes 4-bit group-64 weights");
-        if (!w->fast_ok || !w->small_scales)
-            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "the decode plan needs every |scale| < 2^-1");
+        if (!w->fast_ok || !w->small_scales || w->subnormal_scales)
+            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG,
+                        tag + "the decode plan needs every |scale| < 2^-1 and no subnormal (nonzero, < 2^-126) scale");
         if (w->N % 64 != 0) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "rows must be a multiple of 64");
         const uint32_t fl = phases[i].flags;
         if (fl & ~(G4Q_QMM_RMS_SCALE | G4Q_QMM_OUT_F32 | G4Q_PHASE_ARGMAX | G4Q_PHASE_ALLREDUCE))
@@ -913,6 +1042,12 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
         d.flags = fl;
         d.src = -1;
         d.src_col = 0;
+        d.ldx = phases[i].ldx;
+        d.ldy = phases[i].ldy;
+        d.xwin = 0;
+        d.xslots = d.G;
+        if (kM > 1 && (d.ldx < d.K || d.ldx % 8 != 0 || (!(fl & G4Q_PHASE_ARGMAX) && d.ldy < d.N)))
+            throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "ldx >= K (a multiple of 8) and ldy >= N are required");
         d.src_ranks = (fl & G4Q_PHASE_ALLREDUCE) ? n_ranks : 1;
         d.ar = -1;
         d.sync_before = 0;
@@ -955,10 +1090,35 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
         }
         if (d.K > kmax) kmax = d.K;
     }
+    // Staging of x per token: all K when the tokens' x fits beside the rings and the partial-sum
+    // buffers; otherwise (M = 4 on a long K without an RMS scale, e.g. down_proj) each CTA stages only
+    // the groups of its own range, which is then shorter than a quad row.
+    const void* kfn = decode_kernel_for(n_ranks > 1, kM, false);
+    const size_t red_bytes = (size_t)2 * kWarps * kM * 64 * 4;
+    const size_t fixed = ring_bytes_for(kM) + red_bytes + 16;
+    const size_t smem_max = max_dynamic_smem(kfn);
+    if (fixed >= smem_max) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: shared memory");
+    const size_t x_budget = smem_max - fixed;
+    int max_slots = 1;
+    for (int i = 0; i < n; ++i) {
+        PhaseDev& d = ph[i];
+        const std::string tag = "phase " + std::to_string(i) + ": ";
+        if ((size_t)kM * d.G * 128 > x_budget) {
+            const int nmax = (d.U + sms - 1) / sms;
+            if ((d.flags & G4Q_QMM_RMS_SCALE) || nmax >= d.G || (size_t)kM * nmax * 128 > x_budget)
+                throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "the tokens' x does not fit in shared memory");
+            d.xwin = 1;
+            d.xslots = nmax;
+        }
+        max_slots = std::max(max_slots, d.xslots);
+    }
     // Dataflow: a phase that reads the previous phase's output polls that phase's exchange words (its
     // finished, tagged bf16 values) and needs no barrier. A phase whose x is anything else (an external
     // input or an older output) waits for every CTA of this rank to finish the previous phase first.
+    // A phase "reads all" of its predecessor when its x window covers every producer CTA's quads and
+    // every CTA stages all of it (no per-CTA windows).
     auto full = [&](int i) {
+        if (ph[i].xwin) return false;
         for (int c = 0; c < sms; ++c)
             if (!producers[i][c]) return false;
         return true;
@@ -995,12 +1155,14 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     for (int i = 1; i < n; ++i)
         if (ph[i].sync_before) ph[i - 1].need_done = 1;
     ph[n - 1].need_done = 1;   // the argmax publish (or the plan's end) counts the last phase
-    int64_t buf_words = 64, xbuf_words = 32, rp_words = 64;
+    int64_t buf_words = 64, xbuf_tok = 32, rp_words = 64;
     for (int i = 0; i < n; ++i) {
-        buf_words = std::max<int64_t>(buf_words, (int64_t)ph[i].Q * ph[i].ks * 64);
-        if (ph[i].xout) xbuf_words = std::max<int64_t>(xbuf_words, (int64_t)ph[i].N / 2);
-        if (ph[i].src_ranks > 1) rp_words = std::max<int64_t>(rp_words, (int64_t)ph[i].Q * n_ranks * ph[i].ks * 64);
+        buf_words = std::max<int64_t>(buf_words, (int64_t)ph[i].Q * ph[i].ks * kM * 64);
+        if (ph[i].xout) xbuf_tok = std::max<int64_t>(xbuf_tok, (int64_t)ph[i].N / 2);
+        if (ph[i].src_ranks > 1)
+            rp_words = std::max<int64_t>(rp_words, (int64_t)ph[i].Q * n_ranks * ph[i].ks * kM * 64);
     }
+    const int64_t xbuf_words = xbuf_tok * kM;
     if ((int64_t)kBufs * std::max(buf_words, rp_words) >= (1ll << 31))
         throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: slot buffers above 2^31 words");
     auto* plan = new DecodePlan();
@@ -1012,30 +1174,29 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     plan->buf_words = buf_words;
     plan->rp_words = rp_words;
     plan->xbuf_words = xbuf_words;
-    plan->smem = (size_t)kWarps * kRingBytes + 2 * kWarps * 64 * 4 + (size_t)(kmax + 8) * 2;
-    const void* kfn = n_ranks > 1 ? reinterpret_cast<const void*>(decode_kernel<true>)
-                                  : reinterpret_cast<const void*>(decode_kernel<false>);
-    const void* kfn_trace = n_ranks > 1 ? reinterpret_cast<const void*>(decode_kernel<true, true>)
-                                        : reinterpret_cast<const void*>(decode_kernel<false, true>);
-    if (plan->smem > max_dynamic_smem(kfn)) {
+    plan->xbuf_tok = xbuf_tok;
+    plan->tokens = kM;
+    plan->smem = fixed + (size_t)kM * max_slots * 128;
+    const void* kfn_trace = decode_kernel_for(n_ranks > 1, 1, true);
+    if (plan->smem > smem_max) {
         delete plan;
         throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: K too large for shared memory");
     }
     const size_t slot_bytes = sizeof(unsigned long long) * kBufs * (size_t)buf_words;
     cudaError_t e = cudaMalloc(&plan->d_ph, sizeof(PhaseDev) * n);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_done, sizeof(unsigned int) * (n + 2));
-    if (e == cudaSuccess) e = cudaMalloc(&plan->d_key, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_key, sizeof(unsigned long long) * kMaxPlanTokens);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_slots, slot_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_rp, sizeof(unsigned long long) * kBufs * (size_t)rp_words);
     if (e == cudaSuccess) e = cudaMemset(plan->d_rp, 0, sizeof(unsigned long long) * kBufs * (size_t)rp_words);
-    if (e == cudaSuccess) e = cudaMalloc(&plan->d_xkeys, sizeof(unsigned long long) * 2 * kMaxRanks);
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_xkeys, sizeof(unsigned long long) * kXKeyStride * kMaxRanks);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_xbuf, sizeof(unsigned long long) * kBufs * (size_t)xbuf_words);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_peers, sizeof(void*) * 2 * kMaxRanks);
     if (e == cudaSuccess) e = cudaMemcpy(plan->d_ph, ph.data(), sizeof(PhaseDev) * n, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(plan->d_done, 0, sizeof(unsigned int) * (n + 2));
-    if (e == cudaSuccess) e = cudaMemset(plan->d_key, 0, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(plan->d_key, 0, sizeof(unsigned long long) * kMaxPlanTokens);
     if (e == cudaSuccess) e = cudaMemset(plan->d_slots, 0, slot_bytes);
-    if (e == cudaSuccess) e = cudaMemset(plan->d_xkeys, 0, sizeof(unsigned long long) * 2 * kMaxRanks);
+    if (e == cudaSuccess) e = cudaMemset(plan->d_xkeys, 0, sizeof(unsigned long long) * kXKeyStride * kMaxRanks);
     if (e == cudaSuccess) e = cudaMemset(plan->d_xbuf, 0, sizeof(unsigned long long) * kBufs * (size_t)xbuf_words);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
@@ -1070,7 +1231,7 @@ void decode_plan_buffers(void* h, void** slots, uint64_t* slot_bytes, void** xke
     if (slots) *slots = plan->d_rp;
     if (slot_bytes) *slot_bytes = sizeof(unsigned long long) * kBufs * (uint64_t)plan->rp_words;
     if (xkeys) *xkeys = plan->d_xkeys;
-    if (xkey_bytes) *xkey_bytes = sizeof(unsigned long long) * 2 * kMaxRanks;
+    if (xkey_bytes) *xkey_bytes = sizeof(unsigned long long) * kXKeyStride * kMaxRanks;
 }
 
 void decode_plan_set_peers(void* h, void* const* slots, void* const* xkeys) {
@@ -1102,10 +1263,15 @@ void decode_plan_free(void* h) {
 
 void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offset, int32_t* tokens, float* values,
                      uint64_t* keys, uint16_t* logits, int64_t ld_logits, cudaStream_t st) {
-    (void)ld_logits;
     DecodePlan* plan = checked_plan(h);
     if (plan->device != current_device()) throw Error(G4Q_ERR_INVALID_ARGUMENT, "plan belongs to another device");
-    if (M != 1) throw Error(G4Q_ERR_INVALID_ARGUMENT, "the decode plan runs one token per step (M = 1)");
+    if (M != plan->tokens)
+        throw Error(G4Q_ERR_INVALID_ARGUMENT, "the plan was made for " + std::to_string(plan->tokens) +
+                                                  " tokens per step (M = max_tokens)");
+    if (logits != nullptr && M > 1 && ld_logits < 1)
+        throw Error(G4Q_ERR_INVALID_ARGUMENT, "ld_logits must be the logits' row stride");
+    if (plan->trace != nullptr && M != 1)
+        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "the tracing build runs one token per step");
     for (int r = 0; r < plan->n_ranks; ++r)
         if (!plan->peer_rp[r] || !plan->peer_xkeys[r])
             throw Error(G4Q_ERR_INVALID_ARGUMENT, "tensor-parallel plan: peer buffers not set");
@@ -1129,6 +1295,8 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     a.buf_words = plan->buf_words;
     a.xbuf = plan->d_xbuf;
     a.xbuf_words = plan->xbuf_words;
+    a.xbuf_tok = plan->xbuf_tok;
+    a.ld_logits = ld_logits;
     a.tokens = tokens;
     a.values = values;
     a.keys_out = reinterpret_cast<unsigned long long*>(keys);
@@ -1145,12 +1313,10 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     a.trace = plan->trace;
-    if (plan->n_ranks > 1)
-        check_cuda(cudaLaunchKernelEx(&cfg, plan->trace ? decode_kernel<true, true> : decode_kernel<true>, a),
-                   "cudaLaunchKernelEx(decode)");
-    else
-        check_cuda(cudaLaunchKernelEx(&cfg, plan->trace ? decode_kernel<false, true> : decode_kernel<false>, a),
-                   "cudaLaunchKernelEx(decode)");
+    void* args[] = {&a};
+    check_cuda(cudaLaunchKernelExC(&cfg, decode_kernel_for(plan->n_ranks > 1, plan->tokens, plan->trace != nullptr),
+                                   args),
+               "cudaLaunchKernelEx(decode)");
 }
 
 int64_t decode_plan_trace_words(void* h) {

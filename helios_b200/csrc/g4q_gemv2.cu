@@ -37,8 +37,6 @@ constexpr uint32_t kUnitBytes = kUnitPacked + kUnitSb;
 constexpr uint32_t kRedBytesPerTok = 2 * kWarpsV2 * 64 * 4;   // [quad parity][tok][warp][row]
 constexpr long long kWaitLimitCycles2 = 4000000000ll;
 constexpr uint32_t kOddNibbleMask = 0x00F000F0u;  // q at bits 4-7 of each half: bf16 value q * 2^-129
-constexpr uint32_t kPow64x2 = 0x5F805F80u;        // bf16x2 (2^64, 2^64)
-constexpr uint32_t kPow65x2 = 0x60006000u;        // bf16x2 (2^65, 2^65)
 
 struct Gemv2Args {
     const uint32_t* packed;
@@ -278,7 +276,7 @@ __device__ __forceinline__ void park_quad(const Gemv2Args& a, int* qcnt, float* 
     __syncwarp();
 }
 
-// kRaw: every |scale| < 2^-1, so the odd-nibble rows dequantize from the raw masked bits (q * 2^-129
+// kRaw: every |scale| < 2^-1 and none subnormal, so the odd-nibble rows dequantize from the raw masked bits (q * 2^-129
 // read as bf16, times s * 2^129); otherwise all four rows go through the (128 + q) magic.
 template <bool kRaw>
 __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
@@ -455,8 +453,8 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
             const uint32_t* sbw = reinterpret_cast<const uint32_t*>(st + kUnitPacked) + i * 16 + gi;
             const RowConsts c0 = row_consts(sbw[0]);
             if constexpr (kRaw) {
-                const uint32_t s1 = prmt(sbw[8], 0u, 0x1010u), b1s = prmt(sbw[8], 0u, 0x3232u);
-                const uint32_t s1h = mul_bf16x2(mul_bf16x2(s1, kPow64x2), kPow65x2);
+                const uint32_t b1s = bcast_hi(sbw[8]);
+                const uint32_t s1h = bcast_lo(sbw[8]) + kExp129x2;   // s * 2^129 (no subnormal scales)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const uint32_t w = j == 0 ? wv.x : j == 1 ? wv.y : j == 2 ? wv.z : wv.w;
@@ -594,7 +592,8 @@ void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    check_cuda(cudaLaunchKernelEx(&cfg, w.small_scales ? gemv2_kernel<true> : gemv2_kernel<false>, a), "gemv2 launch");
+    check_cuda(cudaLaunchKernelEx(&cfg, w.small_scales && !w.subnormal_scales ? gemv2_kernel<true> : gemv2_kernel<false>, a),
+               "gemv2 launch");
 }
 
 }  // namespace g4q

@@ -26,9 +26,11 @@ struct Weight {
     uint16_t* mlx_biases = nullptr;
     size_t bytes = 0;
     int* d_flags = nullptr;      // device word: bit0 = a scale outside |s| < 2^120 or non-finite,
-                                 // bit1 = a gathered row id was out of range
+                                 // bit1 = a gathered row id was out of range, bit2 = |s| >= 2^-1,
+                                 // bit3 = a subnormal nonzero scale
     bool fast_ok = true;         // host copy of !(bit0), refreshed by every load
     bool small_scales = true;    // host copy of !(bit2): every |scale| < 2^-1
+    bool subnormal_scales = false;   // host copy of bit3: some scale is subnormal (exponent 0, nonzero)
     // lazily created scratch for the LM-head argmax (keys[16] + counter), zeroed once
     unsigned long long* argmax_scratch = nullptr;
 };

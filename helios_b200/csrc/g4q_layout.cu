@@ -101,6 +101,7 @@ __global__ void repack_sb_kernel(const uint16_t* __restrict__ s, const uint16_t*
         // the decode plan also scales s by 2^129 exactly: |s| < 2^-1 (exponent field < 126)
         const uint32_t e = (sv >> 7) & 0xFFu;
         if (e >= 126u) atomicOr(flags, e >= 247u ? 5 : 4);
+        if (e == 0u && (sv & 0x7Fu) != 0u) atomicOr(flags, 8);   // subnormal: the plan scales s by an exponent add
     }
 }
 
@@ -111,6 +112,7 @@ __global__ void sb_flags_kernel(const uint32_t* __restrict__ sb, int64_t count, 
          idx += (int64_t)gridDim.x * blockDim.x) {
         const uint32_t e = (sb[idx] >> 7) & 0xFFu;
         if (e >= 126u) atomicOr(flags, e >= 247u ? 5 : 4);
+        if (e == 0u && (sb[idx] & 0x7Fu) != 0u) atomicOr(flags, 8);
     }
 }
 

@@ -285,8 +285,11 @@ G4qStatus g4q_rms_norm_residual(const uint16_t* x, int64_t ldx, const uint16_t* 
  * carry G4Q_PHASE_ARGMAX: its y is not stored; instead each row's bf16 logits go through the
  * softcap and a first-index argmax, reported as in g4q_lm_head_argmax. Pointers are fixed at plan
  * creation (device memory); g4q_decode_plan_run launches one cooperative grid on `stream` and
- * allocates nothing, so it can be captured in a CUDA graph. M (tokens per step) <= 2. Runs of one
- * plan must not overlap on the GPU. */
+ * allocates nothing, so it can be captured in a CUDA graph. max_tokens (the M of every step: 1, or
+ * the MTP-verify widths 2 and 4 of decode_block_logits, native_model.cc:1954-2026) fixes the plan's
+ * tokens per step; x and y are then [M, ld] row-major, and run takes exactly that M (logits, when
+ * given, [M, ld_logits]; tokens / values / keys hold M entries). Runs of one plan must not overlap on
+ * the GPU. */
 #define G4Q_PHASE_ARGMAX 0x4u
 /* Row-parallel phase of a tensor-parallel plan (o_proj, down_proj split along K): every rank's
  * partial sums are added across ranks inside the kernel (the allreduce after o/down). */

@@ -16,19 +16,22 @@ from stack_parity import check_decode_step
 pytestmark = pytest.mark.gpu
 
 
-def test_full_width_decode_plan_every_phase(cuda, oracle):
+@pytest.mark.parametrize("M,layers", [(1, 6), (2, 4), (4, 4)])
+def test_full_width_decode_plan_every_phase(cuda, oracle, M, layers):
+    """M tokens per step (1, and the MTP-verify widths 2 and 4: the tokens are the MMA's n dimension;
+    at M = 4 down_proj's 15360-wide x is staged per CTA as the window of its own range)."""
     from helios_b200 import _lib
     from helios_b200.quantized import synth_normal
     from helios_b200.stack import StackConfig, SyntheticStack, activation_seed, decode_keys
-    cfg = StackConfig(layers=6)
-    st = SyntheticStack(cfg, max_tokens=1)
-    st.build_plan(1, keep_layers=True)
-    h0 = synth_normal(activation_seed(0), (1, cfg.hidden))
-    logits = torch.empty((1, cfg.vocab), dtype=torch.bfloat16, device=cuda)
+    cfg = StackConfig(layers=layers)
+    st = SyntheticStack(cfg, max_tokens=M)
+    st.build_plan(M, keep_layers=True)
+    h0 = synth_normal(activation_seed(M), (M, cfg.hidden))
+    logits = torch.empty((M, cfg.vocab), dtype=torch.bfloat16, device=cuda)
     keys, _ = st.decode(h0, logits=logits)
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
-    outs, lg = st.gather_layer_outputs(1, logits)
+    outs, lg = st.gather_layer_outputs(M, logits)
     toks, vals = decode_keys(keys)
     rep = check_decode_step(oracle.stack_shapes(), cfg.layers, u16(h0), outs, toks, vals, logits=lg,
                             softcap=cfg.softcap, eps=cfg.eps)

@@ -327,3 +327,42 @@ def test_lm_head_row_offset_and_keys(cuda, oracle):
     # repeated calls reuse the self-resetting scratch
     tf2, _, _ = Q.lm_head_argmax(x, full)
     assert (tf2 == tf).all()
+
+
+def test_zero_and_subnormal_scales(cuda, oracle):
+    """The decode paths scale s by 2^129 with an exponent add: exact for zero scales (the odd-row
+    dequant still returns the bias) and refused by the plan for subnormal ones, which the stream-K
+    GEMV sends down its all-magic path instead. Both against the oracle's exact product."""
+    from helios_b200 import _lib
+    from helios_b200 import quantized as Q
+    N, K = 4096, 3840
+    w, s, b = oracle.synth_matrix(oracle.matrix_seed(11, 2), N, K)
+    x = Q.synth_normal(oracle.activation_seed(77), (1, K))
+    s0 = s.copy()
+    s0[::7, 3] = 0           # +0.0 scales: q * 0 + b = b for every nibble of those groups
+    s0[1::11, 5] = 0x8000    # -0.0
+    sub = s0.copy()
+    sub[5, 9] = 0x0001       # one subnormal scale
+
+    def upload(scales):
+        return Q.QuantizedWeight.from_mlx(torch.from_numpy(w.view(np.int32)).view(torch.uint32),
+                                          torch.from_numpy(scales.view(np.int16)).view(torch.bfloat16),
+                                          torch.from_numpy(b.view(np.int16)).view(torch.bfloat16))
+
+    for scales, plan_ok in ((s0, True), (sub, False)):
+        qw = upload(scales)
+        ye, _ = oracle.qmm(u16(x), w, scales, b)
+        y = Q.quantized_matmul(x, qw, out_dtype=torch.float32)
+        assert_qmm_close(y.cpu().numpy(), ye, bf16_out=False)
+        yp = torch.empty((1, N), dtype=torch.bfloat16, device=cuda)
+        if plan_ok:
+            plan = Q.DecodePlan([(qw, x, yp, 0)], 1)
+            plan.run(1)
+            torch.cuda.synchronize()
+            assert _lib.device_error() == 0
+            assert_qmm_close(oracle.bf16_to_f32(u16(yp)), ye, bf16_out=True)
+            plan.free()
+        else:
+            with pytest.raises(_lib.G4qError, match="subnormal"):
+                Q.DecodePlan([(qw, x, yp, 0)], 1)
+        qw.free()
