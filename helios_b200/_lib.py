@@ -57,10 +57,17 @@ class G4qDecodePhase(ctypes.Structure):
                 ("ldy", ctypes.c_int64), ("flags", ctypes.c_uint32)]
 
 
+class G4qPhasePrologue(ctypes.Structure):
+    _fields_ = [("post_norm_weight", ctypes.c_void_p), ("residual", ctypes.c_int32),
+                ("layer_scalar", ctypes.c_void_p), ("norm_weight", ctypes.c_void_p),
+                ("residual_out", ctypes.c_void_p), ("ld_residual_out", ctypes.c_int64), ("eps", ctypes.c_float)]
+
+
 DTYPE_BF16 = 0
 DTYPE_F32 = 1
 PHASE_ARGMAX = 0x4
 PHASE_ALLREDUCE = 0x8
+PHASE_GEGLU = 0x10
 PATH_GEMV_STREAMK = 1
 PATH_GEMV_CLUSTER = 2
 PATH_GEMM = 3
@@ -97,6 +104,8 @@ SIGNATURES = {
     "g4q_decode_plan_run": [_P, _I64, _F, _F, _I64, _P, _P, _P, _P, _I64, _P],
     "g4q_decode_plan_free": [_P],
     "g4q_decode_plan_trace": [_P, _P, ctypes.POINTER(_I64)],
+    "g4q_decode_plan_create_ex": [ctypes.POINTER(G4qDecodePhase), ctypes.POINTER(G4qPhasePrologue), _I32, _I32, _I32,
+                                  _I32, ctypes.POINTER(_P)],
     "g4q_decode_plan_create_tp": [ctypes.POINTER(G4qDecodePhase), _I32, _I32, _I32, _I32, ctypes.POINTER(_P)],
     "g4q_decode_plan_buffers": [_P, ctypes.POINTER(_P), ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_P),
                                 ctypes.POINTER(ctypes.c_uint64)],

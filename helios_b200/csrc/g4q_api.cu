@@ -708,6 +708,17 @@ G4qStatus g4q_decode_plan_create(const G4qDecodePhase* phases, int32_t n_phases,
     });
 }
 
+G4qStatus g4q_decode_plan_create_ex(const G4qDecodePhase* phases, const G4qPhasePrologue* prologues,
+                                    int32_t n_phases, int32_t max_tokens, int32_t rank, int32_t n_ranks,
+                                    G4qDecodePlan** out) {
+    return guarded("g4q_decode_plan_create_ex", [&] {
+        require(out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null out pointer");
+        *out = nullptr;
+        *out = reinterpret_cast<G4qDecodePlan*>(
+            decode_plan_create(phases, n_phases, max_tokens, rank, n_ranks, prologues));
+    });
+}
+
 G4qStatus g4q_decode_plan_create_tp(const G4qDecodePhase* phases, int32_t n_phases, int32_t max_tokens,
                                     int32_t rank, int32_t n_ranks, G4qDecodePlan** out) {
     return guarded("g4q_decode_plan_create_tp", [&] {

@@ -36,6 +36,7 @@
 // Every wait is bounded (about two seconds of clocks); a wait that gives up records an error code
 // in the per-device error word and the kernel runs to its end.
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -87,6 +88,16 @@ struct PhaseDev {
     int xwin;         // 0: every CTA stages all of x (slot = group); 1: only the groups of its own range
                       // (slot = unit index relative to the range start; the range is shorter than G)
     int xslots;       // 64-wide slots of x staged per token
+    int nout;         // output features: N, or N / 2 for a GeGLU phase
+    // prologue (G4qPhasePrologue): elementwise work on the staged x before the matmul
+    const uint16_t* post_w;   // post-norm weight of the staged values (bf16 [K]) or null
+    const uint16_t* norm_w;   // input-norm weight (bf16 [K]) or null
+    const uint16_t* scalar;   // layer scalar (one bf16) or null
+    uint16_t* res_user;       // copy of the updated residual stream [M, ld_res_user] or null
+    int64_t ld_res_user;
+    int res_mode;             // 0 none, 1 the staged values start the residual stream, 2 added to it
+    int res_in, res_out;      // residual-stream buffers read (mode 2) and written (modes 1 and 2)
+    float peps;               // eps of the prologue norms
 };
 
 struct DecodeArgs {
@@ -108,6 +119,9 @@ struct DecodeArgs {
     int64_t xbuf_words;                       // words per exchange buffer
     int64_t xbuf_tok;                         // words per token inside an exchange buffer
     int64_t ld_logits;                        // row stride of the optional logits (elements)
+    uint16_t* resbuf;                         // [2][M][res_ld] residual stream of plans with prologues
+    int64_t res_ld;                           // elements per token of a residual buffer
+    float gk_cubic, gk_tanh;                  // GeGLU constants rounded to bf16
     int64_t rp_words;                         // words per rank-partial buffer
     int32_t* tokens;
     float* values;
@@ -391,6 +405,20 @@ __device__ __forceinline__ void publish(const DecodeArgs& a, const PhaseDev& P, 
                                         float v1, float rs, uint32_t tag) {
     const int lane = threadIdx.x & 31;
     const float f0 = __fmul_rn(v0, rs), f1 = __fmul_rn(v1, rs);
+    if (P.flags & G4Q_PHASE_GEGLU) {
+        // paired quad: row lane is gate feature 32q + lane, row lane + 32 the matching up feature;
+        // both rounded to bf16 as the matmul output would be, then the GeGLU
+        const uint32_t o = geglu_bf16(bf16_bits_to_f32(f32_to_bf16_bits(f0)), bf16_bits_to_f32(f32_to_bf16_bits(f1)),
+                                      a.gk_cubic, a.gk_tanh);
+        reinterpret_cast<uint16_t*>(P.y)[(int64_t)tok * P.ldy + (int64_t)q * 32 + lane] = (uint16_t)o;
+        if (P.xout) {
+            const uint32_t n = __shfl_down_sync(0xffffffffu, o, 1);
+            if ((lane & 1) == 0)
+                st_relaxed(a.xbuf + xbuf_w(a, p, tok, q * 32 + lane),
+                           (unsigned long long)(o | (n << 16)) | ((unsigned long long)tag << 32));
+        }
+        return;
+    }
     const int64_t yo = (int64_t)tok * P.ldy + (int64_t)q * 64;
     if (P.flags & G4Q_QMM_OUT_F32) {
         float* y = reinterpret_cast<float*>(P.y) + yo;
@@ -649,6 +677,113 @@ __device__ __forceinline__ void stage_x(const DecodeArgs& a, const PhaseDev& P, 
     }
 }
 
+// Per token, 1/sqrt(mean(v^2) + eps) from every thread's partial sum of squares: warp sums, then
+// every thread adds the warps in warp order, so every thread (and every CTA) gets the same bits;
+// the rounding of g4q_rms_norm (fp32 fma accumulation, correctly rounded reciprocal square root).
+template <int kM>
+__device__ __forceinline__ void cta_inv_rms(CtaShared<kM>& sh, float (&ss)[kM], int K, float eps, float (&inv)[kM]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int tok = 0; tok < kM; ++tok) {
+        float v = ss[tok];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) sh.wss[warp][tok] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int tok = 0; tok < kM; ++tok) {
+        float s = 0.0f;
+        for (int w = 0; w < kWarps; ++w) s += sh.wss[w][tok];
+        inv[tok] = __frsqrt_rn(s / (float)K + eps);
+    }
+    __syncthreads();   // sh.wss is written again by the next reduction
+}
+
+// The phase's prologue, in place on the staged x of every token (all K columns staged: a prologue
+// phase is never windowed). Thread t owns the pair words t, t + kThreads, ... (columns 2w, 2w + 1)
+// in every pass, so no pass needs a barrier of its own beyond the norms' reductions.
+template <int kM>
+__device__ __noinline__ void prologue(const DecodeArgs& a, const PhaseDev& P, uint32_t* xs, CtaShared<kM>& sh,
+                                      int cta) {
+    const int K = P.K, words = K / 2, tstride = P.xslots * 32;
+    auto bfv = [](uint32_t h) { return bf16_bits_to_f32(h & 0xffffu); };
+    auto rb = [](float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f)); };
+    float ss[kM], inv[kM];
+    if (P.post_w != nullptr) {
+#pragma unroll
+        for (int tok = 0; tok < kM; ++tok) {
+            float s = 0.0f;
+            for (int w = threadIdx.x; w < words; w += kThreads) {
+                const uint32_t v = xs[tok * tstride + xperm(w)];
+                const float lo = bfv(v), hi = bfv(v >> 16);
+                s = fmaf(lo, lo, s);
+                s = fmaf(hi, hi, s);
+            }
+            ss[tok] = s;
+        }
+        cta_inv_rms<kM>(sh, ss, K, P.peps, inv);
+#pragma unroll
+        for (int tok = 0; tok < kM; ++tok)
+            for (int w = threadIdx.x; w < words; w += kThreads) {
+                uint32_t* e = xs + tok * tstride + xperm(w);
+                const uint32_t v = *e, wv = __ldg(reinterpret_cast<const uint32_t*>(P.post_w) + w);
+                const float lo = rb(bfv(wv) * rb(bfv(v) * inv[tok]));
+                const float hi = rb(bfv(wv >> 16) * rb(bfv(v >> 16) * inv[tok]));
+                *e = (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+            }
+    }
+    if (P.res_mode != 0 || P.norm_w != nullptr) {
+        // the residual stream was written by CTA 0 in an earlier phase, which fenced before publishing
+        // that phase's first quad; this CTA has polled that quad's words, so a fence orders the reads
+        if (P.res_mode == 2) __threadfence();
+        const float sc = P.scalar != nullptr ? bf16_bits_to_f32(*P.scalar) : 1.0f;
+#pragma unroll
+        for (int tok = 0; tok < kM; ++tok) {
+            const uint32_t* rin = reinterpret_cast<const uint32_t*>(a.resbuf + (P.res_in * kM + tok) * a.res_ld);
+            uint32_t* rout = reinterpret_cast<uint32_t*>(a.resbuf + (P.res_out * kM + tok) * a.res_ld);
+            uint32_t* ruser =
+                P.res_user != nullptr ? reinterpret_cast<uint32_t*>(P.res_user + (int64_t)tok * P.ld_res_user) : nullptr;
+            float s = 0.0f;
+            for (int w = threadIdx.x; w < words; w += kThreads) {
+                uint32_t* e = xs + tok * tstride + xperm(w);
+                uint32_t v = *e;
+                if (P.res_mode == 2) {   // residual add, then the layer scalar, each rounded to bf16
+                    const uint32_t r = __ldcg(rin + w);
+                    float lo = rb(bfv(r) + bfv(v)), hi = rb(bfv(r >> 16) + bfv(v >> 16));
+                    if (P.scalar != nullptr) {
+                        lo = lo * sc;
+                        hi = hi * sc;
+                    }
+                    v = (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+                    *e = v;
+                }
+                if (P.res_mode != 0 && cta == 0) {
+                    rout[w] = v;
+                    if (ruser) ruser[w] = v;
+                }
+                const float lo = bfv(v), hi = bfv(v >> 16);
+                s = fmaf(lo, lo, s);
+                s = fmaf(hi, hi, s);
+            }
+            ss[tok] = s;
+        }
+        if (P.res_mode != 0 && cta == 0) __threadfence();   // before this CTA publishes anything later
+        if (P.norm_w != nullptr) {
+            cta_inv_rms<kM>(sh, ss, K, P.peps, inv);
+#pragma unroll
+            for (int tok = 0; tok < kM; ++tok)
+                for (int w = threadIdx.x; w < words; w += kThreads) {
+                    uint32_t* e = xs + tok * tstride + xperm(w);
+                    const uint32_t v = *e, wv = __ldg(reinterpret_cast<const uint32_t*>(P.norm_w) + w);
+                    const float lo = rb(bfv(wv) * rb(bfv(v) * inv[tok]));
+                    const float hi = rb(bfv(wv >> 16) * rb(bfv(v >> 16) * inv[tok]));
+                    *e = (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+                }
+        }
+    }
+}
+
 // End of a step on a tensor-parallel plan: every rank's last CTA posts its argmax keys to every rank
 // (key words, then the tag with release semantics) and waits for all of them; the maximum per token
 // is the step's key on every rank. Also keeps the ranks within one step of each other.
@@ -792,6 +927,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             if constexpr (kTrace) tr[2] = global_ns();
         }
         __syncthreads();
+        if (P.res_mode != 0 || P.post_w != nullptr || P.norm_w != nullptr) {
+            prologue<kM>(a, P, xs, sh, cta);
+            __syncthreads();
+        }
 
         // ---- this warp's units of phase p
         const int u0 = wstart(warp, ce - cs);
@@ -969,6 +1108,8 @@ struct DecodePlan {
     unsigned long long* peer_rp[kMaxRanks] = {};
     unsigned long long* peer_xkeys[kMaxRanks] = {};
     unsigned long long* trace = nullptr;      // caller's buffer: runs use the tracing kernel while set
+    uint16_t* d_res = nullptr;                // [2][M][res_ld] residual stream of the prologues
+    int64_t res_ld = 8;
 };
 
 constexpr uint64_t kPlanMagic = 0x4734514445434f44ull;
@@ -982,6 +1123,7 @@ static void free_plan_memory(DecodePlan* plan) {
     cudaFree(plan->d_xkeys);
     cudaFree(plan->d_xbuf);
     cudaFree(plan->d_peers);
+    cudaFree(plan->d_res);
 }
 
 static void upload_peers(DecodePlan* plan) {
@@ -993,7 +1135,8 @@ static void upload_peers(DecodePlan* plan) {
     check_cuda(cudaMemcpy(plan->d_peers, table, sizeof(table), cudaMemcpyHostToDevice), "upload peer pointers");
 }
 
-void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, int rank, int n_ranks) {
+void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, int rank, int n_ranks,
+                         const G4qPhasePrologue* prologues) {
     if (n <= 0 || phases == nullptr) throw Error(G4Q_ERR_INVALID_ARGUMENT, "a plan needs at least one phase");
     if (max_tokens != 1 && max_tokens != 2 && max_tokens != 4)
         throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "the decode plan runs 1, 2 or 4 tokens per step (max_tokens)");
@@ -1017,8 +1160,10 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
                         tag + "the decode plan needs every |scale| < 2^-1 and no subnormal (nonzero, < 2^-126) scale");
         if (w->N % 64 != 0) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "rows must be a multiple of 64");
         const uint32_t fl = phases[i].flags;
-        if (fl & ~(G4Q_QMM_RMS_SCALE | G4Q_QMM_OUT_F32 | G4Q_PHASE_ARGMAX | G4Q_PHASE_ALLREDUCE))
+        if (fl & ~(G4Q_QMM_RMS_SCALE | G4Q_QMM_OUT_F32 | G4Q_PHASE_ARGMAX | G4Q_PHASE_ALLREDUCE | G4Q_PHASE_GEGLU))
             throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "unknown flag bits");
+        if ((fl & G4Q_PHASE_GEGLU) && (fl & (G4Q_PHASE_ARGMAX | G4Q_PHASE_ALLREDUCE | G4Q_QMM_OUT_F32)))
+            throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "a GeGLU phase writes bf16 and is neither argmax nor allreduce");
         if ((fl & G4Q_PHASE_ARGMAX) && i != n - 1)
             throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "the argmax phase must be the last phase");
         if ((fl & G4Q_PHASE_ARGMAX) && (fl & G4Q_PHASE_ALLREDUCE))
@@ -1046,8 +1191,36 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
         d.ldy = phases[i].ldy;
         d.xwin = 0;
         d.xslots = d.G;
-        if (kM > 1 && (d.ldx < d.K || d.ldx % 8 != 0 || (!(fl & G4Q_PHASE_ARGMAX) && d.ldy < d.N)))
-            throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "ldx >= K (a multiple of 8) and ldy >= N are required");
+        d.nout = (fl & G4Q_PHASE_GEGLU) ? d.N / 2 : d.N;
+        if (kM > 1 && (d.ldx < d.K || d.ldx % 8 != 0 || (!(fl & G4Q_PHASE_ARGMAX) && d.ldy < d.nout)))
+            throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "ldx >= K (a multiple of 8) and ldy >= the outputs are required");
+        d.post_w = d.norm_w = d.scalar = nullptr;
+        d.res_user = nullptr;
+        d.ld_res_user = 0;
+        d.res_mode = 0;
+        d.res_in = d.res_out = 0;
+        d.peps = 1e-6f;
+        if (prologues != nullptr) {
+            const G4qPhasePrologue& pr = prologues[i];
+            if (pr.residual < 0 || pr.residual > 2) throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "residual must be 0, 1 or 2");
+            if (pr.layer_scalar && pr.residual != 2)
+                throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "a layer scalar scales a residual add (residual = 2)");
+            if (pr.residual_out && (pr.residual == 0 || pr.ld_residual_out < d.K))
+                throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "residual_out needs a residual op and ld >= K");
+            if (!(pr.eps >= 0.0f) || !std::isfinite(pr.eps)) throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "eps");
+            for (const void* q : {(const void*)pr.post_norm_weight, (const void*)pr.norm_weight})
+                if (q && (reinterpret_cast<uintptr_t>(q) & 3u))
+                    throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "norm weights must be 4-byte aligned");
+            d.post_w = pr.post_norm_weight;
+            d.norm_w = pr.norm_weight;
+            d.scalar = pr.layer_scalar;
+            d.res_user = pr.residual_out;
+            d.ld_res_user = pr.ld_residual_out;
+            d.res_mode = pr.residual;
+            d.peps = pr.eps;
+            if ((d.post_w || d.norm_w || d.res_mode) && (fl & G4Q_QMM_RMS_SCALE))
+                throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "a phase with a prologue takes no RMS scale");
+        }
         d.src_ranks = (fl & G4Q_PHASE_ALLREDUCE) ? n_ranks : 1;
         d.ar = -1;
         d.sync_before = 0;
@@ -1071,9 +1244,9 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
         // x inside the previous phase's (bf16) output row: consume it from the slots (dataflow)
         if (i > 0 && !(ph[i - 1].flags & (G4Q_PHASE_ARGMAX | G4Q_QMM_OUT_F32))) {
             const uint16_t* y0 = static_cast<const uint16_t*>(ph[i - 1].y);
-            if (phases[i].x >= y0 && phases[i].x < y0 + ph[i - 1].N) {
+            if (phases[i].x >= y0 && phases[i].x < y0 + ph[i - 1].nout) {
                 const int64_t col = phases[i].x - y0;
-                if (col % 64 != 0 || col + d.K > ph[i - 1].N)
+                if (col % 64 != 0 || col + d.K > ph[i - 1].nout)
                     throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "x must be a 64-aligned column window of phase " +
                                                                 std::to_string(i - 1) + "'s output");
                 d.src = i - 1;
@@ -1084,7 +1257,8 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
         producers[i].assign(sms, d.src < 0 ? 1 : 0);
         if (d.src >= 0) {
             const PhaseDev& S = ph[d.src];
-            const int qa = d.src_col / 64, qb = (d.src_col + d.K) / 64;
+            const int per_q = (S.flags & G4Q_PHASE_GEGLU) ? 32 : 64;   // outputs per producer quad
+            const int qa = d.src_col / per_q, qb = (d.src_col + d.K) / per_q;
             const int64_t cf = (((int64_t)qa * S.G + 1) * sms - 1) / S.U, cl = (((int64_t)qb * S.G) * sms - 1) / S.U;
             for (int64_t c = cf; c <= cl && c < sms; ++c) producers[i][c] = 1;
         }
@@ -1111,6 +1285,34 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
             d.xslots = nmax;
         }
         max_slots = std::max(max_slots, d.xslots);
+    }
+    // Prologues: the staged x must be the whole input (phase 0's external x, or all of the previous
+    // phase's output, staged by every CTA whole), which also makes the residual stream's double
+    // buffer safe: when CTA 0 writes update k + 1, every CTA has finished the phase of update k.
+    int res_cur = -1, res_k = 0;
+    for (int i = 0; i < n; ++i) {
+        PhaseDev& d = ph[i];
+        const bool pro = d.post_w || d.norm_w || d.res_mode;
+        if (!pro) continue;
+        const std::string tag = "phase " + std::to_string(i) + ": ";
+        if (d.xwin) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "a prologue needs all of x staged");
+        if (i > 0 && d.src != i - 1)
+            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "a prologue phase reads the previous phase's output");
+        if (i > 0) {
+            const PhaseDev& S = ph[i - 1];
+            if (d.src_col != 0 || d.K != S.nout)
+                throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "a prologue phase reads all of the previous phase's output");
+        }
+        if (d.res_mode != 0) {
+            if (res_k != 0 && res_k != d.K)
+                throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "the residual stream keeps one width");
+            res_k = d.K;
+            if (d.res_mode == 2 && res_cur < 0)
+                throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "residual = 2 needs an earlier phase with a residual op");
+            d.res_in = res_cur < 0 ? 0 : res_cur;
+            d.res_out = res_cur < 0 ? 0 : 1 - res_cur;
+            res_cur = d.res_out;
+        }
     }
     // Dataflow: a phase that reads the previous phase's output polls that phase's exchange words (its
     // finished, tagged bf16 values) and needs no barrier. A phase whose x is anything else (an external
@@ -1158,7 +1360,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     int64_t buf_words = 64, xbuf_tok = 32, rp_words = 64;
     for (int i = 0; i < n; ++i) {
         buf_words = std::max<int64_t>(buf_words, (int64_t)ph[i].Q * ph[i].ks * kM * 64);
-        if (ph[i].xout) xbuf_tok = std::max<int64_t>(xbuf_tok, (int64_t)ph[i].N / 2);
+        if (ph[i].xout) xbuf_tok = std::max<int64_t>(xbuf_tok, (int64_t)ph[i].nout / 2);
         if (ph[i].src_ranks > 1)
             rp_words = std::max<int64_t>(rp_words, (int64_t)ph[i].Q * n_ranks * ph[i].ks * kM * 64);
     }
@@ -1176,6 +1378,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     plan->xbuf_words = xbuf_words;
     plan->xbuf_tok = xbuf_tok;
     plan->tokens = kM;
+    plan->res_ld = std::max(res_k, 8);
     plan->smem = fixed + (size_t)kM * max_slots * 128;
     const void* kfn_trace = decode_kernel_for(n_ranks > 1, 1, true);
     if (plan->smem > smem_max) {
@@ -1192,6 +1395,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_xkeys, sizeof(unsigned long long) * kXKeyStride * kMaxRanks);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_xbuf, sizeof(unsigned long long) * kBufs * (size_t)xbuf_words);
     if (e == cudaSuccess) e = cudaMalloc(&plan->d_peers, sizeof(void*) * 2 * kMaxRanks);
+    if (e == cudaSuccess) e = cudaMalloc(&plan->d_res, sizeof(uint16_t) * 2 * kM * (size_t)plan->res_ld);
     if (e == cudaSuccess) e = cudaMemcpy(plan->d_ph, ph.data(), sizeof(PhaseDev) * n, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(plan->d_done, 0, sizeof(unsigned int) * (n + 2));
     if (e == cudaSuccess) e = cudaMemset(plan->d_key, 0, sizeof(unsigned long long) * kMaxPlanTokens);
@@ -1297,6 +1501,10 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     a.xbuf_words = plan->xbuf_words;
     a.xbuf_tok = plan->xbuf_tok;
     a.ld_logits = ld_logits;
+    a.resbuf = plan->d_res;
+    a.res_ld = plan->res_ld;
+    a.gk_cubic = bf16_round_host(0.044715f);
+    a.gk_tanh = bf16_round_host(0.7978845608028654f);
     a.tokens = tokens;
     a.values = values;
     a.keys_out = reinterpret_cast<unsigned long long*>(keys);

@@ -166,7 +166,8 @@ void launch_lm_head(const Weight& w, const uint16_t* x, int64_t M, int64_t ldx, 
                     float* values, unsigned long long* keys, cudaStream_t st);
 
 // kernels (g4q_decode.cu): persistent decode-step kernel
-void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, int rank, int n_ranks);
+void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, int rank, int n_ranks,
+                         const G4qPhasePrologue* prologues = nullptr);
 void decode_plan_buffers(void* plan, void** slots, uint64_t* slot_bytes, void** xkeys, uint64_t* xkey_bytes);
 void decode_plan_set_peers(void* plan, void* const* slots, void* const* xkeys);
 void decode_plan_free(void* plan);

@@ -23,14 +23,14 @@ from typing import Optional, Tuple
 import torch
 
 from . import _lib
-from ._lib import (CHAIN_R1, CHAIN_R2, PHASE_ALLREDUCE, PHASE_ARGMAX, QMM_OUT_F32, QMM_RMS_SCALE, G4qError,
-                   G4qInvalidArgument)
+from ._lib import (CHAIN_R1, CHAIN_R2, PHASE_ALLREDUCE, PHASE_ARGMAX, PHASE_GEGLU, QMM_OUT_F32, QMM_RMS_SCALE,
+                   G4qError, G4qInvalidArgument)
 
 __all__ = [
     "QuantizedWeight", "quantized_matmul", "quantized_linear", "norm_quantized_matmul", "quantized_matmul_geglu",
     "LoraAdapter", "geglu", "rms_norm", "rms_norm_residual", "dequantize", "lm_head_argmax", "DecodePlan",
     "synth_matrix", "synth_normal", "CHAIN_R1", "CHAIN_R2", "QMM_RMS_SCALE", "QMM_OUT_F32", "PHASE_ARGMAX",
-    "PHASE_ALLREDUCE", "G4qError", "G4qInvalidArgument",
+    "PHASE_ALLREDUCE", "PHASE_GEGLU", "G4qError", "G4qInvalidArgument",
 ]
 
 
@@ -526,10 +526,29 @@ class DecodePlan:
     and ALLREDUCE phases then sum their partials across ranks inside the kernel.
     """
 
-    def __init__(self, phases, max_tokens: int = 1, *, rank: int = 0, n_ranks: int = 1, group=None):
+    def __init__(self, phases, max_tokens: int = 1, *, rank: int = 0, n_ranks: int = 1, group=None, prologues=None):
+        """``prologues``: None, or one dict (or None) per phase with the keys of G4qPhasePrologue:
+        ``post_norm_weight``, ``residual`` (0/1/2), ``layer_scalar``, ``norm_weight`` (bf16 CUDA tensors or
+        None), ``residual_out`` (bf16 [M, ld] or None), ``eps``."""
         self._keep = []
         self._opened = []
         arr = (_lib.G4qDecodePhase * len(phases))()
+        pro = None
+        if prologues is not None:
+            if len(prologues) != len(phases):
+                raise ValueError("one prologue entry (or None) per phase")
+            pro = (_lib.G4qPhasePrologue * len(phases))()
+            for i, d in enumerate(prologues):
+                d = d or {}
+                pro[i].post_norm_weight = _ptr(d.get("post_norm_weight"))
+                pro[i].residual = int(d.get("residual", 0))
+                pro[i].layer_scalar = _ptr(d.get("layer_scalar"))
+                pro[i].norm_weight = _ptr(d.get("norm_weight"))
+                ro = d.get("residual_out")
+                pro[i].residual_out = _ptr(ro)
+                pro[i].ld_residual_out = 0 if ro is None else ro.stride(0)
+                pro[i].eps = float(d.get("eps", 1e-6))
+                self._keep += [d.get(k) for k in ("post_norm_weight", "layer_scalar", "norm_weight", "residual_out")]
         for i, (w, x, y, flags) in enumerate(phases):
             if x.dtype != torch.bfloat16 or x.stride(-1) != 1:
                 raise ValueError(f"phase {i}: x must be a bf16 view with unit column stride")
@@ -541,7 +560,12 @@ class DecodePlan:
             arr[i].flags = flags
             self._keep += [w, x, y]
         self._h = ctypes.c_void_p()
-        if n_ranks == 1:
+        if pro is not None:
+            _lib.call("g4q_decode_plan_create_ex", arr, pro, len(phases), max_tokens, rank, n_ranks,
+                      ctypes.byref(self._h))
+            if n_ranks > 1:
+                self._connect(rank, n_ranks, group)
+        elif n_ranks == 1:
             _lib.call("g4q_decode_plan_create", arr, len(phases), max_tokens, ctypes.byref(self._h))
         else:
             _lib.call("g4q_decode_plan_create_tp", arr, len(phases), max_tokens, rank, n_ranks, ctypes.byref(self._h))

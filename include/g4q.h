@@ -294,6 +294,9 @@ G4qStatus g4q_rms_norm_residual(const uint16_t* x, int64_t ldx, const uint16_t* 
 /* Row-parallel phase of a tensor-parallel plan (o_proj, down_proj split along K): every rank's
  * partial sums are added across ranks inside the kernel (the allreduce after o/down). */
 #define G4Q_PHASE_ALLREDUCE 0x8u
+/* The phase's weight is a paired gate|up weight (see g4q_qmm_geglu): its output y is
+ * geglu(gate, up), bf16 [M, rows/2], with the same roundings as the matmul followed by g4q_geglu. */
+#define G4Q_PHASE_GEGLU 0x10u
 
 typedef struct G4qDecodePhase {
     const G4qWeight* weight;
@@ -308,6 +311,35 @@ typedef struct G4qDecodePlan G4qDecodePlan;
 
 G4qStatus g4q_decode_plan_create(const G4qDecodePhase* phases, int32_t n_phases, int32_t max_tokens,
                                  G4qDecodePlan** out);
+
+/* Elementwise work a phase applies to its staged x before its matmul: the neighbours of the linears
+ * in layer_forward (native_model.cc:899-970) -- a sub-block's post-norm, residual add and
+ * layer_scalar (:920-926, :954-968, as g4q_rms_norm_residual computes them) and the next sub-block's
+ * input norm (:910-913, :929-932, as g4q_rms_norm computes it). With v the staged values (the
+ * previous phase's output, or the plan's input for phase 0), per token:
+ *   if post_norm_weight: v = bf16(post_norm_weight * bf16(v * inv(v)))
+ *   residual 1: the residual stream starts as v;  residual 2: v = bf16(residual + v), then, with a
+ *               layer_scalar, v = bf16(v * layer_scalar); either way v is the new residual stream
+ *               (kept by the plan; also copied to residual_out [M, ld_residual_out] when given)
+ *   if norm_weight: v = bf16(norm_weight * bf16(v * inv(v)))
+ * with inv(v) = 1/sqrt(mean(v^2) + eps) in fp32. Weights are bf16 [K], the layer scalar one bf16
+ * value, all in device memory. A phase with a prologue takes no G4Q_QMM_RMS_SCALE and must read all
+ * of the previous phase's output (or be phase 0). */
+typedef struct G4qPhasePrologue {
+    const uint16_t* post_norm_weight;
+    int32_t residual;             /* 0 none, 1 start the residual stream, 2 add to it */
+    const uint16_t* layer_scalar;
+    const uint16_t* norm_weight;
+    uint16_t* residual_out;
+    int64_t ld_residual_out;
+    float eps;
+} G4qPhasePrologue;
+
+/* As g4q_decode_plan_create_tp (rank 0 of 1 for a single GPU) with a prologue per phase: prologues
+ * is NULL or an array of n_phases entries (all-zero entries for phases without one). */
+G4qStatus g4q_decode_plan_create_ex(const G4qDecodePhase* phases, const G4qPhasePrologue* prologues,
+                                    int32_t n_phases, int32_t max_tokens, int32_t rank, int32_t n_ranks,
+                                    G4qDecodePlan** out);
 G4qStatus g4q_decode_plan_run(G4qDecodePlan* plan, int64_t M, float eps, float softcap, int64_t row_offset,
                               int32_t* tokens, float* values, uint64_t* keys, uint16_t* logits, int64_t ld_logits,
                               void* stream);
