@@ -8,7 +8,7 @@
 //
 // Why one kernel: at batch 1 every phase is a few microseconds of HBM streaming, so separate
 // launches spend a large share of the step in prologues (staging x) and epilogues (reductions,
-// tails). Here one cooperative grid (one 20-warp CTA per SM) stays resident for the whole step:
+// tails). Here one cooperative grid (one 16-warp CTA per SM) stays resident for the whole step:
 //  * every warp streams its weight units (64 rows x one 64-wide group: 2 KB of packed words +
 //    256 B of scale|bias) through a private ring of cp.async.bulk buffers that runs ahead ACROSS
 //    phase boundaries, so the next phase's weights land while the grid finishes the current one;
@@ -47,7 +47,7 @@
 namespace g4q {
 namespace {
 
-constexpr int kWarps = 20;
+constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxStages = 3;
 constexpr uint32_t kUnitPacked = 4 * 512;
@@ -60,7 +60,8 @@ constexpr int kXKeyStride = 8;                    // key-exchange words per rank
 // the four tokens' x and partial sums (46 KB of weights in flight per SM is still well above what
 // the HBM latency needs).
 template <int kM>
-constexpr int ring_stages() { return kM <= 2 ? 3 : 2; }
+constexpr int ring_stages() { return 3; }
+constexpr uint32_t kFlagPrologue = 0x100u;           // PhaseDev::flags: the phase has a prologue
 constexpr int kSlots = 16;                        // CTA ranges one 64-row quad may be cut into
 constexpr int kBufs = 3;                          // exchange / slot buffers rotate over three phases
 constexpr int kMaxCtaQuads = 64;                  // quads one CTA range may touch in a phase
@@ -398,26 +399,37 @@ __device__ __forceinline__ void send_partial(unsigned long long* const* peers, i
     }
 }
 
+// GeGLU phase: the paired quad's row lane is gate feature 32q + lane, row lane + 32 the matching up
+// feature; both are rounded to bf16 as the matmul output would be, then the GeGLU.
+__device__ __forceinline__ void publish_geglu(const DecodeArgs& a, const PhaseDev& P, int p, int q, int tok, float f0,
+                                           float f1, uint32_t tag) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t o = geglu_bf16(bf16_bits_to_f32(f32_to_bf16_bits(f0)), bf16_bits_to_f32(f32_to_bf16_bits(f1)),
+                                  a.gk_cubic, a.gk_tanh);
+    reinterpret_cast<uint16_t*>(P.y)[(int64_t)tok * P.ldy + (int64_t)q * 32 + lane] = (uint16_t)o;
+    if (P.xout) {
+        const uint32_t n = __shfl_down_sync(0xffffffffu, o, 1);
+        if ((lane & 1) == 0)
+            st_relaxed(a.xbuf + xbuf_w(a, p, tok, q * 32 + lane),
+                       (unsigned long long)(o | (n << 16)) | ((unsigned long long)tag << 32));
+    }
+}
+
 // Finished rows lane and lane + 32 of quad q of phase p for one token (unscaled sums v0, v1):
 // y = v * rs, and for a phase the next one reads, the bf16 values as tagged pairs in the exchange
 // buffer (even lanes store the pairs (lane, lane + 1) and (lane + 32, lane + 33)).
+// kPro: the plan has prologue or GeGLU phases (plans without them run kernels without that code,
+// whose finishers and register allocation stay those of the plain matmul chain).
+template <bool kPro>
 __device__ __forceinline__ void publish(const DecodeArgs& a, const PhaseDev& P, int p, int q, int tok, float v0,
                                         float v1, float rs, uint32_t tag) {
     const int lane = threadIdx.x & 31;
     const float f0 = __fmul_rn(v0, rs), f1 = __fmul_rn(v1, rs);
-    if (P.flags & G4Q_PHASE_GEGLU) {
-        // paired quad: row lane is gate feature 32q + lane, row lane + 32 the matching up feature;
-        // both rounded to bf16 as the matmul output would be, then the GeGLU
-        const uint32_t o = geglu_bf16(bf16_bits_to_f32(f32_to_bf16_bits(f0)), bf16_bits_to_f32(f32_to_bf16_bits(f1)),
-                                      a.gk_cubic, a.gk_tanh);
-        reinterpret_cast<uint16_t*>(P.y)[(int64_t)tok * P.ldy + (int64_t)q * 32 + lane] = (uint16_t)o;
-        if (P.xout) {
-            const uint32_t n = __shfl_down_sync(0xffffffffu, o, 1);
-            if ((lane & 1) == 0)
-                st_relaxed(a.xbuf + xbuf_w(a, p, tok, q * 32 + lane),
-                           (unsigned long long)(o | (n << 16)) | ((unsigned long long)tag << 32));
+    if constexpr (kPro) {
+        if (P.flags & G4Q_PHASE_GEGLU) {
+            publish_geglu(a, P, p, q, tok, f0, f1, tag);
+            return;
         }
-        return;
     }
     const int64_t yo = (int64_t)tok * P.ldy + (int64_t)q * 64;
     if (P.flags & G4Q_QMM_OUT_F32) {
@@ -464,7 +476,7 @@ __device__ __forceinline__ unsigned long long fold_logit(uint16_t* logits, float
 //    CTA, whose share of the quad is the last of its range, polls the others' slots, sums them in CTA
 //    order after its own and publishes (or folds) the quad.
 // No warp waits here except a finisher, for partials that are (or are about to be) stored.
-template <bool kTP, int kM>
+template <bool kTP, int kM, bool kPro>
 __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int p, CtaShared<kM>& sh, float* red,
                                      int q, int first_q, int cs, int ce, int cta, int C, const float (&acc)[4][4],
                                      unsigned long long (&best)[kM]) {
@@ -545,7 +557,7 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
             best[tok] = fold_logit(lg, a.softcap, a.row_offset, q * 64 + lane + 32, __fmul_rn(f[tok].y, sh.rs[tok]),
                                    best[tok]);
         } else {
-            publish(a, P, p, q, tok, f[tok].x, f[tok].y, sh.rs[tok], tag);
+            publish<kPro>(a, P, p, q, tok, f[tok].x, f[tok].y, sh.rs[tok], tag);
         }
     }
 }
@@ -563,7 +575,8 @@ __device__ __forceinline__ int slot_group(const PhaseDev& P, int cs, int j) {
     return P.xwin ? (cs + j) % P.G : j;
 }
 
-constexpr int kMaxStageLoads = 8;   // 16-byte exchange loads per thread and token: 4 * 8 * 640 values
+constexpr int kMaxStageLoads = 8;   // 16-byte exchange loads per thread and token (four values each)
+static_assert(kMaxStageLoads * kThreads * 4 >= kMaxXQuads * 64, "staging must cover the widest x");
 
 // Staging of one token's x from the exchange buffer (out of line: its loads in flight need registers
 // the streaming loop does not have to keep free): the finished bf16 pairs of the producer phase,
@@ -827,7 +840,7 @@ __device__ __forceinline__ void exchange_keys(const DecodeArgs& a, unsigned long
 // of that code. kM: tokens per step (the MMA's n dimension holds them). kTrace: also stamps each
 // CTA's per-phase timeline into a.trace (a profiling build selected at run time; the default
 // instantiations have no trace code).
-template <bool kTP, int kM, bool kTrace = false>
+template <bool kTP, int kM, bool kTrace = false, bool kPro = false>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     constexpr int kS = ring_stages<kM>();
     constexpr uint32_t kRing = kS * kUnitBytes;
@@ -927,9 +940,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             if constexpr (kTrace) tr[2] = global_ns();
         }
         __syncthreads();
-        if (P.res_mode != 0 || P.post_w != nullptr || P.norm_w != nullptr) {
-            prologue<kM>(a, P, xs, sh, cta);
-            __syncthreads();
+        if constexpr (kPro) {
+            if (P.flags & kFlagPrologue) {
+                prologue<kM>(a, P, xs, sh, cta);
+                __syncthreads();
+            }
         }
 
         // ---- this warp's units of phase p
@@ -946,7 +961,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         const int first_q = cq;
         for (int k = 0; k < n_units; ++k) {
             if (cq != acc_q) {
-                park<kTP, kM>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
+                park<kTP, kM, kPro>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -998,7 +1013,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
                 ++cq;
             }
         }
-        if (n_units > 0) park<kTP, kM>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
+        if (n_units > 0) park<kTP, kM, kPro>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
         if constexpr (kTrace) {
             if (lane == 0) tr[3 + warp] = global_ns();
         }
@@ -1064,25 +1079,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     }
 }
 
-// The instantiation a plan launches: tensor parallel or not, tokens per step, tracing (M = 1 only).
-const void* decode_kernel_for(bool tp, int tokens, bool trace) {
-    if (trace) return tp ? reinterpret_cast<const void*>(decode_kernel<true, 1, true>)
-                         : reinterpret_cast<const void*>(decode_kernel<false, 1, true>);
+// The instantiation a plan launches: tensor parallel or not, tokens per step, tracing (M = 1 only),
+// prologue / GeGLU phases present or not.
+template <bool kPro>
+const void* decode_kernel_pick(bool tp, int tokens, bool trace) {
+    if (trace) return tp ? reinterpret_cast<const void*>(decode_kernel<true, 1, true, kPro>)
+                         : reinterpret_cast<const void*>(decode_kernel<false, 1, true, kPro>);
     switch (tokens) {
         case 2:
-            return tp ? reinterpret_cast<const void*>(decode_kernel<true, 2>)
-                      : reinterpret_cast<const void*>(decode_kernel<false, 2>);
+            return tp ? reinterpret_cast<const void*>(decode_kernel<true, 2, false, kPro>)
+                      : reinterpret_cast<const void*>(decode_kernel<false, 2, false, kPro>);
         case 4:
-            return tp ? reinterpret_cast<const void*>(decode_kernel<true, 4>)
-                      : reinterpret_cast<const void*>(decode_kernel<false, 4>);
+            return tp ? reinterpret_cast<const void*>(decode_kernel<true, 4, false, kPro>)
+                      : reinterpret_cast<const void*>(decode_kernel<false, 4, false, kPro>);
         default:
-            return tp ? reinterpret_cast<const void*>(decode_kernel<true, 1>)
-                      : reinterpret_cast<const void*>(decode_kernel<false, 1>);
+            return tp ? reinterpret_cast<const void*>(decode_kernel<true, 1, false, kPro>)
+                      : reinterpret_cast<const void*>(decode_kernel<false, 1, false, kPro>);
     }
 }
 
+const void* decode_kernel_for(bool tp, int tokens, bool trace, bool pro) {
+    return pro ? decode_kernel_pick<true>(tp, tokens, trace) : decode_kernel_pick<false>(tp, tokens, trace);
+}
+
 size_t ring_bytes_for(int tokens) {
-    return (size_t)kWarps * (tokens <= 2 ? 3 : 2) * kUnitBytes;
+    return (size_t)kWarps * 3 * kUnitBytes;
 }
 
 }  // namespace
@@ -1110,6 +1131,7 @@ struct DecodePlan {
     unsigned long long* trace = nullptr;      // caller's buffer: runs use the tracing kernel while set
     uint16_t* d_res = nullptr;                // [2][M][res_ld] residual stream of the prologues
     int64_t res_ld = 8;
+    bool pro = false;                         // prologue or GeGLU phases: the kernels that carry them
 };
 
 constexpr uint64_t kPlanMagic = 0x4734514445434f44ull;
@@ -1220,6 +1242,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
             d.peps = pr.eps;
             if ((d.post_w || d.norm_w || d.res_mode) && (fl & G4Q_QMM_RMS_SCALE))
                 throw Error(G4Q_ERR_INVALID_ARGUMENT, tag + "a phase with a prologue takes no RMS scale");
+            if (d.post_w || d.norm_w || d.res_mode) d.flags |= kFlagPrologue;
         }
         d.src_ranks = (fl & G4Q_PHASE_ALLREDUCE) ? n_ranks : 1;
         d.ar = -1;
@@ -1267,7 +1290,9 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     // Staging of x per token: all K when the tokens' x fits beside the rings and the partial-sum
     // buffers; otherwise (M = 4 on a long K without an RMS scale, e.g. down_proj) each CTA stages only
     // the groups of its own range, which is then shorter than a quad row.
-    const void* kfn = decode_kernel_for(n_ranks > 1, kM, false);
+    bool pro = false;
+    for (int i = 0; i < n; ++i) pro |= (ph[i].flags & (kFlagPrologue | G4Q_PHASE_GEGLU)) != 0;
+    const void* kfn = decode_kernel_for(n_ranks > 1, kM, false, pro);
     const size_t red_bytes = (size_t)2 * kWarps * kM * 64 * 4;
     const size_t fixed = ring_bytes_for(kM) + red_bytes + 16;
     const size_t smem_max = max_dynamic_smem(kfn);
@@ -1378,9 +1403,10 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     plan->xbuf_words = xbuf_words;
     plan->xbuf_tok = xbuf_tok;
     plan->tokens = kM;
+    plan->pro = pro;
     plan->res_ld = std::max(res_k, 8);
     plan->smem = fixed + (size_t)kM * max_slots * 128;
-    const void* kfn_trace = decode_kernel_for(n_ranks > 1, 1, true);
+    const void* kfn_trace = decode_kernel_for(n_ranks > 1, 1, true, pro);
     if (plan->smem > smem_max) {
         delete plan;
         throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: K too large for shared memory");
@@ -1522,7 +1548,7 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     cfg.numAttrs = 1;
     a.trace = plan->trace;
     void* args[] = {&a};
-    check_cuda(cudaLaunchKernelExC(&cfg, decode_kernel_for(plan->n_ranks > 1, plan->tokens, plan->trace != nullptr),
+    check_cuda(cudaLaunchKernelExC(&cfg, decode_kernel_for(plan->n_ranks > 1, plan->tokens, plan->trace != nullptr, plan->pro),
                                    args),
                "cudaLaunchKernelEx(decode)");
 }

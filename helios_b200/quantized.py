@@ -607,8 +607,8 @@ class DecodePlan:
 
     def trace(self, enable: bool = True) -> Optional[torch.Tensor]:
         """Per-phase timeline of the following runs (profiling aid): returns the int64 device buffer
-        [CTAs, phases, 23] of globaltimer stamps (ns) the tracing build of the kernel fills (entry,
-        x's producers done, x staged, then each of the 20 warps' end of units), or None after
+        [CTAs, phases, 19] of globaltimer stamps (ns) the tracing build of the kernel fills (entry,
+        x's producers done, x staged, then each of the 16 warps' end of units), or None after
         switching back to the regular build."""
         words = ctypes.c_int64(0)
         _lib.call("g4q_decode_plan_trace", self._h, None, ctypes.byref(words))

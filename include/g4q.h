@@ -346,8 +346,8 @@ G4qStatus g4q_decode_plan_run(G4qDecodePlan* plan, int64_t M, float eps, float s
 G4qStatus g4q_decode_plan_free(G4qDecodePlan* plan);
 /* Per-phase timeline of a plan's runs, a profiling aid (no reference counterpart; the reference
  * profiles its own phases separately, gemma4_mlx.h:141). *words receives the size of a trace in
- * 64-bit words: grid CTAs x phases x (3 + 20) globaltimer stamps (ns), per CTA and phase: entry,
- * x's producers done, x staged with its RMS scale, then the end of each of the 20 warps' units.
+ * 64-bit words: grid CTAs x phases x (3 + 16) globaltimer stamps (ns), per CTA and phase: entry,
+ * x's producers done, x staged with its RMS scale, then the end of each of the 16 warps' units.
  * With a device buffer of at least that many words set, later runs launch the tracing build of the
  * kernel and overwrite the buffer; NULL switches back to the regular build. */
 G4qStatus g4q_decode_plan_trace(G4qDecodePlan* plan, uint64_t* buffer, int64_t* words);
