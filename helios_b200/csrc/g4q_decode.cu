@@ -957,63 +957,64 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         for (int i = 0; i < 4; ++i)
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
-        int cq = (cs + u0) / G, cg = (cs + u0) - cq * G, acc_q = cq;
+        // the run as segments of whole quads: one park per segment, no per-unit quad bookkeeping
+        int cq = (cs + u0) / G, cg = (cs + u0) - cq * G;
         const int first_q = cq;
-        for (int k = 0; k < n_units; ++k) {
-            if (cq != acc_q) {
-                park<kTP, kM, kPro>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
-                acc_q = cq;
-            }
-            wait_parity(bar0 + 8 * stage, phase_bit, a.err);
-            const uint8_t* st = ring + stage * kUnitBytes;
+        for (int k = 0; k < n_units;) {
+            const int seg = min(n_units - k, G - cg);
+            // x slot of the segment's first unit: its group, or (windowed) its index in the range
             int xslot = cg;
             if constexpr (kM > 1) {
                 if (P.xwin) xslot = u0 + k;
             }
-            const uint4 xa = xt[xslot * 8], xb = xt[xslot * 8 + 1];
-            const uint32_t b0[4] = {xa.x, xa.z, xb.x, xb.z}, b1[4] = {xa.y, xa.w, xb.y, xb.w};
+            const uint4* xp = xt + (size_t)xslot * 8;
+            for (int j = 0; j < seg; ++j, xp += 8) {
+                wait_parity(bar0 + 8 * stage, phase_bit, a.err);
+                const uint8_t* st = ring + stage * kUnitBytes;
+                const uint4 xa = xp[0], xb = xp[1];
+                const uint32_t b0[4] = {xa.x, xa.z, xb.x, xb.z}, b1[4] = {xa.y, xa.w, xb.y, xb.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint4 wv = reinterpret_cast<const uint4*>(st + i * 512)[lane];
-                const uint32_t* sbw = reinterpret_cast<const uint32_t*>(st + kUnitPacked) + i * 16 + gi;
-                // row n0 (nibbles at bits 0-3 / 8-11): (128 + q) magic, RN(q*s) = fma((128+q), s, -128 s);
-                // row n1 (bits 4-7 / 12-15): the masked bits read as bf16 are exactly q * 2^-129, so
-                // RN(q*s) = RN((q * 2^-129) * (s * 2^129)) with s * 2^129 exact for |s| < 2^-1
-                // s * 2^129 is an exponent add (the host refuses weights with subnormal scales)
-                const RowConsts c0 = row_consts(sbw[0]);
-                const uint32_t b1s = bcast_hi(sbw[8]);
-                const uint32_t s1h = bcast_lo(sbw[8]) + kExp129x2;
+                for (int i = 0; i < 4; ++i) {
+                    const uint4 wv = reinterpret_cast<const uint4*>(st + i * 512)[lane];
+                    const uint32_t* sbw = reinterpret_cast<const uint32_t*>(st + kUnitPacked) + i * 16 + gi;
+                    // row n0 (nibbles at bits 0-3 / 8-11): (128 + q) magic, RN(q*s) = fma((128+q), s, -128 s);
+                    // row n1 (bits 4-7 / 12-15): the masked bits read as bf16 are exactly q * 2^-129, so
+                    // RN(q*s) = RN((q * 2^-129) * (s * 2^129)) with s * 2^129 exact for |s| < 2^-1
+                    // s * 2^129 is an exponent add (the host refuses weights with subnormal scales)
+                    const RowConsts c0 = row_consts(sbw[0]);
+                    const uint32_t b1s = bcast_hi(sbw[8]);
+                    const uint32_t s1h = bcast_lo(sbw[8]) + kExp129x2;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t w = j == 0 ? wv.x : j == 1 ? wv.y : j == 2 ? wv.z : wv.w;
-                    const uint32_t w8 = w >> 8;
-                    const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
-                    const uint32_t a1 = add_bf16x2(mul_bf16x2(w & kOddNibbleMask, s1h), b1s);
-                    const uint32_t a2 = deq_r2_fast(lop_nibbles(w8), c0);
-                    const uint32_t a3 = add_bf16x2(mul_bf16x2(w8 & kOddNibbleMask, s1h), b1s);
-                    mma_bf16_16816(acc[i], a0, a1, a2, a3, b0[j], b1[j]);
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const uint32_t w = jj == 0 ? wv.x : jj == 1 ? wv.y : jj == 2 ? wv.z : wv.w;
+                        const uint32_t w8 = w >> 8;
+                        const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
+                        const uint32_t a1 = add_bf16x2(mul_bf16x2(w & kOddNibbleMask, s1h), b1s);
+                        const uint32_t a2 = deq_r2_fast(lop_nibbles(w8), c0);
+                        const uint32_t a3 = add_bf16x2(mul_bf16x2(w8 & kOddNibbleMask, s1h), b1s);
+                        mma_bf16_16816(acc[i], a0, a1, a2, a3, b0[jj], b1[jj]);
+                    }
+                }
+                // the unit has been read: refill the buffer with the warp's next unit (maybe of a later phase)
+                __syncwarp();
+                if (pre.p < a.n_phases) {
+                    if (lane == 0) pre.issue(ring_s + stage * kUnitBytes, bar0 + 8 * stage);
+                    pre.next(a, cta, C, warp);
+                }
+                if (++stage == kS) {
+                    stage = 0;
+                    phase_bit ^= 1u;
                 }
             }
-            // the unit has been read: refill the buffer with the warp's next unit (maybe of a later phase)
-            __syncwarp();
-            if (pre.p < a.n_phases) {
-                if (lane == 0) pre.issue(ring_s + stage * kUnitBytes, bar0 + 8 * stage);
-                pre.next(a, cta, C, warp);
-            }
-            if (++stage == kS) {
-                stage = 0;
-                phase_bit ^= 1u;
-            }
-            if (++cg == G) {
-                cg = 0;
-                ++cq;
-            }
+            park<kTP, kM, kPro>(a, P, p, sh, red, cq, first_q, cs, ce, cta, C, acc, best);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
+            k += seg;
+            ++cq;
+            cg = 0;
         }
-        if (n_units > 0) park<kTP, kM, kPro>(a, P, p, sh, red, acc_q, first_q, cs, ce, cta, C, acc, best);
         if constexpr (kTrace) {
             if (lane == 0) tr[3 + warp] = global_ns();
         }
