@@ -430,67 +430,68 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
         for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
     int cq = (cs + u0) / G, cg = (cs + u0) - cq * G;   // consumer position
     const int first_q = cq;
-    int acc_q = cq;
     int stage = 0;
     uint32_t phase = 0;
-    for (int k = 0; k < n_units; ++k) {
-        if (cq != acc_q) {
-            park_quad(a, qcnt, red, acc_q, first_q, cs, ce, cta, C, acc, rs);
+    // the run as segments of whole quads: one park per segment, no per-unit quad bookkeeping
+    for (int k = 0; k < n_units;) {
+        const int seg = min(n_units - k, G - cg);
+        const uint4* xp = xt + (size_t)(win ? u0 + k : cg) * 8;   // staged slot of the segment's first group
+        for (int j = 0; j < seg; ++j, xp += 8) {
+            wait_parity(bar0 + 8 * stage, phase, a.err);
+            const uint8_t* st = ring + stage * kUnitBytes;
+            const uint4 xa = xp[0], xb = xp[1];
+            const uint32_t b0[4] = {xa.x, xa.z, xb.x, xb.z}, b1[4] = {xa.y, xa.w, xb.y, xb.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 4; ++i) {
+                const uint4 wv = reinterpret_cast<const uint4*>(st + i * 512)[lane];
+                const uint32_t* sbw = reinterpret_cast<const uint32_t*>(st + kUnitPacked) + i * 16 + gi;
+                const RowConsts c0 = row_consts(sbw[0]);
+                if constexpr (kRaw) {
+                    const uint32_t b1s = bcast_hi(sbw[8]);
+                    const uint32_t s1h = bcast_lo(sbw[8]) + kExp129x2;   // s * 2^129 (no subnormal scales)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
-            acc_q = cq;
-        }
-        wait_parity(bar0 + 8 * stage, phase, a.err);
-        const uint8_t* st = ring + stage * kUnitBytes;
-        const int xj = win ? u0 + k : cg;   // staged slot of this unit's group
-        const uint4 xa = xt[xj * 8], xb = xt[xj * 8 + 1];
-        const uint32_t b0[4] = {xa.x, xa.z, xb.x, xb.z}, b1[4] = {xa.y, xa.w, xb.y, xb.w};
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const uint32_t w = jj == 0 ? wv.x : jj == 1 ? wv.y : jj == 2 ? wv.z : wv.w;
+                        const uint32_t w8 = w >> 8;
+                        const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
+                        const uint32_t a1 = add_bf16x2(mul_bf16x2(w & kOddNibbleMask, s1h), b1s);
+                        const uint32_t a2 = deq_r2_fast(lop_nibbles(w8), c0);
+                        const uint32_t a3 = add_bf16x2(mul_bf16x2(w8 & kOddNibbleMask, s1h), b1s);
+                        mma_bf16_16816(acc[i], a0, a1, a2, a3, b0[jj], b1[jj]);
+                    }
+                } else {
+                    const RowConsts c1 = row_consts(sbw[8]);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint4 wv = reinterpret_cast<const uint4*>(st + i * 512)[lane];
-            const uint32_t* sbw = reinterpret_cast<const uint32_t*>(st + kUnitPacked) + i * 16 + gi;
-            const RowConsts c0 = row_consts(sbw[0]);
-            if constexpr (kRaw) {
-                const uint32_t b1s = bcast_hi(sbw[8]);
-                const uint32_t s1h = bcast_lo(sbw[8]) + kExp129x2;   // s * 2^129 (no subnormal scales)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t w = j == 0 ? wv.x : j == 1 ? wv.y : j == 2 ? wv.z : wv.w;
-                    const uint32_t w8 = w >> 8;
-                    const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
-                    const uint32_t a1 = add_bf16x2(mul_bf16x2(w & kOddNibbleMask, s1h), b1s);
-                    const uint32_t a2 = deq_r2_fast(lop_nibbles(w8), c0);
-                    const uint32_t a3 = add_bf16x2(mul_bf16x2(w8 & kOddNibbleMask, s1h), b1s);
-                    mma_bf16_16816(acc[i], a0, a1, a2, a3, b0[j], b1[j]);
-                }
-            } else {
-                const RowConsts c1 = row_consts(sbw[8]);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t w = j == 0 ? wv.x : j == 1 ? wv.y : j == 2 ? wv.z : wv.w;
-                    const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
-                    const uint32_t a1 = deq_r2_fast(lop_nibbles(w >> 4), c1);
-                    const uint32_t a2 = deq_r2_fast(lop_nibbles(w >> 8), c0);
-                    const uint32_t a3 = deq_r2_fast(lop_nibbles(w >> 12), c1);
-                    mma_bf16_16816(acc[i], a0, a1, a2, a3, b0[j], b1[j]);
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const uint32_t w = jj == 0 ? wv.x : jj == 1 ? wv.y : jj == 2 ? wv.z : wv.w;
+                        const uint32_t a0 = deq_r2_fast(lop_nibbles(w), c0);
+                        const uint32_t a1 = deq_r2_fast(lop_nibbles(w >> 4), c1);
+                        const uint32_t a2 = deq_r2_fast(lop_nibbles(w >> 8), c0);
+                        const uint32_t a3 = deq_r2_fast(lop_nibbles(w >> 12), c1);
+                        mma_bf16_16816(acc[i], a0, a1, a2, a3, b0[jj], b1[jj]);
+                    }
                 }
             }
+            // the unit has been read: refill this buffer `stages` units ahead
+            __syncwarp();
+            if (k + j + stages < n_units) {
+                if (lane == 0) issue_unit(a, pq, pg, ring_s + stage * kUnitBytes, bar0 + 8 * stage);
+                step1(pq, pg, G);
+            }
+            if (++stage == stages) {
+                stage = 0;
+                phase ^= 1u;
+            }
         }
-        // the unit has been read: refill this buffer `stages` units ahead
-        __syncwarp();
-        if (k + stages < n_units) {
-            if (lane == 0) issue_unit(a, pq, pg, ring_s + stage * kUnitBytes, bar0 + 8 * stage);
-            step1(pq, pg, G);
-        }
-        if (++stage == stages) {
-            stage = 0;
-            phase ^= 1u;
-        }
-        step1(cq, cg, G);
+        park_quad(a, qcnt, red, cq, first_q, cs, ce, cta, C, acc, rs);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[i][e] = 0.0f;
+        k += seg;
+        ++cq;
+        cg = 0;
     }
-    if (n_units > 0) park_quad(a, qcnt, red, acc_q, first_q, cs, ce, cta, C, acc, rs);
 }
 
 }  // namespace
