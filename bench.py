@@ -19,6 +19,12 @@ roofline: the dominant (only) kernel is the persistent decode kernel, one launch
 qmatmul: BASELINE configs 1 and 2 on the standalone matmul entry point at N = 1: the up_proj
           15360 x 3840 at M = 1 and one layer's seven projections at M in {1, 2, 4, 8}, GB/s of
           algorithmic bytes, launches back to back in a CUDA graph over >= 4x L2 of weight copies.
+decode_real_layers: the same step with the real decoder layer's structure inside the one launch (the
+          four RMSNorms with weights, residual adds, layer scalars, GeGLU on a paired gate|up weight;
+          helios_b200.stack.DecoderStack, the same weight bytes), and its time relative to `value`'s step.
+decode_verify: the MTP verify widths (M = 1, 2, 4, 8 tokens per step) through the decode plan: ms per
+          step and tokens/s, and per layer the step minus an LM-head-only plan of the same width over
+          the layers (BASELINE config 2 through the plan), max over ranks.
 cpu_baseline: the CPU oracle (fp32 accumulation, OpenMP on every host core) on a bounded sample
           (layer 0's seven projections at M = 1), rank 0 at N = 1 only.
 prefill: BASELINE config 5 -- a 16384-token prompt as 8 chunks of 2048 tokens through all 48
@@ -35,6 +41,8 @@ parity: after every timed region, one decode step of a plan with per-layer outpu
 --impl reference: MLX (the reference's library) is absent, so the reference arm times the CPU
           restatement of the reference's CPU quantized_matmul (oracle/, kind "port") on the same
           metric with all host threads; ranks other than 0 exit without work.
+--trace: after the timed regions, one decode step with the plan's tracing build (globaltimer stamps
+          per CTA and phase) summarised per phase kind on rank 0 (the line's "trace" field).
 --case NAME: one small kernel case for an ncu capture (one GPU, a few GB at most; see CASES),
           printing its CUDA-event time per launch.
 """
@@ -144,6 +152,47 @@ def profile_case(a):
     print(json.dumps(out))
 
 
+# words per CTA and phase of a decode-plan trace (g4q_decode_plan_trace): entry, x's producers done,
+# x staged, then the end of each of the kernel's 16 warps' units
+TRACE_WORDS = 3 + 16
+
+
+def trace_summary(tr, layers: int) -> dict:
+    """Per phase kind (q|k|v, o, gate|up, down; medians over the layers) of one traced step, in us:
+    stage = x's producers done -> x staged (median CTA), compute = x staged -> the CTA's last warp
+    done (median and slowest CTA), spread = slowest CTA's end - median CTA's end, lag = the previous
+    phase's slowest CTA end -> this phase's median CTA staged, duration = slowest-CTA end to end."""
+    import numpy as np
+
+    t = tr.astype(np.int64)
+    t = t - t[:, 0, 0].min()
+    entry, prod, staged, wend = t[:, :, 0], t[:, :, 1], t[:, :, 2], t[:, :, 3:]
+    cend = wend.max(axis=2)
+    last_end = cend.max(axis=0)
+    kinds = {"qkv": [], "o": [], "gu": [], "down": []}
+    names = list(kinds)
+    for p in range(1, 4 * layers):
+        kinds[names[p % 4]].append([
+            np.median(staged[:, p] - prod[:, p]), np.median(cend[:, p] - staged[:, p]),
+            (cend[:, p] - staged[:, p]).max(), last_end[p] - np.median(cend[:, p]),
+            np.median(staged[:, p]) - last_end[p - 1], last_end[p] - last_end[p - 1]])
+    out = {"step_us": round(float(last_end[-1]) / 1e3, 1), "per_layer_us": 0.0,
+           "columns": ["stage", "compute_med", "compute_max", "end_spread", "lag", "duration"]}
+    for k, v in kinds.items():
+        m = np.median(np.array(v), axis=0) / 1e3
+        out[k] = [round(float(x), 2) for x in m]
+        out["per_layer_us"] += float(m[5])
+    out["per_layer_us"] = round(out["per_layer_us"], 2)
+    p = 4 * layers
+    out["lm"] = [round(float(x) / 1e3, 2) for x in (np.median(staged[:, p] - prod[:, p]),
+                                                     np.median(cend[:, p] - staged[:, p]),
+                                                     (cend[:, p] - staged[:, p]).max(),
+                                                     last_end[p] - np.median(cend[:, p]),
+                                                     np.median(staged[:, p]) - last_end[p - 1],
+                                                     last_end[p] - last_end[p - 1])]
+    return out
+
+
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -158,6 +207,12 @@ def parse():
     p.add_argument("--no-parity", action="store_true", help="skip the per-phase oracle check after timing")
     p.add_argument("--case", choices=sorted(CASES), help="run one small ncu case instead of the benchmark")
     p.add_argument("--launches", type=int, default=6, help="timed launches of --case")
+    p.add_argument("--no-real-layers", action="store_true",
+                   help="skip the step with the real decoder layer's norms, residuals and GeGLU in the plan")
+    p.add_argument("--trace", action="store_true",
+                   help="after timing, trace one decode step per phase and report a summary (profiling aid)")
+    p.add_argument("--verify-steps", type=int, default=30,
+                   help="timed steps per MTP-verify width through the plan (0: skip that section)")
     return p.parse_args()
 
 
@@ -377,7 +432,7 @@ def main():
     import torch.distributed as dist
 
     from helios_b200 import _lib
-    from helios_b200.quantized import synth_normal
+    from helios_b200.quantized import PHASE_ARGMAX, QMM_RMS_SCALE, DecodePlan, synth_normal
     from helios_b200.stack import StackConfig, SyntheticStack, activation_seed, decode_keys
 
     _lib.load()
@@ -460,6 +515,115 @@ def main():
     clk = clocks.stop() if rank == 0 else None
     tok, _ = decode_keys(key_host)
     del graph
+
+    # ---- MTP verify widths through the plan (decode_block_logits: M tokens per step, one launch) and
+    #      BASELINE config 2 through the plan: per layer, the step minus an LM-head-only plan of the
+    #      same width, over the layers
+    verify = None
+    if args.verify_steps > 0:
+        verify = {"method": "CUDA graph of one plan run per step, CUDA events, max over ranks; per layer = "
+                            "(step - LM-head-only plan) / layers"}
+        for M in (1, 2, 4, 8):
+            hM = synth_normal(activation_seed(M), (M, cfg.hidden), device=dev)
+            xl = torch.zeros((M, cfg.hidden), dtype=torch.bfloat16, device=dev)
+            lm_plan = DecodePlan([(st.lm, xl, None, QMM_RMS_SCALE | PHASE_ARGMAX)], M, rank=st.rank,
+                                 n_ranks=st.size, group=st.group)
+            st.build_plan(M)
+            runs = {"step": lambda: st.decode(hM),
+                    "lm": lambda: lm_plan.run(M, eps=cfg.eps, softcap=cfg.softcap, row_offset=st.v_rows[0],
+                                              tokens=st.tokens[:M], values=st.values[:M], keys=st.keys[:M])}
+            t = {}
+            for name, fn in runs.items():
+                s2 = torch.cuda.Stream()
+                s2.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(s2):
+                    fn()
+                torch.cuda.current_stream().wait_stream(s2)
+                torch.cuda.synchronize()
+                g2 = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g2):
+                    fn()
+                for _ in range(3):
+                    g2.replay()
+                barrier()
+                torch.cuda.synchronize()
+                f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                f0.record()
+                for _ in range(args.verify_steps):
+                    g2.replay()
+                f1.record()
+                torch.cuda.synchronize()
+                barrier()
+                t[name] = over_ranks(f0.elapsed_time(f1) / args.verify_steps)[0]
+                del g2
+            assert _lib.device_error() == 0
+            lay_us = (t["step"] - t["lm"]) * 1e3 / cfg.layers
+            verify[str(M)] = {"ms_per_step": round(t["step"], 5), "tok_s": round(M * 1e3 / t["step"], 1),
+                              "weight_gbs": round(st.local_weight_bytes() * world / (t["step"] * 1e-3) / 1e9, 1),
+                              "lm_head_only_us": round(t["lm"] * 1e3, 2), "us_per_layer": round(lay_us, 2)}
+            lm_plan.free()
+        st.plan.free()
+        st.plan = None
+
+    # ---- the real decoder layer's structure in the same single-launch step: input / post-attention /
+    #      pre-FF / post-FF RMSNorms with their weights, residual adds, layer scalars and the GeGLU on a
+    #      paired gate|up weight, all inside the decode kernel (DecoderStack: same weight bytes)
+    real = None
+    if not args.no_real_layers:
+        from helios_b200.stack import DecoderStack
+        ds = DecoderStack(cfg, rank, world, group, max_tokens=1)
+        ds.build_plan(1)
+        rstep = lambda: ds.decode(h_static)
+        s3 = torch.cuda.Stream()
+        s3.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s3):
+            rstep()
+        torch.cuda.current_stream().wait_stream(s3)
+        torch.cuda.synchronize()
+        g3 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g3):
+            rstep()
+        for _ in range(max(args.warmup, 3)):
+            g3.replay()
+        barrier()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(args.steps):
+            g3.replay()
+        f1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ms_real = over_ranks(f0.elapsed_time(f1) / args.steps)[0]
+        del g3
+        assert _lib.device_error() == 0
+        real = {"workload": "48 real-structure layers (norm weights, residual stream, layer scalars, GeGLU "
+                            "phase) + final norm + LM head, one plan launch per step",
+                "ms_per_step": round(ms_real, 5), "tok_s": round(1e3 / ms_real, 1),
+                "weight_gbs": round(ds.local_weight_bytes() * world / (ms_real * 1e-3) / 1e9, 1),
+                "vs_synthetic_step": round(ms_real / ms, 4), "token": decode_keys(ds.keys[:1])[0][0]}
+        ds.free()
+
+    # ---- per-phase timeline of one step (the plan's tracing build: globaltimer stamps per CTA and
+    #      phase), summarised per phase kind on rank 0; a profiling aid, after the timed regions
+    trace = None
+    if args.trace:
+        st.build_plan(1)
+        buf = st.plan.trace(True)
+        for _ in range(3):
+            st.decode(h_static)
+        torch.cuda.synchronize()
+        barrier()
+        st.decode(h_static)
+        torch.cuda.synchronize()
+        assert _lib.device_error() == 0
+        n_ph = 4 * cfg.layers + 1
+        tr = buf.cpu().view(-1, n_ph, TRACE_WORDS)
+        st.plan.trace(False)
+        st.plan.free()
+        st.plan = None
+        if rank == 0:
+            trace = trace_summary(tr.numpy(), cfg.layers)
 
     # ---- chunked prefill: a 16384-token prompt as 8 chunks of 2048 tokens, each
     #      chunk through all layers on the tcgen05 GEMM path; the LM head on the final chunk's last
@@ -622,6 +786,12 @@ def main():
             line["cpu_baseline"] = cpu
         if prefill is not None:
             line["prefill"] = prefill
+        if verify is not None:
+            line["decode_verify"] = verify
+        if trace is not None:
+            line["trace"] = trace
+        if real is not None:
+            line["decode_real_layers"] = real
         if qmm is not None:
             line["qmatmul"] = qmm
         print(json.dumps(line), flush=True)

@@ -47,20 +47,24 @@
 namespace g4q {
 namespace {
 
-constexpr int kWarps = 16;
+constexpr int kWarps = 16;                        // warps per CTA at M = 1, 2, 4 (the most at any M)
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxStages = 3;
 constexpr uint32_t kUnitPacked = 4 * 512;
 constexpr uint32_t kUnitSb = 64 * 4;
 constexpr uint32_t kUnitBytes = kUnitPacked + kUnitSb;
-constexpr int kMaxPlanTokens = 4;                 // tokens per step (M): 1, 2 or 4
-constexpr int kXKeyStride = 8;                    // key-exchange words per rank: keys[0..M), tag at [7]
+constexpr int kMaxPlanTokens = 8;                 // tokens per step (M): 1, 2, 4 or 8
+constexpr int kXKeyStride = 16;                   // key-exchange words per rank: keys[0..M), tag at [15]
 
-// Ring stages per warp at M tokens: three at M <= 2; two at M = 4, which leaves shared memory for
-// the four tokens' x and partial sums (46 KB of weights in flight per SM is still well above what
-// the HBM latency needs).
+// Warps per CTA and ring stages per warp at M tokens: 16 warps of three stages at M <= 4; at M = 8
+// the partial-sum buffers (2 x 64 rows x 8 tokens of fp32 per warp) and the tokens' x need the room,
+// so 12 warps of two stages (55 KB of weights in flight per SM, still above what HBM latency needs).
 template <int kM>
-constexpr int ring_stages() { return 3; }
+constexpr int warps_of() { return kM == 8 ? 12 : kWarps; }
+template <int kM>
+constexpr int ring_stages() { return kM == 8 ? 2 : 3; }
+int warps_for(int tokens) { return tokens == 8 ? 12 : kWarps; }
+int stages_for(int tokens) { return tokens == 8 ? 2 : 3; }
 constexpr uint32_t kFlagPrologue = 0x100u;           // PhaseDev::flags: the phase has a prologue
 constexpr int kSlots = 16;                        // CTA ranges one 64-row quad may be cut into
 constexpr int kBufs = 3;                          // exchange / slot buffers rotate over three phases
@@ -206,30 +210,33 @@ __device__ __forceinline__ int64_t xbuf_w(const DecodeArgs& a, int p, int tok, i
     return (int64_t)(p % kBufs) * a.xbuf_words + (int64_t)tok * a.xbuf_tok + (n >> 1);
 }
 
-// Rank partials of the allreduce phase with ordinal ar: word index of (quad q, rank r, source CTA
-// offset c, token tok, row 0). The buffers rotate over allreduce ordinals: a rank writes buffer j mod 3
-// again only after every rank has sent allreduce j+2, i.e. after every rank has finished reading
-// allreduce j.
+// Rank partials of the allreduce phase with ordinal ar: word index of (quad q, slot, token tok, row 0),
+// where the partial of rank r's c-th CTA of a quad cut into nc CTA ranges takes slot r * nc + c, so a
+// quad's n_ranks * nc partials are contiguous in rank-major, CTA order (one flattened poll sums them).
+// The buffers rotate over allreduce ordinals: a rank writes buffer j mod 3 again only after every
+// rank has sent allreduce j+2, i.e. after every rank has finished reading allreduce j.
 template <int kM>
-__device__ __forceinline__ int64_t rp_word(const DecodeArgs& a, const PhaseDev& P, int ar, int q, int r, int c,
-                                           int tok) {
-    return (int64_t)(ar % kBufs) * a.rp_words + (((((int64_t)q * a.n_ranks + r) * P.ks + c) * kM + tok) * 64);
+__device__ __forceinline__ int64_t rp_word(const DecodeArgs& a, const PhaseDev& P, int ar, int q, int slot, int tok) {
+    return (int64_t)(ar % kBufs) * a.rp_words + (((((int64_t)q * a.n_ranks * P.ks) + slot) * kM + tok) * 64);
 }
 
 // Warp w owns the contiguous units [wstart(w), wstart(w + 1)) of its CTA's n units of a phase
-// (relative numbering): the first n % kWarps warps take one unit more, warps past n own none.
+// (relative numbering): the first n % kW warps take one unit more, warps past n own none.
+template <int kW>
 __device__ __forceinline__ int wstart(int w, int n) {
-    const int b = n / kWarps, r = n - b * kWarps;
+    const int b = n / kW, r = n - b * kW;
     return w * b + min(w, r);
 }
 
+template <int kW>
 __device__ __forceinline__ int warp_of(int u, int n) {   // owner of relative unit u, 0 <= u < n
-    const int b = n / kWarps, r = n - b * kWarps, big = r * (b + 1);
+    const int b = n / kW, r = n - b * kW, big = r * (b + 1);
     return u < big ? u / (b + 1) : r + (u - big) / b;
 }
 
 // The prefetching position of one warp, across phases: the next unit to issue is group g of the
 // current quad of phase p, at byte offsets off_p / off_s of that phase's packed words / sb.
+template <int kW>
 struct Pre {
     int p, left, g, G;
     uint32_t off_p, off_s, step_p, step_s;
@@ -239,8 +246,8 @@ struct Pre {
         while (p < a.n_phases) {
             const PhaseDev& P = a.ph[p];
             const int cs = range_start(cta, P.U, C), n = range_start(cta + 1, P.U, C) - cs;
-            const int u0 = wstart(w, n);
-            left = wstart(w + 1, n) - u0;
+            const int u0 = wstart<kW>(w, n);
+            left = wstart<kW>(w + 1, n) - u0;
             if (left > 0) {
                 G = P.G;
                 const int u = cs + u0, q = u / G;
@@ -494,7 +501,8 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
     __threadfence_block();
     __syncwarp();
     const int lo = max(cs, q * G), hi = min(ce, (q + 1) * G);
-    const int wa = warp_of(lo - cs, n), wb = warp_of(hi - 1 - cs, n);
+    constexpr int kW = warps_of<kM>();
+    const int wa = warp_of<kW>(lo - cs, n), wb = warp_of<kW>(hi - 1 - cs, n);
     const int qi = q - cs / G;
     if (wb > wa) {
         int last = 0;
@@ -505,7 +513,7 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
         if (lane == 0) sh.qcnt[qi] = 0;
     }
     // warp wa holds q in slot 0 only if q is also its first quad; the others hold it as their first
-    const int slot_a = (cs + wstart(wa, n)) / G == q ? 0 : 1;
+    const int slot_a = (cs + wstart<kW>(wa, n)) / G == q ? 0 : 1;
     float2 f[kM];
 #pragma unroll
     for (int tok = 0; tok < kM; ++tok) {
@@ -527,14 +535,14 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
     if (kTP && P.src_ranks > 1) {
 #pragma unroll
         for (int tok = 0; tok < kM; ++tok)
-            send_partial(a.peer_rp, a.n_ranks, rp_word<kM>(a, P, P.ar, q, a.rank, cta - cf, tok), f[tok].x, f[tok].y,
-                         tag);
+            send_partial(a.peer_rp, a.n_ranks, rp_word<kM>(a, P, P.ar, q, a.rank * (cl - cf + 1) + cta - cf, tok),
+                         f[tok].x, f[tok].y, tag);
         if (cta != cf) return;
         const int nc = cl - cf + 1;
 #pragma unroll
-        for (int tok = 0; tok < kM; ++tok)
-            for (int r = 0; r < a.n_ranks; ++r)   // rank-major, then CTA order: the same bits on every rank
-                f[tok] = poll_sum(a.rp + rp_word<kM>(a, P, P.ar, q, r, 0, tok), nc, kM * 64, tag, f[tok], r > 0, a.err);
+        for (int tok = 0; tok < kM; ++tok)   // rank-major, then CTA order: the same bits on every rank
+            f[tok] = poll_sum(a.rp + rp_word<kM>(a, P, P.ar, q, 0, tok), a.n_ranks * nc, kM * 64, tag, f[tok], false,
+                              a.err);
     } else if (!whole) {
         if (cta != cf) {
 #pragma unroll
@@ -576,6 +584,8 @@ __device__ __forceinline__ int slot_group(const PhaseDev& P, int cs, int j) {
 }
 
 constexpr int kMaxStageLoads = 8;   // 16-byte exchange loads per thread and token (four values each)
+// 16 warps stage the widest x in one pass; with 12 warps (M = 8) the host refuses a phase whose
+// staged x from the exchange buffer exceeds kMaxStageLoads loads per thread
 static_assert(kMaxStageLoads * kThreads * 4 >= kMaxXQuads * 64, "staging must cover the widest x");
 
 // Staging of one token's x from the exchange buffer (out of line: its loads in flight need registers
@@ -585,7 +595,7 @@ static_assert(kMaxStageLoads * kThreads * 4 >= kMaxXQuads * 64, "staging must co
 // kWin: the CTA's window (slot j holds group (cs + j) mod G); otherwise slot j holds group j. The
 // phase's numbers come by value: loads through the phase record would be repeated after every
 // polling load (each is a memory clobber).
-template <bool kWin>
+template <bool kWin, int kT>
 __device__ __noinline__ float stage_xbuf(const unsigned long long* src, int nslots, int cs, int G, uint32_t tag,
                                          uint32_t* xs, bool rms, int* err) {
     float ss = 0.0f;
@@ -605,7 +615,7 @@ __device__ __noinline__ float stage_xbuf(const unsigned long long* src, int nslo
     uint32_t missing = 0;
 #pragma unroll
     for (int j = 0; j < kMaxStageLoads; ++j) {
-        const int i = threadIdx.x + j * kThreads;
+        const int i = threadIdx.x + j * kT;
         if (i < nl) {
             unsigned long long u0, u1;
             ld_relaxed2(src + word_of(i), u0, u1);
@@ -620,7 +630,7 @@ __device__ __noinline__ float stage_xbuf(const unsigned long long* src, int nslo
 #pragma unroll
             for (int j = 0; j < kMaxStageLoads; ++j) {
                 if (missing & (1u << j)) {
-                    const int i = threadIdx.x + j * kThreads;
+                    const int i = threadIdx.x + j * kT;
                     unsigned long long u0, u1;
                     ld_relaxed2(src + word_of(i), u0, u1);
                     w[j][0] = (uint32_t)u0;
@@ -636,7 +646,7 @@ __device__ __noinline__ float stage_xbuf(const unsigned long long* src, int nslo
     }
 #pragma unroll
     for (int j = 0; j < kMaxStageLoads; ++j) {
-        const int i = threadIdx.x + j * kThreads;
+        const int i = threadIdx.x + j * kT;
         if (i < nl) {
             const uint32_t lo = w[j][0], hi = w[j][1];
             xs[xperm(2 * i)] = lo;
@@ -662,7 +672,7 @@ __device__ __forceinline__ void stage_x(const DecodeArgs& a, const PhaseDev& P, 
         uint32_t* xt = xs + (size_t)tok * P.xslots * 32;
         float s = 0.0f;
         if (P.src < 0) {
-            for (int u = threadIdx.x; u < P.xslots * 8; u += kThreads) {
+            for (int u = threadIdx.x; u < P.xslots * 8; u += warps_of<kM>() * 32) {
                 const int g = slot_group(P, cs, u >> 3);
                 const uint4 v = __ldcg(reinterpret_cast<const uint4*>(P.x + (int64_t)tok * P.ldx + (int64_t)g * 64) + (u & 7));
                 xt[xperm(4 * u)] = v.x;
@@ -682,9 +692,11 @@ __device__ __forceinline__ void stage_x(const DecodeArgs& a, const PhaseDev& P, 
         } else {
             const unsigned long long* src = a.xbuf + xbuf_w(a, P.src, tok, P.src_col);
             if (kM > 1 && P.xwin)
-                s = stage_xbuf<kM != 1>(src, P.xslots, cs, P.G, phase_tag(tag0, P.src), xt, rms, a.err);
+                s = stage_xbuf<kM != 1, warps_of<kM>() * 32>(src, P.xslots, cs, P.G, phase_tag(tag0, P.src), xt, rms,
+                                                             a.err);
             else
-                s = stage_xbuf<false>(src, P.xslots, cs, P.G, phase_tag(tag0, P.src), xt, rms, a.err);
+                s = stage_xbuf<false, warps_of<kM>() * 32>(src, P.xslots, cs, P.G, phase_tag(tag0, P.src), xt, rms,
+                                                           a.err);
         }
         ss[tok] = s;
     }
@@ -707,18 +719,19 @@ __device__ __forceinline__ void cta_inv_rms(CtaShared<kM>& sh, float (&ss)[kM], 
 #pragma unroll
     for (int tok = 0; tok < kM; ++tok) {
         float s = 0.0f;
-        for (int w = 0; w < kWarps; ++w) s += sh.wss[w][tok];
+        for (int w = 0; w < warps_of<kM>(); ++w) s += sh.wss[w][tok];
         inv[tok] = __frsqrt_rn(s / (float)K + eps);
     }
     __syncthreads();   // sh.wss is written again by the next reduction
 }
 
 // The phase's prologue, in place on the staged x of every token (all K columns staged: a prologue
-// phase is never windowed). Thread t owns the pair words t, t + kThreads, ... (columns 2w, 2w + 1)
+// phase is never windowed). Thread t owns the pair words t, t + kT, ... (columns 2w, 2w + 1)
 // in every pass, so no pass needs a barrier of its own beyond the norms' reductions.
 template <int kM>
 __device__ __noinline__ void prologue(const DecodeArgs& a, const PhaseDev& P, uint32_t* xs, CtaShared<kM>& sh,
                                       int cta) {
+    constexpr int kT = warps_of<kM>() * 32;
     const int K = P.K, words = K / 2, tstride = P.xslots * 32;
     auto bfv = [](uint32_t h) { return bf16_bits_to_f32(h & 0xffffu); };
     auto rb = [](float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f)); };
@@ -727,7 +740,7 @@ __device__ __noinline__ void prologue(const DecodeArgs& a, const PhaseDev& P, ui
 #pragma unroll
         for (int tok = 0; tok < kM; ++tok) {
             float s = 0.0f;
-            for (int w = threadIdx.x; w < words; w += kThreads) {
+            for (int w = threadIdx.x; w < words; w += kT) {
                 const uint32_t v = xs[tok * tstride + xperm(w)];
                 const float lo = bfv(v), hi = bfv(v >> 16);
                 s = fmaf(lo, lo, s);
@@ -738,7 +751,7 @@ __device__ __noinline__ void prologue(const DecodeArgs& a, const PhaseDev& P, ui
         cta_inv_rms<kM>(sh, ss, K, P.peps, inv);
 #pragma unroll
         for (int tok = 0; tok < kM; ++tok)
-            for (int w = threadIdx.x; w < words; w += kThreads) {
+            for (int w = threadIdx.x; w < words; w += kT) {
                 uint32_t* e = xs + tok * tstride + xperm(w);
                 const uint32_t v = *e, wv = __ldg(reinterpret_cast<const uint32_t*>(P.post_w) + w);
                 const float lo = rb(bfv(wv) * rb(bfv(v) * inv[tok]));
@@ -758,7 +771,7 @@ __device__ __noinline__ void prologue(const DecodeArgs& a, const PhaseDev& P, ui
             uint32_t* ruser =
                 P.res_user != nullptr ? reinterpret_cast<uint32_t*>(P.res_user + (int64_t)tok * P.ld_res_user) : nullptr;
             float s = 0.0f;
-            for (int w = threadIdx.x; w < words; w += kThreads) {
+            for (int w = threadIdx.x; w < words; w += kT) {
                 uint32_t* e = xs + tok * tstride + xperm(w);
                 uint32_t v = *e;
                 if (P.res_mode == 2) {   // residual add, then the layer scalar, each rounded to bf16
@@ -786,7 +799,7 @@ __device__ __noinline__ void prologue(const DecodeArgs& a, const PhaseDev& P, ui
             cta_inv_rms<kM>(sh, ss, K, P.peps, inv);
 #pragma unroll
             for (int tok = 0; tok < kM; ++tok)
-                for (int w = threadIdx.x; w < words; w += kThreads) {
+                for (int w = threadIdx.x; w < words; w += kT) {
                     uint32_t* e = xs + tok * tstride + xperm(w);
                     const uint32_t v = *e, wv = __ldg(reinterpret_cast<const uint32_t*>(P.norm_w) + w);
                     const float lo = rb(bfv(wv) * rb(bfv(v) * inv[tok]));
@@ -841,8 +854,9 @@ __device__ __forceinline__ void exchange_keys(const DecodeArgs& a, unsigned long
 // CTA's per-phase timeline into a.trace (a profiling build selected at run time; the default
 // instantiations have no trace code).
 template <bool kTP, int kM, bool kTrace = false, bool kPro = false>
-__global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(warps_of<kM>() * 32, 1) decode_kernel(DecodeArgs a) {
     constexpr int kS = ring_stages<kM>();
+    constexpr int kW = warps_of<kM>();
     constexpr uint32_t kRing = kS * kUnitBytes;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ CtaShared<kM> sh;
@@ -853,8 +867,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
     const int C = gridDim.x, cta = blockIdx.x;
     uint8_t* ring = smem + (size_t)warp * kRing;
     const uint32_t ring_s = saddr(ring);
-    float* red = reinterpret_cast<float*>(smem + (size_t)kWarps * kRing);
-    uint32_t* xs = reinterpret_cast<uint32_t*>(smem + (size_t)kWarps * kRing + (size_t)2 * kWarps * kM * 64 * 4);
+    float* red = reinterpret_cast<float*>(smem + (size_t)kW * kRing);
+    uint32_t* xs = reinterpret_cast<uint32_t*>(smem + (size_t)kW * kRing + (size_t)2 * kW * kM * 64 * 4);
     const uint32_t bar0 = saddr(&sh.bars[warp][0]);
 
     if (lane == 0) {
@@ -874,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         sh.tag0 = (uint32_t)(e % 0xFFFFFFFFull);
     }
     __syncwarp();
-    Pre pre;
+    Pre<kW> pre;
     pre.p = 0;
     pre.enter(a, cta, C, warp);
 
@@ -932,7 +946,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
                 float r = 1.0f;
                 if (rms) {
                     float s = 0.0f;
-                    for (int w = 0; w < kWarps; ++w) s = __fadd_rn(s, sh.wss[w][tok]);
+                    for (int w = 0; w < kW; ++w) s = __fadd_rn(s, sh.wss[w][tok]);
                     r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)P.K), a.eps)));
                 }
                 sh.rs[tok] = r;
@@ -948,8 +962,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
         }
 
         // ---- this warp's units of phase p
-        const int u0 = wstart(warp, ce - cs);
-        const int n_units = wstart(warp + 1, ce - cs) - u0;
+        const int u0 = wstart<kW>(warp, ce - cs);
+        const int n_units = wstart<kW>(warp + 1, ce - cs) - u0;
         // B fragments: this lane's token, two 16-byte loads per unit from the unit's x slot
         const uint4* xt = reinterpret_cast<const uint4*>(xs) + (size_t)xtok * P.xslots * 8 + 2 * t;
         float acc[4][4];
@@ -1038,7 +1052,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs a) {
             int last_warp = 0;
             if (lane == 0) {
                 __threadfence_block();
-                last_warp = atomicAdd(&sh.warps_finished, 1) == kWarps - 1;
+                last_warp = atomicAdd(&sh.warps_finished, 1) == kW - 1;
             }
             last_warp = __shfl_sync(0xffffffffu, last_warp, 0);
             if (last_warp && lane == 0) {
@@ -1093,6 +1107,9 @@ const void* decode_kernel_pick(bool tp, int tokens, bool trace) {
         case 4:
             return tp ? reinterpret_cast<const void*>(decode_kernel<true, 4, false, kPro>)
                       : reinterpret_cast<const void*>(decode_kernel<false, 4, false, kPro>);
+        case 8:
+            return tp ? reinterpret_cast<const void*>(decode_kernel<true, 8, false, kPro>)
+                      : reinterpret_cast<const void*>(decode_kernel<false, 8, false, kPro>);
         default:
             return tp ? reinterpret_cast<const void*>(decode_kernel<true, 1, false, kPro>)
                       : reinterpret_cast<const void*>(decode_kernel<false, 1, false, kPro>);
@@ -1104,7 +1121,7 @@ const void* decode_kernel_for(bool tp, int tokens, bool trace, bool pro) {
 }
 
 size_t ring_bytes_for(int tokens) {
-    return (size_t)kWarps * 3 * kUnitBytes;
+    return (size_t)warps_for(tokens) * stages_for(tokens) * kUnitBytes;
 }
 
 }  // namespace
@@ -1161,8 +1178,8 @@ static void upload_peers(DecodePlan* plan) {
 void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, int rank, int n_ranks,
                          const G4qPhasePrologue* prologues) {
     if (n <= 0 || phases == nullptr) throw Error(G4Q_ERR_INVALID_ARGUMENT, "a plan needs at least one phase");
-    if (max_tokens != 1 && max_tokens != 2 && max_tokens != 4)
-        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "the decode plan runs 1, 2 or 4 tokens per step (max_tokens)");
+    if (max_tokens != 1 && max_tokens != 2 && max_tokens != 4 && max_tokens != 8)
+        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "the decode plan runs 1, 2, 4 or 8 tokens per step (max_tokens)");
     const int kM = max_tokens;
     if (n_ranks < 1 || n_ranks > kMaxRanks || rank < 0 || rank >= n_ranks)
         throw Error(G4Q_ERR_INVALID_ARGUMENT, "rank must be in [0, n_ranks) with 1 <= n_ranks <= 8");
@@ -1294,7 +1311,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     bool pro = false;
     for (int i = 0; i < n; ++i) pro |= (ph[i].flags & (kFlagPrologue | G4Q_PHASE_GEGLU)) != 0;
     const void* kfn = decode_kernel_for(n_ranks > 1, kM, false, pro);
-    const size_t red_bytes = (size_t)2 * kWarps * kM * 64 * 4;
+    const size_t red_bytes = (size_t)2 * warps_for(kM) * kM * 64 * 4;
     const size_t fixed = ring_bytes_for(kM) + red_bytes + 16;
     const size_t smem_max = max_dynamic_smem(kfn);
     if (fixed >= smem_max) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode plan: shared memory");
@@ -1310,6 +1327,10 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
             d.xwin = 1;
             d.xslots = nmax;
         }
+        // staging from the exchange buffer: sixteen 16-byte loads per slot and token, at most
+        // kMaxStageLoads per thread in one pass (a limit only with the 12 warps of M = 8)
+        if (d.src >= 0 && d.xslots * 16 > kMaxStageLoads * warps_for(kM) * 32)
+            throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, tag + "x too wide to stage at this token count");
         max_slots = std::max(max_slots, d.xslots);
     }
     // Prologues: the staged x must be the whole input (phase 0's external x, or all of the previous
@@ -1444,7 +1465,7 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
                                     (int)max_dynamic_smem(kfn_trace)),
                "cudaFuncSetAttribute(decode, tracing)");
     int per_sm = 0;
-    check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kThreads, plan->smem),
+    check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, warps_for(kM) * 32, plan->smem),
                "occupancy(decode)");
     if (per_sm < 1) throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "decode kernel does not fit on an SM");
     plan->magic = kPlanMagic;
@@ -1539,7 +1560,7 @@ void decode_plan_run(void* h, int M, float eps, float softcap, int64_t row_offse
     a.err = device_scratch().err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(plan->grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(warps_for(plan->tokens) * 32);
     cfg.dynamicSmemBytes = plan->smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1561,6 +1582,8 @@ int64_t decode_plan_trace_words(void* h) {
 
 void decode_plan_set_trace(void* h, uint64_t* buffer, int64_t words) {
     DecodePlan* plan = checked_plan(h);
+    if (buffer != nullptr && plan->tokens != 1)
+        throw Error(G4Q_ERR_UNSUPPORTED_CONFIG, "the tracing build runs plans of one token per step");
     if (buffer != nullptr && words < decode_plan_trace_words(h))
         throw Error(G4Q_ERR_INVALID_ARGUMENT, "trace buffer needs " + std::to_string(decode_plan_trace_words(h)) +
                                                   " 64-bit words");

@@ -27,8 +27,8 @@ from typing import List, Optional
 
 import torch
 
-from .quantized import (PHASE_ALLREDUCE, PHASE_ARGMAX, QMM_RMS_SCALE, DecodePlan, QuantizedWeight, lm_head_argmax,
-                        quantized_matmul, synth_matrix)
+from .quantized import (PHASE_ALLREDUCE, PHASE_ARGMAX, PHASE_GEGLU, QMM_RMS_SCALE, DecodePlan, QuantizedWeight,
+                        lm_head_argmax, quantized_matmul, synth_matrix, synth_normal)
 
 BASE_SEED = 0x48454C494F53
 PROJ_IDS = {"q": 0, "k": 1, "v": 2, "o": 3, "gate": 4, "up": 5, "down": 6, "lm": 7}
@@ -356,6 +356,142 @@ class SyntheticStack:
         for L in self.layers:
             for w in L.values():
                 w.free()
+        self.lm.free()
+
+
+def norm_weight(seed: int, n: int, device=None) -> torch.Tensor:
+    """Seeded synthetic RMSNorm weight: bf16(1 + 0.1 * N(0, 1)), [n]."""
+    return (synth_normal(seed, (n,), device=device).float() * 0.1 + 1.0).to(torch.bfloat16)
+
+
+class DecoderStack:
+    """Seeded synthetic weights with the real decoder layer's structure around the quantized linears
+    (layer_forward, native_model.cc:899-970, attention left out: q stands in for its output, as in
+    SyntheticStack): per layer q|k|v, o, a paired gate|up weight whose phase applies the GeGLU, down,
+    the four RMSNorm weights (input, post-attention, pre-feed-forward, post-feed-forward) and the
+    layer scalar, then the final norm and the LM head. ``build_plan`` makes the whole step ONE decode
+    plan with the norms, residual adds and scalars as phase prologues:
+
+        q|k|v   prologue [post_ffn norm of the previous layer, residual add, its layer scalar]
+                then input_layernorm (layer 0: x starts the residual stream)
+        o       x = q
+        gate|up prologue post_attention_layernorm, residual add, pre_feedforward_layernorm; GeGLU
+        down    x = the GeGLU output
+        LM head prologue the last layer's post_ffn norm, residual add and scalar, then the final norm
+
+    Tensor parallel like SyntheticStack (q/k/v, gate|up and LM-head rows split, o/down K split with
+    the allreduce inside the kernel); the residual stream is kept whole on every rank."""
+
+    def __init__(self, cfg: StackConfig, tp_rank: int = 0, tp_size: int = 1, group=None, max_tokens: int = 8):
+        self.cfg, self.rank, self.size, self.group = cfg, tp_rank, tp_size, group
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        sh = cfg.shapes()
+        plan = shard_plan(cfg, tp_rank, tp_size)
+        self.q_rows, self.kv_rows, self.i_rows = plan["q_rows"], plan["kv_rows"], plan["i_rows"]
+        self.o_cols, self.d_cols, self.v_rows = plan["o_cols"], plan["d_cols"], plan["v_rows"]
+        self.nq = self.q_rows[1] - self.q_rows[0]
+        self.nkv = self.kv_rows[1] - self.kv_rows[0]
+        self.ni = self.i_rows[1] - self.i_rows[0]
+        self.max_tokens = max_tokens
+        self.layers: List[dict] = []
+        i0, i1 = self.i_rows
+        for layer in range(cfg.layers):
+            mats = {p: synth_matrix(matrix_seed(layer, p), *sh[p]) for p in ("q", "k", "v")}
+            qkv = QuantizedWeight.concat([(*mats["q"], self.q_rows), (*mats["k"], self.kv_rows),
+                                          (*mats["v"], self.kv_rows)])
+            del mats
+            o = QuantizedWeight.from_mlx(*synth_matrix(matrix_seed(layer, "o"), *sh["o"]), cols=self.o_cols)
+            gate = synth_matrix(matrix_seed(layer, "gate"), *sh["gate"])
+            up = synth_matrix(matrix_seed(layer, "up"), *sh["up"])
+            gu = QuantizedWeight.geglu_pair(tuple(t[i0:i1] for t in gate), tuple(t[i0:i1] for t in up))
+            del gate, up
+            down = QuantizedWeight.from_mlx(*synth_matrix(matrix_seed(layer, "down"), *sh["down"]), cols=self.d_cols)
+            s = BASE_SEED ^ 0xA000 ^ (layer * 8)
+            self.layers.append({"qkv": qkv, "o": o, "gu": gu, "down": down,
+                                "in_norm": norm_weight(s, cfg.hidden), "post_attn": norm_weight(s + 1, cfg.hidden),
+                                "pre_ffn": norm_weight(s + 2, cfg.hidden), "post_ffn": norm_weight(s + 3, cfg.hidden),
+                                "scalar": torch.tensor([1.0 - (layer % 4) / 16], dtype=torch.bfloat16,
+                                                       device=self.device)})
+        self.lm = QuantizedWeight.from_mlx(*synth_matrix(matrix_seed(0, "lm"), *sh["lm"]), rows=self.v_rows)
+        self.final_norm = norm_weight(BASE_SEED ^ 0xAFFF, cfg.hidden)
+        dev, M = self.device, max_tokens
+        self.tokens = torch.empty(M, dtype=torch.int32, device=dev)
+        self.values = torch.empty(M, dtype=torch.float32, device=dev)
+        self.keys = torch.empty(M, dtype=torch.int64, device=dev)
+        self.plan = None
+        torch.cuda.synchronize()
+
+    def build_plan(self, M: int = 1, keep_layers: bool = False) -> DecodePlan:
+        """The whole step as one plan of M tokens. ``keep_layers``: every layer writes its own output
+        buffers and copies of the residual stream (``self.outs[l]`` with qkv, o, act, h, res_a (the
+        stream before q|k|v's input norm), res_b (before gate|up's)), so every phase's input and
+        output stay readable after the step; the kernel's work and dataflow are the same."""
+        c = self.cfg
+        if self.plan is not None:
+            self.plan.free()
+        if M > self.max_tokens:
+            raise ValueError("M above the stack's max_tokens")
+        bf = dict(dtype=torch.bfloat16, device=self.device)
+        self.h_in = torch.zeros((M, c.hidden), **bf)
+        shared = None if keep_layers else {
+            "qkv": torch.empty((M, self.nq + 2 * self.nkv), **bf), "o": torch.empty((M, c.hidden), **bf),
+            "act": torch.empty((M, self.ni), **bf), "h": torch.empty((M, c.hidden), **bf)}
+        self.outs = []
+        phases, pro, x = [], [], self.h_in
+        ar = PHASE_ALLREDUCE if self.size > 1 else 0
+        for i, L in enumerate(self.layers):
+            if keep_layers:
+                b = {"qkv": torch.empty((M, self.nq + 2 * self.nkv), **bf), "o": torch.empty((M, c.hidden), **bf),
+                     "act": torch.empty((M, self.ni), **bf), "h": torch.empty((M, c.hidden), **bf),
+                     "res_a": torch.empty((M, c.hidden), **bf), "res_b": torch.empty((M, c.hidden), **bf)}
+                self.outs.append(b)
+            else:
+                b = shared
+            if i == 0:
+                pro.append({"residual": 1, "norm_weight": L["in_norm"], "residual_out": b.get("res_a"),
+                            "eps": c.eps})
+            else:
+                P = self.layers[i - 1]
+                pro.append({"post_norm_weight": P["post_ffn"], "residual": 2, "layer_scalar": P["scalar"],
+                            "norm_weight": L["in_norm"], "residual_out": b.get("res_a"), "eps": c.eps})
+            phases.append((L["qkv"], x, b["qkv"], 0))
+            pro.append(None)
+            phases.append((L["o"], b["qkv"][:, : self.nq], b["o"], ar))
+            pro.append({"post_norm_weight": L["post_attn"], "residual": 2, "norm_weight": L["pre_ffn"],
+                        "residual_out": b.get("res_b"), "eps": c.eps})
+            phases.append((L["gu"], b["o"], b["act"], PHASE_GEGLU))
+            pro.append(None)
+            phases.append((L["down"], b["act"], b["h"], ar))
+            x = b["h"]
+        P = self.layers[-1]
+        self.res_final = torch.empty((M, c.hidden), **bf)
+        pro.append({"post_norm_weight": P["post_ffn"], "residual": 2, "layer_scalar": P["scalar"],
+                    "norm_weight": self.final_norm, "residual_out": self.res_final, "eps": c.eps})
+        phases.append((self.lm, x, None, PHASE_ARGMAX))
+        self.plan = DecodePlan(phases, M, rank=self.rank, n_ranks=self.size, group=self.group, prologues=pro)
+        self.plan_tokens = M
+        return self.plan
+
+    def decode(self, h: torch.Tensor, logits: Optional[torch.Tensor] = None):
+        """One step: h [M, hidden] (the plan's M) -> the M greedy keys (LM-head logits into ``logits``,
+        bf16 [M, vocab shard], when given)."""
+        M = h.shape[0]
+        self.h_in[:M].copy_(h)
+        self.plan.run(M, softcap=self.cfg.softcap, row_offset=self.v_rows[0], tokens=self.tokens[:M],
+                      values=self.values[:M], keys=self.keys[:M], logits=logits)
+        return self.keys[:M]
+
+    def local_weight_bytes(self) -> int:
+        mats = [w for L in self.layers for k, w in L.items() if k in ("qkv", "o", "gu", "down")] + [self.lm]
+        return sum(w.rows * w.cols * 9 // 16 for w in mats)
+
+    def free(self):
+        if self.plan is not None:
+            self.plan.free()
+            self.plan = None
+        for L in self.layers:
+            for k in ("qkv", "o", "gu", "down"):
+                L[k].free()
         self.lm.free()
 
 

@@ -286,7 +286,7 @@ G4qStatus g4q_rms_norm_residual(const uint16_t* x, int64_t ldx, const uint16_t* 
  * softcap and a first-index argmax, reported as in g4q_lm_head_argmax. Pointers are fixed at plan
  * creation (device memory); g4q_decode_plan_run launches one cooperative grid on `stream` and
  * allocates nothing, so it can be captured in a CUDA graph. max_tokens (the M of every step: 1, or
- * the MTP-verify widths 2 and 4 of decode_block_logits, native_model.cc:1954-2026) fixes the plan's
+ * the MTP-verify widths 2, 4 and 8 of decode_block_logits, native_model.cc:1954-2026) fixes the plan's
  * tokens per step; x and y are then [M, ld] row-major, and run takes exactly that M (logits, when
  * given, [M, ld_logits]; tokens / values / keys hold M entries). Runs of one plan must not overlap on
  * the GPU. */

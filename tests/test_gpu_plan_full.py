@@ -16,10 +16,11 @@ from stack_parity import check_decode_step
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("M,layers", [(1, 6), (2, 4), (4, 4)])
+@pytest.mark.parametrize("M,layers", [(1, 6), (2, 4), (4, 4), (8, 3)])
 def test_full_width_decode_plan_every_phase(cuda, oracle, M, layers):
-    """M tokens per step (1, and the MTP-verify widths 2 and 4: the tokens are the MMA's n dimension;
-    at M = 4 down_proj's 15360-wide x is staged per CTA as the window of its own range)."""
+    """M tokens per step (1, and the MTP-verify widths 2, 4 and 8: the tokens are the MMA's n dimension;
+    at M = 4 and 8 down_proj's 15360-wide x is staged per CTA as the window of its own range; M = 8
+    runs the 12-warp kernel)."""
     from helios_b200 import _lib
     from helios_b200.quantized import synth_normal
     from helios_b200.stack import StackConfig, SyntheticStack, activation_seed, decode_keys

@@ -35,11 +35,6 @@ pytestmark = pytest.mark.gpu
 LAYERS = 2
 
 
-def _norm_weight(seed, n, device):
-    from helios_b200.quantized import synth_normal
-    return (synth_normal(seed, (n,)).float() * 0.1 + 1.0).to(torch.bfloat16).to(device)
-
-
 def _excess(y_bits, y_exact):
     from stack_parity import _excess_ratio
     return _excess_ratio(y_bits, y_exact)
@@ -53,102 +48,41 @@ def _close_residual(A, got, want, tag):
     assert float(np.abs(g - w).max()) <= 1e-2 * rms, f"{tag}: residual differs by more than 1e-2 * rms"
 
 
-class _Layers:
-    """Real-layer weights on the GPU (paired gate|up) and their norm weights and scalars."""
-
-    def __init__(self, device, cfg):
-        from helios_b200.quantized import QuantizedWeight, synth_matrix
-        from helios_b200.stack import matrix_seed
-        sh = cfg.shapes()
-        self.cfg, self.L = cfg, []
-        for layer in range(LAYERS):
-            mats = {p: synth_matrix(matrix_seed(layer, p), *sh[p]) for p in ("q", "k", "v")}
-            qkv = QuantizedWeight.concat([mats["q"], mats["k"], mats["v"]])
-            del mats
-            o = QuantizedWeight.from_mlx(*synth_matrix(matrix_seed(layer, "o"), *sh["o"]))
-            gu = QuantizedWeight.geglu_pair(synth_matrix(matrix_seed(layer, "gate"), *sh["gate"]),
-                                            synth_matrix(matrix_seed(layer, "up"), *sh["up"]))
-            down = QuantizedWeight.from_mlx(*synth_matrix(matrix_seed(layer, "down"), *sh["down"]))
-            s = 1000 + 10 * layer
-            self.L.append({"qkv": qkv, "o": o, "gu": gu, "down": down,
-                           "in_norm": _norm_weight(s, cfg.hidden, device),
-                           "post_attn": _norm_weight(s + 1, cfg.hidden, device),
-                           "pre_ffn": _norm_weight(s + 2, cfg.hidden, device),
-                           "post_ffn": _norm_weight(s + 3, cfg.hidden, device),
-                           "scalar": torch.tensor([0.75 - 0.125 * layer], dtype=torch.bfloat16, device=device)})
-        self.lm = QuantizedWeight.from_mlx(*synth_matrix(matrix_seed(0, "lm"), *sh["lm"]))
-        self.final_norm = _norm_weight(999, cfg.hidden, device)
-
-    def plan(self, M, device):
-        from helios_b200.quantized import PHASE_ARGMAX, PHASE_GEGLU, DecodePlan
-        c = self.cfg
-        bf = dict(dtype=torch.bfloat16, device=device)
-        self.h_in = torch.zeros((M, c.hidden), **bf)
-        self.outs = []
-        phases, pro, x = [], [], self.h_in
-        for i, L in enumerate(self.L):
-            b = {"qkv": torch.empty((M, c.q_out + 2 * c.kv_out), **bf), "o": torch.empty((M, c.hidden), **bf),
-                 "act": torch.empty((M, c.inter), **bf), "h": torch.empty((M, c.hidden), **bf),
-                 "res_a": torch.empty((M, c.hidden), **bf), "res_b": torch.empty((M, c.hidden), **bf)}
-            self.outs.append(b)
-            if i == 0:
-                pro.append({"residual": 1, "norm_weight": L["in_norm"], "residual_out": b["res_a"], "eps": c.eps})
-            else:
-                P = self.L[i - 1]
-                pro.append({"post_norm_weight": P["post_ffn"], "residual": 2, "layer_scalar": P["scalar"],
-                            "norm_weight": L["in_norm"], "residual_out": b["res_a"], "eps": c.eps})
-            phases.append((L["qkv"], x, b["qkv"], 0))
-            pro.append(None)
-            phases.append((L["o"], b["qkv"][:, : c.q_out], b["o"], 0))
-            pro.append({"post_norm_weight": L["post_attn"], "residual": 2, "norm_weight": L["pre_ffn"],
-                        "residual_out": b["res_b"], "eps": c.eps})
-            phases.append((L["gu"], b["o"], b["act"], PHASE_GEGLU))
-            pro.append(None)
-            phases.append((L["down"], b["act"], b["h"], 0))
-            x = b["h"]
-        P = self.L[-1]
-        self.res_final = torch.empty((M, c.hidden), **bf)
-        pro.append({"post_norm_weight": P["post_ffn"], "residual": 2, "layer_scalar": P["scalar"],
-                    "norm_weight": self.final_norm, "residual_out": self.res_final, "eps": c.eps})
-        phases.append((self.lm, x, None, PHASE_ARGMAX))
-        return DecodePlan(phases, M, prologues=pro)
-
-
 @pytest.fixture(scope="module")
 def layers(cuda):
-    from helios_b200.stack import StackConfig
-    return _Layers(cuda, StackConfig(layers=LAYERS))
+    """helios_b200.stack.DecoderStack: the real layer structure, seeded synthetic weights."""
+    from helios_b200.stack import DecoderStack, StackConfig
+    st = DecoderStack(StackConfig(layers=LAYERS), max_tokens=8)
+    yield st
+    st.free()
 
 
-@pytest.mark.parametrize("M", [1, 2])
+@pytest.mark.parametrize("M", [1, 2, 8])
 def test_real_layer_plan_every_phase(cuda, oracle, layers, M):
     from helios_b200 import _lib
     from helios_b200.quantized import synth_normal
-    from helios_b200.stack import activation_seed, decode_keys
+    from helios_b200.stack import activation_seed
     A, c = oracle, layers.cfg
     A.set_threads(len(os.sched_getaffinity(0)))
     shapes = A.stack_shapes()
-    plan = layers.plan(M, cuda)
+    layers.build_plan(M, keep_layers=True)
     h0 = synth_normal(activation_seed(100 + M), (M, c.hidden))
-    layers.h_in.copy_(h0)
     logits = torch.empty((M, c.vocab), dtype=torch.bfloat16, device=cuda)
-    tokens = torch.empty(M, dtype=torch.int32, device=cuda)
-    values = torch.empty(M, dtype=torch.float32, device=cuda)
-    keys = torch.empty(M, dtype=torch.int64, device=cuda)
-    plan.run(M, softcap=c.softcap, tokens=tokens, values=values, keys=keys, logits=logits)
+    layers.decode(h0, logits=logits)
     torch.cuda.synchronize()
+    tokens, values = layers.tokens[:M], layers.values[:M]
     assert _lib.device_error() == 0
     nw = {k: u16(v) for k, v in (("final", layers.final_norm),)}
     res_prev = None
     worst = {}
-    for i, L in enumerate(layers.L):
+    for i, L in enumerate(layers.layers):
         b = {k: u16(v) for k, v in layers.outs[i].items()}
         w = {k: u16(L[k]) for k in ("in_norm", "post_attn", "pre_ffn", "post_ffn")}
         # the residual stream before the layer and the normalized input of qkv
         if i == 0:
             assert np.array_equal(b["res_a"], u16(h0)), "the first phase starts the residual stream with x"
         else:
-            P = layers.L[i - 1]
+            P = layers.layers[i - 1]
             want = A.rms_norm_residual(u16(layers.outs[i - 1]["h"]), u16(P["post_ffn"]), res_prev,
                                        int(u16(P["scalar"])[0]), c.eps)
             _close_residual(A, b["res_a"], want, f"layer {i} input residual")
@@ -175,7 +109,7 @@ def test_real_layer_plan_every_phase(cuda, oracle, layers, M):
         ye, _ = A.qmm(b["act"], *A.stack_matrix(i, "down", shapes))
         worst[f"{i} down"] = _excess(b["h"], ye)
         res_prev = b["res_b"]
-    P = layers.L[-1]
+    P = layers.layers[-1]
     want = A.rms_norm_residual(u16(layers.outs[-1]["h"]), u16(P["post_ffn"]), res_prev, int(u16(P["scalar"])[0]),
                                c.eps)
     rf = u16(layers.res_final)
@@ -193,17 +127,16 @@ def test_real_layer_plan_every_phase(cuda, oracle, layers, M):
         assert int(tk[m]) == int(t_ref) or abs(float(values[m]) - float(v_ref)) <= 0.125
     # a second step from the same input reproduces every output bit for bit
     first = [u16(t) for b in layers.outs for t in b.values()] + [lg, rf]
-    plan.run(M, softcap=c.softcap, tokens=tokens, values=values, keys=keys, logits=logits)
+    layers.decode(h0, logits=logits)
     torch.cuda.synchronize()
     again = [u16(t) for b in layers.outs for t in b.values()] + [u16(logits), u16(layers.res_final)]
     assert all(np.array_equal(x, y) for x, y in zip(first, again))
-    plan.free()
 
 
 def test_prologue_validation(cuda, layers):
     """Prologue rules the plan enforces before anything runs."""
     from helios_b200.quantized import QMM_RMS_SCALE, PHASE_ARGMAX, DecodePlan, G4qError
-    c, L = layers.cfg, layers.L[0]
+    c, L = layers.cfg, layers.layers[0]
     bf = dict(dtype=torch.bfloat16, device=cuda)
     x = torch.zeros((1, c.hidden), **bf)
     qkv = torch.empty((1, c.q_out + 2 * c.kv_out), **bf)

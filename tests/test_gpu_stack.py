@@ -151,7 +151,7 @@ def test_decode_plan_rejects_bad_phases(cuda, oracle):
     yb = torch.zeros((1, 4096), dtype=torch.bfloat16, device=cuda)
     with pytest.raises(_lib.G4qInvalidArgument):              # argmax phase must be last
         Q.DecodePlan([(big, xb, yb, Q.PHASE_ARGMAX), (big, yb, xb, 0)])
-    for m in (3, 8):                                          # token counts the plan does not take
+    for m in (3, 16):                                         # token counts the plan does not take
         with pytest.raises(_lib.G4qError):
             Q.DecodePlan([(big, xb, yb, 0)], max_tokens=m)
     w.free()
