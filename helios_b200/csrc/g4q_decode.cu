@@ -101,7 +101,8 @@ struct PhaseDev {
     uint16_t* res_user;       // copy of the updated residual stream [M, ld_res_user] or null
     int64_t ld_res_user;
     int res_mode;             // 0 none, 1 the staged values start the residual stream, 2 added to it
-    int res_in, res_out;      // residual-stream buffers read (mode 2) and written (modes 1 and 2)
+    int res_in, res_out;      // residual-stream buffers read (mode 2) and written (modes 1 and 2); res_out
+                              // -1: the stream lives in each CTA's shared memory, res_in words after x
     float peps;               // eps of the prologue norms
 };
 
@@ -760,14 +761,20 @@ __device__ __noinline__ void prologue(const DecodeArgs& a, const PhaseDev& P, ui
             }
     }
     if (P.res_mode != 0 || P.norm_w != nullptr) {
-        // the residual stream was written by CTA 0 in an earlier phase, which fenced before publishing
-        // that phase's first quad; this CTA has polled that quad's words, so a fence orders the reads
-        if (P.res_mode == 2) __threadfence();
+        // Where the stream lives: in this CTA's shared memory when it fits (every CTA stages all of x
+        // in every prologue phase and computes the same bits, so each keeps its own copy, and thread t
+        // always owns the same words: no memory traffic, no fence); otherwise in the plan's global
+        // double buffer, written by CTA 0, which fenced before publishing that phase's first quad --
+        // this CTA has polled that quad's words, so a fence orders its reads.
+        const bool sm = P.res_out < 0;
+        if (P.res_mode == 2 && !sm) __threadfence();
         const float sc = P.scalar != nullptr ? bf16_bits_to_f32(*P.scalar) : 1.0f;
 #pragma unroll
         for (int tok = 0; tok < kM; ++tok) {
-            const uint32_t* rin = reinterpret_cast<const uint32_t*>(a.resbuf + (P.res_in * kM + tok) * a.res_ld);
-            uint32_t* rout = reinterpret_cast<uint32_t*>(a.resbuf + (P.res_out * kM + tok) * a.res_ld);
+            uint32_t* rsm = sm ? xs + P.res_in + tok * (int)(a.res_ld / 2) : nullptr;
+            const uint32_t* rin =
+                sm ? nullptr : reinterpret_cast<const uint32_t*>(a.resbuf + (P.res_in * kM + tok) * a.res_ld);
+            uint32_t* rout = sm ? nullptr : reinterpret_cast<uint32_t*>(a.resbuf + (P.res_out * kM + tok) * a.res_ld);
             uint32_t* ruser =
                 P.res_user != nullptr ? reinterpret_cast<uint32_t*>(P.res_user + (int64_t)tok * P.ld_res_user) : nullptr;
             float s = 0.0f;
@@ -775,7 +782,7 @@ __device__ __noinline__ void prologue(const DecodeArgs& a, const PhaseDev& P, ui
                 uint32_t* e = xs + tok * tstride + xperm(w);
                 uint32_t v = *e;
                 if (P.res_mode == 2) {   // residual add, then the layer scalar, each rounded to bf16
-                    const uint32_t r = __ldcg(rin + w);
+                    const uint32_t r = sm ? rsm[w] : __ldcg(rin + w);
                     float lo = rb(bfv(r) + bfv(v)), hi = rb(bfv(r >> 16) + bfv(v >> 16));
                     if (P.scalar != nullptr) {
                         lo = lo * sc;
@@ -784,9 +791,12 @@ __device__ __noinline__ void prologue(const DecodeArgs& a, const PhaseDev& P, ui
                     v = (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
                     *e = v;
                 }
-                if (P.res_mode != 0 && cta == 0) {
-                    rout[w] = v;
-                    if (ruser) ruser[w] = v;
+                if (P.res_mode != 0) {
+                    if (sm)
+                        rsm[w] = v;
+                    else if (cta == 0)
+                        rout[w] = v;
+                    if (ruser && cta == 0) ruser[w] = v;
                 }
                 const float lo = bfv(v), hi = bfv(v >> 16);
                 s = fmaf(lo, lo, s);
@@ -794,7 +804,7 @@ __device__ __noinline__ void prologue(const DecodeArgs& a, const PhaseDev& P, ui
             }
             ss[tok] = s;
         }
-        if (P.res_mode != 0 && cta == 0) __threadfence();   // before this CTA publishes anything later
+        if (P.res_mode != 0 && cta == 0 && !sm) __threadfence();   // before this CTA publishes anything later
         if (P.norm_w != nullptr) {
             cta_inv_rms<kM>(sh, ss, K, P.peps, inv);
 #pragma unroll
@@ -1428,6 +1438,16 @@ void* decode_plan_create(const G4qDecodePhase* phases, int n, int max_tokens, in
     plan->pro = pro;
     plan->res_ld = std::max(res_k, 8);
     plan->smem = fixed + (size_t)kM * max_slots * 128;
+    // the residual stream in every CTA's shared memory, after the x region, when it fits: its phases
+    // carry res_out = -1 and the stream's word offset from x in res_in
+    if (res_k > 0 && plan->smem + (size_t)kM * plan->res_ld * 2 <= smem_max) {
+        for (int i = 0; i < n; ++i)
+            if (ph[i].res_mode != 0) {
+                ph[i].res_out = -1;
+                ph[i].res_in = (int)(kM * max_slots * 32);
+            }
+        plan->smem += (size_t)kM * plan->res_ld * 2;
+    }
     const void* kfn_trace = decode_kernel_for(n_ranks > 1, 1, true, pro);
     if (plan->smem > smem_max) {
         delete plan;
