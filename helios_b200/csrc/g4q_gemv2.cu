@@ -28,13 +28,13 @@
 namespace g4q {
 namespace {
 
-constexpr int kWarpsV2 = 16;
-constexpr int kThreadsV2 = kWarpsV2 * 32;
+constexpr int kWarpsV2 = 16;                  // warps per CTA (12 when the tokens' x needs the room)
 constexpr int kStages = 3;                    // the most ring stages (the launch may use 2)
 constexpr uint32_t kUnitPacked = 4 * 512;     // four 16-row tiles x one group
 constexpr uint32_t kUnitSb = 64 * 4;
 constexpr uint32_t kUnitBytes = kUnitPacked + kUnitSb;
-constexpr uint32_t kRedBytesPerTok = 2 * kWarpsV2 * 64 * 4;   // [quad parity][tok][warp][row]
+// partial-sum bytes per token of a CTA of w warps: [quad parity][tok][warp][row]
+constexpr uint32_t red_bytes_per_tok(int w) { return 2u * (uint32_t)w * 64u * 4u; }
 constexpr long long kWaitLimitCycles2 = 4000000000ll;
 constexpr uint32_t kOddNibbleMask = 0x00F000F0u;  // q at bits 4-7 of each half: bf16 value q * 2^-129
 
@@ -128,14 +128,16 @@ __device__ __forceinline__ int cta_of_unit(int u, int U, int C) {
 }
 
 // Warp w owns the contiguous units [wstart(w), wstart(w + 1)) of its CTA's n units (relative
-// numbering): the first n % kWarpsV2 warps take one unit more, warps past n own none.
+// numbering): the first n % kW warps take one unit more, warps past n own none.
+template <int kW>
 __device__ __forceinline__ int wstart(int w, int n) {
-    const int b = n / kWarpsV2, r = n - b * kWarpsV2;
+    const int b = n / kW, r = n - b * kW;
     return w * b + min(w, r);
 }
 
+template <int kW>
 __device__ __forceinline__ int warp_of(int u, int n) {   // owner of relative unit u, 0 <= u < n
-    const int b = n / kWarpsV2, r = n - b * kWarpsV2, big = r * (b + 1);
+    const int b = n / kW, r = n - b * kW, big = r * (b + 1);
     return u < big ? u / (b + 1) : r + (u - big) / b;
 }
 
@@ -178,6 +180,7 @@ __device__ __forceinline__ int xperm(int w) {
 // waits. The last contributing warp (arrival counter of the quad's first warp) sums the partials in
 // warp order, then stores a quad whole in this CTA or leaves the CTA's partial in its global slot;
 // the last CTA to arrive at a cut quad sums the slots in CTA order. Results are bit-reproducible.
+template <int kW>
 __device__ __forceinline__ void park_quad(const Gemv2Args& a, int* qcnt, float* red, int q, int first_q, int cs,
                                           int ce, int cta, int C, const float (&acc)[4][4], const float* rs) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, t = lane & 3;
@@ -193,7 +196,7 @@ __device__ __forceinline__ void park_quad(const Gemv2Args& a, int* qcnt, float* 
     __threadfence_block();
     __syncwarp();
     const int lo = max(cs, q * G), hi = min(ce, (q + 1) * G);
-    const int wa = warp_of(lo - cs, n), wb = warp_of(hi - 1 - cs, n);
+    const int wa = warp_of<kW>(lo - cs, n), wb = warp_of<kW>(hi - 1 - cs, n);
     if (wb > wa) {   // shared with other warps: only the last of them goes on
         int last = 0;
         if (lane == 0) last = atomicAdd(&qcnt[wa], 1) == wb - wa;
@@ -203,7 +206,7 @@ __device__ __forceinline__ void park_quad(const Gemv2Args& a, int* qcnt, float* 
         if (lane == 0) qcnt[wa] = 0;
     }
     // warp wa holds q in slot 0 only if q is also its first quad; the others hold it as their first
-    const int slot_a = (cs + wstart(wa, n)) / G == q ? 0 : 1;
+    const int slot_a = (cs + wstart<kW>(wa, n)) / G == q ? 0 : 1;
     const bool whole = cs <= q * G && ce >= (q + 1) * G;
     const int nout = 64 * M;
     float* base = a.slots + (size_t)q * 8 * 512;
@@ -278,14 +281,14 @@ __device__ __forceinline__ void park_quad(const Gemv2Args& a, int* qcnt, float* 
 
 // kRaw: every |scale| < 2^-1 and none subnormal, so the odd-nibble rows dequantize from the raw masked bits (q * 2^-129
 // read as bf16, times s * 2^129); otherwise all four rows go through the (128 + q) magic.
-template <bool kRaw>
-__global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
+template <bool kRaw, int kW>
+__global__ void __launch_bounds__(kW * 32, 1) gemv2_kernel(Gemv2Args a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) unsigned long long bars[kWarpsV2][kStages];
-    __shared__ float wss[kWarpsV2][8];
+    __shared__ __align__(8) unsigned long long bars[kW][kStages];
+    __shared__ float wss[kW][8];
     __shared__ float rs[8];
     __shared__ float ninv[8];   // fused RMSNorm: per-token inverse RMS
-    __shared__ int qcnt[kWarpsV2];
+    __shared__ int qcnt[kW];
     // the warp index through a shuffle from lane 0: provably warp-uniform, so the compiler keeps it
     // and everything derived from it (ring and barrier addresses, unit cursors) in uniform registers
     const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0), lane = threadIdx.x & 31, gi = lane >> 2,
@@ -298,19 +301,19 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
     uint8_t* ring = smem + (size_t)warp * ring_bytes;
     const uint32_t ring_s = smem_addr(ring);
     const uint32_t bar0 = smem_addr(&bars[warp][0]);
-    float* red = reinterpret_cast<float*>(smem + (size_t)kWarpsV2 * ring_bytes);
-    uint32_t* xs = reinterpret_cast<uint32_t*>(smem + (size_t)kWarpsV2 * ring_bytes + (size_t)kRedBytesPerTok * M);
+    float* red = reinterpret_cast<float*>(smem + (size_t)kW * ring_bytes);
+    uint32_t* xs = reinterpret_cast<uint32_t*>(smem + (size_t)kW * ring_bytes + (size_t)red_bytes_per_tok(kW) * M);
 
     // this warp's run of units
     const int n = ce - cs;
-    const int u0 = wstart(warp, n);
-    const int n_units = wstart(warp + 1, n) - u0;
+    const int u0 = wstart<kW>(warp, n);
+    const int n_units = wstart<kW>(warp + 1, n) - u0;
     int pq = (cs + u0) / G, pg = (cs + u0) - pq * G;   // producer position
     if (lane == 0) {
         for (int s = 0; s < stages; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * s));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (threadIdx.x < kWarpsV2) qcnt[threadIdx.x] = 0;
+    if (threadIdx.x < kW) qcnt[threadIdx.x] = 0;
     __syncwarp();
     for (int s = 0; s < stages && s < n_units; ++s) {
         if (lane == 0) issue_unit(a, pq, pg, ring_s + s * kUnitBytes, bar0 + 8 * s);
@@ -337,7 +340,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
         for (int m = 0; m < M; ++m) {
             float ss = 0.0f;
             const uint4* xr = reinterpret_cast<const uint4*>(a.x + (int64_t)m * a.ldx);
-            for (int u = threadIdx.x; u < a.K / 8; u += kThreadsV2) {
+            for (int u = threadIdx.x; u < a.K / 8; u += (kW * 32)) {
                 const uint4 v = xr[u];
                 const uint32_t pv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -354,7 +357,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
         __syncthreads();
         if (threadIdx.x < M) {
             float s = 0.0f;
-            for (int w = 0; w < kWarpsV2; ++w) s = __fadd_rn(s, wss[w][threadIdx.x]);
+            for (int w = 0; w < kW; ++w) s = __fadd_rn(s, wss[w][threadIdx.x]);
             ninv[threadIdx.x] = __frsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)a.K), a.eps));
         }
         __syncthreads();
@@ -363,7 +366,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
                 const uint4* xr = reinterpret_cast<const uint4*>(a.x + (int64_t)m * a.ldx);
                 const uint4* wr = reinterpret_cast<const uint4*>(a.norm_w);
                 uint4* outr = reinterpret_cast<uint4*>(a.xn + (int64_t)m * a.ldxn);
-                for (int u = threadIdx.x; u < a.K / 8; u += kThreadsV2) outr[u] = norm_vec(xr[u], wr[u], ninv[m]);
+                for (int u = threadIdx.x; u < a.K / 8; u += (kW * 32)) outr[u] = norm_vec(xr[u], wr[u], ninv[m]);
             }
         }
     }
@@ -371,7 +374,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
         float ss = 0.0f;
         const uint4* xr = reinterpret_cast<const uint4*>(a.x + (int64_t)m * a.ldx);
         uint32_t* xm = xs + (size_t)m * words;
-        for (int u = threadIdx.x; u < a.xg * 8; u += kThreadsV2) {
+        for (int u = threadIdx.x; u < a.xg * 8; u += (kW * 32)) {
             int g = g0 + (u >> 3);
             if (g >= G) g -= G;
             uint4 v = xr[g * 8 + (u & 7)];
@@ -391,7 +394,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
             }
         }
         if (rms && win) {   // the RMS scale needs all of x
-            for (int u = threadIdx.x; u < a.K / 8; u += kThreadsV2) {
+            for (int u = threadIdx.x; u < a.K / 8; u += (kW * 32)) {
                 const uint4 v = xr[u];
                 const uint32_t pv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -413,7 +416,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
         float r = 1.0f;
         if (rms && threadIdx.x < M) {
             float s = 0.0f;
-            for (int w = 0; w < kWarpsV2; ++w) s = __fadd_rn(s, wss[w][threadIdx.x]);
+            for (int w = 0; w < kW; ++w) s = __fadd_rn(s, wss[w][threadIdx.x]);
             r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)a.K), a.eps)));
         }
         rs[threadIdx.x] = r;
@@ -483,7 +486,7 @@ __global__ void __launch_bounds__(kThreadsV2, 1) gemv2_kernel(Gemv2Args a) {
                 phase ^= 1u;
             }
         }
-        park_quad(a, qcnt, red, cq, first_q, cs, ce, cta, C, acc, rs);
+        park_quad<kW>(a, qcnt, red, cq, first_q, cs, ce, cta, C, acc, rs);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -510,8 +513,8 @@ static int gemv2_grid(int U, int G, int sms) {
     return grid;
 }
 
-static size_t gemv2_smem(int stages, int64_t M, int64_t xg) {
-    return (size_t)kWarpsV2 * stages * kUnitBytes + (size_t)kRedBytesPerTok * M + (size_t)xg * 64 * M * 2;
+static size_t gemv2_smem(int warps, int stages, int64_t M, int64_t xg) {
+    return (size_t)warps * stages * kUnitBytes + (size_t)red_bytes_per_tok(warps) * M + (size_t)xg * 64 * M * 2;
 }
 
 // groups of x each CTA stages: all G, or the window of its range when every range is shorter
@@ -520,11 +523,17 @@ static int gemv2_xgroups(int U, int G, int grid) {
     return nmax < G ? nmax : G;
 }
 
-// 3 ring stages when they fit beside the tokens' x, else 2 (0: does not fit at all)
-static int gemv2_stages(int64_t M, int64_t xg) {
-    for (int s = 3; s >= 2; --s)
-        if (gemv2_smem(s, M, xg) <= 220 * 1024) return s;
-    return 0;
+// Warps per CTA and ring stages: 16 warps of 3 stages when they fit beside the tokens' x, else 16 of
+// 2, else 12 warps of 2 (e.g. down_proj's 15360-wide x at 8 tokens, whose window per CTA takes 100 KB);
+// warps 0: does not fit at all.
+struct Gemv2Shape {
+    int warps, stages;
+};
+static Gemv2Shape gemv2_shape(int64_t M, int64_t xg) {
+    const Gemv2Shape tries[] = {{kWarpsV2, 3}, {kWarpsV2, 2}, {12, 2}};
+    for (const Gemv2Shape& t : tries)
+        if (gemv2_smem(t.warps, t.stages, M, xg) <= 220 * 1024) return t;
+    return {0, 0};
 }
 
 bool gemv2_supported(const QmmCall& c) {
@@ -534,19 +543,21 @@ bool gemv2_supported(const QmmCall& c) {
     const int G = (int)(c.w->K / 64);
     const int grid = gemv2_grid((int)units, G, device_sm_count());
     if (grid <= 0) return false;
-    return gemv2_stages(c.M, gemv2_xgroups((int)units, G, grid)) != 0;
+    return gemv2_shape(c.M, gemv2_xgroups((int)units, G, grid)).warps != 0;
 }
 
 void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     static bool attr_set[64] = {false};
     const int dev = current_device();
+    const void* kernels[2][2] = {{reinterpret_cast<const void*>(gemv2_kernel<false, kWarpsV2>),
+                                  reinterpret_cast<const void*>(gemv2_kernel<false, 12>)},
+                                 {reinterpret_cast<const void*>(gemv2_kernel<true, kWarpsV2>),
+                                  reinterpret_cast<const void*>(gemv2_kernel<true, 12>)}};
     if (!attr_set[dev & 63]) {
-        check_cuda(cudaFuncSetAttribute(gemv2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)max_dynamic_smem(reinterpret_cast<const void*>(gemv2_kernel<true>))),
-                   "cudaFuncSetAttribute(gemv2)");
-        check_cuda(cudaFuncSetAttribute(gemv2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)max_dynamic_smem(reinterpret_cast<const void*>(gemv2_kernel<false>))),
-                   "cudaFuncSetAttribute(gemv2)");
+        for (auto& row : kernels)
+            for (const void* k : row)
+                check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_dynamic_smem(k)),
+                           "cudaFuncSetAttribute(gemv2)");
         attr_set[dev & 63] = true;
     }
     const Weight& w = *c.w;
@@ -581,20 +592,22 @@ void launch_gemv2(const QmmCall& c, cudaStream_t st) {
     a.xn = c.norm_w != nullptr ? c.xn : nullptr;
     a.ldxn = c.ldxn;
     a.xg = gemv2_xgroups(a.U, a.G, grid);
-    a.stages = gemv2_stages(a.M, a.xg);
-    if (a.stages == 0) throw Error(G4Q_ERR_RUNTIME, "gemv2: x does not fit in shared memory");
+    const Gemv2Shape shape = gemv2_shape(a.M, a.xg);
+    if (shape.warps == 0) throw Error(G4Q_ERR_RUNTIME, "gemv2: x does not fit in shared memory");
+    a.stages = shape.stages;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreadsV2);
-    cfg.dynamicSmemBytes = gemv2_smem(a.stages, a.M, a.xg);
+    cfg.blockDim = dim3(shape.warps * 32);
+    cfg.dynamicSmemBytes = gemv2_smem(shape.warps, a.stages, a.M, a.xg);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    check_cuda(cudaLaunchKernelEx(&cfg, w.small_scales && !w.subnormal_scales ? gemv2_kernel<true> : gemv2_kernel<false>, a),
-               "gemv2 launch");
+    void* args[] = {&a};
+    const void* k = kernels[w.small_scales && !w.subnormal_scales ? 1 : 0][shape.warps == kWarpsV2 ? 0 : 1];
+    check_cuda(cudaLaunchKernelExC(&cfg, k, args), "gemv2 launch");
 }
 
 }  // namespace g4q

@@ -32,6 +32,9 @@ def test_decode_gemv_baseline_shapes(cuda, oracle, proj, M):
     from helios_b200 import quantized as Q
     N, K = SHAPES[proj]
     qw, x, (ow, os_, ob) = make(oracle, Q, proj, N, K, M, chunk=M)
+    # every BASELINE shape at M <= 8 runs the stream-K GEMV (down_proj at M = 8 with 12 warps per CTA)
+    from helios_b200 import _lib
+    assert qw.qmm_path(M) == (_lib.PATH_GEMV_STREAMK, 0)
     ye, yb = oracle.qmm(u16(x), ow, os_, ob)
     y = Q.quantized_matmul(x, qw)
     assert y.shape == (M, N) and y.dtype == torch.bfloat16
