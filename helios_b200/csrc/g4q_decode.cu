@@ -213,7 +213,8 @@ __device__ __forceinline__ int64_t xbuf_w(const DecodeArgs& a, int p, int tok, i
 
 // Rank partials of the allreduce phase with ordinal ar: word index of (quad q, slot, token tok, row 0),
 // where the partial of rank r's c-th CTA of a quad cut into nc CTA ranges takes slot r * nc + c, so a
-// quad's n_ranks * nc partials are contiguous in rank-major, CTA order (one flattened poll sums them).
+// quad's n_ranks * nc partials are contiguous in rank-major, CTA order (one flattened poll sums them);
+// at 4 and 8 tokens per step rank r's summed partial takes slot r.
 // The buffers rotate over allreduce ordinals: a rank writes buffer j mod 3 again only after every
 // rank has sent allreduce j+2, i.e. after every rank has finished reading allreduce j.
 template <int kM>
@@ -534,16 +535,45 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
     int cf, cl;
     quad_ctas(P, q, C, cf, cl);
     if (kTP && P.src_ranks > 1) {
+        if constexpr (kM >= 4) {
+            // two levels: the finisher polls each token's partials one token after another, so at 4 and
+            // 8 tokens the quad's first CTA sums this rank's CTA partials first (local slots, CTA
+            // order), then sends one rank partial (slot = rank) to every rank and sums the ranks' in
+            // rank order -- n_ranks sources per token to poll instead of n_ranks x (CTAs of the quad)
+            if (!whole) {
+                if (cta != cf) {
 #pragma unroll
-        for (int tok = 0; tok < kM; ++tok)
-            send_partial(a.peer_rp, a.n_ranks, rp_word<kM>(a, P, P.ar, q, a.rank * (cl - cf + 1) + cta - cf, tok),
-                         f[tok].x, f[tok].y, tag);
-        if (cta != cf) return;
-        const int nc = cl - cf + 1;
+                    for (int tok = 0; tok < kM; ++tok) {
+                        unsigned long long* sl = a.slots + slot_w<kM>(a, P, p, q, cta - cf, tok);
+                        st_relaxed(sl + lane, tagged(f[tok].x, tag));
+                        st_relaxed(sl + lane + 32, tagged(f[tok].y, tag));
+                    }
+                    return;
+                }
 #pragma unroll
-        for (int tok = 0; tok < kM; ++tok)   // rank-major, then CTA order: the same bits on every rank
-            f[tok] = poll_sum(a.rp + rp_word<kM>(a, P, P.ar, q, 0, tok), a.n_ranks * nc, kM * 64, tag, f[tok], false,
-                              a.err);
+                for (int tok = 0; tok < kM; ++tok)
+                    f[tok] = poll_sum(a.slots + slot_w<kM>(a, P, p, q, 1, tok), cl - cf, kM * 64, tag, f[tok], true,
+                                      a.err);
+            }
+#pragma unroll
+            for (int tok = 0; tok < kM; ++tok)
+                send_partial(a.peer_rp, a.n_ranks, rp_word<kM>(a, P, P.ar, q, a.rank, tok), f[tok].x, f[tok].y, tag);
+#pragma unroll
+            for (int tok = 0; tok < kM; ++tok)
+                f[tok] = poll_sum(a.rp + rp_word<kM>(a, P, P.ar, q, 0, tok), a.n_ranks, kM * 64, tag, f[tok], false,
+                                  a.err);
+        } else {
+#pragma unroll
+            for (int tok = 0; tok < kM; ++tok)
+                send_partial(a.peer_rp, a.n_ranks, rp_word<kM>(a, P, P.ar, q, a.rank * (cl - cf + 1) + cta - cf, tok),
+                             f[tok].x, f[tok].y, tag);
+            if (cta != cf) return;
+            const int nc = cl - cf + 1;
+#pragma unroll
+            for (int tok = 0; tok < kM; ++tok)   // rank-major, then CTA order: the same bits on every rank
+                f[tok] = poll_sum(a.rp + rp_word<kM>(a, P, P.ar, q, 0, tok), a.n_ranks * nc, kM * 64, tag, f[tok],
+                                  false, a.err);
+        }
     } else if (!whole) {
         if (cta != cf) {
 #pragma unroll

@@ -121,7 +121,7 @@ def test_tensor_parallel_decode_plan_two_gpus(cuda, oracle):
     assert toks[0] == ref["tokens"][0] or abs(vals[0] - ref["values"][0]) <= 0.125
 
 
-def _full_plan_worker(rank, world, port, out_q):
+def _full_plan_worker(rank, world, port, out_q, M=1):
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -134,16 +134,16 @@ def _full_plan_worker(rank, world, port, out_q):
         from helios_b200.quantized import synth_normal
         from helios_b200.stack import StackConfig, SyntheticStack, activation_seed, decode_keys
         cfg = StackConfig(layers=4)
-        st = SyntheticStack(cfg, rank, world, dist.group.WORLD, max_tokens=1)
-        st.build_plan(1, keep_layers=True)
-        h0 = synth_normal(activation_seed(0), (1, cfg.hidden))
-        logits = torch.empty((1, st.v_rows[1] - st.v_rows[0]), dtype=torch.bfloat16, device="cuda")
+        st = SyntheticStack(cfg, rank, world, dist.group.WORLD, max_tokens=M)
+        st.build_plan(M, keep_layers=True)
+        h0 = synth_normal(activation_seed(M), (M, cfg.hidden))
+        logits = torch.empty((M, st.v_rows[1] - st.v_rows[0]), dtype=torch.bfloat16, device="cuda")
         keys, _ = st.decode(h0, logits=logits)
         torch.cuda.synchronize()
         err = _lib.device_error()
         all_keys = [torch.empty_like(keys) for _ in range(world)]
         dist.all_gather(all_keys, keys)
-        outs, lg = st.gather_layer_outputs(1, logits)
+        outs, lg = st.gather_layer_outputs(M, logits)
         if rank == 0:
             # checked in this process: the per-layer outputs are too large for the result pipe while
             # the parent is still joining the ranks
@@ -163,16 +163,18 @@ def _full_plan_worker(rank, world, port, out_q):
         dist.destroy_process_group()
 
 
-def test_tensor_parallel_full_width_plan_every_phase(cuda, oracle):
+@pytest.mark.parametrize("M", [1, 4])
+def test_tensor_parallel_full_width_plan_every_phase(cuda, oracle, M):
     """The tensor-parallel decode plan at the benchmark's full width (4 layers + the 262144-row LM head
-    over 2 GPUs): every phase, the allreduced o/down outputs included, against the oracle on its own
-    gathered GPU input, and the same key on both ranks."""
+    over 2 GPUs), at 1 token and at the MTP-verify width 4 (whose allreduce phases sum each rank's CTA
+    partials on the rank first): every phase, the allreduced o/down outputs included, against the
+    oracle on its own gathered GPU input, and the same keys on both ranks."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
-    mp.start_processes(_full_plan_worker, args=(2, _free_port(), q), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_full_plan_worker, args=(2, _free_port(), q, M), nprocs=2, join=True, start_method="spawn")
     res = [q.get(), q.get()]
     rep, same, _ = next(r for r in res if r[0] is not None)
     assert all(r[2] == 0 for r in res)
