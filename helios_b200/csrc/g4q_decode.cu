@@ -214,7 +214,7 @@ __device__ __forceinline__ int64_t xbuf_w(const DecodeArgs& a, int p, int tok, i
 // Rank partials of the allreduce phase with ordinal ar: word index of (quad q, slot, token tok, row 0),
 // where the partial of rank r's c-th CTA of a quad cut into nc CTA ranges takes slot r * nc + c, so a
 // quad's n_ranks * nc partials are contiguous in rank-major, CTA order (one flattened poll sums them);
-// at 4 and 8 tokens per step rank r's summed partial takes slot r.
+// at 4 and 8 tokens per step, and at 2 on more than two ranks, rank r's summed partial takes slot r.
 // The buffers rotate over allreduce ordinals: a rank writes buffer j mod 3 again only after every
 // rank has sent allreduce j+2, i.e. after every rank has finished reading allreduce j.
 template <int kM>
@@ -534,12 +534,16 @@ __device__ __forceinline__ void park(const DecodeArgs& a, const PhaseDev& P, int
     const uint32_t tag = phase_tag(sh.tag0, p);
     int cf, cl;
     quad_ctas(P, q, C, cf, cl);
+    bool two_level = false;
+    if constexpr (kM >= 4) two_level = true;
+    if constexpr (kM == 2) two_level = a.n_ranks > 2;
     if (kTP && P.src_ranks > 1) {
-        if constexpr (kM >= 4) {
+        if (two_level) {
             // two levels: the finisher polls each token's partials one token after another, so at 4 and
-            // 8 tokens the quad's first CTA sums this rank's CTA partials first (local slots, CTA
-            // order), then sends one rank partial (slot = rank) to every rank and sums the ranks' in
-            // rank order -- n_ranks sources per token to poll instead of n_ranks x (CTAs of the quad)
+            // 8 tokens (and at 2 on more than two ranks) the quad's first CTA sums this rank's CTA
+            // partials first (local slots, CTA order), then sends one rank partial (slot = rank) to
+            // every rank and sums the ranks' in rank order -- n_ranks sources per token to poll
+            // instead of n_ranks x (CTAs of the quad)
             if (!whole) {
                 if (cta != cf) {
 #pragma unroll
