@@ -42,7 +42,8 @@ parity: after every timed region, one decode step of a plan with per-layer outpu
           restatement of the reference's CPU quantized_matmul (oracle/, kind "port") on the same
           metric with all host threads; ranks other than 0 exit without work.
 --trace: after the timed regions, one decode step with the plan's tracing build (globaltimer stamps
-          per CTA and phase) summarised per phase kind on rank 0 (the line's "trace" field).
+          per CTA and phase) summarised per phase kind on rank 0 (the line's "trace" field, and
+          "decode_real_layers.trace" for the real-layer step).
 --case NAME: one small kernel case for an ncu capture (one GPU, a few GB at most; see CASES),
           printing its CUDA-event time per launch.
 """
@@ -602,6 +603,20 @@ def main():
                 "ms_per_step": round(ms_real, 5), "tok_s": round(1e3 / ms_real, 1),
                 "weight_gbs": round(ds.local_weight_bytes() * world / (ms_real * 1e-3) / 1e9, 1),
                 "vs_synthetic_step": round(ms_real / ms, 4), "token": decode_keys(ds.keys[:1])[0][0]}
+        if args.trace:   # the same per-phase timeline summary as the linears-only step's `trace`
+            buf = ds.plan.trace(True)
+            for _ in range(3):
+                ds.decode(h_static)
+            torch.cuda.synchronize()
+            barrier()
+            ds.decode(h_static)
+            torch.cuda.synchronize()
+            assert _lib.device_error() == 0
+            n_ph = 4 * cfg.layers + 1
+            rtr = buf.cpu().view(-1, n_ph, TRACE_WORDS)
+            ds.plan.trace(False)
+            if rank == 0:
+                real["trace"] = trace_summary(rtr.numpy(), cfg.layers)
         ds.free()
 
     # ---- per-phase timeline of one step (the plan's tracing build: globaltimer stamps per CTA and
