@@ -61,3 +61,47 @@ def test_missing_library_fails_loudly(tmp_path):
             _lib.load(tmp_path / "nope.so")
     finally:
         _lib._lib = saved
+
+
+# Public structs whose layout the bindings (ctypes here, a Rust #[repr(C)] mirror for the reference's
+# host) depend on: name -> fields, in declaration order.
+PINNED = {
+    "G4qVersionInfo": ["abi_version", "backend_name", "backend_version"],
+    "G4qWeightInfo": ["rows", "cols", "bits", "group_size", "device_bytes", "device", "fast_path_ok", "error_flags"],
+    "G4qDecodePhase": ["weight", "x", "ldx", "y", "ldy", "flags"],
+    "G4qPhasePrologue": ["post_norm_weight", "residual", "layer_scalar", "norm_weight", "residual_out",
+                         "ld_residual_out", "eps"],
+}
+
+
+def test_struct_layouts_match_the_binding(tmp_path):
+    """Layout pins of the C ABI's structs: sizeof / offsetof from the C compiler on include/g4q.h
+    equal the ctypes binding's, field by field (a binding built from the header cannot drift)."""
+    import shutil
+    import subprocess
+
+    from helios_b200 import _lib
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lines = ['#include "g4q.h"', "#include <stddef.h>", "#include <stdio.h>", "int main(void) {"]
+    for s, fields in PINNED.items():
+        lines.append(f'    printf("{s} size %zu\\n", sizeof({s}));')
+        for f in fields:
+            lines.append(f'    printf("{s} {f} %zu\\n", offsetof({s}, {f}));')
+    lines += ["    return 0;", "}"]
+    src = tmp_path / "pins.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "pins"
+    subprocess.run([cc, "-std=c11", "-Wall", "-Werror", "-I", str(ROOT / "include"), str(src), "-o", str(exe)],
+                   check=True, capture_output=True)
+    got = {}
+    for ln in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        s, f, v = ln.split()
+        got[(s, f)] = int(v)
+    for s, fields in PINNED.items():
+        cls = getattr(_lib, s)
+        assert [f for f, _ in cls._fields_] == fields, s
+        assert got[(s, "size")] == ctypes.sizeof(cls), s
+        for f in fields:
+            assert got[(s, f)] == getattr(cls, f).offset, (s, f)
