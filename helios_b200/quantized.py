@@ -518,8 +518,10 @@ class DecodePlan:
 
     ``phases`` is a list of ``(weight, x, y, flags)``: ``x`` a bf16 CUDA tensor view [M, K] (row stride a
     multiple of 8), ``y`` a bf16/fp32 CUDA tensor view [M, N] or None for the final argmax phase;
-    ``flags`` from QMM_RMS_SCALE / QMM_OUT_F32 / PHASE_ARGMAX / PHASE_ALLREDUCE. Phase i may read
-    phase i-1's output. Tensor addresses are baked into the plan: keep the tensors alive and reuse them.
+    ``flags`` from QMM_RMS_SCALE / QMM_OUT_F32 / PHASE_ARGMAX / PHASE_ALLREDUCE / PHASE_GEGLU (a
+    paired gate|up weight whose y is the [M, rows / 2] GeGLU). Phase i may read phase i-1's output.
+    ``max_tokens``: the tokens of every step, 1, 2, 4 or 8. Tensor addresses are baked into the plan:
+    keep the tensors alive and reuse them.
 
     Tensor parallel: pass ``rank``/``n_ranks`` and the process ``group``; every rank builds the plan of
     its own shards (collectively), the plans exchange their slot buffers by CUDA IPC over the group,
