@@ -751,7 +751,6 @@ G4qStatus g4q_comm_create(int32_t rank, int32_t n_ranks, int64_t max_elems, G4qC
     return guarded("g4q_comm_create", [&] {
         require(out != nullptr, G4Q_ERR_INVALID_ARGUMENT, "requires a non-null out pointer");
         *out = nullptr;
-        (void)device_scratch();
         *out = reinterpret_cast<G4qComm*>(comm_create(rank, n_ranks, max_elems));
     });
 }

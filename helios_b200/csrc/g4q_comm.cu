@@ -274,6 +274,7 @@ void* comm_create(int rank, int n_ranks, int64_t max_elems) {
         throw Error(G4Q_ERR_INVALID_ARGUMENT, "rank must be in [0, n_ranks) with 1 <= n_ranks <= 8");
     if (max_elems <= 0 || max_elems > (1ll << 31))
         throw Error(G4Q_ERR_INVALID_ARGUMENT, "max_elems must be in [1, 2^31]");
+    (void)device_scratch();   // the device error word the allreduce's bounded waits report into
     Comm* c = new (std::nothrow) Comm();
     if (!c) throw Error(G4Q_ERR_MEMORY_GUARD, "host allocation failed");
     c->device = current_device();

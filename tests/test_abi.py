@@ -52,6 +52,49 @@ def test_status_and_message_on_invalid_arguments_without_gpu():
         _lib.call("g4q_runtime_version", None)
 
 
+def test_plan_comm_ipc_and_noalloc_reject_bad_arguments_without_gpu():
+    """Handles, ranks, sizes and pointers are checked on the host before any CUDA call, so every one
+    of these returns G4Q_ERR_INVALID_ARGUMENT with its message on a machine without a GPU."""
+    from helios_b200 import _lib
+    L = _lib.load()
+    bogus = ctypes.cast(ctypes.create_string_buffer(256), ctypes.c_void_p)
+    p = ctypes.c_void_p(256)                        # never dereferenced: validation fails first
+    out, words, nbytes = ctypes.c_void_p(), ctypes.c_int64(), ctypes.c_uint64()
+    cases = [
+        (lambda: L.g4q_decode_plan_run(None, 1, 1e-6, 30.0, 0, None, None, None, None, 0, None),
+         "invalid decode plan handle"),
+        (lambda: L.g4q_decode_plan_run(bogus, 1, 1e-6, 30.0, -1, None, None, None, None, 0, None),
+         "row_offset out of range"),
+        (lambda: L.g4q_decode_plan_free(bogus), "invalid decode plan handle"),
+        (lambda: L.g4q_decode_plan_trace(bogus, None, None), "words must be non-null"),
+        (lambda: L.g4q_decode_plan_trace(bogus, None, ctypes.byref(words)), "invalid decode plan handle"),
+        (lambda: L.g4q_decode_plan_buffers(bogus, ctypes.byref(out), ctypes.byref(nbytes), ctypes.byref(out),
+                                           ctypes.byref(nbytes)), "invalid decode plan handle"),
+        (lambda: L.g4q_decode_plan_create(None, 1, 1, None), "non-null out pointer"),
+        (lambda: L.g4q_decode_plan_create_ex(None, None, 0, 1, 0, 1, ctypes.byref(out)), "at least one phase"),
+        (lambda: L.g4q_comm_create(0, 2, 16, None), "non-null out pointer"),
+        (lambda: L.g4q_comm_create(2, 2, 16, ctypes.byref(out)), "rank must be in [0, n_ranks)"),
+        (lambda: L.g4q_comm_create(0, 9, 16, ctypes.byref(out)), "1 <= n_ranks <= 8"),
+        (lambda: L.g4q_comm_create(0, 2, 0, ctypes.byref(out)), "max_elems must be in [1, 2^31]"),
+        (lambda: L.g4q_comm_free(bogus), "invalid communicator handle"),
+        (lambda: L.g4q_allreduce(bogus, p, 8, 0, None), "invalid communicator handle"),
+        (lambda: L.g4q_ipc_handle(None, None), "non-null pointers"),
+        (lambda: L.g4q_ipc_open(None, None), "non-null pointers"),
+        (lambda: L.g4q_ipc_close(None), "non-null pointer"),
+        (lambda: L.g4q_device_error(None, 0), "non-null code pointer"),
+        (lambda: L.g4q_lm_head_argmax_noalloc(None, None, 16, 64, None, 1, 64, 30.0, 0, 1e-6, 0, None, 0,
+                                              None, None, None, None), "non-null device pointers"),
+        (lambda: L.g4q_lm_head_argmax_noalloc(p, p, 16, 64, p, 17, 64, 30.0, 0, 1e-6, 0, None, 0,
+                                              None, None, None, None), "M must be in [1, 16]"),
+        (lambda: L.g4q_lm_head_argmax_noalloc(p, p, 15, 64, p, 1, 64, 30.0, 0, 1e-6, 0, None, 0,
+                                              None, None, None, None), "positive multiple of 16"),
+        (lambda: L.g4q_dequantize_mlx(None, None, None, 16, 64, 4, 64, 0, None, None), "non-null"),
+    ]
+    for call, message in cases:
+        assert call() == _lib.G4Q_ERR_INVALID_ARGUMENT, message
+        assert message in _lib.last_error(), (message, _lib.last_error())
+
+
 def test_missing_library_fails_loudly(tmp_path):
     from helios_b200 import _lib
     saved = _lib._lib
