@@ -1,6 +1,7 @@
 """CPU: the benchmark's host-side pieces -- the per-phase trace summary and the reference arm's line."""
 import importlib.util
 import json
+import os
 import subprocess
 import sys
 from pathlib import Path
@@ -56,3 +57,13 @@ def test_reference_arm_prints_one_json_line(oracle):
     assert line["cpu_baseline"]["kind"] in ("port", "reference") and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
     assert line["e2e"]["value"] == line["value"]
+
+
+def test_reference_arm_other_ranks_exit_without_work():
+    """Under torchrun only rank 0 runs and prints the reference arm; rank 1 of 2 exits 0 at once."""
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--gpus", "2",
+                        "--steps", "1", "--warmup", "1"], capture_output=True, text=True, timeout=120,
+                       cwd=ROOT, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert not [ln for ln in r.stdout.splitlines() if ln.startswith("{")], r.stdout[-2000:]
