@@ -148,3 +148,77 @@ def test_struct_layouts_match_the_binding(tmp_path):
         assert got[(s, "size")] == ctypes.sizeof(cls), s
         for f in fields:
             assert got[(s, f)] == getattr(cls, f).offset, (s, f)
+
+
+C_HOST = r'''
+#include "g4q.h"
+#include <pthread.h>
+#include <stdio.h>
+#include <string.h>
+
+static int expect(G4qStatus got, G4qStatus want, const char* needle) {
+    char msg[512];
+    if (got != want) { printf("status %d, expected %d\n", (int)got, (int)want); return 1; }
+    if (g4q_get_last_error(msg, sizeof msg) != G4Q_OK) return 1;
+    if (needle && !strstr(msg, needle)) { printf("message '%s' lacks '%s'\n", msg, needle); return 1; }
+    if (!needle && msg[0]) { printf("message '%s' after success\n", msg); return 1; }
+    return 0;
+}
+
+static void* other_thread(void* arg) {
+    char msg[512];
+    int* bad = (int*)arg;
+    g4q_get_last_error(msg, sizeof msg);
+    if (msg[0]) { printf("thread sees '%s'\n", msg); *bad = 1; }
+    *bad |= expect(g4q_decode_plan_free(NULL), G4Q_ERR_INVALID_ARGUMENT, "invalid decode plan handle");
+    return NULL;
+}
+
+int main(void) {
+    G4qVersionInfo v;
+    G4qWeight* w = NULL;
+    pthread_t t;
+    char small[8];
+    int bad = 0;
+    bad |= expect(g4q_runtime_version(&v), G4Q_OK, NULL);
+    if (v.abi_version != G4Q_ABI_VERSION || strcmp(v.backend_name, "g4q_b200") != 0) bad = 1;
+    bad |= expect(g4q_weight_create(64, 128, 4, 64, NULL), G4Q_ERR_INVALID_ARGUMENT, "non-null out pointer");
+    bad |= expect(g4q_weight_create(64, 128, 3, 64, &w), G4Q_ERR_UNSUPPORTED_CONFIG, "bits=3");
+    bad |= expect(g4q_weight_create(60, 128, 4, 64, &w), G4Q_ERR_UNSUPPORTED_CONFIG, "multiple of 16");
+    if (w != NULL) bad = 1;
+    /* the last error is per thread: another thread neither sees nor overwrites this one */
+    if (pthread_create(&t, NULL, other_thread, &bad) != 0 || pthread_join(t, NULL) != 0) return 3;
+    bad |= expect(G4Q_ERR_UNSUPPORTED_CONFIG, G4Q_ERR_UNSUPPORTED_CONFIG, "multiple of 16");
+    /* a short buffer receives a terminated prefix */
+    if (g4q_get_last_error(small, sizeof small) != G4Q_OK || strlen(small) != sizeof small - 1) bad = 1;
+    if (g4q_get_last_error(NULL, 0) != G4Q_ERR_INVALID_ARGUMENT) bad = 1;
+    /* a successful call clears it */
+    bad |= expect(g4q_runtime_version(&v), G4Q_OK, NULL);
+    printf("%s %s: %s\n", v.backend_name, v.backend_version, bad ? "FAIL" : "ok");
+    return bad;
+}
+'''
+
+
+def test_c_host_program_links_and_reads_statuses(tmp_path):
+    """A C host (as the reference's Rust crate or C++ runtime would be) compiled against the header
+    with strict warnings, linked to the library: version, statuses and the per-thread last error,
+    all of which work without a GPU."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+
+    from helios_b200 import _lib
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    so = Path(_lib.load()._name)
+    src = tmp_path / "host.c"
+    src.write_text(C_HOST)
+    exe = tmp_path / "host"
+    subprocess.run([cc, "-std=c11", "-Wall", "-Wextra", "-Werror", "-I", str(ROOT / "include"), str(src),
+                    "-o", str(exe), "-L", str(so.parent), "-lg4q", f"-Wl,-rpath,{so.parent}", "-pthread"],
+                   check=True, capture_output=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.strip().endswith(": ok"), r.stdout
